@@ -1,0 +1,153 @@
+"""tcgen05 GEMM (rgpt_gemm_bf16) against a plain PyTorch fp32 reference.
+
+Tolerance: inputs are bf16, accumulation fp32, so the only differences vs the
+fp32 reference of the same bf16 inputs are summation order and the final bf16
+rounding of bf16 outputs: rel. Frobenius error <= 1e-2 for bf16 outputs and
+<= 1e-4 for fp32 outputs.
+"""
+import pytest
+import torch
+
+from rgpt_b200 import native as nv
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def ref_act(name, x):
+    import torch.nn.functional as F
+    if name == "squared_relu":
+        return torch.relu(x) ** 2
+    if name == "gelu":
+        return F.gelu(x, approximate="tanh")
+    if name == "silu":
+        return F.silu(x)
+    if name == "mish":
+        return F.mish(x)
+    return x
+
+
+def ref_act_grad(name, x):
+    x = x.detach().clone().requires_grad_(True)
+    y = ref_act(name, x)
+    (g,) = torch.autograd.grad(y.sum(), x)
+    return g
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 320), (296, 392, 200), (128, 128, 64), (1024, 2048, 512)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_layouts_store_bf16(cuda, M, N, K, a_mn, b_mn):
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + N + K)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    b = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+    A = a.t().contiguous().t() if a_mn else a  # same values, MN-major storage
+    B = b.t().contiguous().t() if b_mn else b
+    out = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    nv.gemm(A, B, out)
+    ref = a.float() @ b.float().t()
+    assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
+def test_gemm_store_f32_exactish(cuda, a_mn, b_mn):
+    M, N, K = 384, 256, 448
+    g = torch.Generator(device=cuda).manual_seed(1)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    b = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+    A = a.t().contiguous().t() if a_mn else a
+    B = b.t().contiguous().t() if b_mn else b
+    out = torch.empty(M, N, device=cuda, dtype=torch.float32)
+    nv.gemm(A, B, out, epi=nv.EPI_STORE_F32, alpha=0.5)
+    ref = 0.5 * (a.float() @ b.float().t())
+    assert rel_err(out, ref) < 1e-4
+
+
+def test_gemm_weight_grad_splitk_accum(cuda):
+    # dW += dY^T X with the contraction over a long token dim (split-K + atomics)
+    T, Nout, Kin = 8192, 512, 256
+    g = torch.Generator(device=cuda).manual_seed(2)
+    dy = torch.randn(T, Nout, device=cuda, generator=g).bfloat16()
+    x = torch.randn(T, Kin, device=cuda, generator=g).bfloat16()
+    dw = torch.randn(Nout, Kin, device=cuda, generator=g)
+    ref = dw + dy.float().t() @ x.float()
+    nv.gemm(dy.t(), x.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
+    assert rel_err(dw, ref) < 1e-4
+
+
+@pytest.mark.parametrize("act", ["squared_relu", "gelu", "silu", "mish"])
+def test_gemm_act_fwd_bwd(cuda, act):
+    M, N, K = 512, 1024, 256
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    pre = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    post = torch.empty_like(pre)
+    nv.gemm(x, w, pre, epi=nv.EPI_ACT_FWD, act=nv.act_id(act), out2=post)
+    ref_pre = x.float() @ w.float().t()
+    assert rel_err(pre, ref_pre) < 1e-2
+    assert rel_err(post, ref_act(act, ref_pre)) < 2e-2
+    # backward: dpre = (dY @ W2^T) * act'(pre) with W2 [N, Kout] -> here dY [M, 128], W2 [N, 128]
+    dy = torch.randn(M, 128, device=cuda, generator=g).bfloat16()
+    w2 = (torch.randn(N, 128, device=cuda, generator=g) * 0.05).bfloat16()
+    dpre = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    nv.gemm(dy, w2, dpre, epi=nv.EPI_ACT_BWD, act=nv.act_id(act), c=pre)
+    ref = (dy.float() @ w2.float().t()) * ref_act_grad(act, pre.float())
+    assert rel_err(dpre, ref) < 2e-2
+
+
+def test_gemm_resid_colscale(cuda):
+    M, N, K = 1024, 512, 512
+    g = torch.Generator(device=cuda).manual_seed(4)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+    x = torch.randn(M, N, device=cuda, generator=g)
+    ls = torch.rand(N, device=cuda, generator=g)
+    ref = x + (a.float() @ w.float().t()) * ls
+    out = torch.empty_like(x)
+    nv.gemm(a, w, out, epi=nv.EPI_RESID_F32, c=x, colscale=ls)
+    assert rel_err(out, ref) < 1e-5
+    # in place, no scale
+    ref2 = x + a.float() @ w.float().t()
+    nv.gemm(a, w, x, epi=nv.EPI_RESID_F32, c=x)
+    assert rel_err(x, ref2) < 1e-5
+
+
+def test_gemm_batched_poly(cuda):
+    # X' = a*X + (B @ X) batched, with B symmetric, X MN-major as the B operand
+    nb, R, C = 6, 256, 512
+    g = torch.Generator(device=cuda).manual_seed(5)
+    X = (torch.randn(nb, R, C, device=cuda, generator=g) * 0.05).bfloat16()
+    S = torch.randn(nb, R, R, device=cuda, generator=g)
+    Bm = ((S + S.transpose(1, 2)) * 0.05).bfloat16()
+    out = torch.empty_like(X)
+    # logical B operand [N=C, K=R] = X^T per batch -> X.transpose(1,2) has unit stride on N
+    nv.gemm(Bm, X.transpose(1, 2), out, epi=nv.EPI_POLY_BF16, alpha=1.0, beta=3.4445, c=X)
+    ref = 3.4445 * X.float() + Bm.float() @ X.float()
+    assert rel_err(out, ref) < 1e-2
+    # A = X X^T batched (both K-major)
+    A = torch.empty(nb, R, R, device=cuda, dtype=torch.bfloat16)
+    nv.gemm(X, X, A)
+    assert rel_err(A, X.float() @ X.float().transpose(1, 2)) < 1e-2
+
+
+def test_gemm_lm_head_shape(cuda):
+    # vocab-sized N (not a multiple of the 256-wide tile)
+    M, N, K = 2048, 50304, 512
+    g = torch.Generator(device=cuda).manual_seed(6)
+    h = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.02).bfloat16()
+    out = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    nv.gemm(h, w, out)
+    assert rel_err(out, h.float() @ w.float().t()) < 1e-2
+
+
+def test_gemm_rejects_bad_shapes(cuda):
+    a = torch.randn(64, 64, device=cuda).bfloat16()
+    out = torch.empty(64, 64, device=cuda, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="M>=128"):
+        nv.gemm(a, a, out)
