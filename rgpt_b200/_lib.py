@@ -37,6 +37,10 @@ _SIGNATURES: dict[str, list] = {
         _c_vp, _c_ll, _c_ll,  # C, ldc, c_bstride
         _c_vp, _c_int, _c_vp,  # colscale, splitk, stream
     ],
+    "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_attn_bwd_prep": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_attn_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_ll, _c_vp, _c_ll,
+                      _c_int, _c_int, _c_int, _c_int, _c_vp],
 }
 
 _lock = threading.Lock()

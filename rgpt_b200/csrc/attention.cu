@@ -1,0 +1,760 @@
+// Causal flash attention (head_dim 64) on tcgen05 tensor cores, with the G1
+// output gate fused in.
+//
+// Reference semantics (model/attention.py:52-61):
+//   o  = softmax(q k^T / sqrt(64) + causal mask) v       (F.scaled_dot_product_attention)
+//   og = o * gate                                        (G1 gate, gate = sigmoid(...))
+//
+// HBM layouts (token-major, no transposes anywhere):
+//   q, k : qk [B*T, 2*d]   columns [0, d) = q heads, [d, 2d) = k heads (post QK-norm + RoPE)
+//   v    : qkv[B*T, 3*d]   columns [2d, 3d)  (read in place from the QKV projection output)
+//   o, og, gate, do : [B*T, d]
+//   lse, D : [B, H, T] fp32
+// A 4-D TMA map (64, H, T, B) per operand fetches one 128-row x 64-column tile of
+// one head, with rows past T zero-filled.
+//
+// Forward CTA (192 threads) = one 128-query tile of one (b, h):
+//   warp 0 TMA (Q once, then K/V tiles in a 2-deep ring)
+//   warp 1 TMEM alloc + tcgen05.mma: S = Q K^T into a double-buffered TMEM S,
+//          then O_j = P_j V_j into a double-buffered TMEM O
+//   warps 2-5: one thread per query row: online softmax on S (tcgen05.ld), P as
+//          bf16 into 128B-swizzled smem for the P V MMA, O accumulated in registers.
+// Backward CTA = one 128-key tile of one (b, h), looping over query tiles:
+//   S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
+//   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> fp32 atomics).
+#include <cudaTypedefs.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "rgpt.h"
+
+namespace rgpt {
+
+constexpr int ATT_TILE = 128;   // query rows / keys per tile
+constexpr int ATT_D = 64;       // head dim
+constexpr int ATT_THREADS = 192;
+constexpr uint32_t TILE_BYTES = ATT_TILE * ATT_D * 2;  // 16 KB, one 128x64 bf16 tile
+
+int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch,
+                      uint64_t ld_elems, uint64_t bstride_elems, uint32_t box_inner, uint32_t box_outer);
+
+static PFN_cuTensorMapEncodeTiled_v12000 att_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// (64, H, T, B) view of a token-major [B*T, row_stride] bf16 matrix starting at `base`.
+static int make_head_map(CUtensorMap* map, const void* base, int H, int T, int B, long long row_stride) {
+  auto enc = att_encode_fn();
+  if (enc == nullptr) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride * 2) % 16 != 0)
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "attention operand base/row stride not 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)ATT_D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ATT_D * 2, (cuuint64_t)row_stride * 2, (cuuint64_t)T * row_stride * 2};
+  cuuint32_t box[4] = {ATT_D, 1, ATT_TILE, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return rgpt_set_error(RGPT_ERR_INTERNAL, "attention tensor map encode failed (%d)", (int)r);
+  return RGPT_OK;
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Store 8 fp32 values of row `r` (as bf16) into 16-byte chunk `chunk` of a
+// 128-row x 64-column K-major SW128 tile.
+__device__ __forceinline__ void st_sw128_chunk(uint8_t* tile, int r, int chunk, const float* v) {
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(tile + r * 128 + ((chunk ^ (r & 7)) << 4)) = o;
+}
+
+// ============================================================================ forward
+struct AttnFwdParams {
+  int B, T, H, d;
+  float scale_log2;  // softmax scale * log2(e)
+  __nv_bfloat16* o;  // [B*T, d]
+  __nv_bfloat16* og; // [B*T, d] (gated) or null
+  const __nv_bfloat16* gate;  // [B*T, d] or null
+  float* lse;        // [B, H, T] natural-log LSE of the scaled scores
+};
+
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                        // 16 KB
+  uint8_t* sK = sQ + TILE_BYTES;             // 2 x 16 KB
+  uint8_t* sV = sK + 2 * TILE_BYTES;         // 2 x 16 KB
+  uint8_t* sP = sV + 2 * TILE_BYTES;         // 2 buffers x (2 atoms x 16 KB)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * TILE_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;    // [2]
+  uint64_t* o_full = bars + 11;   // [2]
+  uint64_t* o_empty = bars + 13;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_qt = (p.T + ATT_TILE - 1) / ATT_TILE;
+  const int qt = n_qt - 1 - blockIdx.x;  // heaviest (longest causal row) tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int q0 = qt * ATT_TILE;
+  const int last_key = min(q0 + ATT_TILE - 1, p.T - 1);
+  const int nkv = last_key / ATT_TILE + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_4d(sQ, &tmQ, q_full, 0, h, q0, b);
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
+        tma_load_4d(sK + s * TILE_BYTES, &tmK, &kv_full[s], 0, h, j * ATT_TILE, b);
+        tma_load_4d(sV + s * TILE_BYTES, &tmV, &kv_full[s], 0, h, j * ATT_TILE, b);
+      }
+      if (!ok) {
+        mbar_wait(q_full, 0, nullptr);
+        for (int s = 0; s < 2; ++s) mbar_wait(&kv_full[s], 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t IDESC_O = make_idesc_bf16(128, 64, 0, 1);
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      const uint32_t q_addr = smem_u32(sQ);
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&p_full[s], ph, abort_flag)) return false;
+        if (!mbar_wait(&o_empty[s], ph ^ 1, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(sP + s * 2 * TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sV + s * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < ATT_TILE / 16; ++kk) {
+          const uint64_t adesc = make_sw128_desc(p_addr + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = make_sw128_desc(v_addr + kk * 2048, TILE_BYTES, 1024);
+          umma_bf16(tmem + 256 + s * 64, adesc, bdesc, IDESC_O, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[s]);
+        umma_commit(&kv_empty[s]);
+        return true;
+      };
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&kv_full[s], ph, abort_flag) || !mbar_wait(&s_empty[s], ph ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + s * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < ATT_D / 16; ++kk) {
+          umma_bf16(tmem + s * 128, make_sw128_desc(q_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(k_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+      }
+      if (ok) issue_pv(nkv - 1);
+    }
+    __syncwarp();
+  } else {
+    // softmax / epilogue: one thread per query row
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qrow = q0 + r;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    float o_acc[ATT_D];
+#pragma unroll
+    for (int i = 0; i < ATT_D; ++i) o_acc[i] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+    bool ok = true;
+
+    auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
+      int v = 1;
+      if (lane == 0) v = mbar_wait(bar, ph, abort_flag) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, v, 0) != 0;
+    };
+    auto accumulate_o = [&](int i, float alpha) -> bool {
+      const int s = i & 1;
+      if (!wait_all(&o_full[s], (i >> 1) & 1)) return false;
+      tc_fence_after();
+      uint32_t v[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld32(t_lane + 256 + s * 64 + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) o_acc[c * 32 + t] = o_acc[c * 32 + t] * alpha + __uint_as_float(v[t]);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[s]);
+      return true;
+    };
+
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      if (!wait_all(&s_full[s], (j >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (j == nkv - 1);
+      const int kbase = j * ATT_TILE;
+      // pass 1: row max of the scaled, masked scores
+      float mx = -INFINITY;
+      uint32_t v[32];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(t_lane + s * 128 + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int key = kbase + c * 32 + t;
+          float x = __uint_as_float(v[t]) * p.scale_log2;
+          if (diag && (key > qrow || key >= p.T)) x = -INFINITY;
+          mx = fmaxf(mx, x);
+        }
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = exp2f(m_run - m_new);
+      // pass 2: P = exp2(x - m_new) -> bf16 swizzled smem, row sum
+      float sum = 0.f;
+      uint8_t* pbuf = sP + s * 2 * TILE_BYTES;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(t_lane + s * 128 + c * 32, v);
+        tmem_wait_ld();
+        float pv[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int key = kbase + c * 32 + t;
+          float x = __uint_as_float(v[t]) * p.scale_log2;
+          if (diag && (key > qrow || key >= p.T)) x = -INFINITY;
+          pv[t] = exp2f(x - m_new);
+          sum += pv[t];
+        }
+        uint8_t* atom = pbuf + (c >> 1) * TILE_BYTES;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) st_sw128_chunk(atom, r, (c & 1) * 4 + t, pv + 8 * t);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      fence_proxy_async_smem();
+      mbar_arrive(&p_full[s]);
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      if (j >= 1 && !accumulate_o(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok) ok = accumulate_o(nkv - 1, alpha_prev);
+    if (ok && qrow < p.T) {
+      const float inv_l = 1.0f / l_run;
+      const long long row = (long long)b * p.T + qrow;
+      __nv_bfloat16* orow = p.o + row * p.d + h * ATT_D;
+      float ov[ATT_D];
+#pragma unroll
+      for (int i = 0; i < ATT_D; ++i) ov[i] = o_acc[i] * inv_l;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 w;
+        w.x = pack_bf16x2(ov[8 * c + 0], ov[8 * c + 1]);
+        w.y = pack_bf16x2(ov[8 * c + 2], ov[8 * c + 3]);
+        w.z = pack_bf16x2(ov[8 * c + 4], ov[8 * c + 5]);
+        w.w = pack_bf16x2(ov[8 * c + 6], ov[8 * c + 7]);
+        reinterpret_cast<uint4*>(orow)[c] = w;
+      }
+      if (p.og != nullptr) {
+        const uint4* grow = reinterpret_cast<const uint4*>(p.gate + row * p.d + h * ATT_D);
+        uint4* ogrow = reinterpret_cast<uint4*>(p.og + row * p.d + h * ATT_D);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 g = grow[c];
+          uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float2 gf = unpack_bf16x2(gw[e]);
+            // gate the bf16-rounded o, as the reference multiplies the stored attention output
+            ow[e] = pack_bf16x2(bf16_round(ov[8 * c + 2 * e]) * gf.x, bf16_round(ov[8 * c + 2 * e + 1]) * gf.y);
+          }
+          ogrow[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+      // natural-log LSE of the scaled scores
+      p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================ backward prep
+// do = dog * gate; dgate_pre = dog * o * gate * (1 - gate); D = rowsum(do * o)   (8 threads per (token, head))
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dog, const __nv_bfloat16* __restrict__ o,
+                                     const __nv_bfloat16* __restrict__ gate, __nv_bfloat16* __restrict__ dout,
+                                     __nv_bfloat16* __restrict__ dgate_pre, float* __restrict__ Dvec, int B, int T,
+                                     int H, int d) {
+  const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long rowhead = gid >> 3;  // (token, head) index
+  const int part = gid & 7;
+  const long long total = (long long)B * T * H;
+  const bool valid = rowhead < total;
+  const long long tok = valid ? rowhead / H : 0;
+  const int h = valid ? (int)(rowhead % H) : 0;
+  const long long off = tok * d + h * ATT_D + part * 8;
+  float dsum = 0.f;
+  if (valid) {
+    uint4 vg = *reinterpret_cast<const uint4*>(dog + off);
+    uint4 vo = *reinterpret_cast<const uint4*>(o + off);
+    uint32_t g4[4] = {vg.x, vg.y, vg.z, vg.w}, o4[4] = {vo.x, vo.y, vo.z, vo.w};
+    uint32_t do4[4], dg4[4];
+    uint4 vgate = gate ? *reinterpret_cast<const uint4*>(gate + off) : make_uint4(0, 0, 0, 0);
+    uint32_t gt4[4] = {vgate.x, vgate.y, vgate.z, vgate.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 gg = unpack_bf16x2(g4[e]);
+      float2 oo = unpack_bf16x2(o4[e]);
+      float2 gt = gate ? unpack_bf16x2(gt4[e]) : make_float2(1.f, 1.f);
+      float d0 = gg.x * gt.x, d1 = gg.y * gt.y;
+      do4[e] = pack_bf16x2(d0, d1);
+      float2 dr = unpack_bf16x2(do4[e]);  // D uses the rounded dO that the MMAs see
+      dsum += dr.x * oo.x + dr.y * oo.y;
+      dg4[e] = pack_bf16x2(gg.x * oo.x * gt.x * (1.f - gt.x), gg.y * oo.y * gt.y * (1.f - gt.y));
+    }
+    *reinterpret_cast<uint4*>(dout + off) = make_uint4(do4[0], do4[1], do4[2], do4[3]);
+    if (gate) *reinterpret_cast<uint4*>(dgate_pre + off) = make_uint4(dg4[0], dg4[1], dg4[2], dg4[3]);
+  }
+  dsum += __shfl_xor_sync(0xffffffffu, dsum, 1);
+  dsum += __shfl_xor_sync(0xffffffffu, dsum, 2);
+  dsum += __shfl_xor_sync(0xffffffffu, dsum, 4);
+  if (valid && part == 0) {
+    const long long b = tok / T, t = tok % T;
+    Dvec[(b * H + h) * T + t] = dsum;
+  }
+}
+
+// ============================================================================ backward
+struct AttnBwdParams {
+  int B, T, H, d;
+  float scale;       // softmax scale (1/sqrt(64))
+  float scale_log2;  // scale * log2(e)
+  const float* lse;  // [B, H, T] natural log
+  const float* Dvec; // [B, H, T]
+  float* dq;         // [B*T, d] fp32, accumulated with atomics (caller zeroes)
+  float* dk;         // [B*T, dk_stride] fp32
+  long long dk_stride;
+  __nv_bfloat16* dv; // [B*T, dv_stride] bf16
+  long long dv_stride;
+};
+
+__global__ void __launch_bounds__(ATT_THREADS, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    AttnBwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;                     // 16 KB
+  uint8_t* sV = sK + TILE_BYTES;          // 16 KB
+  uint8_t* sQ = sV + TILE_BYTES;          // 2 x 16 KB
+  uint8_t* sDO = sQ + 2 * TILE_BYTES;     // 2 x 16 KB
+  uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T  : 2 atoms (queries 0-63, 64-127) x 16 KB
+  uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T : 2 atoms x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * TILE_BYTES);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* sdp_full = bars + 5;
+  uint64_t* ds_ready = bars + 6;  // P^T, dS^T written, S^T/dP^T TMEM read
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_empty = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kt = blockIdx.x;  // heaviest key tiles (most query tiles) have the lowest index
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int k0 = kt * ATT_TILE;
+  const int n_qt = (p.T + ATT_TILE - 1) / ATT_TILE;
+  const int qt0 = kt;  // query tiles qt >= kt see these keys
+  const int nq = n_qt - qt0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(ds_ready, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: S^T [0,128) dP^T [128,256) dV [256,320) dK [320,384) dQ [384,448)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      bool ok = true;
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_4d(sK, &tmK, kv_full, 0, h, k0, b);
+      tma_load_4d(sV, &tmV, kv_full, 0, h, k0, b);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int s = i & 1;
+        if (!mbar_wait(&qd_empty[s], ((i >> 1) & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int qrow0 = (qt0 + i) * ATT_TILE;
+        mbar_arrive_expect_tx(&qd_full[s], 2 * TILE_BYTES);
+        tma_load_4d(sQ + s * TILE_BYTES, &tmQ, &qd_full[s], 0, h, qrow0, b);
+        tma_load_4d(sDO + s * TILE_BYTES, &tmDO, &qd_full[s], 0, h, qrow0, b);
+      }
+      if (!ok) {
+        mbar_wait(kv_full, 0, nullptr);
+        for (int s = 0; s < 2; ++s) mbar_wait(&qd_full[s], 0, nullptr);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, 0, 0);   // K Q^T, V dO^T
+      constexpr uint32_t IDESC_KV = make_idesc_bf16(128, 64, 0, 1);   // P^T dO, dS^T Q  (B MN-major)
+      constexpr uint32_t IDESC_Q = make_idesc_bf16(128, 64, 1, 1);    // dS K (A, B MN-major)
+      bool ok = mbar_wait(kv_full, 0, abort_flag);
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
+      for (int i = 0; i < nq && ok; ++i) {
+        const int s = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&qd_full[s], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        // S^T / dP^T TMEM is free: the softmax threads read it before arriving on ds_ready(i-1),
+        // which this thread waited on in the previous iteration.
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES), do_addr = smem_u32(sDO + s * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < ATT_D / 16; ++kk) {
+          umma_bf16(tmem + 0, make_sw128_desc(k_addr + kk * 32, 16, 1024), make_sw128_desc(q_addr + kk * 32, 16, 1024),
+                    IDESC_S, kk > 0 ? 1u : 0u);
+          umma_bf16(tmem + 128, make_sw128_desc(v_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(ds_ready, i & 1, abort_flag) || !mbar_wait(dq_empty, (i & 1) ^ 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < ATT_TILE / 16; ++kk) {
+          const uint32_t a_off = (kk >> 2) * TILE_BYTES + (kk & 3) * 32;  // K-major over queries
+          // dV += P^T dO ; dK += dS^T Q   (B operands: the same smem tiles, read MN-major)
+          umma_bf16(tmem + 256, make_sw128_desc(p_addr + a_off, 16, 1024),
+                    make_sw128_desc(do_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tmem + 320, make_sw128_desc(ds_addr + a_off, 16, 1024),
+                    make_sw128_desc(q_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
+          // dQ = dS K : A = dS^T read MN-major (rows = keys), B = K read MN-major
+          umma_bf16(tmem + 384, make_sw128_desc(ds_addr + kk * 2048, TILE_BYTES, 1024),
+                    make_sw128_desc(k_addr + kk * 2048, TILE_BYTES, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[s]);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row (S^T / dP^T / dV / dK) and query row (dQ)
+    const int key = k0 + r;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    bool ok = true;
+    auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
+      int v = 1;
+      if (lane == 0) v = mbar_wait(bar, ph, abort_flag) ? 1 : 0;
+      return __shfl_sync(0xffffffffu, v, 0) != 0;
+    };
+    const float* lse_bh = p.lse + ((long long)b * p.H + h) * p.T;
+    const float* D_bh = p.Dvec + ((long long)b * p.H + h) * p.T;
+    for (int i = 0; i < nq; ++i) {
+      const int qrow0 = (qt0 + i) * ATT_TILE;
+      if (!wait_all(sdp_full, i & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = (i == 0);
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(t_lane + 0 + c * 32, sv);
+        tmem_ld32(t_lane + 128 + c * 32, dv);
+        tmem_wait_ld();
+        float pr[32], ds[32];
+#pragma unroll
+        for (int t = 0; t < 32; ++t) {
+          const int q = qrow0 + c * 32 + t;
+          // lse / D are the same address for every lane of the warp: one broadcast load each
+          const bool live = q < p.T && key < p.T && !(diag && q < key);
+          const int qc = q < p.T ? q : p.T - 1;
+          float pv = live ? exp2f(__uint_as_float(sv[t]) * p.scale_log2 - __ldg(lse_bh + qc) * 1.4426950408889634f)
+                          : 0.f;
+          pr[t] = pv;
+          ds[t] = pv * (__uint_as_float(dv[t]) - __ldg(D_bh + qc)) * p.scale;
+        }
+        uint8_t* patom = sP + (c >> 1) * TILE_BYTES;
+        uint8_t* datom = sDS + (c >> 1) * TILE_BYTES;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          st_sw128_chunk(patom, r, (c & 1) * 4 + t, pr + 8 * t);
+          st_sw128_chunk(datom, r, (c & 1) * 4 + t, ds + 8 * t);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(ds_ready);
+      if (!wait_all(dq_full, i & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      // dQ rows: TMEM lane r = query row qrow0 + r
+      const int q = qrow0 + r;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_lane + 384 + c * 32, v);
+        tmem_wait_ld();
+        if (q < p.T) {
+          float4* dst = reinterpret_cast<float4*>(p.dq + ((long long)b * p.T + q) * p.d + h * ATT_D + c * 32);
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            atomicAdd(dst + t, make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                                           __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3])));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+    }
+    // dK, dV rows (key-major) once every query tile has been folded in. Every lane runs the
+    // warp-collective TMEM loads; only the stores are predicated on the row being inside T.
+    if (ok) {
+      const bool valid = key < p.T;
+      const long long row = (long long)b * p.T + (valid ? key : 0);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(t_lane + 256 + c * 32, v);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + c * 32);
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            dst[t] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
+                                pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
+                                pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
+                                pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
+        }
+        tmem_ld32(t_lane + 320 + c * 32, v);
+        tmem_wait_ld();
+        if (valid) {
+          float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + c * 32);
+#pragma unroll
+          for (int t = 0; t < 8; ++t)
+            dkd[t] = make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                                 __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+constexpr uint32_t FWD_SMEM = 9 * TILE_BYTES + 256 + 1024;
+constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 256 + 1024;
+
+}  // namespace rgpt
+
+using namespace rgpt;
+
+static int check_attn_args(int B, int T, int H, int d) {
+  if (B < 1 || T < 1 || H < 1 || d != H * ATT_D)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention needs head_dim 64 and d == H*64 (B=%d T=%d H=%d d=%d)", B, T,
+                          H, d);
+  return RGPT_OK;
+}
+
+extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse, int B,
+                             int T, int H, int d, void* stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int st = rgpt_check_device(dev);
+  if (st) return st;
+  if ((st = check_attn_args(B, T, H, d))) return st;
+  if (o == nullptr || lse == nullptr || (og != nullptr && gate == nullptr))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention outputs missing (og needs gate)");
+  CUtensorMap tq, tk, tv;
+  const __nv_bfloat16* qkb = reinterpret_cast<const __nv_bfloat16*>(qk);
+  const __nv_bfloat16* qkvb = reinterpret_cast<const __nv_bfloat16*>(qkv);
+  if ((st = make_head_map(&tq, qkb, H, T, B, 2LL * d))) return st;
+  if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d))) return st;
+  if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d))) return st;
+  AttnFwdParams p;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.d = d;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o);
+  p.og = reinterpret_cast<__nv_bfloat16*>(og);
+  p.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
+  p.lse = lse;
+  static bool attr[64] = {false};
+  if (!attr[dev]) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
+      return rgpt_check_launch("attn_fwd set smem");
+    attr[dev] = true;
+  }
+  dim3 grid((T + ATT_TILE - 1) / ATT_TILE, H, B);
+  attn_fwd_kernel<<<grid, ATT_THREADS, FWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  return rgpt_check_launch("attn_fwd_kernel");
+}
+
+extern "C" int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,
+                                  float* Dvec, int B, int T, int H, int d, void* stream) {
+  int st = check_attn_args(B, T, H, d);
+  if (st) return st;
+  if (gate != nullptr && dgate_pre == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gate needs dgate_pre");
+  const long long threads = (long long)B * T * H * 8;
+  const int block = 256;
+  const long long grid = (threads + block - 1) / block;
+  attn_bwd_prep_kernel<<<(unsigned)grid, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dog), reinterpret_cast<const __nv_bfloat16*>(o),
+      reinterpret_cast<const __nv_bfloat16*>(gate), reinterpret_cast<__nv_bfloat16*>(dout),
+      reinterpret_cast<__nv_bfloat16*>(dgate_pre), Dvec, B, T, H, d);
+  return rgpt_check_launch("attn_bwd_prep_kernel");
+}
+
+extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, const float* lse, const float* Dvec,
+                             float* dq, float* dk, long long dk_stride, void* dv, long long dv_stride, int B, int T,
+                             int H, int d, void* stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int st = rgpt_check_device(dev);
+  if (st) return st;
+  if ((st = check_attn_args(B, T, H, d))) return st;
+  if ((reinterpret_cast<uintptr_t>(dq) & 15) || (reinterpret_cast<uintptr_t>(dk) & 15) ||
+      (reinterpret_cast<uintptr_t>(dv) & 15) || (dk_stride % 4) || (dv_stride % 8))
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "attention gradient buffers must be 16-byte aligned");
+  CUtensorMap tq, tk, tv, tdo;
+  const __nv_bfloat16* qkb = reinterpret_cast<const __nv_bfloat16*>(qk);
+  const __nv_bfloat16* qkvb = reinterpret_cast<const __nv_bfloat16*>(qkv);
+  if ((st = make_head_map(&tq, qkb, H, T, B, 2LL * d))) return st;
+  if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d))) return st;
+  if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d))) return st;
+  if ((st = make_head_map(&tdo, dout, H, T, B, (long long)d))) return st;
+  AttnBwdParams p;
+  p.B = B;
+  p.T = T;
+  p.H = H;
+  p.d = d;
+  p.scale = 0.125f;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  p.lse = lse;
+  p.Dvec = Dvec;
+  p.dq = dq;
+  p.dk = dk;
+  p.dk_stride = dk_stride;
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  p.dv_stride = dv_stride;
+  static bool attr[64] = {false};
+  if (!attr[dev]) {
+    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) != cudaSuccess)
+      return rgpt_check_launch("attn_bwd set smem");
+    attr[dev] = true;
+  }
+  dim3 grid((T + ATT_TILE - 1) / ATT_TILE, H, B);
+  attn_bwd_kernel<<<grid, ATT_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, p);
+  return rgpt_check_launch("attn_bwd_kernel");
+}

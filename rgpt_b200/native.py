@@ -79,3 +79,45 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
               d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
               ptr(colscale), splitk, _lib.stream_ptr(out.device))
     return out
+
+
+# ----------------------------------------------------------------------------- attention
+def _check(t, dtype, name):
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must have unit column stride")
+
+
+def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: torch.Tensor,
+             og: torch.Tensor | None, lse: torch.Tensor, B: int, T: int, H: int) -> None:
+    """Causal attention over token-major q/k (qk [B*T, 2d]) and v (qkv[:, 2d:3d]).
+
+    Writes o [B*T, d] (bf16), og = o * gate (if gate given) and lse [B, H, T] (fp32)."""
+    d = H * 64
+    for t, n in ((qk, "qk"), (qkv, "qkv"), (o, "o")):
+        _check(t, torch.bfloat16, n)
+    if qk.shape != (B * T, 2 * d) or qkv.shape != (B * T, 3 * d) or o.shape != (B * T, d):
+        raise ValueError("attention shapes do not match [B*T, 2d] / [B*T, 3d] / [B*T, d]")
+    if lse.dtype != torch.float32 or lse.numel() != B * H * T:
+        raise ValueError("lse must be fp32 [B, H, T]")
+    _lib.call("rgpt_attn_fwd", ptr(qk), ptr(qkv), ptr(gate), ptr(o), ptr(og), ptr(lse), B, T, H, d,
+              _lib.stream_ptr(o.device))
+
+
+def attn_bwd_prep(dog: torch.Tensor, o: torch.Tensor, gate: torch.Tensor | None, do: torch.Tensor,
+                  dgate_pre: torch.Tensor | None, D: torch.Tensor, B: int, T: int, H: int) -> None:
+    """do = dog*gate, dgate_pre = dog*o*gate*(1-gate), D = rowsum(do*o) per (token, head)."""
+    d = H * 64
+    _lib.call("rgpt_attn_bwd_prep", ptr(dog), ptr(o), ptr(gate), ptr(do), ptr(dgate_pre), ptr(D), B, T, H, d,
+              _lib.stream_ptr(o.device))
+
+
+def attn_bwd(qk: torch.Tensor, qkv: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, D: torch.Tensor,
+             dq: torch.Tensor, dk: torch.Tensor, dv: torch.Tensor, B: int, T: int, H: int) -> None:
+    """dq (fp32, accumulated: caller zeroes), dk (fp32) and dv (bf16, may be a strided column view)."""
+    d = H * 64
+    if dq.dtype != torch.float32 or dk.dtype != torch.float32 or dv.dtype != torch.bfloat16:
+        raise TypeError("dq/dk must be fp32 and dv bf16")
+    _lib.call("rgpt_attn_bwd", ptr(qk), ptr(qkv), ptr(do), ptr(lse), ptr(D), ptr(dq), ptr(dk), dk.stride(0),
+              ptr(dv), dv.stride(0), B, T, H, d, _lib.stream_ptr(do.device))
