@@ -47,14 +47,16 @@ enum RgptEpilogue {
   RGPT_EPI_ACCUM_F32 = 2,  /* D f32 += alpha*acc (split-K allowed: fp32 atomics)    */
   RGPT_EPI_ACT_FWD = 3,    /* D bf16 = alpha*acc (pre), D2 bf16 = act(alpha*acc)    */
   RGPT_EPI_ACT_BWD = 4,    /* D bf16 = alpha*acc * act'(C), C bf16 (pre)            */
-  RGPT_EPI_RESID_F32 = 5,  /* D f32 = C f32 + alpha*acc*colscale[n] (colscale opt.) */
+  RGPT_EPI_RESID_F32 = 5,  /* D f32 = C f32 + alpha*acc*colscale[n] (colscale opt.);
+                              D2 f32 (optional) = alpha*acc, the unscaled branch output */
   RGPT_EPI_POLY_BF16 = 6   /* D bf16 = beta*C + alpha*acc, C bf16                   */
 };
 enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4 };
 
-/* Requirements: M >= 128, N >= 128, K >= 64; 16-byte aligned base pointers;
+/* Requirements: M, N, K >= 1 (tiles past the edges are zero-filled / masked); 16-byte aligned base pointers;
  * leading dimensions and batch strides multiples of 8 elements (16 bytes).
- * splitk: 0 = automatic (only for ACCUM_F32), 1 = none, >1 = explicit (ACCUM_F32 only). */
+ * splitk: 0 = automatic (only for ACCUM_F32), 1 = none, >1 = explicit (ACCUM_F32 only).
+ * alpha_dev: optional device scalar; the effective alpha is alpha * (*alpha_dev). */
 int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bstride,
                    const void* B, int b_mn_major, long long ldb, long long b_bstride,
                    int M, int N, int K, int batch,
@@ -62,7 +64,100 @@ int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bst
                    void* D, long long ldd, long long d_bstride,
                    void* D2, long long ldd2, long long d2_bstride,
                    const void* C, long long ldc, long long c_bstride,
-                   const float* colscale, int splitk, void* stream);
+                   const float* colscale, int splitk, const float* alpha_dev, void* stream);
+
+
+/* ------------------------------------------------------------------ attention
+ * Causal softmax attention, head_dim 64, scale 1/8, token-major operands:
+ *   qk  [B*T, 2d] bf16 (q heads | k heads, after QK norm + RoPE), qkv [B*T, 3d] bf16 (v = cols [2d,3d)),
+ *   gate/o/og/dout/dgate_pre [B*T, d] bf16, lse/Dvec [B, H, T] fp32.
+ * Replaces F.scaled_dot_product_attention(is_causal=True) and the G1 gate multiply,
+ * model/attention.py:56-61 (forward) and their autograd backward. */
+int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse,
+                  int B, int T, int H, int d, void* stream);
+/* dout = dog*gate; dgate_pre = dog*o*gate*(1-gate); Dvec = rowsum(dout*o). gate may be null (ungated). */
+int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,
+                       float* Dvec, int B, int T, int H, int d, void* stream);
+/* dq [B*T, d] fp32 is ACCUMULATED (caller zeroes it); dk fp32 and dv bf16 are written with row strides. */
+int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, const float* lse, const float* Dvec,
+                  float* dq, float* dk, long long dk_stride, void* dv, long long dv_stride,
+                  int B, int T, int H, int d, void* stream);
+
+/* ------------------------------------------------------------------ norms
+ * y = x * s(sum x^2) * affine over rows of length d. Kinds follow model/norm.py. */
+enum RgptNormKind {
+  RGPT_NORM_IDENTITY = 0,
+  RGPT_NORM_RMS_AFFINE = 1, /* RMSNorm (Gemma, (1+w)), model/norm.py:8-34          */
+  RGPT_NORM_RMS = 2,        /* functional_rms_norm (eps = FLT_EPSILON), :37-38     */
+  RGPT_NORM_L2_TEMP = 3,    /* L2Norm (learned temp), :44-51                       */
+  RGPT_NORM_L2 = 4,         /* functional_l2_norm, :54-55                          */
+  RGPT_NORM_ELASTIC = 5,    /* HybridElasticNorm, :58-95                           */
+  RGPT_NORM_ELASTICBALL = 6,/* ElasticBallNorm / DualElasticBallNorm, :97-141      */
+  RGPT_NORM_HYPERBALL = 7   /* HyperballNorm / functional_hyperball_norm, :40-42,156-162 */
+};
+/* Residual-stream norm: x fp32 [M, d] -> y bf16 [M, d]; stat[M] = s (optional).
+ * With qout != null also computes the 2-way q_head, qout[M,2] = y @ qw^T + qb (model/gpt.py:107-109).
+ * d in {128, 256, 512, 1024, 2048}. Replaces RMSNorm.forward & co (model/norm.py). */
+int rgpt_rownorm_fwd(const float* x, void* y, float* stat, const float* w, float temp, int kind, float eps,
+                     float alpha, int M, int d, const float* qw, const float* qb, float* qout, void* stream);
+/* Norm backward fused with the residual-gradient add (model/transformer_block.py:43-57):
+ *   g_out = g_in + dx; g_bf16 = bf16(g_out * ls); dls += sum_rows g_out*raw; dw += sum_rows dy*x*s.
+ * q_head mode (dq != null): dy = dq @ qw, plus dqw += dq^T h, dqb += sum dq. Optional pointers may be null. */
+int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w, float temp, int kind, float eps, float alpha,
+                     int M, int d, const float* g_in, float* g_out, void* g_bf16, const float* ls,
+                     const float* raw, float* dls, float* dw, float* dtemp, const float* dq, const float* qw,
+                     const void* h, float* dqw, float* dqb, void* stream);
+
+/* ------------------------------------------------------------------ QKV prep
+ * Per (token, head): QK norm (QKNorm, model/norm.py:182-204), G1 gate sigmoid(q_n Wg^T + bg)
+ * (model/attention.py:45-48, gate_proj shared by all heads), RoPE (model/rope.py:38-57).
+ * qkv [M, 3d] bf16 -> qk [M, 2d] bf16, gate [M, d] bf16. inv_freq[32] as model/rope.py:11.
+ * sq/sk are constant post-scales (asymmetric hyperball 1.0/1.1; otherwise 1). */
+int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* gate, const float* wg, const float* bg,
+                      const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq, const float* wk,
+                      float tq, float tk, float sq, float sk, int M, int T, int H, void* stream);
+/* Backward: dq, dk fp32 [M, d] (grads of the roped q, k), dgp bf16 [M, d] (grad of the gate
+ * pre-activation) -> dqkv q/k column blocks (bf16); dwg/dbg (and dwq/dwk, dtq/dtk) ACCUMULATED. */
+int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const void* dgp, void* dqkv,
+                      const float* wg, float* dwg, float* dbg, float* dwq, float* dwk, float* dtq, float* dtk,
+                      const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq, const float* wk,
+                      float tq, float tk, float sq, float sk, int M, int T, int H, void* stream);
+
+/* ------------------------------------------------------------------ embedding / loss
+ * nn.Embedding forward (model/gpt.py:95) and its backward (dx rows ACCUMULATED into demb). */
+int rgpt_embedding_fwd(const long long* ids, const float* emb, float* x, int M, int d, int V, void* stream);
+int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M, int d, int V, void* stream);
+/* Cross entropy over bf16 logits rows (F.cross_entropy with ignore_index, trainer.py:148) plus the
+ * row argmax (model/gpt.py:119-120). scale_buf[2] = {grad_scale/count, count}; loss_out = mean loss.
+ * write_grad: logits are overwritten in place by bf16 (softmax - onehot) * grad_scale / count. */
+int rgpt_cross_entropy(void* logits, long long ld, int M, int V, const long long* labels, int ignore_index,
+                       float grad_scale, float* loss_rows, int* argmax, float* scale_buf, float* loss_out,
+                       int write_grad, void* stream);
+/* rGPT halting losses (model/gpt.py:105-141, trainer.py:150-162): q [R, M, 2], argmax [R, M].
+ * losses[0] += halt BCE mean, losses[1] += q_continue BCE mean; dq = grad_scale * d(total)/dq. */
+int rgpt_halt_losses(const float* q, const int* argmax, const long long* labels, int R, int M, float grad_scale,
+                     float* dq, float* losses, void* stream);
+
+/* ------------------------------------------------------------------ optimizer */
+typedef struct RgptAdamwTensor {
+  float* p; const float* g; float* m; float* v; unsigned short* shadow; long long n;
+} RgptAdamwTensor;
+typedef struct RgptMuonTensor {
+  float* param; const float* grad; unsigned short* mom; unsigned short* shadow;
+} RgptMuonTensor;
+/* foreach_adamw_step (optimizer.py:80-116) over a device table of tensors split into chunks
+ * (chunk_tensor[i], chunk_start[i]); shadow (bf16 copy of p) optional per tensor. */
+int rgpt_adamw(const RgptAdamwTensor* table, const int* chunk_tensor, const long long* chunk_start, int n_chunks,
+               int chunk_elems, float lr, float wd, float beta1, float beta2, float eps, int step, void* stream);
+/* muon_update's momentum/Nesterov/transposition (optimizer.py:51-69, :23-26) for n same-shape [R, C]
+ * matrices into the bf16 NS stack X (zero-padded, leading dim ldx); sumsq[n] ACCUMULATES ||X||_F^2. */
+int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, void* X, long long x_bstride, int ldx,
+                   float beta, int nesterov, float* sumsq, void* stream);
+/* X /= max(||X||_F, 1e-7) per matrix (optimizer.py:31-32). */
+int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, int cols, int n, const float* sumsq, void* stream);
+/* p = p*(1 - lr*wd) - muon_lr * bf16(X*scale) (optimizer.py:209-227); shadow = bf16(p). */
+int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C, const void* X, long long x_bstride, int ldx,
+                    float lr, float wd, float muon_lr, float scale, void* stream);
 
 #ifdef __cplusplus
 }

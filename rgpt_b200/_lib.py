@@ -35,8 +35,29 @@ _SIGNATURES: dict[str, list] = {
         _c_vp, _c_ll, _c_ll,  # D, ldd, d_bstride
         _c_vp, _c_ll, _c_ll,  # D2, ldd2, d2_bstride
         _c_vp, _c_ll, _c_ll,  # C, ldc, c_bstride
-        _c_vp, _c_int, _c_vp,  # colscale, splitk, stream
+        _c_vp, _c_int, _c_vp, _c_vp,  # colscale, splitk, alpha_dev, stream
     ],
+    "rgpt_rownorm_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
+                         _c_vp, _c_vp, _c_vp, _c_vp],
+    "rgpt_rownorm_bwd": [_c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
+                         _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+                         _c_vp, _c_vp],
+    "rgpt_qkv_prep_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp,
+                          _c_float, _c_float, _c_float, _c_float, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_qkv_prep_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
+                          _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float, _c_float, _c_float,
+                          _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_embedding_fwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_embedding_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_cross_entropy": [_c_vp, _c_ll, _c_int, _c_int, _c_vp, _c_int, _c_float, _c_vp, _c_vp, _c_vp, _c_vp,
+                           _c_int, _c_vp],
+    "rgpt_halt_losses": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_float, _c_vp, _c_vp, _c_vp],
+    "rgpt_adamw": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_float, _c_float, _c_float, _c_float, _c_float, _c_int,
+                   _c_vp],
+    "rgpt_muon_prep": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_int, _c_vp, _c_vp],
+    "rgpt_ns_scale": [_c_vp, _c_ll, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp],
+    "rgpt_muon_apply": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_float, _c_float,
+                        _c_float, _c_vp],
     "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_attn_bwd_prep": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_attn_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_ll, _c_vp, _c_ll,
@@ -82,11 +103,18 @@ def last_error() -> str:
     return buf.value.decode(errors="replace")
 
 
-def call(name: str, *args) -> None:
+# Kernels each entry point enqueues (rgpt_cross_entropy: up to 3, counted by its wrapper).
+_KERNELS_PER_CALL = {"rgpt_last_error": 0, "rgpt_device_error": 0, "rgpt_version": 0}
+launch_count = 0  # native kernels enqueued by this process (read by the benchmark)
+
+
+def call(name: str, *args, kernels: int | None = None) -> None:
     """Invoke entry point `name`; raise RuntimeError on a non-zero status."""
+    global launch_count
     rc = getattr(load(), name)(*args)
     if rc != 0:
         raise RuntimeError(f"{name} failed (status {rc}): {last_error()}")
+    launch_count += _KERNELS_PER_CALL.get(name, 1) if kernels is None else kernels
 
 
 def device_error() -> int:

@@ -46,6 +46,7 @@ struct EpiParams {
   const void* c;
   long long ldc, c_bstride;
   const float* colscale;
+  const float* alpha_dev;  // optional device scalar multiplying alpha (loss-gradient scale)
 };
 
 constexpr int GEMM_BM = 128;
@@ -74,8 +75,9 @@ __device__ __forceinline__ void decode_unit(int u, const GemmShape& sh, int& b, 
 __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const GemmShape& sh, int b, int gm, int gn0,
                                                const uint32_t (&r)[32]) {
   float v[32];
+  const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * ep.alpha;
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
   const bool full = (gn0 + 32 <= sh.N);
   const int ncols = full ? 32 : (sh.N - gn0);
 
@@ -194,6 +196,16 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const GemmSh
     case RGPT_EPI_RESID_F32: {
       const float* c = reinterpret_cast<const float*>(ep.c) + b * ep.c_bstride + (long long)gm * ep.ldc + gn0;
       float* d = reinterpret_cast<float*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
+      if (ep.d2 != nullptr) {  // raw branch output (before scale and residual), for the layer-scale gradient
+        float* d2 = reinterpret_cast<float*>(ep.d2) + b * ep.d2_bstride + (long long)gm * ep.ldd2 + gn0;
+        if (full) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<float4*>(d2)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+          for (int j = 0; j < ncols; ++j) d2[j] = v[j];
+        }
+      }
       if (full) {
         const float4* c4 = reinterpret_cast<const float4*>(c);
         float4* d4 = reinterpret_cast<float4*>(d);
@@ -304,20 +316,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], L::STAGE_BYTES);
+          // MN-major operands arrive as 64-wide sub-boxes; a sub-box lying wholly past M (or N)
+          // is not loaded: its smem only feeds output rows/columns the epilogue never stores.
+          const int a_sub = A_MN ? min(GEMM_BM / 64, (sh.M - mt * GEMM_BM + 63) / 64) : 1;
+          const int b_sub = B_MN ? min(BN / 64, (sh.N - nt * BN + 63) / 64) : 1;
+          const uint32_t bytes = (A_MN ? a_sub * (64 * GEMM_BK * 2) : L::A_BYTES) +
+                                 (B_MN ? b_sub * (64 * GEMM_BK * 2) : L::B_BYTES);
+          mbar_arrive_expect_tx(&full_bar[stage], bytes);
           const int k0 = kb * GEMM_BK;
           uint8_t* a_dst = sA + stage * L::A_BYTES;
           uint8_t* b_dst = sB + stage * L::B_BYTES;
           if (A_MN) {
-#pragma unroll
-            for (int i = 0; i < GEMM_BM / 64; ++i)
+            for (int i = 0; i < a_sub; ++i)
               tma_load_3d(a_dst + i * (64 * GEMM_BK * 2), &tmA, &full_bar[stage], mt * GEMM_BM + i * 64, k0, b);
           } else {
             tma_load_3d(a_dst, &tmA, &full_bar[stage], k0, mt * GEMM_BM, b);
           }
           if (B_MN) {
-#pragma unroll
-            for (int i = 0; i < BN / 64; ++i)
+            for (int i = 0; i < b_sub; ++i)
               tma_load_3d(b_dst + i * (64 * GEMM_BK * 2), &tmB, &full_bar[stage], nt * BN + i * 64, k0, b);
           } else {
             tma_load_3d(b_dst, &tmB, &full_bar[stage], k0, nt * BN, b);
@@ -481,14 +497,14 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
                               int b_mn_major, long long ldb, long long b_bstride, int M, int N, int K, int batch,
                               int epi, int act, float alpha, float beta, void* D, long long ldd, long long d_bstride,
                               void* D2, long long ldd2, long long d2_bstride, const void* C, long long ldc,
-                              long long c_bstride, const float* colscale, int splitk, void* stream) {
+                              long long c_bstride, const float* colscale, int splitk, const float* alpha_dev, void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
   if (st) return st;
   if (batch < 1) batch = 1;
-  if (M < GEMM_BM || K < GEMM_BK || N < 128)
-    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M>=128, N>=128, K>=64 (got M=%d N=%d K=%d)", M, N, K);
+  if (M < 1 || N < 1 || K < 1)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M, N, K >= 1 (got M=%d N=%d K=%d)", M, N, K);
   if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_POLY_BF16)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown epilogue %d", epi);
   if (D == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm output pointer is null");
@@ -498,15 +514,15 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "output leading dim / pointer not 16-byte aligned");
   if (epi == RGPT_EPI_ACT_FWD && (D2 == nullptr || ldd2 % 8 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "ACT_FWD needs an aligned second output");
+  if (epi == RGPT_EPI_RESID_F32 && D2 != nullptr && (ldd2 % 4 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "RESID_F32 raw output must be 16-byte aligned");
   if ((epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_RESID_F32 || epi == RGPT_EPI_POLY_BF16) &&
       (C == nullptr || ldc % vec != 0 || (reinterpret_cast<uintptr_t>(C) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "epilogue input C missing or not 16-byte aligned");
   if (colscale != nullptr && (reinterpret_cast<uintptr_t>(colscale) & 15) != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "colscale must be 16-byte aligned");
-  if (N % 8 != 0 && (epi != RGPT_EPI_STORE_F32 && epi != RGPT_EPI_ACCUM_F32))
-    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "bf16 outputs need N %% 8 == 0 (N=%d)", N);
 
-  const int BN = (N >= 256) ? 256 : 128;
+  const int BN = (N > 128) ? 256 : 128;
   GemmShape sh;
   sh.M = M;
   sh.N = N;
@@ -560,6 +576,7 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   ep.ldc = ldc;
   ep.c_bstride = c_bstride;
   ep.colscale = colscale;
+  ep.alpha_dev = alpha_dev;
 
   const int grid = sh.num_units < nsm ? sh.num_units : nsm;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

@@ -1,0 +1,1041 @@
+// Bandwidth-bound row kernels of the training step.
+//
+//   rownorm_fwd      residual-stream norm (fp32 in, bf16 out) with an optional fused
+//                    2-output q_head (rGPT halting logits)            model/norm.py, model/gpt.py:107-109
+//   rownorm_bwd      norm backward fused with the residual-gradient add, the bf16 copy
+//                    of the gradient scaled by the next branch's layer scale, the norm
+//                    weight grad and the layer-scale grad              model/transformer_block.py:43-57
+//   qkv_prep_fwd/bwd QK-norm + G1 gate (sigmoid(q_n Wg^T + b)) + RoPE per (token, head)
+//                                                                      model/attention.py:38-54, model/rope.py
+//   embedding_fwd/bwd                                                  model/gpt.py:95
+//   cross_entropy    row-wise logsumexp, loss, argmax and in-place bf16 dlogits  trainer.py:148, model/gpt.py:119-120
+//   halt_losses      the rGPT q-head BCE losses and their gradients   model/gpt.py:105-141, trainer.py:150-162
+//
+// Norm family (y = x * s(S) * a, S = sum x^2 over the row, a = affine):
+//   RMS_AFFINE  Gemma RMSNorm, s = rsqrt(S/d + eps), a = 1 + w          model/norm.py:21-34
+//   RMS         F.rms_norm with eps = FLT_EPSILON                       model/norm.py:37-38
+//   L2_TEMP     s = 1/(sqrt(S) + eps), a = temp                         model/norm.py:50-51
+//   L2          s = 1/(sqrt(S) + eps)                                   model/norm.py:54-55
+//   ELASTIC     h = sqrt(d) rsqrt(max(S, eps)); s = h if h < 1 else h^alpha   model/norm.py:83-95
+//   ELASTICBALL s = (sqrt(d) / sqrt(S + eps))^alpha                     model/norm.py:118-132
+//   HYPERBALL   s = rsqrt(1 + S/d)                                      model/norm.py:40-42
+// Backward: dx = s (a.dy) + 2 s'(S) (sum a.dy.x) x.
+#include <math.h>
+
+#include "common.cuh"
+#include "rgpt.h"
+
+namespace rgpt {
+
+struct NS2 {
+  float s, ds;
+};
+
+__device__ __forceinline__ NS2 norm_scale(int kind, float S, int d, float eps, float alpha) {
+  NS2 r;
+  switch (kind) {
+    case RGPT_NORM_RMS_AFFINE:
+    case RGPT_NORM_RMS: {
+      const float v = S / d + eps;
+      r.s = rsqrtf(v);
+      r.ds = -0.5f * r.s / v / d;
+      break;
+    }
+    case RGPT_NORM_L2_TEMP:
+    case RGPT_NORM_L2: {
+      const float n = sqrtf(S);
+      r.s = 1.0f / (n + eps);
+      r.ds = n > 0.f ? -r.s * r.s / (2.0f * n) : 0.f;
+      break;
+    }
+    case RGPT_NORM_ELASTIC: {
+      const float Sc = fmaxf(S, eps);
+      const float hs = sqrtf((float)d) * rsqrtf(Sc);
+      const float dh = (S >= eps) ? -hs / (2.0f * Sc) : 0.f;
+      if (hs < 1.0f) {
+        r.s = hs;
+        r.ds = dh;
+      } else {
+        r.s = powf(hs, alpha);
+        r.ds = alpha * powf(hs, alpha - 1.0f) * dh;
+      }
+      break;
+    }
+    case RGPT_NORM_ELASTICBALL: {
+      const float v = S + eps;
+      r.s = powf((float)d / v, 0.5f * alpha);
+      r.ds = -0.5f * alpha * r.s / v;
+      break;
+    }
+    case RGPT_NORM_HYPERBALL: {
+      const float v = 1.0f + S / d;
+      r.s = rsqrtf(v);
+      r.ds = -0.5f * r.s / v / d;
+      break;
+    }
+    default:
+      r.s = 1.f;
+      r.ds = 0.f;
+  }
+  return r;
+}
+
+// ============================================================================ residual norm
+// One warp per row; each lane owns NV float4 (d = 128 * NV).
+template <int NV>
+__global__ void rownorm_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, float* __restrict__ stat,
+                                   const float* __restrict__ w, float temp, int kind, float eps, float alpha, int M,
+                                   int d, const float* __restrict__ qw, const float* __restrict__ qb,
+                                   float* __restrict__ qout) {
+  const int warps = blockDim.x >> 5;
+  const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * d);
+  float4 v[NV];
+  float S = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    v[i] = xr[lane + 32 * i];
+    S += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+  }
+  S = warp_sum(S);
+  const NS2 ns = norm_scale(kind, S, d, eps, alpha);
+  if (stat) stat[row] = ns.s;
+  float q0 = 0.f, q1 = 0.f;
+  uint2* yr = reinterpret_cast<uint2*>(y + row * d);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    float4 a = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (kind == RGPT_NORM_RMS_AFFINE) {
+      float4 ww = reinterpret_cast<const float4*>(w)[lane + 32 * i];
+      a = make_float4(1.f + ww.x, 1.f + ww.y, 1.f + ww.z, 1.f + ww.w);
+    } else if (kind == RGPT_NORM_L2_TEMP) {
+      a = make_float4(temp, temp, temp, temp);
+    }
+    float4 o = make_float4(v[i].x * ns.s * a.x, v[i].y * ns.s * a.y, v[i].z * ns.s * a.z, v[i].w * ns.s * a.w);
+    yr[lane + 32 * i] = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+    if (qout) {
+      // q_head sees the same rounded activations the lm_head GEMM sees
+      const float ox = bf16_round(o.x), oy = bf16_round(o.y), oz = bf16_round(o.z), ow = bf16_round(o.w);
+      float4 w0 = reinterpret_cast<const float4*>(qw)[c / 4];
+      float4 w1 = reinterpret_cast<const float4*>(qw + d)[c / 4];
+      q0 += ox * w0.x + oy * w0.y + oz * w0.z + ow * w0.w;
+      q1 += ox * w1.x + oy * w1.y + oz * w1.z + ow * w1.w;
+    }
+  }
+  if (qout) {
+    q0 = warp_sum(q0);
+    q1 = warp_sum(q1);
+    if (lane == 0) {
+      qout[row * 2 + 0] = q0 + qb[0];
+      qout[row * 2 + 1] = q1 + qb[1];
+    }
+  }
+}
+
+// Backward. dy = grad of the norm output (fp32) or, in q_head mode (dq != null),
+// dy = dq[row,0]*qw[0,:] + dq[row,1]*qw[1,:]. Then
+//   g_out = g_in + dx          (fp32, may alias g_in; g_in may be null = 0)
+//   g_bf16 = bf16(g_out * ls)  (optional; ls optional)
+//   dls  += g_out * raw        (optional: layer-scale grad of the branch that produced raw)
+//   dw   += dy * x * s         (RMS_AFFINE weight grad)     dtemp += sum(dy * x * s) (L2_TEMP)
+//   dqw  += dq^T h, dqb += dq  (q_head mode, h = the forward norm output in bf16)
+template <int NV, bool QM>
+__global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+                                   const float* __restrict__ w, float temp, int kind, float eps, float alpha, int M,
+                                   int d, const float* __restrict__ g_in, float* __restrict__ g_out,
+                                   __nv_bfloat16* __restrict__ g_bf16, const float* __restrict__ ls,
+                                   const float* __restrict__ raw, float* __restrict__ dls, float* __restrict__ dw,
+                                   float* __restrict__ dtemp, const float* __restrict__ dq,
+                                   const float* __restrict__ qw, const __nv_bfloat16* __restrict__ h,
+                                   float* __restrict__ dqw, float* __restrict__ dqb) {
+  extern __shared__ float red[];  // per-CTA column partials: [d] dw, [d] dls, [2d] dqw
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const bool need_dw = (dw != nullptr && kind == RGPT_NORM_RMS_AFFINE);
+  const bool need_dls = (dls != nullptr && raw != nullptr);
+  constexpr bool qmode = QM;
+  for (int i = threadIdx.x; i < 4 * d; i += blockDim.x) red[i] = 0.f;
+  __syncthreads();
+  float dtemp_acc = 0.f, dqb0 = 0.f, dqb1 = 0.f;
+  // column partials owned by this lane, accumulated over the rows this warp visits
+  float4 pdw[NV], pdls[NV], pq0[QM ? NV : 1], pq1[QM ? NV : 1];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) pdw[i] = pdls[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < (QM ? NV : 1); ++i) pq0[i] = pq1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto affine = [&](int i) -> float4 {
+    if (kind == RGPT_NORM_RMS_AFFINE) {
+      float4 ww = reinterpret_cast<const float4*>(w)[lane + 32 * i];
+      return make_float4(1.f + ww.x, 1.f + ww.y, 1.f + ww.z, 1.f + ww.w);
+    }
+    if (kind == RGPT_NORM_L2_TEMP) return make_float4(temp, temp, temp, temp);
+    return make_float4(1.f, 1.f, 1.f, 1.f);
+  };
+
+  for (long long row = (long long)blockIdx.x * warps + wid; row < M; row += (long long)gridDim.x * warps) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * d);
+    float4 xv[NV], dv[NV];
+    float S = 0.f;
+    float q0 = 0.f, q1 = 0.f;
+    if (qmode) {
+      q0 = dq[row * 2 + 0];
+      q1 = dq[row * 2 + 1];
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      xv[i] = xr[lane + 32 * i];
+      S += xv[i].x * xv[i].x + xv[i].y * xv[i].y + xv[i].z * xv[i].z + xv[i].w * xv[i].w;
+      if (qmode) {
+        float4 w0 = reinterpret_cast<const float4*>(qw)[lane + 32 * i];
+        float4 w1 = reinterpret_cast<const float4*>(qw + d)[lane + 32 * i];
+        dv[i] = make_float4(q0 * w0.x + q1 * w1.x, q0 * w0.y + q1 * w1.y, q0 * w0.z + q1 * w1.z,
+                            q0 * w0.w + q1 * w1.w);
+      } else {
+        dv[i] = reinterpret_cast<const float4*>(dy + row * d)[lane + 32 * i];
+      }
+    }
+    S = warp_sum(S);
+    const NS2 ns = norm_scale(kind, S, d, eps, alpha);
+    float c = 0.f, xdy = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float4 av = affine(i);
+      c += av.x * dv[i].x * xv[i].x + av.y * dv[i].y * xv[i].y + av.z * dv[i].z * xv[i].z + av.w * dv[i].w * xv[i].w;
+      xdy += dv[i].x * xv[i].x + dv[i].y * xv[i].y + dv[i].z * xv[i].z + dv[i].w * xv[i].w;
+    }
+    c = warp_sum(c);
+    const float k2 = 2.0f * ns.ds * c;
+    if (kind == RGPT_NORM_L2_TEMP) dtemp_acc += warp_sum(xdy) * ns.s;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float4 av = affine(i);
+      float4 g = make_float4(ns.s * av.x * dv[i].x + k2 * xv[i].x, ns.s * av.y * dv[i].y + k2 * xv[i].y,
+                             ns.s * av.z * dv[i].z + k2 * xv[i].z, ns.s * av.w * dv[i].w + k2 * xv[i].w);
+      if (g_in) {
+        float4 gi = reinterpret_cast<const float4*>(g_in + row * d)[lane + 32 * i];
+        g.x += gi.x;
+        g.y += gi.y;
+        g.z += gi.z;
+        g.w += gi.w;
+      }
+      reinterpret_cast<float4*>(g_out + row * d)[lane + 32 * i] = g;
+      if (g_bf16) {
+        float4 s4 = ls ? reinterpret_cast<const float4*>(ls)[lane + 32 * i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        reinterpret_cast<uint2*>(g_bf16 + row * d)[lane + 32 * i] =
+            make_uint2(pack_bf16x2(g.x * s4.x, g.y * s4.y), pack_bf16x2(g.z * s4.z, g.w * s4.w));
+      }
+      if (need_dls) {
+        float4 rv = reinterpret_cast<const float4*>(raw + row * d)[lane + 32 * i];
+        pdls[i].x += g.x * rv.x;
+        pdls[i].y += g.y * rv.y;
+        pdls[i].z += g.z * rv.z;
+        pdls[i].w += g.w * rv.w;
+      }
+      if (need_dw) {
+        pdw[i].x += dv[i].x * xv[i].x * ns.s;
+        pdw[i].y += dv[i].y * xv[i].y * ns.s;
+        pdw[i].z += dv[i].z * xv[i].z * ns.s;
+        pdw[i].w += dv[i].w * xv[i].w * ns.s;
+      }
+      if constexpr (QM) if (dqw) {
+        uint2 hv = reinterpret_cast<const uint2*>(h + row * d)[lane + 32 * i];
+        float2 h01 = unpack_bf16x2(hv.x), h23 = unpack_bf16x2(hv.y);
+        pq0[i].x += q0 * h01.x;
+        pq0[i].y += q0 * h01.y;
+        pq0[i].z += q0 * h23.x;
+        pq0[i].w += q0 * h23.y;
+        pq1[i].x += q1 * h01.x;
+        pq1[i].y += q1 * h01.y;
+        pq1[i].z += q1 * h23.x;
+        pq1[i].w += q1 * h23.y;
+      }
+    }
+    dqb0 += q0;
+    dqb1 += q1;
+  }
+  // fold lane partials into the CTA's shared partials, then one atomic per column per CTA
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c0 = 4 * (lane + 32 * i);
+    if (need_dw) {
+      atomicAdd(&red[c0 + 0], pdw[i].x);
+      atomicAdd(&red[c0 + 1], pdw[i].y);
+      atomicAdd(&red[c0 + 2], pdw[i].z);
+      atomicAdd(&red[c0 + 3], pdw[i].w);
+    }
+    if (need_dls) {
+      atomicAdd(&red[d + c0 + 0], pdls[i].x);
+      atomicAdd(&red[d + c0 + 1], pdls[i].y);
+      atomicAdd(&red[d + c0 + 2], pdls[i].z);
+      atomicAdd(&red[d + c0 + 3], pdls[i].w);
+    }
+    if constexpr (QM) if (dqw) {
+      atomicAdd(&red[2 * d + c0 + 0], pq0[i].x);
+      atomicAdd(&red[2 * d + c0 + 1], pq0[i].y);
+      atomicAdd(&red[2 * d + c0 + 2], pq0[i].z);
+      atomicAdd(&red[2 * d + c0 + 3], pq0[i].w);
+      atomicAdd(&red[3 * d + c0 + 0], pq1[i].x);
+      atomicAdd(&red[3 * d + c0 + 1], pq1[i].y);
+      atomicAdd(&red[3 * d + c0 + 2], pq1[i].z);
+      atomicAdd(&red[3 * d + c0 + 3], pq1[i].w);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    if (need_dw) atomicAdd(&dw[i], red[i]);
+    if (need_dls) atomicAdd(&dls[i], red[d + i]);
+    if (qmode && dqw) {
+      atomicAdd(&dqw[i], red[2 * d + i]);
+      atomicAdd(&dqw[d + i], red[3 * d + i]);
+    }
+  }
+  if (lane == 0) {
+    if (kind == RGPT_NORM_L2_TEMP && dtemp) atomicAdd(dtemp, dtemp_acc);
+    if (qmode && dqb) {
+      atomicAdd(&dqb[0], dqb0);
+      atomicAdd(&dqb[1], dqb1);
+    }
+  }
+}
+
+// ============================================================================ QKV prep
+// One thread per (token, head). Reads the raw q, k of the QKV projection, applies
+// the QK norm, the G1 gate and RoPE, and writes:
+//   qk   [M, 2d]  (roped normalised q | k, bf16)  -- the attention operands
+//   gate [M, d]   sigmoid(q_n Wg^T + bg)          -- gate_proj is shared by every head
+struct QkNormArgs {
+  int kind;
+  float eps, alpha;
+  const float* wq;  // RMS_AFFINE weights (64) for q / k, or null
+  const float* wk;
+  float tq, tk;     // L2_TEMP temps
+  float sq, sk;     // constant post-scales (asymmetric hyperball: 1.0 / 1.1)
+};
+
+__device__ __forceinline__ void load_row64(const __nv_bfloat16* p, float* v) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 u = reinterpret_cast<const uint4*>(p)[c];
+    float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), e = unpack_bf16x2(u.z), f = unpack_bf16x2(u.w);
+    v[8 * c + 0] = a.x;
+    v[8 * c + 1] = a.y;
+    v[8 * c + 2] = b.x;
+    v[8 * c + 3] = b.y;
+    v[8 * c + 4] = e.x;
+    v[8 * c + 5] = e.y;
+    v[8 * c + 6] = f.x;
+    v[8 * c + 7] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store_row64(__nv_bfloat16* p, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    reinterpret_cast<uint4*>(p)[c] =
+        make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
+                   pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
+}
+
+// affine factor of the QK norm for element i
+__device__ __forceinline__ float qk_affine(const QkNormArgs& a, bool is_q, int i) {
+  if (a.kind == RGPT_NORM_RMS_AFFINE) return 1.0f + (is_q ? a.wq[i] : a.wk[i]);
+  if (a.kind == RGPT_NORM_L2_TEMP) return is_q ? a.tq : a.tk;
+  return 1.0f;
+}
+
+__device__ __forceinline__ void rope_fwd64(float* v, const float* cs, const float* sn) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float a = v[i], b = v[i + 32];
+    v[i] = a * cs[i] - b * sn[i];
+    v[i + 32] = b * cs[i] + a * sn[i];
+  }
+}
+
+__device__ __forceinline__ void rope_bwd64(float* v, const float* cs, const float* sn) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float a = v[i], b = v[i + 32];
+    v[i] = a * cs[i] + b * sn[i];
+    v[i + 32] = b * cs[i] - a * sn[i];
+  }
+}
+
+__global__ void __launch_bounds__(128) qkv_prep_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                                           __nv_bfloat16* __restrict__ qk,
+                                                           __nv_bfloat16* __restrict__ gate,
+                                                           const float* __restrict__ wg, const float* __restrict__ bg,
+                                                           const float* __restrict__ inv_freq, QkNormArgs na, int M,
+                                                           int T, int H) {
+  __shared__ float sW[64 * 64];
+  __shared__ float sB[64];
+  __shared__ float sF[32];
+  const bool gated = (wg != nullptr);
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) sW[i] = gated ? wg[i] : 0.f;
+  if (threadIdx.x < 64) sB[threadIdx.x] = gated ? bg[threadIdx.x] : 0.f;
+  if (threadIdx.x < 32) sF[threadIdx.x] = inv_freq[threadIdx.x];
+  __syncthreads();
+  const long long rh = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (rh >= (long long)M * H) return;
+  const long long tok = rh / H;
+  const int h = (int)(rh % H);
+  const int d = H * 64;
+  const int t = (int)(tok % T);
+  float cs[32], sn[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float ang = (float)t * sF[i];
+    sincosf(ang, &sn[i], &cs[i]);
+  }
+  float v[64];
+  // ---- q
+  load_row64(qkv + tok * 3 * d + h * 64, v);
+  if (na.kind != RGPT_NORM_IDENTITY) {
+    float S = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) S += v[i] * v[i];
+    const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = v[i] * ns.s * qk_affine(na, true, i) * na.sq;
+  }
+  if (gated) {
+    __nv_bfloat16* grow = gate + tok * d + h * 64;
+#pragma unroll 1
+    for (int j0 = 0; j0 < 64; j0 += 8) {
+      float gv[8];
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) {
+        const float4* wr = reinterpret_cast<const float4*>(sW + (j0 + jj) * 64);
+        float acc = sB[j0 + jj];
+#pragma unroll
+        for (int i4 = 0; i4 < 16; ++i4) {
+          float4 w4 = wr[i4];
+          acc += v[4 * i4] * w4.x + v[4 * i4 + 1] * w4.y + v[4 * i4 + 2] * w4.z + v[4 * i4 + 3] * w4.w;
+        }
+        gv[jj] = 1.0f / (1.0f + expf(-acc));
+      }
+      reinterpret_cast<uint4*>(grow)[j0 / 8] =
+          make_uint4(pack_bf16x2(gv[0], gv[1]), pack_bf16x2(gv[2], gv[3]), pack_bf16x2(gv[4], gv[5]),
+                     pack_bf16x2(gv[6], gv[7]));
+    }
+  }
+  rope_fwd64(v, cs, sn);
+  store_row64(qk + tok * 2 * d + h * 64, v);
+  // ---- k
+  load_row64(qkv + tok * 3 * d + d + h * 64, v);
+  if (na.kind != RGPT_NORM_IDENTITY) {
+    float S = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) S += v[i] * v[i];
+    const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) v[i] = v[i] * ns.s * qk_affine(na, false, i) * na.sk;
+  }
+  rope_fwd64(v, cs, sn);
+  store_row64(qk + tok * 2 * d + d + h * 64, v);
+}
+
+// Backward of qkv_prep. One thread per (token, head); a CTA of 128 rows also
+// reduces the gate-weight gradient dWg = sum_rows dgp^T q_n (64x64) through smem.
+//   dq, dk : fp32 [M, d] grads of the roped q / k;   dgp : bf16 [M, d] grad of the gate pre-activation
+//   dqkv   : bf16 [M, 3d], q and k column blocks written here (v is written by the attention backward)
+__global__ void __launch_bounds__(128) qkv_prep_bwd_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ dq, const float* __restrict__ dk,
+    const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv, const float* __restrict__ wg,
+    float* __restrict__ dwg, float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk,
+    float* __restrict__ dtq, float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M,
+    int T, int H) {
+  extern __shared__ float qsm[];
+  float* sW = qsm;                                                     // [64*64]
+  float* sF = sW + 64 * 64;                                            // [32]
+  float (*sG)[65] = reinterpret_cast<float (*)[65]>(sF + 32);          // [128][65] dgp rows of this tile
+  float (*sQn)[65] = reinterpret_cast<float (*)[65]>(sF + 32 + 128 * 65);  // [128][65] q_n rows of this tile
+  const bool gated = (wg != nullptr);
+  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) sW[i] = gated ? wg[i] : 0.f;
+  if (threadIdx.x < 32) sF[threadIdx.x] = inv_freq[threadIdx.x];
+  // dWg block owned by this thread: row j = tid/2, columns (tid&1)*32 .. +32
+  const int own_j = threadIdx.x >> 1, own_i0 = (threadIdx.x & 1) * 32;
+  float acc_w[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) acc_w[i] = 0.f;
+  float acc_b = 0.f;
+  const int d = H * 64;
+  const long long rows = (long long)M * H;
+  const int lane = threadIdx.x & 31;
+  __syncthreads();
+
+  for (long long base = (long long)blockIdx.x * 128; base < rows; base += (long long)gridDim.x * 128) {
+    const long long rh = base + threadIdx.x;
+    const bool valid = rh < rows;
+    const long long tok = valid ? rh / H : 0;
+    const int h = valid ? (int)(rh % H) : 0;
+    const int t = (int)(tok % T);
+    float cs[32], sn[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) sincosf((float)t * sF[i], &sn[i], &cs[i]);
+    float x[64], g[64];
+    // ------------------------------------------------ q
+    if (valid) {
+      load_row64(qkv + tok * 3 * d + h * 64, x);
+      const float4* src = reinterpret_cast<const float4*>(dq + tok * d + h * 64);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float4 u = src[c];
+        g[4 * c] = u.x;
+        g[4 * c + 1] = u.y;
+        g[4 * c + 2] = u.z;
+        g[4 * c + 3] = u.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) x[i] = g[i] = 0.f;
+    }
+    rope_bwd64(g, cs, sn);  // g = d q_n (before the gate contribution)
+    NS2 ns{1.f, 0.f};
+    if (na.kind != RGPT_NORM_IDENTITY) {
+      float S = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) S += x[i] * x[i];
+      ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+    }
+    // stage q_n and dgp rows for the dWg reduction, add the gate path into g
+    if (gated) {
+      float gp[64];
+      if (valid) {
+        load_row64(dgp + tok * d + h * 64, gp);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) gp[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        sG[threadIdx.x][i] = gp[i];
+        sQn[threadIdx.x][i] = x[i] * ns.s * qk_affine(na, true, i) * na.sq;
+      }
+      // d q_n += dgp @ Wg  (Wg row j is the weight vector of gate output j)
+#pragma unroll 1
+      for (int j = 0; j < 64; ++j) {
+        const float gj = gp[j];
+        const float4* wr = reinterpret_cast<const float4*>(sW + j * 64);
+#pragma unroll
+        for (int i4 = 0; i4 < 16; ++i4) {
+          float4 w4 = wr[i4];
+          g[4 * i4] += gj * w4.x;
+          g[4 * i4 + 1] += gj * w4.y;
+          g[4 * i4 + 2] += gj * w4.z;
+          g[4 * i4 + 3] += gj * w4.w;
+        }
+      }
+    }
+    // norm backward (affine a, post-scale sq); identity norm has s = 1, s' = 0
+    {
+      float c = 0.f, xdy = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float a = qk_affine(na, true, i) * na.sq;
+        c += a * g[i] * x[i];
+        xdy += g[i] * x[i];
+      }
+      const float k2 = 2.0f * ns.ds * c;
+      if (na.kind == RGPT_NORM_RMS_AFFINE && dwq) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float v = warp_sum(valid ? g[i] * x[i] * ns.s : 0.f);
+          if (lane == 0) atomicAdd(&dwq[i], v);
+        }
+      }
+      if (na.kind == RGPT_NORM_L2_TEMP && dtq) {
+        float v = warp_sum(valid ? xdy * ns.s : 0.f);
+        if (lane == 0) atomicAdd(dtq, v);
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) g[i] = ns.s * qk_affine(na, true, i) * na.sq * g[i] + k2 * x[i];
+    }
+    if (valid) store_row64(dqkv + tok * 3 * d + h * 64, g);
+    // ------------------------------------------------ k
+    if (valid) {
+      load_row64(qkv + tok * 3 * d + d + h * 64, x);
+      const float4* src = reinterpret_cast<const float4*>(dk + tok * d + h * 64);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float4 u = src[c];
+        g[4 * c] = u.x;
+        g[4 * c + 1] = u.y;
+        g[4 * c + 2] = u.z;
+        g[4 * c + 3] = u.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) x[i] = g[i] = 0.f;
+    }
+    rope_bwd64(g, cs, sn);
+    {
+      ns = NS2{1.f, 0.f};
+      if (na.kind != RGPT_NORM_IDENTITY) {
+        float S = 0.f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) S += x[i] * x[i];
+        ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+      }
+      float c = 0.f, xdy = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        c += qk_affine(na, false, i) * na.sk * g[i] * x[i];
+        xdy += g[i] * x[i];
+      }
+      const float k2 = 2.0f * ns.ds * c;
+      if (na.kind == RGPT_NORM_RMS_AFFINE && dwk) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float v = warp_sum(valid ? g[i] * x[i] * ns.s : 0.f);
+          if (lane == 0) atomicAdd(&dwk[i], v);
+        }
+      }
+      if (na.kind == RGPT_NORM_L2_TEMP && dtk) {
+        float v = warp_sum(valid ? xdy * ns.s : 0.f);
+        if (lane == 0) atomicAdd(dtk, v);
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) g[i] = ns.s * qk_affine(na, false, i) * na.sk * g[i] + k2 * x[i];
+    }
+    if (valid) store_row64(dqkv + tok * 3 * d + d + h * 64, g);
+    // ------------------------------------------------ dWg, dbg from this tile
+    if (gated) {
+      __syncthreads();
+#pragma unroll 1
+      for (int r = 0; r < 128; ++r) {
+        const float gj = sG[r][own_j];
+        acc_b += (own_i0 == 0) ? gj : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc_w[i] += gj * sQn[r][own_i0 + i];
+      }
+      __syncthreads();
+    }
+  }
+  if (gated) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) atomicAdd(&dwg[own_j * 64 + own_i0 + i], acc_w[i]);
+    if (own_i0 == 0) atomicAdd(&dbg[own_j], acc_b);
+  }
+}
+
+// ============================================================================ embedding
+__global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const float* __restrict__ emb,
+                                     float* __restrict__ x, int M, int d, int V, int* __restrict__ err) {
+  const int warps = blockDim.x >> 5;
+  const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const long long id = ids[row];
+  const int lane = threadIdx.x & 31;
+  float4* dst = reinterpret_cast<float4*>(x + row * d);
+  if (id < 0 || id >= V) {
+    if (lane == 0) atomicCAS(err, 0, RGPT_DEVERR_BAD_ARGS);
+    for (int c = lane; c < d / 4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(emb + id * d);
+  for (int c = lane; c < d / 4; c += 32) dst[c] = src[c];
+}
+
+__global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const float* __restrict__ dx,
+                                     float* __restrict__ demb, int M, int d, int V) {
+  const int warps = blockDim.x >> 5;
+  const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const long long id = ids[row];
+  if (id < 0 || id >= V) return;
+  const int lane = threadIdx.x & 31;
+  const float4* src = reinterpret_cast<const float4*>(dx + row * d);
+  float4* dst = reinterpret_cast<float4*>(demb + id * d);
+  for (int c = lane; c < d / 4; c += 32) atomicAdd(dst + c, src[c]);
+}
+
+// ============================================================================ cross entropy
+// count valid labels; scale_out = grad_scale / count
+__global__ void ce_count_kernel(const long long* __restrict__ labels, int M, int ignore_index, float grad_scale,
+                                float* __restrict__ scale_out, float* __restrict__ count_out) {
+  __shared__ int s[32];
+  int c = 0;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) c += (labels[i] != ignore_index) ? 1 : 0;
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int tot = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += s[i];
+    count_out[0] = (float)tot;
+    scale_out[0] = tot > 0 ? grad_scale / (float)tot : 0.f;
+  }
+}
+
+// One CTA per row of bf16 logits [M, V]. Online max / sum-exp with 16-byte loads,
+// argmax (first index of the maximum), loss_row = lse - x[label] (0 if ignored).
+// With write_grad, overwrites the row with bf16 (softmax - onehot) * (*scale).
+__global__ void __launch_bounds__(512) cross_entropy_kernel(__nv_bfloat16* __restrict__ logits, long long ld, int V,
+                                                            const long long* __restrict__ labels, int ignore_index,
+                                                            float* __restrict__ loss_rows, int* __restrict__ argmax,
+                                                            const float* __restrict__ scale, int write_grad) {
+  const long long row = blockIdx.x;
+  __nv_bfloat16* x = logits + row * ld;
+  const int nvec = V / 8;
+  float m = -INFINITY, s = 0.f, best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(x)[v];
+    uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+    float f[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 p = unpack_bf16x2(w4[e]);
+      f[2 * e] = p.x;
+      f[2 * e + 1] = p.y;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) lm = fmaxf(lm, f[e]);
+    if (lm > best) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (f[e] == lm) {
+          best = lm;
+          besti = v * 8 + e;
+          break;
+        }
+    }
+    const float nm = fmaxf(m, lm);
+    float acc = s * expf(m - nm);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += expf(f[e] - nm);
+    s = acc;
+    m = nm;
+  }
+  for (int j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {  // tail (V % 8)
+    const float f = __bfloat162float(x[j]);
+    if (f > best) {
+      best = f;
+      besti = j;
+    }
+    const float nm = fmaxf(m, f);
+    s = s * expf(m - nm) + expf(f - nm);
+    m = nm;
+  }
+  // block reduction of (m, s) and (best, besti)
+  __shared__ float sm[32], ss[32], sb[32];
+  __shared__ int sbi[32];
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = (nm == -INFINITY) ? 0.f : s * expf(m - nm) + os * expf(om - nm);
+    m = nm;
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ob > best || (ob == best && oi < besti)) {
+      best = ob;
+      besti = oi;
+    }
+  }
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    sm[wid] = m;
+    ss[wid] = s;
+    sb[wid] = best;
+    sbi[wid] = besti;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    besti = lane < nw ? sbi[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, om);
+      s = (nm == -INFINITY) ? 0.f : s * expf(m - nm) + os * expf(om - nm);
+      m = nm;
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+      if (ob > best || (ob == best && oi < besti)) {
+        best = ob;
+        besti = oi;
+      }
+    }
+    if (lane == 0) {
+      sm[0] = m;
+      ss[0] = s;
+      sbi[0] = besti;
+    }
+  }
+  __syncthreads();
+  m = sm[0];
+  s = ss[0];
+  const float lse = m + logf(s);
+  const long long label = labels[row];
+  const bool valid = label != ignore_index && label >= 0 && label < V;
+  if (threadIdx.x == 0) {
+    if (loss_rows) loss_rows[row] = valid ? lse - __bfloat162float(x[label]) : 0.f;
+    if (argmax) argmax[row] = sbi[0];
+  }
+  if (!write_grad) return;
+  __syncthreads();  // the label logit was read above before any thread overwrites it
+  const float sc = valid ? scale[0] : 0.f;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(x)[v];
+    uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o4[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 p = unpack_bf16x2(w4[e]);
+      const int j = v * 8 + 2 * e;
+      float g0 = expf(p.x - lse) - (j == label ? 1.f : 0.f);
+      float g1 = expf(p.y - lse) - (j + 1 == label ? 1.f : 0.f);
+      o4[e] = pack_bf16x2(g0 * sc, g1 * sc);
+    }
+    reinterpret_cast<uint4*>(x)[v] = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+  for (int j = nvec * 8 + threadIdx.x; j < V; j += blockDim.x) {
+    const float f = __bfloat162float(x[j]);
+    x[j] = __float2bfloat16((expf(f - lse) - (j == label ? 1.f : 0.f)) * sc);
+  }
+}
+
+// sum of loss rows / count -> out[0] (mean CE over valid labels), also adds into accum (optional)
+__global__ void ce_finalize_kernel(const float* __restrict__ loss_rows, int M, const float* __restrict__ count,
+                                   float* __restrict__ out) {
+  __shared__ float s[32];
+  float a = 0.f;
+  for (int i = threadIdx.x; i < M; i += blockDim.x) a += loss_rows[i];
+  a = warp_sum(a);
+  if ((threadIdx.x & 31) == 0) s[threadIdx.x >> 5] = a;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += s[i];
+    out[0] = t / count[0];
+  }
+}
+
+// ============================================================================ rGPT halting losses
+// q [R, M, 2] (halt, continue logits per recurrence step), correct [R, M] (argmax == label)
+// halt loss   = (1/R) sum_i mean_m BCE(q[i,m,0], correct[i,m])
+// q_cont loss = (1/R) sum_i mean_m BCE(q[i,m,1], target[i,m]),
+//   target[i] = sigmoid(max(q[i+1,m,0], q[i+1,m,1])) for i < R-1, sigmoid(q[R-1,m,0]) for the last step
+// losses[0] += halt loss, losses[1] += q_cont loss; dq = d(total)/dq * grad_scale
+__device__ __forceinline__ float bce_logits(float x, float y) {
+  return fmaxf(x, 0.f) - x * y + log1pf(expf(-fabsf(x)));
+}
+
+__global__ void halt_losses_kernel(const float* __restrict__ q, const int* __restrict__ argmax,
+                                   const long long* __restrict__ labels, int R, int M, float grad_scale,
+                                   float* __restrict__ dq, float* __restrict__ losses) {
+  const int m = blockIdx.x * blockDim.x + threadIdx.x;
+  float lh = 0.f, lc = 0.f;
+  if (m < M) {
+    const long long lab = labels[m];
+    const float inv = 1.0f / ((float)R * (float)M);
+    for (int i = 0; i < R; ++i) {
+      const float qh = q[((long long)i * M + m) * 2 + 0];
+      const float qc = q[((long long)i * M + m) * 2 + 1];
+      const float y = (argmax[(long long)i * M + m] == lab) ? 1.f : 0.f;
+      float tgt;
+      if (i < R - 1) {
+        const float a = q[((long long)(i + 1) * M + m) * 2 + 0], b = q[((long long)(i + 1) * M + m) * 2 + 1];
+        tgt = 1.0f / (1.0f + expf(-fmaxf(a, b)));
+      } else {
+        tgt = 1.0f / (1.0f + expf(-qh));
+      }
+      lh += bce_logits(qh, y);
+      lc += bce_logits(qc, tgt);
+      dq[((long long)i * M + m) * 2 + 0] = (1.0f / (1.0f + expf(-qh)) - y) * inv * grad_scale;
+      dq[((long long)i * M + m) * 2 + 1] = (1.0f / (1.0f + expf(-qc)) - tgt) * inv * grad_scale;
+    }
+    lh /= (float)R * (float)M;
+    lc /= (float)R * (float)M;
+  }
+  lh = warp_sum(lh);
+  lc = warp_sum(lc);
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(&losses[0], lh);
+    atomicAdd(&losses[1], lc);
+  }
+}
+
+}  // namespace rgpt
+
+using namespace rgpt;
+
+static int norm_nv(int d) {
+  if (d % 128 != 0) return 0;
+  const int nv = d / 128;
+  return (nv == 1 || nv == 2 || nv == 4 || nv == 8 || nv == 16) ? nv : 0;
+}
+
+extern "C" int rgpt_rownorm_fwd(const float* x, void* y, float* stat, const float* w, float temp, int kind, float eps,
+                                float alpha, int M, int d, const float* qw, const float* qb, float* qout,
+                                void* stream) {
+  const int nv = norm_nv(d);
+  if (nv == 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rownorm needs d in {128,256,512,1024,2048} (got %d)", d);
+  if (kind == RGPT_NORM_RMS_AFFINE && w == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rmsnorm needs w");
+  if (qout && (qw == nullptr || qb == nullptr)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "q_head needs qw/qb");
+  const int block = 256, rows_per = block / 32;
+  const int grid = (M + rows_per - 1) / rows_per;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
+#define RN_F(N) rownorm_fwd_kernel<N><<<grid, block, 0, s>>>(x, yb, stat, w, temp, kind, eps, alpha, M, d, qw, qb, qout)
+  switch (nv) {
+    case 1: RN_F(1); break;
+    case 2: RN_F(2); break;
+    case 4: RN_F(4); break;
+    case 8: RN_F(8); break;
+    default: RN_F(16); break;
+  }
+#undef RN_F
+  return rgpt_check_launch("rownorm_fwd_kernel");
+}
+
+extern "C" int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w, float temp, int kind, float eps,
+                                float alpha, int M, int d, const float* g_in, float* g_out, void* g_bf16,
+                                const float* ls, const float* raw, float* dls, float* dw, float* dtemp,
+                                const float* dq, const float* qw, const void* h, float* dqw, float* dqb,
+                                void* stream) {
+  const int nv = norm_nv(d);
+  if (nv == 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rownorm needs d in {128,256,512,1024,2048} (got %d)", d);
+  if (dy == nullptr && dq == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rownorm_bwd needs dy or dq");
+  if (dq && (qw == nullptr)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "q_head mode needs qw");
+  if (dqw && h == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dqw needs h");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int block = 256, rows_per = block / 32;
+  int grid = (M + rows_per - 1) / rows_per;
+  const int cap = rgpt_num_sms(dev) * 4;
+  if (grid > cap) grid = cap;
+  const size_t smem = 4 * d * sizeof(float);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  __nv_bfloat16* gb = reinterpret_cast<__nv_bfloat16*>(g_bf16);
+  const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(h);
+#define RN_B(N)                                                                                               \
+  do {                                                                                                        \
+    if (dq)                                                                                                   \
+      rownorm_bwd_kernel<N, true><<<grid, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, \
+                                                           ls, raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);    \
+    else                                                                                                      \
+      rownorm_bwd_kernel<N, false><<<grid, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, \
+                                                            ls, raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);   \
+  } while (0)
+  switch (nv) {
+    case 1: RN_B(1); break;
+    case 2: RN_B(2); break;
+    case 4: RN_B(4); break;
+    case 8: RN_B(8); break;
+    default: RN_B(16); break;
+  }
+#undef RN_B
+  return rgpt_check_launch("rownorm_bwd_kernel");
+}
+
+static QkNormArgs qk_args(int kind, float eps, float alpha, const float* wq, const float* wk, float tq, float tk,
+                          float sq, float sk) {
+  QkNormArgs a;
+  a.kind = kind;
+  a.eps = eps;
+  a.alpha = alpha;
+  a.wq = wq;
+  a.wk = wk;
+  a.tq = tq;
+  a.tk = tk;
+  a.sq = sq;
+  a.sk = sk;
+  return a;
+}
+
+extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* gate, const float* wg, const float* bg,
+                                 const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq,
+                                 const float* wk, float tq, float tk, float sq, float sk, int M, int T, int H,
+                                 void* stream) {
+  if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
+  if (qk_kind == RGPT_NORM_RMS_AFFINE && (wq == nullptr || wk == nullptr))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rmsnorm QK norm needs weights");
+  if ((wg == nullptr) != (gate == nullptr) || (wg && bg == nullptr))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gate output needs gate weight and bias");
+  const long long rows = (long long)M * H;
+  const int block = 128;
+  qkv_prep_fwd_kernel<<<(unsigned)((rows + block - 1) / block), block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
+      reinterpret_cast<__nv_bfloat16*>(gate), wg, bg, inv_freq, qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk),
+      M, T, H);
+  return rgpt_check_launch("qkv_prep_fwd_kernel");
+}
+
+extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const void* dgp, void* dqkv,
+                                 const float* wg, float* dwg, float* dbg, float* dwq, float* dwk, float* dtq,
+                                 float* dtk, const float* inv_freq, int qk_kind, float eps, float alpha,
+                                 const float* wq, const float* wk, float tq, float tk, float sq, float sk, int M, int T,
+                                 int H, void* stream) {
+  if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
+  if (wg && (dgp == nullptr || dwg == nullptr || dbg == nullptr))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gated backward needs dgp, dwg, dbg");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long rows = (long long)M * H;
+  long long grid = (rows + 127) / 128;
+  const long long cap = rgpt_num_sms(dev) * 2;
+  if (grid > cap) grid = cap;
+  const size_t smem = (64 * 64 + 32 + 2 * 128 * 65) * sizeof(float);
+  static bool attr[64] = {false};
+  if (!attr[dev]) {
+    if (cudaFuncSetAttribute(qkv_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return rgpt_check_launch("qkv_prep_bwd set smem");
+    attr[dev] = true;
+  }
+  qkv_prep_bwd_kernel<<<(unsigned)grid, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, reinterpret_cast<const __nv_bfloat16*>(dgp),
+      reinterpret_cast<__nv_bfloat16*>(dqkv), wg, dwg, dbg, dwq, dwk, dtq, dtk, inv_freq,
+      qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
+  return rgpt_check_launch("qkv_prep_bwd_kernel");
+}
+
+extern "C" int rgpt_embedding_fwd(const long long* ids, const float* emb, float* x, int M, int d, int V,
+                                  void* stream) {
+  if (d % 4 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "embedding dim must be a multiple of 4");
+  const int block = 256, rows_per = block / 32;
+  int* err = nullptr;
+  cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_rgpt_device_error);
+  embedding_fwd_kernel<<<(M + rows_per - 1) / rows_per, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, emb, x, M, d, V, err);
+  return rgpt_check_launch("embedding_fwd_kernel");
+}
+
+extern "C" int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M, int d, int V,
+                                  void* stream) {
+  if (d % 4 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "embedding dim must be a multiple of 4");
+  const int block = 256, rows_per = block / 32;
+  embedding_bwd_kernel<<<(M + rows_per - 1) / rows_per, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      ids, dx, demb, M, d, V);
+  return rgpt_check_launch("embedding_bwd_kernel");
+}
+
+extern "C" int rgpt_cross_entropy(void* logits, long long ld, int M, int V, const long long* labels, int ignore_index,
+                                  float grad_scale, float* loss_rows, int* argmax, float* scale_buf, float* loss_out,
+                                  int write_grad, void* stream) {
+  if ((reinterpret_cast<uintptr_t>(logits) & 15) || (ld % 8))
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "logits must be 16-byte aligned with ld %% 8 == 0");
+  if ((write_grad || loss_out) && scale_buf == nullptr)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "scale_buf (2 floats) required for loss / grad");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (scale_buf) ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
+  cross_entropy_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, labels, ignore_index,
+                                         loss_rows, argmax, scale_buf, write_grad);
+  if (loss_out && loss_rows) ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
+  return rgpt_check_launch("cross_entropy_kernel");
+}
+
+extern "C" int rgpt_halt_losses(const float* q, const int* argmax, const long long* labels, int R, int M,
+                                float grad_scale, float* dq, float* losses, void* stream) {
+  const int block = 256;
+  halt_losses_kernel<<<(M + block - 1) / block, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      q, argmax, labels, R, M, grad_scale, dq, losses);
+  return rgpt_check_launch("halt_losses_kernel");
+}

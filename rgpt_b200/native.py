@@ -50,9 +50,15 @@ def _out(t: torch.Tensor | None):
     return ptr(t), t.stride(-2), (t.stride(0) if t.dim() == 3 else 0)
 
 
+# Optional GEMM timing hook: when set to a list, every gemm() call appends
+# (start_event, end_event, flops) recorded on the launching stream.
+gemm_events: list | None = None
+
+
 def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_STORE_BF16,
          act: int = 0, alpha: float = 1.0, beta: float = 0.0, out2: torch.Tensor | None = None,
-         c: torch.Tensor | None = None, colscale: torch.Tensor | None = None, splitk: int = 1) -> torch.Tensor:
+         c: torch.Tensor | None = None, colscale: torch.Tensor | None = None, splitk: int = 1,
+         alpha_dev: torch.Tensor | None = None) -> torch.Tensor:
     """out = epilogue(A @ B^T) for logical A [(b,) M, K] and B [(b,) N, K] (bf16).
 
     Either operand may be K-major (unit stride on K) or MN-major (unit stride
@@ -73,11 +79,19 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
     d, ldd, dbs = _out(out)
     d2, ldd2, d2bs = _out(out2)
     cp, ldc, cbs = _out(c)
+    ev = gemm_events
+    if ev is not None:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
     _lib.call("rgpt_gemm_bf16",
               ptr(A), a_mn, lda, abs_, ptr(B), b_mn, ldb, bbs,
               M, N, K, batch, epi, act, float(alpha), float(beta),
               d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
-              ptr(colscale), splitk, _lib.stream_ptr(out.device))
+              ptr(colscale), splitk, ptr(alpha_dev), _lib.stream_ptr(out.device))
+    if ev is not None:
+        e1.record()
+        ev.append((e0, e1, 2.0 * M * N * K * batch))
     return out
 
 
@@ -121,3 +135,97 @@ def attn_bwd(qk: torch.Tensor, qkv: torch.Tensor, do: torch.Tensor, lse: torch.T
         raise TypeError("dq/dk must be fp32 and dv bf16")
     _lib.call("rgpt_attn_bwd", ptr(qk), ptr(qkv), ptr(do), ptr(lse), ptr(D), ptr(dq), ptr(dk), dk.stride(0),
               ptr(dv), dv.stride(0), B, T, H, d, _lib.stream_ptr(do.device))
+
+
+# ----------------------------------------------------------------------------- norms
+NORM_IDENTITY, NORM_RMS_AFFINE, NORM_RMS, NORM_L2_TEMP, NORM_L2, NORM_ELASTIC, NORM_ELASTICBALL, NORM_HYPERBALL = range(8)
+FLT_EPS = 1.1920928955078125e-07  # torch.finfo(torch.float32).eps
+
+
+def rownorm_fwd(x: torch.Tensor, y: torch.Tensor, kind: int, eps: float, *, w: torch.Tensor | None = None,
+                temp: float = 1.0, alpha: float = 0.5, stat: torch.Tensor | None = None,
+                qw: torch.Tensor | None = None, qb: torch.Tensor | None = None,
+                qout: torch.Tensor | None = None) -> None:
+    M, d = x.shape
+    _lib.call("rgpt_rownorm_fwd", ptr(x), ptr(y), ptr(stat), ptr(w), float(temp), kind, float(eps), float(alpha),
+              M, d, ptr(qw), ptr(qb), ptr(qout), _lib.stream_ptr(x.device))
+
+
+def rownorm_bwd(x: torch.Tensor, dy: torch.Tensor | None, kind: int, eps: float, g_out: torch.Tensor, *,
+                w: torch.Tensor | None = None, temp: float = 1.0, alpha: float = 0.5,
+                g_in: torch.Tensor | None = None, g_bf16: torch.Tensor | None = None,
+                ls: torch.Tensor | None = None, raw: torch.Tensor | None = None, dls: torch.Tensor | None = None,
+                dw: torch.Tensor | None = None, dtemp: torch.Tensor | None = None,
+                dq: torch.Tensor | None = None, qw: torch.Tensor | None = None, h: torch.Tensor | None = None,
+                dqw: torch.Tensor | None = None, dqb: torch.Tensor | None = None) -> None:
+    M, d = x.shape
+    _lib.call("rgpt_rownorm_bwd", ptr(x), ptr(dy), ptr(w), float(temp), kind, float(eps), float(alpha), M, d,
+              ptr(g_in), ptr(g_out), ptr(g_bf16), ptr(ls), ptr(raw), ptr(dls), ptr(dw), ptr(dtemp),
+              ptr(dq), ptr(qw), ptr(h), ptr(dqw), ptr(dqb), _lib.stream_ptr(x.device))
+
+
+# ----------------------------------------------------------------------------- QKV prep
+def qkv_prep_fwd(qkv, qk, gate, wg, bg, inv_freq, qk_kind, eps, alpha, M, T, H, *, wq=None, wk=None,
+                 tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
+    _lib.call("rgpt_qkv_prep_fwd", ptr(qkv), ptr(qk), ptr(gate), ptr(wg), ptr(bg), ptr(inv_freq), qk_kind,
+              float(eps), float(alpha), ptr(wq), ptr(wk), float(tq), float(tk), float(sq), float(sk), M, T, H,
+              _lib.stream_ptr(qkv.device))
+
+
+def qkv_prep_bwd(qkv, dq, dk, dgp, dqkv, wg, dwg, dbg, inv_freq, qk_kind, eps, alpha, M, T, H, *, dwq=None,
+                 dwk=None, dtq=None, dtk=None, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
+    _lib.call("rgpt_qkv_prep_bwd", ptr(qkv), ptr(dq), ptr(dk), ptr(dgp), ptr(dqkv), ptr(wg), ptr(dwg), ptr(dbg),
+              ptr(dwq), ptr(dwk), ptr(dtq), ptr(dtk), ptr(inv_freq), qk_kind, float(eps), float(alpha), ptr(wq),
+              ptr(wk), float(tq), float(tk), float(sq), float(sk), M, T, H, _lib.stream_ptr(qkv.device))
+
+
+# ----------------------------------------------------------------------------- embedding / loss
+def embedding_fwd(ids: torch.Tensor, emb: torch.Tensor, x: torch.Tensor) -> None:
+    M = ids.numel()
+    V, d = emb.shape
+    _lib.call("rgpt_embedding_fwd", ptr(ids), ptr(emb), ptr(x), M, d, V, _lib.stream_ptr(x.device))
+
+
+def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, demb: torch.Tensor) -> None:
+    M = ids.numel()
+    V, d = demb.shape
+    _lib.call("rgpt_embedding_bwd", ptr(ids), ptr(dx), ptr(demb), M, d, V, _lib.stream_ptr(dx.device))
+
+
+def cross_entropy(logits: torch.Tensor, labels: torch.Tensor, *, ignore_index: int = -100, grad_scale: float = 1.0,
+                  loss_rows: torch.Tensor | None = None, argmax: torch.Tensor | None = None,
+                  scale_buf: torch.Tensor | None = None, loss_out: torch.Tensor | None = None,
+                  write_grad: bool = False) -> None:
+    M, V = logits.shape
+    nk = 1 + (scale_buf is not None) + (loss_out is not None and loss_rows is not None)
+    _lib.call("rgpt_cross_entropy", ptr(logits), logits.stride(0), M, V, ptr(labels), int(ignore_index),
+              float(grad_scale), ptr(loss_rows), ptr(argmax), ptr(scale_buf), ptr(loss_out), int(write_grad),
+              _lib.stream_ptr(logits.device), kernels=nk)
+
+
+def halt_losses(q: torch.Tensor, argmax: torch.Tensor, labels: torch.Tensor, dq: torch.Tensor,
+                losses: torch.Tensor, grad_scale: float = 1.0) -> None:
+    R, M = q.shape[0], q.shape[1]
+    _lib.call("rgpt_halt_losses", ptr(q), ptr(argmax), ptr(labels), R, M, float(grad_scale), ptr(dq), ptr(losses),
+              _lib.stream_ptr(q.device))
+
+
+# ----------------------------------------------------------------------------- optimizer
+def adamw(table: torch.Tensor, chunk_tensor: torch.Tensor, chunk_start: torch.Tensor, chunk_elems: int,
+          lr: float, wd: float, beta1: float, beta2: float, eps: float, step: int) -> None:
+    _lib.call("rgpt_adamw", ptr(table), ptr(chunk_tensor), ptr(chunk_start), chunk_tensor.numel(), chunk_elems,
+              float(lr), float(wd), float(beta1), float(beta2), float(eps), int(step), _lib.stream_ptr(table.device))
+
+
+def muon_prep(table, n, R, C, X, beta, nesterov, sumsq) -> None:
+    _lib.call("rgpt_muon_prep", ptr(table), n, R, C, ptr(X), X.stride(0), X.stride(1), float(beta), int(nesterov),
+              ptr(sumsq), _lib.stream_ptr(X.device))
+
+
+def ns_scale(X, rows, cols, n, sumsq) -> None:
+    _lib.call("rgpt_ns_scale", ptr(X), X.stride(0), X.stride(1), rows, cols, n, ptr(sumsq), _lib.stream_ptr(X.device))
+
+
+def muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale) -> None:
+    _lib.call("rgpt_muon_apply", ptr(table), n, R, C, ptr(X), X.stride(0), X.stride(1), float(lr), float(wd),
+              float(muon_lr), float(scale), _lib.stream_ptr(X.device))

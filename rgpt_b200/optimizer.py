@@ -1,0 +1,321 @@
+"""Muon / DistMuon with the reference's constructor and state layout (optimizer.py).
+
+Every step runs on sm_100a kernels:
+  * AdamW groups: one multi-tensor launch per group (rgpt_adamw), also refreshing
+    the bf16 shadows the GEMMs read.
+  * Muon groups: matrices are batched by shape class. Per class: one
+    momentum/Nesterov/transpose kernel writes a bf16 stack X and its Frobenius
+    norms, one scale kernel, then ns_steps x 3 batched tcgen05 GEMMs
+        A = X X^T;  B = b*A + c*A^2 (fused epilogue);  X = a*X + B X (fused epilogue)
+    and one apply kernel (weight decay, lr * multiplier, bf16 shadow).
+State keys match the reference: momentum_buffer (bf16), exp_avg, exp_avg_sq and
+the group counter _adam_step, so optimizer state_dicts interchange.
+
+Names: the reference README calls these NorMuon / DistNorMuon with a
+polar_express orthogonaliser; its code implements Muon / DistMuon with the
+fixed quintic zeropower_via_newtonschulz5 (optimizer.py:8-45). Both names are
+exported with the code's semantics; the NS coefficients are a parameter.
+"""
+from __future__ import annotations
+
+import math
+from typing import Any, Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import native as nv
+
+NS_COEFFS = (3.4445, -4.7750, 2.0315)  # optimizer.py:19
+_ADAM_CHUNK = 16384
+
+
+def _muon_scale(m: int, n: int) -> float:
+    """sqrt(max(1, m/n)) (optimizer.py:130-133)."""
+    r = m / n
+    return math.sqrt(r) if r > 1.0 else 1.0
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def trainer_param_groups(model, tie_word_embeddings=False, weight_decay=0.1):
+    """The Trainer's three groups (trainer.py:66-95): Muon / AdamW-decay / AdamW-no-decay."""
+    muon, dec, nodec = [], [], []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        if not tie_word_embeddings and "lm_head" in name:
+            dec.append(p)
+        elif "emb" in name:
+            nodec.append(p)
+        elif p.ndim >= 2:
+            muon.append(p)
+        elif "norm" in name or "bias" in name:
+            nodec.append(p)
+        else:
+            dec.append(p)
+    return [
+        {"params": muon, "use_muon": True},
+        {"params": dec, "use_muon": False, "weight_decay": weight_decay},
+        {"params": nodec, "use_muon": False, "weight_decay": 0.0},
+    ]
+
+
+def _table(rows: List[List[int]], device) -> torch.Tensor:
+    return torch.tensor(rows, dtype=torch.int64).to(device, non_blocking=False)
+
+
+class _NSWorkspace:
+    """bf16 Newton-Schulz buffers for n matrices of one shape class (rows <= cols after transpose)."""
+
+    def __init__(self, n, xr, xc, device):
+        self.n, self.xr, self.xc = n, xr, xc
+        rp, cp = _pad8(xr), _pad8(xc)
+        self.X = torch.zeros(n, rp, cp, device=device, dtype=torch.bfloat16)
+        self.X2 = torch.zeros_like(self.X)
+        self.A = torch.zeros(n, rp, rp, device=device, dtype=torch.bfloat16)
+        self.B = torch.zeros_like(self.A)
+        self.sumsq = torch.zeros(n, device=device, dtype=torch.float32)
+
+
+def newton_schulz_batched(ws: _NSWorkspace, steps: int, coeffs=NS_COEFFS) -> torch.Tensor:
+    """Run the quintic NS iteration in place on ws.X (already normalised); returns the result buffer."""
+    a, b, c = coeffs
+    X, X2 = ws.X, ws.X2
+    for _ in range(steps):
+        nv.gemm(X, X, ws.A)                                                     # A = X X^T
+        nv.gemm(ws.A, ws.A, ws.B, epi=nv.EPI_POLY_BF16, alpha=c, beta=b, c=ws.A)  # B = b*A + c*A@A
+        nv.gemm(ws.B, X.transpose(1, 2), X2, epi=nv.EPI_POLY_BF16, alpha=1.0, beta=a, c=X)  # X = a*X + B@X
+        X, X2 = X2, X
+    return X
+
+
+def _muon_rows(params, grads, moms) -> List[List[int]]:
+    rows = []
+    for p, g, m in zip(params, grads, moms):
+        sh = getattr(p, "_rgpt_shadow", None)
+        rows.append([p.data_ptr(), g.data_ptr(), m.data_ptr(), sh.data_ptr() if sh is not None else 0])
+    return rows
+
+
+class Muon(torch.optim.Optimizer):
+    """Muon for 2-D weights (group use_muon=True) + AdamW for the rest (optimizer.py:143-272)."""
+
+    def __init__(self, params: List[Dict[str, Any]], lr: float = 3e-4, weight_decay: float = 0.01,
+                 momentum: float = 0.95, nesterov: bool = True, adam_betas: Tuple[float, float] = (0.9, 0.95),
+                 adam_eps: float = 1e-8, muon_lr_multiplier: float = 100.0, ns_steps: int = 5,
+                 ns_coeffs: Tuple[float, float, float] = NS_COEFFS):
+        defaults = dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov,
+                        adam_betas=adam_betas, adam_eps=adam_eps, muon_lr_multiplier=muon_lr_multiplier,
+                        ns_steps=ns_steps, ns_coeffs=tuple(ns_coeffs))
+        super().__init__(params, defaults)
+        self._cache: Dict[Any, Any] = {}
+
+    # ------------------------------------------------------------------ grads
+    @torch.no_grad()
+    def zero_grad(self, set_to_none: bool = True):
+        """Gradients that live in a model's native gradient arena are zeroed in place (their
+        storage is what the backward kernels accumulate into); others follow torch semantics."""
+        arenas = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                arena = getattr(p, "_rgpt_grad_arena", None)
+                if arena is not None and p.grad is not None:
+                    arenas[id(arena)] = arena
+                elif p.grad is not None:
+                    if set_to_none:
+                        p.grad = None
+                    else:
+                        p.grad.zero_()
+        for a in arenas.values():
+            a.zero_()
+
+    # ------------------------------------------------------------------ step
+    @torch.no_grad()
+    def step(self, closure: Optional[Any] = None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for gi, group in enumerate(self.param_groups):
+            if group.get("use_muon", False):
+                self._muon_group(gi, group, [p for p in group["params"] if p.grad is not None])
+            else:
+                self._adamw_group(gi, group, [p for p in group["params"] if p.grad is not None])
+        return loss
+
+    def _muon_group(self, gi, group, params, owned=None):
+        if not params:
+            return
+        lr = float(group["lr"])
+        wd = float(group["weight_decay"])
+        muon_lr = lr * float(group["muon_lr_multiplier"])
+        beta = float(group["momentum"])
+        nesterov = bool(group["nesterov"])
+        steps = int(group.get("ns_steps", 5))
+        coeffs = tuple(group.get("ns_coeffs", NS_COEFFS))
+        classes: Dict[Tuple[int, int], List[torch.Tensor]] = {}
+        for p in params:
+            st = self.state[p]
+            if len(st) == 0:
+                st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+            R, C = p.shape[0], p.numel() // p.shape[0]
+            classes.setdefault((R, C), []).append(p)
+        for (R, C), ps in classes.items():
+            grads = [p.grad for p in ps]
+            moms = [self.state[p]["momentum_buffer"] for p in ps]
+            rows = _muon_rows(ps, grads, moms)
+            key = ("muon", gi, R, C, tuple(r[0] for r in rows), tuple(r[1] for r in rows))
+            ent = self._cache.get(key)
+            if ent is None:
+                xr, xc = (C, R) if R > C else (R, C)
+                ent = (_table(rows, ps[0].device), _NSWorkspace(len(ps), xr, xc, ps[0].device))
+                self._cache[key] = ent
+            table, ws = ent
+            n = len(ps)
+            ws.sumsq.zero_()
+            nv.muon_prep(table, n, R, C, ws.X, beta, nesterov, ws.sumsq)
+            nv.ns_scale(ws.X, ws.xr, ws.xc, n, ws.sumsq)
+            out = newton_schulz_batched(ws, steps, coeffs)
+            nv.muon_apply(table, n, R, C, out, lr, wd, muon_lr, _muon_scale(R, C))
+
+    def _adamw_group(self, gi, group, params):
+        if not params:
+            return
+        lr = float(group["lr"])
+        wd = float(group["weight_decay"])
+        beta1, beta2 = group["adam_betas"]
+        eps = float(group["adam_eps"])
+        step_i = int(group.get("_adam_step", 0)) + 1
+        group["_adam_step"] = step_i
+        for p in params:
+            st = self.state[p]
+            if len(st) == 0:
+                st["exp_avg"] = torch.zeros_like(p)
+                st["exp_avg_sq"] = torch.zeros_like(p)
+        rows = []
+        for p in params:
+            st = self.state[p]
+            sh = getattr(p, "_rgpt_shadow", None)
+            rows.append([p.data_ptr(), p.grad.data_ptr(), st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(),
+                         sh.data_ptr() if sh is not None else 0, p.numel()])
+        key = ("adamw", gi, tuple(tuple(r) for r in rows))
+        ent = self._cache.get(key)
+        if ent is None:
+            ct, cs = [], []
+            for ti, p in enumerate(params):
+                for s in range(0, p.numel(), _ADAM_CHUNK):
+                    ct.append(ti)
+                    cs.append(s)
+            dev = params[0].device
+            ent = (_table(rows, dev), torch.tensor(ct, dtype=torch.int32).to(dev),
+                   torch.tensor(cs, dtype=torch.int64).to(dev))
+            self._cache[key] = ent
+        table, ct, cs = ent
+        nv.adamw(table, ct, cs, _ADAM_CHUNK, lr, wd, float(beta1), float(beta2), eps, step_i)
+
+
+class DistMuon(Muon):
+    """Data-parallel Muon (optimizer.py:278-415).
+
+    The reference relies on DDP to all-reduce gradients and then repeats the
+    whole update on every rank. Here gradients are averaged across ranks by
+    this optimizer (the model is not wrapped in DDP), so the update is the
+    same as the reference's on DDP-averaged gradients."""
+
+    def __init__(self, params, *args, process_group=None, **kwargs):
+        super().__init__(params, *args, **kwargs)
+        self.process_group = process_group
+
+    @torch.no_grad()
+    def step(self, closure: Optional[Any] = None):
+        if dist.is_available() and dist.is_initialized() and dist.get_world_size(self.process_group) > 1:
+            self._average_grads()
+        return super().step(closure)
+
+    def _average_grads(self):
+        ws = dist.get_world_size(self.process_group)
+        arenas, loose = {}, []
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                a = getattr(p, "_rgpt_grad_arena", None)
+                if a is not None:
+                    arenas[id(a)] = a
+                else:
+                    loose.append(p.grad)
+        for a in arenas.values():
+            dist.all_reduce(a, op=dist.ReduceOp.SUM, group=self.process_group)
+            a.mul_(1.0 / ws)
+        for g in loose:
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.process_group)
+            g.mul_(1.0 / ws)
+
+
+# Names used by the reference's README.
+NorMuon = Muon
+DistNorMuon = DistMuon
+
+
+# ---------------------------------------------------------------------- functional API
+@torch.no_grad()
+def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, coeffs=NS_COEFFS) -> torch.Tensor:
+    """Native quintic Newton-Schulz orthogonalisation of a 2-D (or batched 3-D) CUDA tensor (optimizer.py:8-45).
+
+    Returns bf16 with G's shape."""
+    if not G.is_cuda:
+        raise RuntimeError("zeropower_via_newtonschulz5 runs on CUDA tensors only (no CPU path)")
+    squeeze = G.dim() == 2
+    Gb = G.unsqueeze(0) if squeeze else G
+    n, R, C = Gb.shape
+    transposed = R > C
+    Xs = Gb.transpose(1, 2) if transposed else Gb
+    xr, xc = Xs.shape[1], Xs.shape[2]
+    ws = _NSWorkspace(n, xr, xc, G.device)
+    ws.X[:, :xr, :xc].copy_(Xs.to(torch.bfloat16))
+    ws.sumsq.copy_(ws.X.float().pow(2).sum(dim=(1, 2)))
+    nv.ns_scale(ws.X, xr, xc, n, ws.sumsq)
+    out = newton_schulz_batched(ws, steps, coeffs)[:, :xr, :xc]
+    out = out.transpose(1, 2) if transposed else out
+    out = out.contiguous()
+    return out[0] if squeeze else out
+
+
+polar_express = zeropower_via_newtonschulz5
+
+
+@torch.no_grad()
+def muon_update(grad_2d: torch.Tensor, momentum_2d: torch.Tensor, beta: float = 0.95, ns_steps: int = 5,
+                nesterov: bool = True, scale: float = 1.0) -> torch.Tensor:
+    """Momentum + Nesterov + NS + scale for one matrix (optimizer.py:51-74); updates momentum in place."""
+    R, C = grad_2d.shape
+    dev = grad_2d.device
+    g = grad_2d.float().contiguous()
+    xr, xc = (C, R) if R > C else (R, C)
+    ws = _NSWorkspace(1, xr, xc, dev)
+    dummy = torch.zeros(R, C, device=dev, dtype=torch.float32)
+    table = _table([[dummy.data_ptr(), g.data_ptr(), momentum_2d.data_ptr(), 0]], dev)
+    nv.muon_prep(table, 1, R, C, ws.X, beta, nesterov, ws.sumsq)
+    nv.ns_scale(ws.X, xr, xc, 1, ws.sumsq)
+    out = newton_schulz_batched(ws, ns_steps)[0, :xr, :xc]
+    out = out.t() if R > C else out
+    return (out.float() * scale).to(torch.bfloat16)
+
+
+@torch.no_grad()
+def foreach_adamw_step(params, grads, exp_avgs, exp_avg_sqs, step, lr, wd, beta1, beta2, eps) -> None:
+    """foreach_adamw_step (optimizer.py:80-116) as one native multi-tensor launch."""
+    rows, ct, cs = [], [], []
+    for ti, (p, g, m, v) in enumerate(zip(params, grads, exp_avgs, exp_avg_sqs)):
+        rows.append([p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), 0, p.numel()])
+        for s in range(0, p.numel(), _ADAM_CHUNK):
+            ct.append(ti)
+            cs.append(s)
+    if not rows:
+        return
+    dev = params[0].device
+    nv.adamw(_table(rows, dev), torch.tensor(ct, dtype=torch.int32).to(dev), torch.tensor(cs, dtype=torch.int64).to(dev),
+             _ADAM_CHUNK, lr, wd, beta1, beta2, eps, step)

@@ -146,8 +146,23 @@ def test_gemm_lm_head_shape(cuda):
     assert rel_err(out, h.float() @ w.float().t()) < 1e-2
 
 
-def test_gemm_rejects_bad_shapes(cuda):
-    a = torch.randn(64, 64, device=cuda).bfloat16()
-    out = torch.empty(64, 64, device=cuda, dtype=torch.bfloat16)
-    with pytest.raises(RuntimeError, match="M>=128"):
-        nv.gemm(a, a, out)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True), (False, True)])
+def test_gemm_small_and_ragged_shapes(cuda, a_mn, b_mn):
+    # the reference kernel test's own shapes (M,N,K,Out = 128,256,128,64) and smaller edges
+    for M, N, K in [(128, 64, 256), (40, 24, 72), (64, 200, 8)]:
+        g = torch.Generator(device=cuda).manual_seed(M + N + K)
+        a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+        b = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+        A = a.t().contiguous().t() if a_mn else a
+        B = b.t().contiguous().t() if b_mn else b
+        out = torch.empty(M, N, device=cuda, dtype=torch.float32)
+        nv.gemm(A, B, out, epi=nv.EPI_STORE_F32)
+        assert rel_err(out, a.float() @ b.float().t()) < 1e-4, (M, N, K)
+
+
+def test_gemm_rejects_misaligned_leading_dim(cuda):
+    a = torch.randn(128, 100, device=cuda).bfloat16()[:, :99]  # ld 100 -> 200 bytes, not a multiple of 16
+    out = torch.empty(128, 128, device=cuda, dtype=torch.bfloat16)
+    w = torch.randn(128, 99, device=cuda).bfloat16()
+    with pytest.raises(RuntimeError, match="16 bytes"):
+        nv.gemm(a, w, out)
