@@ -42,7 +42,7 @@ __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int*
     const float denom = sqrtf(v) * inv_sqrt_bc2 + eps;
     p = p - lr * ((m / denom) * inv_bc1);
     t.p[i] = p;
-    if (t.shadow) t.shadow[i] = __float2bfloat16(p);
+    if (t.shadow) t.shadow[i] = __bfloat16_as_ushort(__float2bfloat16(p));
   }
 }
 
@@ -62,9 +62,9 @@ __global__ void muon_prep_kernel(const RgptMuonTensor* __restrict__ tab, int R, 
     if (r < R && c < C) {
       const long long i = (long long)r * C + c;
       const float gb = __bfloat162float(__float2bfloat16(t.grad[i]));  // grad.to(bf16)
-      const float m_old = __bfloat162float(t.mom[i]);
+      const float m_old = __bfloat162float(__ushort_as_bfloat16(t.mom[i]));
       const float m_new = __bfloat162float(__float2bfloat16(lerpf_torch(m_old, gb, 1.0f - beta)));
-      t.mom[i] = __float2bfloat16(m_new);
+      t.mom[i] = __bfloat16_as_ushort(__float2bfloat16(m_new));
       x = nesterov ? __bfloat162float(__float2bfloat16(lerpf_torch(gb, m_new, beta))) : m_new;
       ss += x * x;
     }
@@ -134,7 +134,7 @@ __global__ void muon_apply_kernel(const RgptMuonTensor* __restrict__ tab, int R,
       if (decay != 1.0f) p *= decay;
       p += neg_lr * u;
       t.param[i] = p;
-      if (t.shadow) t.shadow[i] = __float2bfloat16(p);
+      if (t.shadow) t.shadow[i] = __bfloat16_as_ushort(__float2bfloat16(p));
     }
   }
 }

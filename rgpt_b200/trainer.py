@@ -1,0 +1,255 @@
+"""Trainer with the reference's constructor and methods (trainer.py:19-322).
+
+Same parameter grouping (Muon / AdamW-decay / AdamW-no-decay), LR schedules,
+gradient accumulation, validation and checkpoint dictionary as the reference.
+The hot loop runs the fused native path (GPT.forward_loss: forward, loss and
+in-place dlogits in one pass; loss.backward() runs the native backward), and
+reads losses back once per optimizer step instead of twice per micro-batch.
+
+Differences, all on purpose:
+  * No DDP wrapper: with world_size > 1 the optimizer is DistMuon, which
+    averages gradients over NCCL itself (the reference's DDP all-reduces every
+    micro-batch; here it happens once per optimizer step).
+  * Compute is bf16 with fp32 accumulation and fp32 master weights whatever
+    training.dtype says (no GradScaler needed for bf16).
+  * The per-parameter gradient-norm print (one host sync per parameter) is
+    opt-in (training.log_grad_norm) and done as one reduction.
+  * load_checkpoint() resumes from save_checkpoint()'s dictionary (the
+    reference saves but never loads).
+"""
+from __future__ import annotations
+
+import math
+import os
+from pathlib import Path
+
+import torch
+import torch.nn.functional as F
+
+from .model.config import as_config
+from .optimizer import DistMuon, Muon, trainer_param_groups
+
+
+def _output_dir(cfg):
+    try:
+        import hydra  # type: ignore
+
+        return Path(hydra.core.hydra_config.HydraConfig.get().runtime.output_dir)
+    except Exception:
+        return Path(cfg.get("output_dir", "outputs"))
+
+
+class _Logger:
+    """Rank-0 scalar logger (TensorBoard when available, else a JSON-lines file)."""
+
+    def __init__(self, out_dir: Path, rank: int):
+        self.rank = rank
+        self.writer = None
+        self.fh = None
+        if rank != 0:
+            return
+        out_dir.mkdir(parents=True, exist_ok=True)
+        try:
+            from torch.utils.tensorboard import SummaryWriter
+
+            self.writer = SummaryWriter(log_dir=str(out_dir))
+        except Exception:
+            self.fh = open(out_dir / "metrics.jsonl", "a")
+
+    def log(self, metrics: dict, step: int):
+        if self.rank != 0:
+            return
+        if self.writer is not None:
+            for k, v in metrics.items():
+                self.writer.add_scalar(k, v, step)
+        elif self.fh is not None:
+            import json
+
+            self.fh.write(json.dumps({"step": step, **metrics}) + "\n")
+            self.fh.flush()
+
+
+class Trainer:
+    def __init__(self, cfg, model, train_loader, val_loader, test_loader, device, rank, world_size):
+        self.cfg = as_config(cfg) if not hasattr(cfg, "training") else cfg
+        self.train_loader, self.val_loader, self.test_loader = train_loader, val_loader, test_loader
+        self.device = device
+        self.rank, self.world_size = rank, world_size
+        self.is_ddp = world_size > 1
+        self.is_main_process = rank == 0
+        self.model = model.to(device)
+        tcfg = self.cfg.training
+        get = (lambda c, k, d=None: c.get(k, d)) if hasattr(tcfg, "get") else (lambda c, k, d=None: getattr(c, k, d))
+        self.grad_accum_steps = get(tcfg, "grad_accum_steps", 1)
+        self.early_stopping_patience = get(tcfg, "early_stopping_patience", 3)
+        self.log_grad_norm = bool(get(tcfg, "log_grad_norm", False))
+        pad_id = self.cfg.model.get("pad_token_id", -100) if hasattr(self.cfg.model, "get") else -100
+        self.pad_id = -100 if pad_id is None else pad_id
+
+        ocfg = tcfg.optimizer
+        self.muon_lr_multiplier = get(ocfg, "muon_lr_multiplier", 100.0)
+        tie = self.cfg.model.get("tie_word_embeddings", True) if hasattr(self.cfg.model, "get") else True
+        groups = trainer_param_groups(self.model, tie_word_embeddings=tie, weight_decay=ocfg.weight_decay)
+        opt_cls = DistMuon if self.is_ddp else Muon
+        self.optimizer = opt_cls(groups, lr=ocfg.lr, weight_decay=ocfg.weight_decay,
+                                 muon_lr_multiplier=self.muon_lr_multiplier)
+
+        scfg = tcfg.scheduler
+        name = get(scfg, "name", "linear")
+        self.total_steps = tcfg.total_steps
+        warmup = get(scfg, "warmup_steps", 1000)
+        if name in ("linear", "cosine"):
+            from transformers import get_cosine_schedule_with_warmup, get_linear_schedule_with_warmup
+
+            fn = get_linear_schedule_with_warmup if name == "linear" else get_cosine_schedule_with_warmup
+            self.scheduler = fn(self.optimizer, warmup, self.total_steps)
+        elif name == "onecycle":
+            from torch.optim.lr_scheduler import OneCycleLR
+
+            max_lr = get(scfg, "max_lr", 0.01)
+            self.scheduler = OneCycleLR(
+                self.optimizer,
+                max_lr=[max_lr * self.muon_lr_multiplier if g.get("use_muon") else max_lr
+                        for g in self.optimizer.param_groups],
+                total_steps=self.total_steps, pct_start=get(scfg, "pct_start", 0.3), anneal_strategy="cos")
+        else:
+            self.scheduler = None
+        self.grad_clip = get(tcfg, "grad_clip", None)
+        self.output_dir = _output_dir(self.cfg)
+        mname = self.cfg.model.get("name", "model") if hasattr(self.cfg.model, "get") else "model"
+        self.best_model_path = self.output_dir / f"best_{mname}.pth"
+        self.best_metric = float("inf")
+        self.best_epoch, self.epochs_no_improve, self.global_step = 0, 0, 0
+        self.logger = _Logger(self.output_dir, rank)
+
+    # ------------------------------------------------------------------ losses
+    def compute_loss(self, outputs, labels):
+        """Reference-API loss on GPT.forward's outputs (trainer.py:139-167)."""
+        if not isinstance(outputs, (list, tuple)) or len(outputs) == 1:
+            return F.cross_entropy(outputs.float().reshape(-1, outputs.size(-1)), labels.reshape(-1),
+                                   ignore_index=self.pad_id)
+        logits, halt, qs, targets = outputs
+        token = F.cross_entropy(logits.float().reshape(-1, logits.size(-1)), labels.reshape(-1),
+                                ignore_index=self.pad_id)
+        q_cont = torch.zeros((), device=logits.device)
+        if len(qs) > 0:
+            for i in range(len(qs)):
+                q_cont = q_cont + F.binary_cross_entropy_with_logits(qs[i][..., 1], targets[i])
+            q_cont = q_cont / len(qs)
+        avg_halt = halt / len(qs) if len(qs) > 0 else 0
+        total = token + q_cont + avg_halt
+        return total, token.item(), (q_cont + avg_halt).item()
+
+    def train_step(self, micro_batches):
+        """One optimizer step over `micro_batches` (list of (input_ids, labels) with 1 extra token).
+
+        Returns device tensors (total, token, q) summed over micro-batches."""
+        self.model.train()
+        acc = torch.zeros(3, device=self.device)
+        inv = 1.0 / len(micro_batches)
+        for src, tgt in micro_batches:
+            src = src.to(self.device, non_blocking=True)
+            tgt = tgt.to(self.device, non_blocking=True)
+            total, tok, q = self.model.forward_loss(src[:, :-1], tgt[:, 1:].contiguous())
+            (total * inv).backward()
+            acc += torch.stack([total.detach() * inv, tok.detach() * inv, q.detach()])
+        if self.log_grad_norm and self.is_main_process:
+            norms = [p.grad.norm() for p in self.model.parameters() if p.grad is not None]
+            print(f"Gradient norm: {torch.stack(norms).norm().item():.4f}")
+        if self.grad_clip is not None:
+            torch.nn.utils.clip_grad_norm_(self.model.parameters(), self.grad_clip)
+        self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+        if self.scheduler is not None:
+            self.scheduler.step()
+        self.global_step += 1
+        return acc
+
+    def train(self):
+        val_every = self.cfg.training.get("val_every_n_steps", 1000) if hasattr(self.cfg.training, "get") else 1000
+        it = iter(self.train_loader)
+        while self.global_step < self.total_steps:
+            micro = []
+            for _ in range(self.grad_accum_steps):
+                try:
+                    batch = next(it)
+                except StopIteration:
+                    it = iter(self.train_loader)
+                    batch = next(it)
+                micro.append((batch["src"], batch["tgt"]))
+            acc = self.train_step(micro)
+            if self.is_main_process:
+                tot, tok, q = acc.tolist()
+                lr = self.optimizer.param_groups[0]["lr"]
+                self.logger.log({"Loss/train_total": tot, "Loss/train_token": tok, "Loss/train_q": q, "lr": lr},
+                                self.global_step)
+            final = self.global_step == self.total_steps
+            if (self.global_step > 0 and self.global_step % val_every == 0) or final:
+                val = self._validate_loss(self.val_loader)
+                if self.is_main_process:
+                    self.logger.log({"Loss/val_fineweb": val}, self.global_step)
+                    if val < self.best_metric:
+                        self.best_metric, self.best_epoch = val, self.global_step
+                        self.save_checkpoint(self.best_model_path, self.global_step)
+                        self.epochs_no_improve = 0
+                    else:
+                        self.epochs_no_improve += 1
+                if self.is_ddp:
+                    import torch.distributed as dist
+
+                    dist.barrier()
+                if 0 < self.early_stopping_patience <= self.epochs_no_improve:
+                    break
+        if self.is_main_process:
+            print(f"Training complete. Best Loss: {self.best_metric:.4f}")
+
+    @torch.no_grad()
+    def _validate_loss(self, dataloader):
+        self.model.eval()
+        total = torch.zeros((), device=self.device)
+        count = 0
+        for batch in dataloader:
+            src = batch["src"].to(self.device)
+            tgt = batch["tgt"].to(self.device)
+            tot, tok, _ = self.model.forward_loss(src[:, :-1], tgt[:, 1:].contiguous())
+            total += tok
+            count += 1
+        avg = total / count if count > 0 else total
+        if self.is_ddp:
+            import torch.distributed as dist
+
+            dist.all_reduce(avg, op=dist.ReduceOp.AVG)
+        self.model.train()
+        return avg.item()
+
+    def test(self):
+        if self.is_main_process:
+            print("Testing the model...")
+        loss = self._validate_loss(self.test_loader)
+        if self.is_main_process:
+            self.logger.log({"Loss/test": loss}, self.global_step)
+            print(f"Test Loss: {loss:.4f}")
+        return loss
+
+    # ------------------------------------------------------------------ checkpoints
+    def _get_model_for_saving(self):
+        m = self.model.module if hasattr(self.model, "module") else self.model
+        return m._orig_mod if hasattr(m, "_orig_mod") else m
+
+    def save_checkpoint(self, path, epoch):
+        """Same dictionary as the reference (trainer.py:311-322), written by rank 0."""
+        if not self.is_main_process:
+            return
+        Path(path).parent.mkdir(parents=True, exist_ok=True)
+        torch.save({"model_state_dict": self._get_model_for_saving().state_dict(),
+                    "optimizer_state_dict": self.optimizer.state_dict(),
+                    "best_metric": self.best_metric, "global_step": self.global_step}, path)
+
+    def load_checkpoint(self, path):
+        """Resume from a save_checkpoint() file (model, optimizer state, counters)."""
+        ck = torch.load(path, map_location=self.device, weights_only=False)
+        self._get_model_for_saving().load_state_dict(ck["model_state_dict"])
+        self.optimizer.load_state_dict(ck["optimizer_state_dict"])
+        self.best_metric = ck.get("best_metric", float("inf"))
+        self.global_step = ck.get("global_step", 0)
+        return ck
