@@ -133,6 +133,17 @@ int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M
 int rgpt_cross_entropy(void* logits, long long ld, int M, int V, const long long* labels, int ignore_index,
                        float grad_scale, float* loss_rows, int* argmax, float* scale_buf, float* loss_out,
                        int write_grad, void* stream);
+/* Allocation-free variant of rgpt_cross_entropy (no counterpart in the reference). For callers that
+ * cannot allocate device memory (plugin hosts that hand over only input/output buffers, processes whose
+ * device memory is fully reserved by another allocator): the per-row losses and the scale/count pair live
+ * in a static device array inside this library (1 MiB, held by every GPU that loads it until exit).
+ * Same outputs as rgpt_cross_entropy: loss_out[0] = mean loss, argmax (optional), in-place dlogits when
+ * write_grad. M is limited to 262144 rows; larger M is rejected with RGPT_ERR_BAD_SHAPE. The first call on
+ * a device resolves the array's device address, so make that first call before any stream capture.
+ * Calls share the array: calls that overlap on the GPU (e.g. on two streams) race. Nothing in it needs to
+ * start at zero; each call rewrites what it reads. No cudaMalloc/cudaFree is made. */
+int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int V, const long long* labels, int ignore_index,
+                               float grad_scale, float* loss_out, int* argmax, int write_grad, void* stream);
 /* rGPT halting losses (model/gpt.py:105-141, trainer.py:150-162): q [R, M, 2], argmax [R, M].
  * losses[0] += halt BCE mean, losses[1] += q_continue BCE mean; dq = grad_scale * d(total)/dq. */
 int rgpt_halt_losses(const float* q, const int* argmax, const long long* labels, int R, int M, float grad_scale,

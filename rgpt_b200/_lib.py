@@ -51,6 +51,8 @@ _SIGNATURES: dict[str, list] = {
     "rgpt_embedding_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_cross_entropy": [_c_vp, _c_ll, _c_int, _c_int, _c_vp, _c_int, _c_float, _c_vp, _c_vp, _c_vp, _c_vp,
                            _c_int, _c_vp],
+    "rgpt_cross_entropy_noalloc": [_c_vp, _c_ll, _c_int, _c_int, _c_vp, _c_int, _c_float, _c_vp, _c_vp, _c_int,
+                                   _c_vp],
     "rgpt_halt_losses": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_float, _c_vp, _c_vp, _c_vp],
     "rgpt_adamw": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_float, _c_float, _c_float, _c_float, _c_float, _c_int,
                    _c_vp],
@@ -104,7 +106,8 @@ def last_error() -> str:
 
 
 # Kernels each entry point enqueues (rgpt_cross_entropy: up to 3, counted by its wrapper).
-_KERNELS_PER_CALL = {"rgpt_last_error": 0, "rgpt_device_error": 0, "rgpt_version": 0}
+_KERNELS_PER_CALL = {"rgpt_last_error": 0, "rgpt_device_error": 0, "rgpt_version": 0,
+                     "rgpt_cross_entropy_noalloc": 3}
 launch_count = 0  # native kernels enqueued by this process (read by the benchmark)
 
 

@@ -1039,3 +1039,59 @@ extern "C" int rgpt_halt_losses(const float* q, const int* argmax, const long lo
       q, argmax, labels, R, M, grad_scale, dq, losses);
   return rgpt_check_launch("halt_losses_kernel");
 }
+
+// ============================================================================ allocation-free cross entropy
+// For callers that cannot allocate device memory: plugin-style hosts whose enqueue
+// contract hands over only the input/output buffers, and processes whose device memory
+// is already fully reserved by another framework's pool, so a cudaMalloc would fail.
+// The scratch that rgpt_cross_entropy takes from its caller (per-row losses and the
+// {grad_scale/count, count} pair) lives instead in this file-scope array, which every
+// GPU that loads the library holds until the process exits (1 MiB + 256 B).
+#define RGPT_CE_NOALLOC_MAX_ROWS 262144
+static __device__ __align__(256) float g_ce_noalloc_scratch[RGPT_CE_NOALLOC_MAX_ROWS + 64];
+
+// Device address of the scratch array for `dev`, resolved once per device with that device
+// current. (In host code the array's name only stands in for the symbol.)
+static float* ce_noalloc_scratch(int dev, int* status) {
+  static float* addr[64] = {nullptr};
+  if (dev < 0 || dev >= 64) {
+    *status = rgpt_set_error(RGPT_ERR_INTERNAL, "device index %d out of range", dev);
+    return nullptr;
+  }
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      *status = rgpt_set_error(RGPT_ERR_INTERNAL, "cudaGetSymbolAddress(cross-entropy scratch) failed: %s",
+                               cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = reinterpret_cast<float*>(p);
+  }
+  return addr[dev];
+}
+
+extern "C" int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int V, const long long* labels,
+                                          int ignore_index, float grad_scale, float* loss_out, int* argmax,
+                                          int write_grad, void* stream) {
+  if (M < 1 || M > RGPT_CE_NOALLOC_MAX_ROWS)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE,
+                          "rgpt_cross_entropy_noalloc handles 1..%d rows (got %d); use rgpt_cross_entropy for more",
+                          RGPT_CE_NOALLOC_MAX_ROWS, M);
+  if (loss_out == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "loss_out is required");
+  if ((reinterpret_cast<uintptr_t>(logits) & 15) || (ld % 8))
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "logits must be 16-byte aligned with ld %% 8 == 0");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int st = RGPT_OK;
+  float* scratch = ce_noalloc_scratch(dev, &st);
+  if (scratch == nullptr) return st;
+  float* loss_rows = scratch;                           // M floats, every one rewritten by this call
+  float* scale_buf = scratch + RGPT_CE_NOALLOC_MAX_ROWS;  // {grad_scale/count, count}, rewritten by this call
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
+  cross_entropy_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, labels, ignore_index,
+                                         loss_rows, argmax, scale_buf, write_grad);
+  ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
+  return rgpt_check_launch("cross_entropy_noalloc");
+}
