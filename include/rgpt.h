@@ -49,7 +49,8 @@ enum RgptEpilogue {
   RGPT_EPI_ACT_BWD = 4,    /* D bf16 = alpha*acc * act'(C), C bf16 (pre)            */
   RGPT_EPI_RESID_F32 = 5,  /* D f32 = C f32 + alpha*acc*colscale[n] (colscale opt.);
                               D2 f32 (optional) = alpha*acc, the unscaled branch output */
-  RGPT_EPI_POLY_BF16 = 6   /* D bf16 = beta*C + alpha*acc, C bf16                   */
+  RGPT_EPI_POLY_BF16 = 6,  /* D bf16 = beta*C + alpha*acc, C bf16                   */
+  RGPT_EPI_BIAS_SIGMOID_BF16 = 7 /* D bf16 = sigmoid(alpha*acc + colscale[n]) (G1 gate)   */
 };
 enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4 };
 
@@ -109,19 +110,20 @@ int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w, float temp
                      const void* h, float* dqw, float* dqb, void* stream);
 
 /* ------------------------------------------------------------------ QKV prep
- * Per (token, head): QK norm (QKNorm, model/norm.py:182-204), G1 gate sigmoid(q_n Wg^T + bg)
- * (model/attention.py:45-48, gate_proj shared by all heads), RoPE (model/rope.py:38-57).
- * qkv [M, 3d] bf16 -> qk [M, 2d] bf16, gate [M, d] bf16. inv_freq[32] as model/rope.py:11.
- * sq/sk are constant post-scales (asymmetric hyperball 1.0/1.1; otherwise 1). */
-int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* gate, const float* wg, const float* bg,
-                      const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq, const float* wk,
-                      float tq, float tk, float sq, float sk, int M, int T, int H, void* stream);
-/* Backward: dq, dk fp32 [M, d] (grads of the roped q, k), dgp bf16 [M, d] (grad of the gate
- * pre-activation) -> dqkv q/k column blocks (bf16); dwg/dbg (and dwq/dwk, dtq/dtk) ACCUMULATED. */
-int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const void* dgp, void* dqkv,
-                      const float* wg, float* dwg, float* dbg, float* dwq, float* dwk, float* dtq, float* dtk,
-                      const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq, const float* wk,
-                      float tq, float tk, float sq, float sk, int M, int T, int H, void* stream);
+ * Per (token, head): QK norm (QKNorm, model/norm.py:182-204) and RoPE (model/rope.py:38-57).
+ * qkv [M, 3d] bf16 -> qk [M, 2d] bf16 (roped normalised q | k), qn [M, d] bf16 (normalised q before
+ * RoPE, the input of the G1 gate GEMM sigmoid(qn Wg^T + bg), model/attention.py:45-48; may be null).
+ * inv_freq[32] as model/rope.py:11. sq/sk: constant post-scales (asymmetric hyperball 1.0/1.1, else 1). */
+int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const float* inv_freq, int qk_kind, float eps,
+                      float alpha, const float* wq, const float* wk, float tq, float tk, float sq, float sk,
+                      int M, int T, int H, void* stream);
+/* Backward: dq, dk fp32 [M, d] (grads of the roped q, k) and dqn_gate fp32 [M, d] (= dgp Wg from the
+ * gate GEMM, may be null) -> the q/k column blocks of dqkv (bf16). dbg += column sums of dgp (bf16
+ * [M, d]); dwq/dwk (RMS_AFFINE QK norms) and dtq/dtk (L2_TEMP) are ACCUMULATED. */
+int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const float* dqn_gate, const void* dgp,
+                      void* dqkv, float* dbg, float* dwq, float* dwk, float* dtq, float* dtk, const float* inv_freq,
+                      int qk_kind, float eps, float alpha, const float* wq, const float* wk, float tq, float tk,
+                      float sq, float sk, int M, int T, int H, void* stream);
 
 /* ------------------------------------------------------------------ embedding / loss
  * nn.Embedding forward (model/gpt.py:95) and its backward (dx rows ACCUMULATED into demb). */

@@ -42,10 +42,10 @@ _SIGNATURES: dict[str, list] = {
     "rgpt_rownorm_bwd": [_c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
                          _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                          _c_vp, _c_vp],
-    "rgpt_qkv_prep_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp,
-                          _c_float, _c_float, _c_float, _c_float, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_qkv_prep_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float,
+                          _c_float, _c_float, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_qkv_prep_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
-                          _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float, _c_float, _c_float,
+                          _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float, _c_float, _c_float,
                           _c_int, _c_int, _c_int, _c_vp],
     "rgpt_embedding_fwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_embedding_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],

@@ -50,15 +50,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 att_encode_fn() {
   return fn;
 }
 
-// (64, H, T, B) view of a token-major [B*T, row_stride] bf16 matrix starting at `base`.
-static int make_head_map(CUtensorMap* map, const void* base, int H, int T, int B, long long row_stride) {
+// (64, H, T, B) view of a token-major [B*T, row_stride] bf16 matrix starting at `base`;
+// one box = `box_rows` rows x 64 columns of one head (128-byte swizzle).
+static int make_head_map(CUtensorMap* map, const void* base, int H, int T, int B, long long row_stride,
+                         int box_rows = ATT_TILE) {
   auto enc = att_encode_fn();
   if (enc == nullptr) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride * 2) % 16 != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "attention operand base/row stride not 16-byte aligned");
   cuuint64_t dims[4] = {(cuuint64_t)ATT_D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)ATT_D * 2, (cuuint64_t)row_stride * 2, (cuuint64_t)T * row_stride * 2};
-  cuuint32_t box[4] = {ATT_D, 1, ATT_TILE, 1};
+  cuuint32_t box[4] = {ATT_D, 1, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -66,6 +68,38 @@ static int make_head_map(CUtensorMap* map, const void* base, int H, int T, int B
   if (r != CUDA_SUCCESS) return rgpt_set_error(RGPT_ERR_INTERNAL, "attention tensor map encode failed (%d)", (int)r);
   return RGPT_OK;
 }
+
+// fp32 (64, H, T, B) view of a token-major [B*T, d] fp32 matrix, 32 x 32 boxes (128-byte swizzle):
+// the target of the per-warp dQ bulk reduce-adds.
+static int make_head_map_f32(CUtensorMap* map, const float* base, int H, int T, int B, long long row_stride) {
+  auto enc = att_encode_fn();
+  if (enc == nullptr) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride * 4) % 16 != 0)
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "dq base/row stride not 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)ATT_D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ATT_D * 4, (cuuint64_t)row_stride * 4, (cuuint64_t)T * row_stride * 4};
+  cuuint32_t box[4] = {32, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return rgpt_set_error(RGPT_ERR_INTERNAL, "dq tensor map encode failed (%d)", (int)r);
+  return RGPT_OK;
+}
+
+// Bulk add of a 32 x 32 fp32 smem tile into global memory through a tensor map (rows past the
+// tensor's extent are skipped by the hardware). Coordinates are never negative here.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2,
+                                                  int c3) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2, int c3) {
@@ -97,16 +131,22 @@ struct AttnFwdParams {
   float* lse;        // [B, H, T] natural-log LSE of the scaled scores
 };
 
-__global__ void __launch_bounds__(ATT_THREADS, 1)
+constexpr int FWD_KT = 64;                                  // keys per tile in the forward
+constexpr uint32_t KV_TILE_BYTES = FWD_KT * ATT_D * 2;      // 8 KB
+constexpr uint32_t P_TILE_BYTES = ATT_TILE * FWD_KT * 2;    // 16 KB: [128 queries x 64 keys] bf16
+
+// Forward CTA: 128 queries of one (b, h), 64-key tiles. 256 TMEM columns and ~80 KB of smem
+// let two CTAs share an SM, so one CTA's softmax overlaps the other's tensor-core work.
+__global__ void __launch_bounds__(ATT_THREADS, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                        // 16 KB
-  uint8_t* sK = sQ + TILE_BYTES;             // 2 x 16 KB
-  uint8_t* sV = sK + 2 * TILE_BYTES;         // 2 x 16 KB
-  uint8_t* sP = sV + 2 * TILE_BYTES;         // 2 buffers x (2 atoms x 16 KB)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 4 * TILE_BYTES);
+  uint8_t* sK = sQ + TILE_BYTES;             // 2 x 8 KB
+  uint8_t* sV = sK + 2 * KV_TILE_BYTES;      // 2 x 8 KB
+  uint8_t* sP = sV + 2 * KV_TILE_BYTES;      // 2 x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_TILE_BYTES);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
@@ -124,7 +164,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   const int h = blockIdx.y, b = blockIdx.z;
   const int q0 = qt * ATT_TILE;
   const int last_key = min(q0 + ATT_TILE - 1, p.T - 1);
-  const int nkv = last_key / ATT_TILE + 1;
+  const int nkv = last_key / FWD_KT + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -141,14 +181,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,128) S1 [128,256) O0 [256,320) O1 [320,384)
+  // TMEM columns: S0 [0,64) S1 [64,128) O0 [128,192) O1 [192,256)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -161,9 +201,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        tma_load_4d(sK + s * TILE_BYTES, &tmK, &kv_full[s], 0, h, j * ATT_TILE, b);
-        tma_load_4d(sV + s * TILE_BYTES, &tmV, &kv_full[s], 0, h, j * ATT_TILE, b);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_TILE_BYTES);
+        tma_load_4d(sK + s * KV_TILE_BYTES, &tmK, &kv_full[s], 0, h, j * FWD_KT, b);
+        tma_load_4d(sV + s * KV_TILE_BYTES, &tmV, &kv_full[s], 0, h, j * FWD_KT, b);
       }
       if (!ok) {
         mbar_wait(q_full, 0, nullptr);
@@ -173,7 +213,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t IDESC_S = make_idesc_bf16(128, FWD_KT, 0, 0);
       constexpr uint32_t IDESC_O = make_idesc_bf16(128, 64, 0, 1);
       bool ok = mbar_wait(q_full, 0, abort_flag);
       const uint32_t q_addr = smem_u32(sQ);
@@ -183,13 +223,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         if (!mbar_wait(&p_full[s], ph, abort_flag)) return false;
         if (!mbar_wait(&o_empty[s], ph ^ 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + s * 2 * TILE_BYTES);
-        const uint32_t v_addr = smem_u32(sV + s * TILE_BYTES);
+        const uint32_t p_addr = smem_u32(sP + s * P_TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sV + s * KV_TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < ATT_TILE / 16; ++kk) {
-          const uint64_t adesc = make_sw128_desc(p_addr + (kk >> 2) * TILE_BYTES + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = make_sw128_desc(v_addr + kk * 2048, TILE_BYTES, 1024);
-          umma_bf16(tmem + 256 + s * 64, adesc, bdesc, IDESC_O, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < FWD_KT / 16; ++kk) {
+          const uint64_t adesc = make_sw128_desc(p_addr + kk * 32, 16, 1024);
+          const uint64_t bdesc = make_sw128_desc(v_addr + kk * 2048, KV_TILE_BYTES, 1024);
+          umma_bf16(tmem + 128 + s * 64, adesc, bdesc, IDESC_O, kk > 0 ? 1u : 0u);
         }
         umma_commit(&o_full[s]);
         umma_commit(&kv_empty[s]);
@@ -203,10 +243,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sK + s * KV_TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          umma_bf16(tmem + s * 128, make_sw128_desc(q_addr + kk * 32, 16, 1024),
+          umma_bf16(tmem + s * 64, make_sw128_desc(q_addr + kk * 32, 16, 1024),
                     make_sw128_desc(k_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[s]);
@@ -239,7 +279,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       uint32_t v[32];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        tmem_ld32(t_lane + 256 + s * 64 + c * 32, v);
+        tmem_ld32(t_lane + 128 + s * 64 + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
         for (int t = 0; t < 32; ++t) o_acc[c * 32 + t] = o_acc[c * 32 + t] * alpha + __uint_as_float(v[t]);
@@ -256,47 +296,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const bool diag = (j == nkv - 1);
-      const int kbase = j * ATT_TILE;
-      // pass 1: row max of the scaled, masked scores
+      const int kbase = j * FWD_KT;
+      const bool masked = (kbase + FWD_KT > q0) || (kbase + FWD_KT > p.T);  // tiles on the diagonal / past T
+      uint32_t v[2][32];
+      tmem_ld32(t_lane + s * 64, v[0]);
+      tmem_ld32(t_lane + s * 64 + 32, v[1]);
+      tmem_wait_ld();
       float mx = -INFINITY;
-      uint32_t v[32];
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(t_lane + s * 128 + c * 32, v);
-        tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
           const int key = kbase + c * 32 + t;
-          float x = __uint_as_float(v[t]) * p.scale_log2;
-          if (diag && (key > qrow || key >= p.T)) x = -INFINITY;
+          float x = __uint_as_float(v[c][t]) * p.scale_log2;
+          if (masked && (key > qrow || key >= p.T)) x = -INFINITY;
+          v[c][t] = __float_as_uint(x);
           mx = fmaxf(mx, x);
         }
       }
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);  // S is in registers now; the TMEM buffer can be refilled
       const float m_new = fmaxf(m_run, mx);
       const float alpha = exp2f(m_run - m_new);
-      // pass 2: P = exp2(x - m_new) -> bf16 swizzled smem, row sum
       float sum = 0.f;
-      uint8_t* pbuf = sP + s * 2 * TILE_BYTES;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(t_lane + s * 128 + c * 32, v);
-        tmem_wait_ld();
+      uint8_t* pbuf = sP + s * P_TILE_BYTES;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         float pv[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          const int key = kbase + c * 32 + t;
-          float x = __uint_as_float(v[t]) * p.scale_log2;
-          if (diag && (key > qrow || key >= p.T)) x = -INFINITY;
-          pv[t] = exp2f(x - m_new);
+          pv[t] = exp2f(__uint_as_float(v[c][t]) - m_new);
           sum += pv[t];
         }
-        uint8_t* atom = pbuf + (c >> 1) * TILE_BYTES;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) st_sw128_chunk(atom, r, (c & 1) * 4 + t, pv + 8 * t);
+        for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
       }
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[s]);
       l_run = l_run * alpha + sum;
@@ -349,7 +383,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, 256);
   }
 }
 
@@ -405,17 +439,22 @@ struct AttnBwdParams {
   float scale_log2;  // scale * log2(e)
   const float* lse;  // [B, H, T] natural log
   const float* Dvec; // [B, H, T]
-  float* dq;         // [B*T, d] fp32, accumulated with atomics (caller zeroes)
   float* dk;         // [B*T, dk_stride] fp32
   long long dk_stride;
   __nv_bfloat16* dv; // [B*T, dv_stride] bf16
   long long dv_stride;
 };
 
-__global__ void __launch_bounds__(ATT_THREADS, 1)
+constexpr int ATT_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
+constexpr uint32_t DQ_STAGE_BYTES = 32 * 32 * 4;  // one warp's 32 x 32 fp32 dQ tile
+
+// Backward CTA = one 128-key tile of one (b, h). The 8 softmax warps come in pairs that
+// share TMEM lane quadrants: warp pair (w, w+4) owns key rows 32*(w%4).. and splits the
+// 128 query columns of P^T/dS^T (and later the 64 head columns of dQ/dK/dV) in halves.
+__global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    AttnBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, AttnBwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                     // 16 KB
@@ -424,7 +463,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint8_t* sDO = sQ + 2 * TILE_BYTES;     // 2 x 16 KB
   uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T  : 2 atoms (queries 0-63, 64-127) x 16 KB
   uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T : 2 atoms x 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDS + 2 * TILE_BYTES);
+  uint8_t* sDQ = sDS + 2 * TILE_BYTES;    // 8 x 4 KB dQ staging (one per softmax warp)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDQ + 8 * DQ_STAGE_BYTES);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
@@ -450,12 +490,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&qd_empty[i], 1);
     }
     mbar_init(sdp_full, 1);
-    mbar_init(ds_ready, 128);
+    mbar_init(ds_ready, 256);
     mbar_init(dq_full, 1);
-    mbar_init(dq_empty, 128);
+    mbar_init(dq_empty, 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tmDQ);
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -539,10 +580,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
     __syncwarp();
   } else {
-    const int quarter = warp & 3;
+    const int sw = warp - 2;            // 0..7
+    const int quarter = warp & 3;       // TMEM lane quadrant
+    const int half = sw >> 2;           // which half of the columns this warp handles
     const int r = quarter * 32 + lane;  // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const int key = k0 + r;
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* stage = sDQ + sw * DQ_STAGE_BYTES;
     bool ok = true;
     auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
       int v = 1;
@@ -560,7 +604,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tc_fence_after();
       const bool diag = (i == 0);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = half * 2 + cc;  // 32-column chunk of the 128 queries
         uint32_t sv[32], dv[32];
         tmem_ld32(t_lane + 0 + c * 32, sv);
         tmem_ld32(t_lane + 128 + c * 32, dv);
@@ -577,12 +622,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           pr[t] = pv;
           ds[t] = pv * (__uint_as_float(dv[t]) - __ldg(D_bh + qc)) * p.scale;
         }
-        uint8_t* patom = sP + (c >> 1) * TILE_BYTES;
-        uint8_t* datom = sDS + (c >> 1) * TILE_BYTES;
+        uint8_t* patom = sP + half * TILE_BYTES;
+        uint8_t* datom = sDS + half * TILE_BYTES;
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
-          st_sw128_chunk(patom, r, (c & 1) * 4 + t, pr + 8 * t);
-          st_sw128_chunk(datom, r, (c & 1) * 4 + t, ds + 8 * t);
+          st_sw128_chunk(patom, r, cc * 4 + t, pr + 8 * t);
+          st_sw128_chunk(datom, r, cc * 4 + t, ds + 8 * t);
         }
       }
       tc_fence_before();
@@ -593,52 +638,55 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         break;
       }
       tc_fence_after();
-      // dQ rows: TMEM lane r = query row qrow0 + r
-      const int q = qrow0 + r;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
+      // dQ rows (TMEM lane r = query row qrow0 + r), this warp's 32 of the 64 head columns
+      {
         uint32_t v[32];
-        tmem_ld32(t_lane + 384 + c * 32, v);
+        tmem_ld32(t_lane + 384 + half * 32, v);
         tmem_wait_ld();
-        if (q < p.T) {
-          float4* dst = reinterpret_cast<float4*>(p.dq + ((long long)b * p.T + q) * p.d + h * ATT_D + c * 32);
+        if (lane == 0) bulk_wait_read0();  // the previous bulk reduce has finished reading the stage
+        __syncwarp();
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            atomicAdd(dst + t, make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
-                                           __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3])));
+        for (int j = 0; j < 8; ++j)
+          *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]), __uint_as_float(v[4 * j + 2]),
+                          __uint_as_float(v[4 * j + 3]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && qrow0 + quarter * 32 < p.T) {  // boxes wholly past T carry only zeros
+          tma_reduce_add_4d(&tmDQ, stage, half * 32, h, qrow0 + quarter * 32, b);
+          bulk_commit();
         }
       }
       tc_fence_before();
       mbar_arrive(dq_empty);
     }
+    if (lane == 0) bulk_wait0();  // every dQ reduce has landed before the CTA retires
+    __syncwarp();
     // dK, dV rows (key-major) once every query tile has been folded in. Every lane runs the
     // warp-collective TMEM loads; only the stores are predicated on the row being inside T.
     if (ok) {
       const bool valid = key < p.T;
       const long long row = (long long)b * p.T + (valid ? key : 0);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld32(t_lane + 256 + c * 32, v);
-        tmem_wait_ld();
-        if (valid) {
-          uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + c * 32);
+      uint32_t v[32];
+      tmem_ld32(t_lane + 256 + half * 32, v);
+      tmem_wait_ld();
+      if (valid) {
+        uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + half * 32);
 #pragma unroll
-          for (int t = 0; t < 4; ++t)
-            dst[t] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
-                                pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
-                                pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
-                                pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
-        }
-        tmem_ld32(t_lane + 320 + c * 32, v);
-        tmem_wait_ld();
-        if (valid) {
-          float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + c * 32);
+        for (int t = 0; t < 4; ++t)
+          dst[t] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
+                              pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
+                              pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
+                              pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
+      }
+      tmem_ld32(t_lane + 320 + half * 32, v);
+      tmem_wait_ld();
+      if (valid) {
+        float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + half * 32);
 #pragma unroll
-          for (int t = 0; t < 8; ++t)
-            dkd[t] = make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
-                                 __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
-        }
+        for (int t = 0; t < 8; ++t)
+          dkd[t] = make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
+                               __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
       }
     }
     tc_fence_before();
@@ -651,8 +699,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   }
 }
 
-constexpr uint32_t FWD_SMEM = 9 * TILE_BYTES + 256 + 1024;
-constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 256 + 1024;
+constexpr uint32_t FWD_SMEM = TILE_BYTES + 4 * KV_TILE_BYTES + 2 * P_TILE_BYTES + 256 + 1024;
+constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 256 + 1024;
 
 }  // namespace rgpt
 
@@ -678,8 +726,8 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
   const __nv_bfloat16* qkb = reinterpret_cast<const __nv_bfloat16*>(qk);
   const __nv_bfloat16* qkvb = reinterpret_cast<const __nv_bfloat16*>(qkv);
   if ((st = make_head_map(&tq, qkb, H, T, B, 2LL * d))) return st;
-  if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d))) return st;
-  if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d))) return st;
+  if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d, FWD_KT))) return st;
+  if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d, FWD_KT))) return st;
   AttnFwdParams p;
   p.B = B;
   p.T = T;
@@ -727,13 +775,14 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
   if ((reinterpret_cast<uintptr_t>(dq) & 15) || (reinterpret_cast<uintptr_t>(dk) & 15) ||
       (reinterpret_cast<uintptr_t>(dv) & 15) || (dk_stride % 4) || (dv_stride % 8))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "attention gradient buffers must be 16-byte aligned");
-  CUtensorMap tq, tk, tv, tdo;
+  CUtensorMap tq, tk, tv, tdo, tdq;
   const __nv_bfloat16* qkb = reinterpret_cast<const __nv_bfloat16*>(qk);
   const __nv_bfloat16* qkvb = reinterpret_cast<const __nv_bfloat16*>(qkv);
   if ((st = make_head_map(&tq, qkb, H, T, B, 2LL * d))) return st;
   if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d))) return st;
   if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d))) return st;
   if ((st = make_head_map(&tdo, dout, H, T, B, (long long)d))) return st;
+  if ((st = make_head_map_f32(&tdq, dq, H, T, B, (long long)d))) return st;
   AttnBwdParams p;
   p.B = B;
   p.T = T;
@@ -743,7 +792,6 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   p.lse = lse;
   p.Dvec = Dvec;
-  p.dq = dq;
   p.dk = dk;
   p.dk_stride = dk_stride;
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
@@ -755,6 +803,6 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
     attr[dev] = true;
   }
   dim3 grid((T + ATT_TILE - 1) / ATT_TILE, H, B);
-  attn_bwd_kernel<<<grid, ATT_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<<<grid, ATT_BWD_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, tdq, p);
   return rgpt_check_launch("attn_bwd_kernel");
 }

@@ -248,6 +248,24 @@ __device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const GemmSh
       }
       break;
     }
+    case RGPT_EPI_BIAS_SIGMOID_BF16: {
+      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
+      const float* bias = ep.colscale + gn0;
+      if (full) {
+        uint4* d4 = reinterpret_cast<uint4*>(d);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float g[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) g[e] = 1.0f / (1.0f + expf(-(v[8 * q + e] + bias[8 * q + e])));
+          d4[q] = make_uint4(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]), pack_bf16x2(g[4], g[5]),
+                             pack_bf16x2(g[6], g[7]));
+        }
+      } else {
+        for (int j = 0; j < ncols; ++j) d[j] = __float2bfloat16(1.0f / (1.0f + expf(-(v[j] + bias[j]))));
+      }
+      break;
+    }
     default:
       break;
   }
@@ -505,7 +523,7 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   if (batch < 1) batch = 1;
   if (M < 1 || N < 1 || K < 1)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M, N, K >= 1 (got M=%d N=%d K=%d)", M, N, K);
-  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_POLY_BF16)
+  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_BIAS_SIGMOID_BF16)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown epilogue %d", epi);
   if (D == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm output pointer is null");
   const bool out_f32 = (epi == RGPT_EPI_STORE_F32 || epi == RGPT_EPI_ACCUM_F32 || epi == RGPT_EPI_RESID_F32);
@@ -519,6 +537,8 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   if ((epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_RESID_F32 || epi == RGPT_EPI_POLY_BF16) &&
       (C == nullptr || ldc % vec != 0 || (reinterpret_cast<uintptr_t>(C) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "epilogue input C missing or not 16-byte aligned");
+  if (epi == RGPT_EPI_BIAS_SIGMOID_BF16 && colscale == nullptr)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "BIAS_SIGMOID needs the bias vector (colscale)");
   if (colscale != nullptr && (reinterpret_cast<uintptr_t>(colscale) & 15) != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "colscale must be 16-byte aligned");
 

@@ -302,10 +302,13 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
 }
 
 // ============================================================================ QKV prep
-// One thread per (token, head). Reads the raw q, k of the QKV projection, applies
-// the QK norm, the G1 gate and RoPE, and writes:
-//   qk   [M, 2d]  (roped normalised q | k, bf16)  -- the attention operands
-//   gate [M, d]   sigmoid(q_n Wg^T + bg)          -- gate_proj is shared by every head
+// One warp per (token, head) row; lane l holds elements 2l, 2l+1 of the 64-wide head
+// (4-byte loads: a warp moves one contiguous 128-byte row). RoPE partners i and
+// i + 32 live in lanes l and l ^ 16. Forward writes
+//   qk [M, 2d]  roped, normalised q | k (the attention operands, bf16)
+//   qn [M, d]   normalised q before RoPE (bf16), the input of the gate GEMM
+// The G1 gate itself, sigmoid(q_n Wg^T + bg), is a tcgen05 GEMM with a bias+sigmoid
+// epilogue, and its backward runs as GEMMs too (dqn += dgp Wg, dWg += dgp^T q_n).
 struct QkNormArgs {
   int kind;
   float eps, alpha;
@@ -315,310 +318,166 @@ struct QkNormArgs {
   float sq, sk;     // constant post-scales (asymmetric hyperball: 1.0 / 1.1)
 };
 
-__device__ __forceinline__ void load_row64(const __nv_bfloat16* p, float* v) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    uint4 u = reinterpret_cast<const uint4*>(p)[c];
-    float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), e = unpack_bf16x2(u.z), f = unpack_bf16x2(u.w);
-    v[8 * c + 0] = a.x;
-    v[8 * c + 1] = a.y;
-    v[8 * c + 2] = b.x;
-    v[8 * c + 3] = b.y;
-    v[8 * c + 4] = e.x;
-    v[8 * c + 5] = e.y;
-    v[8 * c + 6] = f.x;
-    v[8 * c + 7] = f.y;
+__device__ __forceinline__ float2 qk_affine2(const QkNormArgs& a, bool is_q, int i0) {
+  if (a.kind == RGPT_NORM_RMS_AFFINE) {
+    const float* w = is_q ? a.wq : a.wk;
+    return make_float2(1.0f + w[i0], 1.0f + w[i0 + 1]);
   }
-}
-
-__device__ __forceinline__ void store_row64(__nv_bfloat16* p, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 8; ++c)
-    reinterpret_cast<uint4*>(p)[c] =
-        make_uint4(pack_bf16x2(v[8 * c], v[8 * c + 1]), pack_bf16x2(v[8 * c + 2], v[8 * c + 3]),
-                   pack_bf16x2(v[8 * c + 4], v[8 * c + 5]), pack_bf16x2(v[8 * c + 6], v[8 * c + 7]));
-}
-
-// affine factor of the QK norm for element i
-__device__ __forceinline__ float qk_affine(const QkNormArgs& a, bool is_q, int i) {
-  if (a.kind == RGPT_NORM_RMS_AFFINE) return 1.0f + (is_q ? a.wq[i] : a.wk[i]);
-  if (a.kind == RGPT_NORM_L2_TEMP) return is_q ? a.tq : a.tk;
-  return 1.0f;
-}
-
-__device__ __forceinline__ void rope_fwd64(float* v, const float* cs, const float* sn) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float a = v[i], b = v[i + 32];
-    v[i] = a * cs[i] - b * sn[i];
-    v[i + 32] = b * cs[i] + a * sn[i];
+  if (a.kind == RGPT_NORM_L2_TEMP) {
+    const float t = is_q ? a.tq : a.tk;
+    return make_float2(t, t);
   }
+  return make_float2(1.0f, 1.0f);
 }
 
-__device__ __forceinline__ void rope_bwd64(float* v, const float* cs, const float* sn) {
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float a = v[i], b = v[i + 32];
-    v[i] = a * cs[i] + b * sn[i];
-    v[i + 32] = b * cs[i] - a * sn[i];
-  }
+// rotate-half RoPE on a lane's pair (x0, x1) = elements 2l, 2l+1
+__device__ __forceinline__ float2 rope_pair(float2 x, float2 c, float2 sn, bool second_half, int dir) {
+  const float p0 = __shfl_xor_sync(0xffffffffu, x.x, 16);
+  const float p1 = __shfl_xor_sync(0xffffffffu, x.y, 16);
+  // forward: first half y = x c - partner s; second half y = x c + partner s (dir = +1); backward flips the sign
+  const float sg = (second_half ? 1.0f : -1.0f) * (float)dir;
+  return make_float2(x.x * c.x + sg * p0 * sn.x, x.y * c.y + sg * p1 * sn.y);
 }
 
-__global__ void __launch_bounds__(128) qkv_prep_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+__global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                            __nv_bfloat16* __restrict__ qk,
-                                                           __nv_bfloat16* __restrict__ gate,
-                                                           const float* __restrict__ wg, const float* __restrict__ bg,
-                                                           const float* __restrict__ inv_freq, QkNormArgs na, int M,
-                                                           int T, int H) {
-  __shared__ float sW[64 * 64];
-  __shared__ float sB[64];
-  __shared__ float sF[32];
-  const bool gated = (wg != nullptr);
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) sW[i] = gated ? wg[i] : 0.f;
-  if (threadIdx.x < 64) sB[threadIdx.x] = gated ? bg[threadIdx.x] : 0.f;
-  if (threadIdx.x < 32) sF[threadIdx.x] = inv_freq[threadIdx.x];
-  __syncthreads();
-  const long long rh = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (rh >= (long long)M * H) return;
-  const long long tok = rh / H;
-  const int h = (int)(rh % H);
+                                                           __nv_bfloat16* __restrict__ qn_out,
+                                                           const float* __restrict__ inv_freq, QkNormArgs na,
+                                                           int M, int T, int H) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long rows = (long long)M * H;
   const int d = H * 64;
-  const int t = (int)(tok % T);
-  float cs[32], sn[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    const float ang = (float)t * sF[i];
-    sincosf(ang, &sn[i], &cs[i]);
-  }
-  float v[64];
-  // ---- q
-  load_row64(qkv + tok * 3 * d + h * 64, v);
-  if (na.kind != RGPT_NORM_IDENTITY) {
-    float S = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) S += v[i] * v[i];
-    const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = v[i] * ns.s * qk_affine(na, true, i) * na.sq;
-  }
-  if (gated) {
-    __nv_bfloat16* grow = gate + tok * d + h * 64;
-#pragma unroll 1
-    for (int j0 = 0; j0 < 64; j0 += 8) {
-      float gv[8];
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const float4* wr = reinterpret_cast<const float4*>(sW + (j0 + jj) * 64);
-        float acc = sB[j0 + jj];
-#pragma unroll
-        for (int i4 = 0; i4 < 16; ++i4) {
-          float4 w4 = wr[i4];
-          acc += v[4 * i4] * w4.x + v[4 * i4 + 1] * w4.y + v[4 * i4 + 2] * w4.z + v[4 * i4 + 3] * w4.w;
-        }
-        gv[jj] = 1.0f / (1.0f + expf(-acc));
-      }
-      reinterpret_cast<uint4*>(grow)[j0 / 8] =
-          make_uint4(pack_bf16x2(gv[0], gv[1]), pack_bf16x2(gv[2], gv[3]), pack_bf16x2(gv[4], gv[5]),
-                     pack_bf16x2(gv[6], gv[7]));
+  const int i0 = 2 * lane;
+  const bool second = lane >= 16;
+  const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
+  for (long long rh = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rh < rows; rh += warps) {
+    const long long tok = rh / H;
+    const int h = (int)(rh % H);
+    const float t = (float)(tok % T);
+    float2 c, sn;
+    sincosf(t * f0, &sn.x, &c.x);
+    sincosf(t * f1, &sn.y, &c.y);
+    // ---- q
+    float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + h * 64 + i0));
+    if (na.kind != RGPT_NORM_IDENTITY) {
+      const float S = warp_sum(x.x * x.x + x.y * x.y);
+      const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+      const float2 a = qk_affine2(na, true, i0);
+      x = make_float2(x.x * ns.s * a.x * na.sq, x.y * ns.s * a.y * na.sq);
     }
+    if (qn_out) *reinterpret_cast<uint32_t*>(qn_out + tok * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
+    x = rope_pair(x, c, sn, second, 1);
+    *reinterpret_cast<uint32_t*>(qk + tok * 2 * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
+    // ---- k
+    x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + d + h * 64 + i0));
+    if (na.kind != RGPT_NORM_IDENTITY) {
+      const float S = warp_sum(x.x * x.x + x.y * x.y);
+      const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+      const float2 a = qk_affine2(na, false, i0);
+      x = make_float2(x.x * ns.s * a.x * na.sk, x.y * ns.s * a.y * na.sk);
+    }
+    x = rope_pair(x, c, sn, second, 1);
+    *reinterpret_cast<uint32_t*>(qk + tok * 2 * d + d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
   }
-  rope_fwd64(v, cs, sn);
-  store_row64(qk + tok * 2 * d + h * 64, v);
-  // ---- k
-  load_row64(qkv + tok * 3 * d + d + h * 64, v);
-  if (na.kind != RGPT_NORM_IDENTITY) {
-    float S = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) S += v[i] * v[i];
-    const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = v[i] * ns.s * qk_affine(na, false, i) * na.sk;
-  }
-  rope_fwd64(v, cs, sn);
-  store_row64(qk + tok * 2 * d + d + h * 64, v);
 }
 
-// Backward of qkv_prep. One thread per (token, head); a CTA of 128 rows also
-// reduces the gate-weight gradient dWg = sum_rows dgp^T q_n (64x64) through smem.
-//   dq, dk : fp32 [M, d] grads of the roped q / k;   dgp : bf16 [M, d] grad of the gate pre-activation
-//   dqkv   : bf16 [M, 3d], q and k column blocks written here (v is written by the attention backward)
-__global__ void __launch_bounds__(128) qkv_prep_bwd_kernel(
+// Backward of the norm + RoPE. dq, dk: fp32 [M, d] grads of the roped q / k;
+// dqn_gate: fp32 [M, d] = dgp Wg (the gate GEMM's contribution to d q_n), may be null;
+// dgp: bf16 [M, d] grad of the gate pre-activation, only summed here into dbg.
+// Writes the q and k column blocks of dqkv (bf16); ACCUMULATES dbg, dwq/dwk, dtq/dtk.
+__global__ void __launch_bounds__(256) qkv_prep_bwd_kernel(
     const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ dq, const float* __restrict__ dk,
-    const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv, const float* __restrict__ wg,
-    float* __restrict__ dwg, float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk,
-    float* __restrict__ dtq, float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M,
-    int T, int H) {
-  extern __shared__ float qsm[];
-  float* sW = qsm;                                                     // [64*64]
-  float* sF = sW + 64 * 64;                                            // [32]
-  float (*sG)[65] = reinterpret_cast<float (*)[65]>(sF + 32);          // [128][65] dgp rows of this tile
-  float (*sQn)[65] = reinterpret_cast<float (*)[65]>(sF + 32 + 128 * 65);  // [128][65] q_n rows of this tile
-  const bool gated = (wg != nullptr);
-  for (int i = threadIdx.x; i < 64 * 64; i += blockDim.x) sW[i] = gated ? wg[i] : 0.f;
-  if (threadIdx.x < 32) sF[threadIdx.x] = inv_freq[threadIdx.x];
-  // dWg block owned by this thread: row j = tid/2, columns (tid&1)*32 .. +32
-  const int own_j = threadIdx.x >> 1, own_i0 = (threadIdx.x & 1) * 32;
-  float acc_w[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) acc_w[i] = 0.f;
-  float acc_b = 0.f;
-  const int d = H * 64;
-  const long long rows = (long long)M * H;
+    const float* __restrict__ dqn_gate, const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv,
+    float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dtq,
+    float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M, int T, int H) {
   const int lane = threadIdx.x & 31;
-  __syncthreads();
-
-  for (long long base = (long long)blockIdx.x * 128; base < rows; base += (long long)gridDim.x * 128) {
-    const long long rh = base + threadIdx.x;
-    const bool valid = rh < rows;
-    const long long tok = valid ? rh / H : 0;
-    const int h = valid ? (int)(rh % H) : 0;
-    const int t = (int)(tok % T);
-    float cs[32], sn[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) sincosf((float)t * sF[i], &sn[i], &cs[i]);
-    float x[64], g[64];
-    // ------------------------------------------------ q
-    if (valid) {
-      load_row64(qkv + tok * 3 * d + h * 64, x);
-      const float4* src = reinterpret_cast<const float4*>(dq + tok * d + h * 64);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float4 u = src[c];
-        g[4 * c] = u.x;
-        g[4 * c + 1] = u.y;
-        g[4 * c + 2] = u.z;
-        g[4 * c + 3] = u.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) x[i] = g[i] = 0.f;
-    }
-    rope_bwd64(g, cs, sn);  // g = d q_n (before the gate contribution)
-    NS2 ns{1.f, 0.f};
-    if (na.kind != RGPT_NORM_IDENTITY) {
-      float S = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) S += x[i] * x[i];
-      ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
-    }
-    // stage q_n and dgp rows for the dWg reduction, add the gate path into g
-    if (gated) {
-      float gp[64];
-      if (valid) {
-        load_row64(dgp + tok * d + h * 64, gp);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) gp[i] = 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        sG[threadIdx.x][i] = gp[i];
-        sQn[threadIdx.x][i] = x[i] * ns.s * qk_affine(na, true, i) * na.sq;
-      }
-      // d q_n += dgp @ Wg  (Wg row j is the weight vector of gate output j)
-#pragma unroll 1
-      for (int j = 0; j < 64; ++j) {
-        const float gj = gp[j];
-        const float4* wr = reinterpret_cast<const float4*>(sW + j * 64);
-#pragma unroll
-        for (int i4 = 0; i4 < 16; ++i4) {
-          float4 w4 = wr[i4];
-          g[4 * i4] += gj * w4.x;
-          g[4 * i4 + 1] += gj * w4.y;
-          g[4 * i4 + 2] += gj * w4.z;
-          g[4 * i4 + 3] += gj * w4.w;
-        }
-      }
-    }
-    // norm backward (affine a, post-scale sq); identity norm has s = 1, s' = 0
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long rows = (long long)M * H;
+  const int d = H * 64;
+  const int i0 = 2 * lane;
+  const bool second = lane >= 16;
+  const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
+  float2 acc_b = make_float2(0.f, 0.f), acc_wq = make_float2(0.f, 0.f), acc_wk = make_float2(0.f, 0.f);
+  float acc_tq = 0.f, acc_tk = 0.f;
+  for (long long rh = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rh < rows; rh += warps) {
+    const long long tok = rh / H;
+    const int h = (int)(rh % H);
+    const float t = (float)(tok % T);
+    float2 c, sn;
+    sincosf(t * f0, &sn.x, &c.x);
+    sincosf(t * f1, &sn.y, &c.y);
+    const long long col = (long long)h * 64 + i0;
+    // ---- q
     {
-      float c = 0.f, xdy = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float a = qk_affine(na, true, i) * na.sq;
-        c += a * g[i] * x[i];
-        xdy += g[i] * x[i];
+      float2 g = *reinterpret_cast<const float2*>(dq + tok * d + col);
+      g = rope_pair(g, c, sn, second, -1);
+      if (dqn_gate) {
+        const float2 gg = *reinterpret_cast<const float2*>(dqn_gate + tok * d + col);
+        g.x += gg.x;
+        g.y += gg.y;
       }
-      const float k2 = 2.0f * ns.ds * c;
-      if (na.kind == RGPT_NORM_RMS_AFFINE && dwq) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          float v = warp_sum(valid ? g[i] * x[i] * ns.s : 0.f);
-          if (lane == 0) atomicAdd(&dwq[i], v);
-        }
+      if (dgp) {
+        const float2 gp = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dgp + tok * d + col));
+        acc_b.x += gp.x;
+        acc_b.y += gp.y;
       }
-      if (na.kind == RGPT_NORM_L2_TEMP && dtq) {
-        float v = warp_sum(valid ? xdy * ns.s : 0.f);
-        if (lane == 0) atomicAdd(dtq, v);
+      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + col));
+      NS2 ns{1.f, 0.f};
+      if (na.kind != RGPT_NORM_IDENTITY) ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
+      const float2 a = qk_affine2(na, true, i0);
+      const float ax = a.x * na.sq, ay = a.y * na.sq;
+      const float cc = warp_sum(ax * g.x * x.x + ay * g.y * x.y);
+      const float k2 = 2.0f * ns.ds * cc;
+      if (na.kind == RGPT_NORM_RMS_AFFINE) {
+        acc_wq.x += g.x * x.x * ns.s * na.sq;
+        acc_wq.y += g.y * x.y * ns.s * na.sq;
       }
-#pragma unroll
-      for (int i = 0; i < 64; ++i) g[i] = ns.s * qk_affine(na, true, i) * na.sq * g[i] + k2 * x[i];
+      if (na.kind == RGPT_NORM_L2_TEMP) acc_tq += (g.x * x.x + g.y * x.y) * ns.s * na.sq;
+      *reinterpret_cast<uint32_t*>(dqkv + tok * 3 * d + col) =
+          pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
     }
-    if (valid) store_row64(dqkv + tok * 3 * d + h * 64, g);
-    // ------------------------------------------------ k
-    if (valid) {
-      load_row64(qkv + tok * 3 * d + d + h * 64, x);
-      const float4* src = reinterpret_cast<const float4*>(dk + tok * d + h * 64);
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float4 u = src[c];
-        g[4 * c] = u.x;
-        g[4 * c + 1] = u.y;
-        g[4 * c + 2] = u.z;
-        g[4 * c + 3] = u.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) x[i] = g[i] = 0.f;
-    }
-    rope_bwd64(g, cs, sn);
+    // ---- k
     {
-      ns = NS2{1.f, 0.f};
-      if (na.kind != RGPT_NORM_IDENTITY) {
-        float S = 0.f;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) S += x[i] * x[i];
-        ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
+      float2 g = *reinterpret_cast<const float2*>(dk + tok * d + col);
+      g = rope_pair(g, c, sn, second, -1);
+      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + d + col));
+      NS2 ns{1.f, 0.f};
+      if (na.kind != RGPT_NORM_IDENTITY) ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
+      const float2 a = qk_affine2(na, false, i0);
+      const float ax = a.x * na.sk, ay = a.y * na.sk;
+      const float cc = warp_sum(ax * g.x * x.x + ay * g.y * x.y);
+      const float k2 = 2.0f * ns.ds * cc;
+      if (na.kind == RGPT_NORM_RMS_AFFINE) {
+        acc_wk.x += g.x * x.x * ns.s * na.sk;
+        acc_wk.y += g.y * x.y * ns.s * na.sk;
       }
-      float c = 0.f, xdy = 0.f;
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        c += qk_affine(na, false, i) * na.sk * g[i] * x[i];
-        xdy += g[i] * x[i];
-      }
-      const float k2 = 2.0f * ns.ds * c;
-      if (na.kind == RGPT_NORM_RMS_AFFINE && dwk) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          float v = warp_sum(valid ? g[i] * x[i] * ns.s : 0.f);
-          if (lane == 0) atomicAdd(&dwk[i], v);
-        }
-      }
-      if (na.kind == RGPT_NORM_L2_TEMP && dtk) {
-        float v = warp_sum(valid ? xdy * ns.s : 0.f);
-        if (lane == 0) atomicAdd(dtk, v);
-      }
-#pragma unroll
-      for (int i = 0; i < 64; ++i) g[i] = ns.s * qk_affine(na, false, i) * na.sk * g[i] + k2 * x[i];
-    }
-    if (valid) store_row64(dqkv + tok * 3 * d + d + h * 64, g);
-    // ------------------------------------------------ dWg, dbg from this tile
-    if (gated) {
-      __syncthreads();
-#pragma unroll 1
-      for (int r = 0; r < 128; ++r) {
-        const float gj = sG[r][own_j];
-        acc_b += (own_i0 == 0) ? gj : 0.f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc_w[i] += gj * sQn[r][own_i0 + i];
-      }
-      __syncthreads();
+      if (na.kind == RGPT_NORM_L2_TEMP) acc_tk += (g.x * x.x + g.y * x.y) * ns.s * na.sk;
+      *reinterpret_cast<uint32_t*>(dqkv + tok * 3 * d + d + col) =
+          pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
     }
   }
-  if (gated) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) atomicAdd(&dwg[own_j * 64 + own_i0 + i], acc_w[i]);
-    if (own_i0 == 0) atomicAdd(&dbg[own_j], acc_b);
+  // per-column partials: each lane owns columns i0, i0+1 of the 64-wide head
+  if (dbg) {
+    atomicAdd(&dbg[i0], acc_b.x);
+    atomicAdd(&dbg[i0 + 1], acc_b.y);
+  }
+  if (na.kind == RGPT_NORM_RMS_AFFINE) {
+    if (dwq) {
+      atomicAdd(&dwq[i0], acc_wq.x);
+      atomicAdd(&dwq[i0 + 1], acc_wq.y);
+    }
+    if (dwk) {
+      atomicAdd(&dwk[i0], acc_wk.x);
+      atomicAdd(&dwk[i0 + 1], acc_wk.y);
+    }
+  }
+  if (na.kind == RGPT_NORM_L2_TEMP) {
+    const float tq = warp_sum(acc_tq), tk = warp_sum(acc_tk);
+    if (lane == 0) {
+      if (dtq) atomicAdd(dtq, tq);
+      if (dtk) atomicAdd(dtk, tk);
+    }
   }
 }
 
@@ -950,49 +809,36 @@ static QkNormArgs qk_args(int kind, float eps, float alpha, const float* wq, con
   return a;
 }
 
-extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* gate, const float* wg, const float* bg,
-                                 const float* inv_freq, int qk_kind, float eps, float alpha, const float* wq,
-                                 const float* wk, float tq, float tk, float sq, float sk, int M, int T, int H,
-                                 void* stream) {
+static int prep_grid(long long rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long want = (rows + 7) / 8;  // 8 warps per 256-thread CTA
+  const long long cap = (long long)rgpt_num_sms(dev) * 16;
+  return (int)(want < cap ? want : cap);
+}
+
+extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const float* inv_freq, int qk_kind, float eps,
+                                 float alpha, const float* wq, const float* wk, float tq, float tk, float sq, float sk,
+                                 int M, int T, int H, void* stream) {
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
   if (qk_kind == RGPT_NORM_RMS_AFFINE && (wq == nullptr || wk == nullptr))
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rmsnorm QK norm needs weights");
-  if ((wg == nullptr) != (gate == nullptr) || (wg && bg == nullptr))
-    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gate output needs gate weight and bias");
-  const long long rows = (long long)M * H;
-  const int block = 128;
-  qkv_prep_fwd_kernel<<<(unsigned)((rows + block - 1) / block), block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  qkv_prep_fwd_kernel<<<prep_grid((long long)M * H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
-      reinterpret_cast<__nv_bfloat16*>(gate), wg, bg, inv_freq, qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk),
-      M, T, H);
+      reinterpret_cast<__nv_bfloat16*>(qn), inv_freq, qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
   return rgpt_check_launch("qkv_prep_fwd_kernel");
 }
 
-extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const void* dgp, void* dqkv,
-                                 const float* wg, float* dwg, float* dbg, float* dwq, float* dwk, float* dtq,
+extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const float* dqn_gate,
+                                 const void* dgp, void* dqkv, float* dbg, float* dwq, float* dwk, float* dtq,
                                  float* dtk, const float* inv_freq, int qk_kind, float eps, float alpha,
                                  const float* wq, const float* wk, float tq, float tk, float sq, float sk, int M, int T,
                                  int H, void* stream) {
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
-  if (wg && (dgp == nullptr || dwg == nullptr || dbg == nullptr))
-    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gated backward needs dgp, dwg, dbg");
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const long long rows = (long long)M * H;
-  long long grid = (rows + 127) / 128;
-  const long long cap = rgpt_num_sms(dev) * 2;
-  if (grid > cap) grid = cap;
-  const size_t smem = (64 * 64 + 32 + 2 * 128 * 65) * sizeof(float);
-  static bool attr[64] = {false};
-  if (!attr[dev]) {
-    if (cudaFuncSetAttribute(qkv_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return rgpt_check_launch("qkv_prep_bwd set smem");
-    attr[dev] = true;
-  }
-  qkv_prep_bwd_kernel<<<(unsigned)grid, 128, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, reinterpret_cast<const __nv_bfloat16*>(dgp),
-      reinterpret_cast<__nv_bfloat16*>(dqkv), wg, dwg, dbg, dwq, dwk, dtq, dtk, inv_freq,
+  if (dbg && dgp == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dbg needs dgp");
+  qkv_prep_bwd_kernel<<<prep_grid((long long)M * H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, dqn_gate, reinterpret_cast<const __nv_bfloat16*>(dgp),
+      reinterpret_cast<__nv_bfloat16*>(dqkv), dbg, dwq, dwk, dtq, dtk, inv_freq,
       qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
   return rgpt_check_launch("qkv_prep_bwd_kernel");
 }

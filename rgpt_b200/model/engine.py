@@ -80,6 +80,7 @@ class _Acts:
         self.qkv = [e(M, 3 * d) for _ in range(napp)]
         self.qk = [e(M, 2 * d) for _ in range(napp)]
         self.gate = [e(M, d) for _ in range(napp)] if eng.g1 else [None] * napp
+        self.qn = [e(M, d) for _ in range(napp)] if eng.g1 else [None] * napp
         self.o = [e(M, d) for _ in range(napp)]
         self.og = [e(M, d) for _ in range(napp)] if eng.g1 else self.o
         self.lse = [e(B, H, T, dt=f32) for _ in range(napp)]
@@ -175,11 +176,15 @@ class Engine:
             self._add_shadow(at.out_proj.weight, wo)
             self._add_shadow(ff.fc1.weight, w1)
             self._add_shadow(ff.fc2.weight, w2)
+            wg = None
+            if self.g1:
+                wg = torch.empty(64, 64, device=dev, dtype=torch.bfloat16)
+                self._add_shadow(at.gate_proj.weight, wg)
             gq = self.grads_of(at.q_proj.weight)
             dwqkv = torch.as_strided(self.grad_arena, (3 * d, d), (d, 1), gq.storage_offset())
             # q, k, v are registered consecutively, so their arena slices form one [3d, d] block
             assert dwqkv[2 * d:].data_ptr() == self.grads_of(at.v_proj.weight).data_ptr()
-            self.layer_w.append(dict(wqkv=wqkv, wo=wo, w1=w1, w2=w2, dwqkv=dwqkv))
+            self.layer_w.append(dict(wqkv=wqkv, wo=wo, w1=w1, w2=w2, wg=wg, dwqkv=dwqkv))
         self.lm_w = torch.empty(self.V, d, device=dev, dtype=torch.bfloat16)
         self._add_shadow(m.lm_head.weight, self.lm_w)
         rope = m.layers[0].attn.rotary_emb
@@ -338,10 +343,12 @@ class Engine:
         nv.rownorm_fwd(x, A.hn[app], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0, alpha=alpha)
         nv.gemm(A.hn[app], W["wqkv"], A.qkv[app])
         qs = self._qk_spec(at)
-        nv.qkv_prep_fwd(A.qkv[app], A.qk[app], A.gate[app],
-                        at.gate_proj.weight if self.g1 else None, at.gate_proj.bias if self.g1 else None,
-                        self.inv_freq, qs["kind"], qs["eps"], qs["alpha"], M, T, H, wq=qs["wq"], wk=qs["wk"],
-                        tq=qs["tq"], tk=qs["tk"], sq=qs["sq"], sk=qs["sk"])
+        nv.qkv_prep_fwd(A.qkv[app], A.qk[app], A.qn[app], self.inv_freq, qs["kind"], qs["eps"], qs["alpha"],
+                        M, T, H, wq=qs["wq"], wk=qs["wk"], tq=qs["tq"], tk=qs["tk"], sq=qs["sq"], sk=qs["sk"])
+        if self.g1:
+            # G1 gate = sigmoid(q_n Wg^T + bg), one [M*H, 64] x [64, 64] GEMM with a bias+sigmoid epilogue
+            nv.gemm(A.qn[app].view(M * H, 64), W["wg"], A.gate[app].view(M * H, 64),
+                    epi=nv.EPI_BIAS_SIGMOID_BF16, colscale=at.gate_proj.bias)
         nv.attn_fwd(A.qk[app], A.qkv[app], A.gate[app], A.o[app], A.og[app] if self.g1 else None, A.lse[app],
                     B, T, H)
         nv.gemm(A.og[app], W["wo"], A.h[app], epi=nv.EPI_RESID_F32, c=x,
@@ -437,11 +444,17 @@ class Engine:
         nv.attn_bwd(A.qk[app], A.qkv[app], A.do, A.lse[app], A.D, A.dqa, A.dka, A.dqkv[:, 2 * d:], B, T, H)
         qs = self._qk_spec(at)
         qn = pre + "attn.qk_norm."
-        nv.qkv_prep_bwd(A.qkv[app], A.dqa, A.dka, A.dgp if self.g1 else None, A.dqkv,
-                        at.gate_proj.weight if self.g1 else None,
-                        G[pre + "attn.gate_proj.weight"] if self.g1 else None,
-                        G[pre + "attn.gate_proj.bias"] if self.g1 else None,
+        dqn_gate = None
+        if self.g1:
+            # gate backward on tensor cores: d q_n += dgp Wg ; dWg += dgp^T q_n (split-K over M*H rows)
+            dgp2 = A.dgp.view(M * H, 64)
+            dqn_gate = A.dy32.view(M * H, 64)
+            nv.gemm(dgp2, W["wg"].t(), dqn_gate, epi=nv.EPI_STORE_F32)
+            nv.gemm(dgp2.t(), A.qn[app].view(M * H, 64).t(), G[pre + "attn.gate_proj.weight"],
+                    epi=nv.EPI_ACCUM_F32, splitk=0)
+        nv.qkv_prep_bwd(A.qkv[app], A.dqa, A.dka, dqn_gate, A.dgp if self.g1 else None, A.dqkv,
                         self.inv_freq, qs["kind"], qs["eps"], qs["alpha"], M, T, H,
+                        dbg=G[pre + "attn.gate_proj.bias"] if self.g1 else None,
                         dwq=G.get(qn + "q_norm_fn.weight"), dwk=G.get(qn + "k_norm_fn.weight"),
                         dtq=G.get(qn + "q_norm_fn.temp"), dtk=G.get(qn + "k_norm_fn.temp"),
                         wq=qs["wq"], wk=qs["wk"], tq=qs["tq"], tk=qs["tk"], sq=qs["sq"], sk=qs["sk"])

@@ -17,6 +17,7 @@ EPI_ACT_FWD = 3
 EPI_ACT_BWD = 4
 EPI_RESID_F32 = 5
 EPI_POLY_BF16 = 6
+EPI_BIAS_SIGMOID_BF16 = 7
 
 ACTIVATIONS = {"none": 0, "identity": 0, "squared_relu": 1, "gelu": 2, "silu": 3, "mish": 4}
 
@@ -165,16 +166,15 @@ def rownorm_bwd(x: torch.Tensor, dy: torch.Tensor | None, kind: int, eps: float,
 
 
 # ----------------------------------------------------------------------------- QKV prep
-def qkv_prep_fwd(qkv, qk, gate, wg, bg, inv_freq, qk_kind, eps, alpha, M, T, H, *, wq=None, wk=None,
+def qkv_prep_fwd(qkv, qk, qn, inv_freq, qk_kind, eps, alpha, M, T, H, *, wq=None, wk=None,
                  tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
-    _lib.call("rgpt_qkv_prep_fwd", ptr(qkv), ptr(qk), ptr(gate), ptr(wg), ptr(bg), ptr(inv_freq), qk_kind,
-              float(eps), float(alpha), ptr(wq), ptr(wk), float(tq), float(tk), float(sq), float(sk), M, T, H,
-              _lib.stream_ptr(qkv.device))
+    _lib.call("rgpt_qkv_prep_fwd", ptr(qkv), ptr(qk), ptr(qn), ptr(inv_freq), qk_kind, float(eps), float(alpha),
+              ptr(wq), ptr(wk), float(tq), float(tk), float(sq), float(sk), M, T, H, _lib.stream_ptr(qkv.device))
 
 
-def qkv_prep_bwd(qkv, dq, dk, dgp, dqkv, wg, dwg, dbg, inv_freq, qk_kind, eps, alpha, M, T, H, *, dwq=None,
-                 dwk=None, dtq=None, dtk=None, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
-    _lib.call("rgpt_qkv_prep_bwd", ptr(qkv), ptr(dq), ptr(dk), ptr(dgp), ptr(dqkv), ptr(wg), ptr(dwg), ptr(dbg),
+def qkv_prep_bwd(qkv, dq, dk, dqn_gate, dgp, dqkv, inv_freq, qk_kind, eps, alpha, M, T, H, *, dbg=None,
+                 dwq=None, dwk=None, dtq=None, dtk=None, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
+    _lib.call("rgpt_qkv_prep_bwd", ptr(qkv), ptr(dq), ptr(dk), ptr(dqn_gate), ptr(dgp), ptr(dqkv), ptr(dbg),
               ptr(dwq), ptr(dwk), ptr(dtq), ptr(dtk), ptr(inv_freq), qk_kind, float(eps), float(alpha), ptr(wq),
               ptr(wk), float(tq), float(tk), float(sq), float(sk), M, T, H, _lib.stream_ptr(qkv.device))
 
