@@ -16,6 +16,46 @@ enum ActKind : int { ACT_NONE = 0, ACT_SQRELU = 1, ACT_GELU = 2, ACT_SILU = 3, A
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// Compile-time activation (one instantiation per kind keeps unrolled epilogues small).
+template <int ACT>
+__device__ __forceinline__ float act_fwd_t(float x) {
+  if constexpr (ACT == ACT_SQRELU) {
+    const float r = fmaxf(x, 0.0f);
+    return r * r;
+  } else if constexpr (ACT == ACT_GELU) {
+    const float k = 0.7978845608028654f;
+    return 0.5f * x * (1.0f + tanhf(k * (x + 0.044715f * x * x * x)));
+  } else if constexpr (ACT == ACT_SILU) {
+    return x * sigmoidf_(x);
+  } else if constexpr (ACT == ACT_MISH) {
+    const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
+    return x * tanhf(sp);
+  } else {
+    return x;
+  }
+}
+
+template <int ACT>
+__device__ __forceinline__ float act_grad_t(float x) {
+  if constexpr (ACT == ACT_SQRELU) {
+    return 2.0f * fmaxf(x, 0.0f);
+  } else if constexpr (ACT == ACT_GELU) {
+    const float k = 0.7978845608028654f;
+    const float x2 = x * x;
+    const float t = tanhf(k * (x + 0.044715f * x2 * x));
+    return 0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * (k * (1.0f + 3.0f * 0.044715f * x2));
+  } else if constexpr (ACT == ACT_SILU) {
+    const float s = sigmoidf_(x);
+    return s * (1.0f + x * (1.0f - s));
+  } else if constexpr (ACT == ACT_MISH) {
+    const float sp = x > 20.0f ? x : logf(1.0f + expf(x));
+    const float t = tanhf(sp);
+    return t + x * (1.0f - t * t) * sigmoidf_(x);
+  } else {
+    return 1.0f;
+  }
+}
+
 __device__ __forceinline__ float act_fwd(int act, float x) {
   switch (act) {
     case ACT_SQRELU: {

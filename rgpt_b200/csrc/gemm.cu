@@ -10,17 +10,21 @@
 // CTA layout (192 threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: 128-byte-swizzled tiles into a STAGES-deep smem ring
 //   warp 1      allocates TMEM, issues tcgen05.mma (one elected thread), commits
-//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (each thread owns one
-//               row), apply the fused epilogue, store to HBM
+//   warps 2..5  epilogue: each warp owns 32 accumulator rows (one TMEM lane quadrant);
+//               per column chunk it tcgen05.ld's the fp32 accumulator, applies the
+//               fused epilogue, stages the result in swizzled smem and writes it with
+//               a TMA bulk store (or a TMA bulk reduce-add for accumulating outputs)
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of
-// tile i overlaps the main loop of tile i+1.
+// tile i overlaps the main loop of tile i+1. Tiles are visited in groups of
+// GROUP_M row tiles so that consecutive CTAs share A and B panels in L2.
 //
 // Epilogues fuse what the reference runs as separate torch ops:
-//   ACT_FWD   pre = acc, post = act(acc)          (model/kernels.py:127-200)
-//   ACT_BWD   dpre = acc * act'(pre)              (model/kernels.py:207-281)
-//   RESID_F32 x_out = x_in + acc * layer_scale    (model/transformer_block.py:43-57)
-//   POLY_BF16 beta*C + alpha*acc                  (optimizer.py:36-41, Newton-Schulz)
-//   ACCUM_F32 grad += acc (split-K via fp32 vector atomics)
+//   ACT_FWD      pre = acc, post = act(acc)          (model/kernels.py:127-200)
+//   ACT_BWD      dpre = acc * act'(pre)              (model/kernels.py:207-281)
+//   RESID_F32    x_out = x_in + acc * layer_scale    (model/transformer_block.py:43-57)
+//   POLY_BF16    beta*C + alpha*acc                  (optimizer.py:36-41, Newton-Schulz)
+//   BIAS_SIGMOID sigmoid(acc + bias)                 (model/attention.py:45-48, G1 gate)
+//   ACCUM_F32    grad += acc (bulk reduce-add, so split-K needs no separate reduction)
 #include <cudaTypedefs.h>
 #include <stdio.h>
 
@@ -39,241 +43,164 @@ struct GemmShape {
 struct EpiParams {
   int kind, act;
   float alpha, beta;
-  void* d;
-  long long ldd, d_bstride;
-  void* d2;
-  long long ldd2, d2_bstride;
   const void* c;
   long long ldc, c_bstride;
   const float* colscale;
   const float* alpha_dev;  // optional device scalar multiplying alpha (loss-gradient scale)
+  int has_d2;
 };
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
+constexpr int GROUP_M = 8;
+constexpr uint32_t EPI_STAGE_BYTES = 4096;  // one warp's 32 rows x 128 bytes
 
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
   static constexpr uint32_t BAR_BYTES = 256;
-  static constexpr uint32_t TOTAL = STAGES * STAGE_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+  static constexpr uint32_t TOTAL = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
 };
 
 __device__ __forceinline__ void decode_unit(int u, const GemmShape& sh, int& b, int& mt, int& nt, int& ks) {
   ks = u % sh.splitk;
-  u /= sh.splitk;
-  mt = u % sh.m_tiles;
-  u /= sh.m_tiles;
-  nt = u % sh.n_tiles;
-  b = u / sh.n_tiles;
+  int t = u / sh.splitk;
+  const int per_batch = sh.m_tiles * sh.n_tiles;
+  b = t / per_batch;
+  t %= per_batch;
+  const int group_span = GROUP_M * sh.n_tiles;
+  const int first_m = (t / group_span) * GROUP_M;
+  const int gsize = min(sh.m_tiles - first_m, GROUP_M);
+  const int r = t % group_span;
+  mt = first_m + r % gsize;
+  nt = r / gsize;
 }
 
-// Apply the epilogue to 32 consecutive accumulator columns of one row.
-__device__ __forceinline__ void epilogue_chunk(const EpiParams& ep, const GemmShape& sh, int b, int gm, int gn0,
-                                               const uint32_t (&r)[32]) {
-  float v[32];
-  const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
-  const bool full = (gn0 + 32 <= sh.N);
-  const int ncols = full ? 32 : (sh.N - gn0);
+// ------------------------------------------------------------------ bulk stores
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0, int c1, int c2) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_g() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-  switch (ep.kind) {
-    case RGPT_EPI_STORE_BF16: {
-      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (full) {
-        uint4* d4 = reinterpret_cast<uint4*>(d);
+// Row `lane` of a 32-row x 128-byte staging tile, 16-byte chunk j, 128-byte swizzle.
+__device__ __forceinline__ uint8_t* stage_ptr(uint8_t* buf, int lane, int j) {
+  return buf + lane * 128 + ((j ^ (lane & 7)) << 4);
+}
+__device__ __forceinline__ void stage_f32x32(uint8_t* buf, int lane, const float* v) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 o;
-          o.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-          o.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-          o.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-          o.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-          d4[q] = o;
-        }
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(stage_ptr(buf, lane, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+__device__ __forceinline__ void stage_bf16x64(uint8_t* buf, int lane, const float* v) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4*>(stage_ptr(buf, lane, j)) =
+        make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                   pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+}
+
+// Epilogue input C: a warp's 32 rows x 128 bytes per chunk (64 bf16 or 32 fp32 columns).
+// The warp loads it coalesced (each instruction covers 4 full 128-byte rows), keeps it in
+// registers as the prefetch for the next chunk, and later bounces it through its swizzled
+// staging buffer to get one row per thread. Rows >= M and columns >= N read as zero.
+template <int EB>  // element bytes: 2 (bf16) or 4 (fp32)
+__device__ __forceinline__ void load_c_chunk(const EpiParams& ep, const GemmShape& sh, int b, int row0, int gn0,
+                                             int lane, uint4 (&pf)[8]) {
+  constexpr int PER = 16 / EB;  // elements per 16-byte piece
+  const int piece = lane & 7;
+  const int col = gn0 + piece * PER;
+  const char* base = reinterpret_cast<const char*>(ep.c) + ((long long)b * ep.c_bstride) * EB;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int row = row0 + 4 * i + (lane >> 3);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < sh.M && col < sh.N) {
+      const char* p = base + ((long long)row * ep.ldc + col) * EB;
+      if (col + PER <= sh.N) {
+        v = *reinterpret_cast<const uint4*>(p);
       } else {
-        for (int j = 0; j < ncols; ++j) d[j] = __float2bfloat16(v[j]);
+        uint32_t w[4] = {0, 0, 0, 0};
+        for (int e = 0; e < PER && col + e < sh.N; ++e) {
+          if (EB == 2)
+            reinterpret_cast<uint16_t*>(w)[e] = reinterpret_cast<const uint16_t*>(p)[e];
+          else
+            w[e] = reinterpret_cast<const uint32_t*>(p)[e];
+        }
+        v = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      break;
     }
-    case RGPT_EPI_STORE_F32: {
-      float* d = reinterpret_cast<float*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (full) {
-        float4* d4 = reinterpret_cast<float4*>(d);
+    pf[i] = v;
+  }
+}
+// pf (coalesced layout) -> staging buffer -> cc (row `lane`, 8 pieces). Caller guarantees the
+// buffer is free; leaves it free again (reads complete before the trailing __syncwarp).
+__device__ __forceinline__ void bounce_c_chunk(uint8_t* buf, int lane, const uint4 (&pf)[8], uint4 (&cc)[8]) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      } else {
-        for (int j = 0; j < ncols; ++j) d[j] = v[j];
-      }
-      break;
+  for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(stage_ptr(buf, 4 * i + (lane >> 3), lane & 7)) = pf[i];
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(buf, lane, j));
+  __syncwarp();
+}
+
+// Activation applied to 32 values: forward (ACT_FWD) or derivative times v (ACT_BWD, c = pre).
+template <int ACT>
+__device__ __forceinline__ void act_fwd32(float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = act_fwd_t<ACT>(v[j]);
+}
+template <int ACT>
+__device__ __forceinline__ void act_bwd32(float* v, const uint4* c) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t w4[4] = {c[q].x, c[q].y, c[q].z, c[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 cv = unpack_bf16x2(w4[e]);
+      v[8 * q + 2 * e] *= act_grad_t<ACT>(cv.x);
+      v[8 * q + 2 * e + 1] *= act_grad_t<ACT>(cv.y);
     }
-    case RGPT_EPI_ACCUM_F32: {
-      float* d = reinterpret_cast<float*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (sh.splitk > 1) {
-        if (full) {
-          float4* d4 = reinterpret_cast<float4*>(d);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) atomicAdd(d4 + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
-        } else {
-          for (int j = 0; j < ncols; ++j) atomicAdd(d + j, v[j]);
-        }
-      } else {
-        if (full) {
-          float4* d4 = reinterpret_cast<float4*>(d);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            float4 o = d4[q];
-            o.x += v[4 * q];
-            o.y += v[4 * q + 1];
-            o.z += v[4 * q + 2];
-            o.w += v[4 * q + 3];
-            d4[q] = o;
-          }
-        } else {
-          for (int j = 0; j < ncols; ++j) d[j] += v[j];
-        }
-      }
-      break;
-    }
-    case RGPT_EPI_ACT_FWD: {
-      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      __nv_bfloat16* d2 =
-          reinterpret_cast<__nv_bfloat16*>(ep.d2) + b * ep.d2_bstride + (long long)gm * ep.ldd2 + gn0;
-      if (full) {
-        uint4* p4 = reinterpret_cast<uint4*>(d);
-        uint4* q4 = reinterpret_cast<uint4*>(d2);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 o, a;
-          o.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
-          o.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
-          o.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
-          o.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
-          a.x = pack_bf16x2(act_fwd(ep.act, v[8 * q + 0]), act_fwd(ep.act, v[8 * q + 1]));
-          a.y = pack_bf16x2(act_fwd(ep.act, v[8 * q + 2]), act_fwd(ep.act, v[8 * q + 3]));
-          a.z = pack_bf16x2(act_fwd(ep.act, v[8 * q + 4]), act_fwd(ep.act, v[8 * q + 5]));
-          a.w = pack_bf16x2(act_fwd(ep.act, v[8 * q + 6]), act_fwd(ep.act, v[8 * q + 7]));
-          p4[q] = o;
-          q4[q] = a;
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) {
-          d[j] = __float2bfloat16(v[j]);
-          d2[j] = __float2bfloat16(act_fwd(ep.act, v[j]));
-        }
-      }
-      break;
-    }
-    case RGPT_EPI_ACT_BWD: {
-      const __nv_bfloat16* c =
-          reinterpret_cast<const __nv_bfloat16*>(ep.c) + b * ep.c_bstride + (long long)gm * ep.ldc + gn0;
-      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (full) {
-        const uint4* c4 = reinterpret_cast<const uint4*>(c);
-        uint4* d4 = reinterpret_cast<uint4*>(d);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 pc = c4[q];
-          uint32_t pw[4] = {pc.x, pc.y, pc.z, pc.w};
-          uint32_t ow[4];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            float2 pre = unpack_bf16x2(pw[h]);
-            ow[h] = pack_bf16x2(v[8 * q + 2 * h] * act_grad(ep.act, pre.x),
-                                v[8 * q + 2 * h + 1] * act_grad(ep.act, pre.y));
-          }
-          d4[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) d[j] = __float2bfloat16(v[j] * act_grad(ep.act, __bfloat162float(c[j])));
-      }
-      break;
-    }
-    case RGPT_EPI_RESID_F32: {
-      const float* c = reinterpret_cast<const float*>(ep.c) + b * ep.c_bstride + (long long)gm * ep.ldc + gn0;
-      float* d = reinterpret_cast<float*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (ep.d2 != nullptr) {  // raw branch output (before scale and residual), for the layer-scale gradient
-        float* d2 = reinterpret_cast<float*>(ep.d2) + b * ep.d2_bstride + (long long)gm * ep.ldd2 + gn0;
-        if (full) {
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            reinterpret_cast<float4*>(d2)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        } else {
-          for (int j = 0; j < ncols; ++j) d2[j] = v[j];
-        }
-      }
-      if (full) {
-        const float4* c4 = reinterpret_cast<const float4*>(c);
-        float4* d4 = reinterpret_cast<float4*>(d);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 x = c4[q];
-          float4 s = ep.colscale ? reinterpret_cast<const float4*>(ep.colscale + gn0)[q] : make_float4(1.f, 1.f, 1.f, 1.f);
-          x.x += v[4 * q] * s.x;
-          x.y += v[4 * q + 1] * s.y;
-          x.z += v[4 * q + 2] * s.z;
-          x.w += v[4 * q + 3] * s.w;
-          d4[q] = x;
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) d[j] = c[j] + v[j] * (ep.colscale ? ep.colscale[gn0 + j] : 1.0f);
-      }
-      break;
-    }
-    case RGPT_EPI_POLY_BF16: {
-      const __nv_bfloat16* c =
-          reinterpret_cast<const __nv_bfloat16*>(ep.c) + b * ep.c_bstride + (long long)gm * ep.ldc + gn0;
-      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      if (full) {
-        const uint4* c4 = reinterpret_cast<const uint4*>(c);
-        uint4* d4 = reinterpret_cast<uint4*>(d);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 pc = c4[q];
-          uint32_t pw[4] = {pc.x, pc.y, pc.z, pc.w};
-          uint32_t ow[4];
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            float2 cv = unpack_bf16x2(pw[h]);
-            ow[h] = pack_bf16x2(ep.beta * cv.x + v[8 * q + 2 * h], ep.beta * cv.y + v[8 * q + 2 * h + 1]);
-          }
-          d4[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) d[j] = __float2bfloat16(ep.beta * __bfloat162float(c[j]) + v[j]);
-      }
-      break;
-    }
-    case RGPT_EPI_BIAS_SIGMOID_BF16: {
-      __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(ep.d) + b * ep.d_bstride + (long long)gm * ep.ldd + gn0;
-      const float* bias = ep.colscale + gn0;
-      if (full) {
-        uint4* d4 = reinterpret_cast<uint4*>(d);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float g[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) g[e] = 1.0f / (1.0f + expf(-(v[8 * q + e] + bias[8 * q + e])));
-          d4[q] = make_uint4(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]), pack_bf16x2(g[4], g[5]),
-                             pack_bf16x2(g[6], g[7]));
-        }
-      } else {
-        for (int j = 0; j < ncols; ++j) d[j] = __float2bfloat16(1.0f / (1.0f + expf(-(v[j] + bias[j]))));
-      }
-      break;
-    }
-    default:
-      break;
+  }
+}
+__device__ __forceinline__ void act_fwd32_rt(int act, float* v) {
+  switch (act) {
+    case ACT_SQRELU: act_fwd32<ACT_SQRELU>(v); break;
+    case ACT_GELU: act_fwd32<ACT_GELU>(v); break;
+    case ACT_SILU: act_fwd32<ACT_SILU>(v); break;
+    case ACT_MISH: act_fwd32<ACT_MISH>(v); break;
+    default: break;
+  }
+}
+__device__ __forceinline__ void act_bwd32_rt(int act, float* v, const uint4* c) {
+  switch (act) {
+    case ACT_SQRELU: act_bwd32<ACT_SQRELU>(v, c); break;
+    case ACT_GELU: act_bwd32<ACT_GELU>(v, c); break;
+    case ACT_SILU: act_bwd32<ACT_SILU>(v, c); break;
+    case ACT_MISH: act_bwd32<ACT_MISH>(v, c); break;
+    default: break;
   }
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN>
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                         GemmShape sh, EpiParams ep) {
   using L = GemmSmem<BN, STAGES>;
   constexpr uint32_t TMEM_COLS = 2 * BN;
@@ -283,7 +210,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * L::B_BYTES);
+  uint8_t* sEpi = sB + STAGES * L::B_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + L::EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -308,6 +236,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -418,26 +347,157 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   } else {
     // ------------------------------------------------------------ epilogue warps
     const int quarter = warp & 3;  // TMEM lane quadrant this warp may access
-    const int row = quarter * 32 + lane;
+    uint8_t* buf0 = sEpi + (warp - 2) * 2 * EPI_STAGE_BYTES;
+    uint8_t* buf1 = buf0 + EPI_STAGE_BYTES;
+    int which = 0;
+    constexpr bool bf16_out = (EPI == RGPT_EPI_STORE_BF16 || EPI == RGPT_EPI_ACT_FWD || EPI == RGPT_EPI_ACT_BWD ||
+                               EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_BIAS_SIGMOID_BF16);
+    constexpr bool reads_c = (EPI == RGPT_EPI_ACT_BWD || EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_RESID_F32);
+    const bool dual = (EPI == RGPT_EPI_ACT_FWD) || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
+    const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < sh.num_units; u += gridDim.x) {
       int b, mt, nt, ks;
       decode_unit(u, sh, b, mt, nt, ks);
+      const int row0 = mt * GEMM_BM + quarter * 32;  // first output row of this warp
+      const int gm = row0 + lane;
+      const bool rows_live = row0 < sh.M;
+      uint4 pf[8];  // epilogue input prefetch (first chunk issued while the MMAs still run)
+      if constexpr (reads_c) load_c_chunk<bf16_out ? 2 : 4>(ep, sh, b, row0, nt * BN, lane, pf);
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int gm = mt * GEMM_BM + row;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if constexpr (bf16_out) {
+        auto chunk_bf16 = [&](int c0) {
+          const int gn0 = nt * BN + c0;
+          const bool live = rows_live && gn0 < sh.N;  // warp-uniform
+          uint8_t* s0 = which ? buf1 : buf0;
+          uint8_t* s1 = which ? buf0 : buf1;
+          uint4 cc[8];
+          if (live) {
+            if (lane == 0) {
+              if (dual) bulk_wait_read_0();
+              else bulk_wait_read_1();  // the store issued from this buffer two chunks ago has read it
+            }
+            __syncwarp();
+            if constexpr (reads_c) bounce_c_chunk(s0, lane, pf, cc);
+          }
+          if constexpr (reads_c) {
+            if (c0 + 64 < BN) load_c_chunk<2>(ep, sh, b, row0, gn0 + 64, lane, pf);  // next chunk in flight
+          }
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {  // two 32-column halves of the 64-column box
+            uint32_t r[32];
+            tmem_ld32(t_row + c0 + hf * 32, r);
+            tmem_wait_ld();
+            if (!live) continue;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+            if constexpr (EPI == RGPT_EPI_ACT_BWD) {
+              act_bwd32_rt(ep.act, v, &cc[hf * 4]);
+            } else if constexpr (EPI == RGPT_EPI_POLY_BF16) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint4 cq = cc[hf * 4 + q];
+                const uint32_t w4[4] = {cq.x, cq.y, cq.z, cq.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 cv = unpack_bf16x2(w4[e]);
+                  v[8 * q + 2 * e] += ep.beta * cv.x;
+                  v[8 * q + 2 * e + 1] += ep.beta * cv.y;
+                }
+              }
+            } else if constexpr (EPI == RGPT_EPI_BIAS_SIGMOID_BF16) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int col = gn0 + hf * 32 + j;
+                const float bias = (col < sh.N) ? __ldg(ep.colscale + col) : 0.f;
+                v[j] = 1.0f / (1.0f + expf(-(v[j] + bias)));
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(stage_ptr(s0, lane, hf * 4 + j)) =
+                  make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                             pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+            if constexpr (EPI == RGPT_EPI_ACT_FWD) {
+              act_fwd32_rt(ep.act, v);
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                *reinterpret_cast<uint4*>(stage_ptr(s1, lane, hf * 4 + j)) =
+                    make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                               pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+            }
+          }
+          if (!live) return;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmD, s0, gn0, row0, b);
+            if constexpr (EPI == RGPT_EPI_ACT_FWD) tma_store_3d(&tmD2, s1, gn0, row0, b);
+            bulk_commit_g();
+          }
+          if (!dual) which ^= 1;
+        };
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c0, r);
-        tmem_wait_ld();
-        const int gn0 = nt * BN + c0;
-        if (gm < sh.M && gn0 < sh.N) epilogue_chunk(ep, sh, b, gm, gn0, r);
+        for (int c0 = 0; c0 < BN; c0 += 64) chunk_bf16(c0);
+      } else {
+        constexpr bool resid = EPI == RGPT_EPI_RESID_F32;
+        auto chunk_f32 = [&](int c0) {
+          const int gn0 = nt * BN + c0;
+          const bool live = rows_live && gn0 < sh.N;
+          uint32_t r[32];
+          tmem_ld32(t_row + c0, r);
+          tmem_wait_ld();
+          if (!live) {
+            if constexpr (resid) {
+              if (c0 + 32 < BN) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);
+            }
+            return;
+          }
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+          uint8_t* s0 = which ? buf1 : buf0;
+          uint8_t* s1 = which ? buf0 : buf1;
+          if (lane == 0) {
+            if (dual) bulk_wait_read_0();
+            else bulk_wait_read_1();
+          }
+          __syncwarp();
+          if constexpr (resid) {
+            uint4 cc[8];
+            bounce_c_chunk(s0, lane, pf, cc);
+            if (c0 + 32 < BN) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);  // next chunk in flight
+            if (ep.has_d2) stage_f32x32(s1, lane, v);  // raw branch output
+            const float* cs = reinterpret_cast<const float*>(cc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float sc = (ep.colscale != nullptr && gn0 + j < sh.N) ? __ldg(ep.colscale + gn0 + j) : 1.0f;
+              v[j] = cs[j] + v[j] * sc;
+            }
+          }
+          stage_f32x32(s0, lane, v);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (EPI == RGPT_EPI_ACCUM_F32) {
+              tma_reduce_add_3d(&tmD, s0, gn0, row0, b);
+            } else {
+              tma_store_3d(&tmD, s0, gn0, row0, b);
+              if (resid && ep.has_d2) tma_store_3d(&tmD2, s1, gn0, row0, b);
+            }
+            bulk_commit_g();
+          }
+          if (!dual) which ^= 1;
+        };
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) chunk_f32(c0);
       }
       tc_fence_before();
       __syncwarp();
@@ -447,6 +507,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         acc_phase ^= 1u;
       }
     }
+    if (lane == 0) bulk_wait_all();  // every bulk store has landed before the CTA retires
+    __syncwarp();
   }
 
   __syncthreads();
@@ -470,41 +532,80 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor map (inner, outer, batch) with a 128-byte swizzle.
-int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch,
-                      uint64_t ld_elems, uint64_t bstride_elems, uint32_t box_inner, uint32_t box_outer) {
+// 3-D tensor map (inner, outer, batch) with a 128-byte swizzle; elem_bytes 2 (bf16) or 4 (fp32).
+static int make_tmap_3d(CUtensorMap* map, const void* ptr, int elem_bytes, uint64_t inner, uint64_t outer,
+                        uint64_t batch, uint64_t ld_elems, uint64_t bstride_elems, uint32_t box_inner,
+                        uint32_t box_outer) {
   auto enc = get_encode_fn();
   if (enc == nullptr) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "TMA base pointer %p is not 16-byte aligned", ptr);
   if (batch <= 1) bstride_elems = ld_elems * outer;
-  if ((ld_elems * 2) % 16 != 0 || (bstride_elems * 2) % 16 != 0)
+  if ((ld_elems * elem_bytes) % 16 != 0 || (bstride_elems * elem_bytes) % 16 != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "TMA strides must be multiples of 16 bytes (ld=%llu, bstride=%llu)",
                           (unsigned long long)ld_elems, (unsigned long long)bstride_elems);
   cuuint64_t dims[3] = {inner, outer, batch < 1 ? 1 : batch};
-  cuuint64_t strides[2] = {ld_elems * 2, bstride_elems * 2};
+  cuuint64_t strides[2] = {ld_elems * elem_bytes, bstride_elems * elem_bytes};
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = enc(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return RGPT_OK;
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN>
-static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmShape& sh, const EpiParams& ep,
-                       int grid, cudaStream_t stream) {
-  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN>;
+int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t batch,
+                      uint64_t ld_elems, uint64_t bstride_elems, uint32_t box_inner, uint32_t box_outer) {
+  return make_tmap_3d(map, ptr, 2, inner, outer, batch, ld_elems, bstride_elems, box_inner, box_outer);
+}
+
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
+static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
+                       const GemmShape& sh, const EpiParams& ep, int grid, cudaStream_t stream, int dev) {
+  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI>;
   constexpr uint32_t smem = GemmSmem<BN, STAGES>::TOTAL;
-  static bool attr_set = false;  // per process; attribute applies to every device context
-  if (!attr_set) {
+  static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
+  static bool attr_set[64] = {false};
+  if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return rgpt_check_launch("gemm set smem attribute");
-    attr_set = true;
+    attr_set[dev] = true;
   }
-  kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, sh, ep);
+  kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, sh, ep);
   return rgpt_check_launch("gemm_bf16_tc_kernel");
+}
+
+template <int BN, int STAGES, int A_MN, int B_MN>
+static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+                        const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep, int grid, cudaStream_t s,
+                        int dev) {
+  switch (epi) {
+    case RGPT_EPI_STORE_BF16: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_STORE_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_STORE_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_STORE_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_ACCUM_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACCUM_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_ACT_FWD: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_ACT_BWD: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_RESID_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_RESID_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    case RGPT_EPI_POLY_BF16: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_POLY_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
+  }
+}
+
+static int dispatch_gemm(int BN, int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                         const CUtensorMap& td, const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep,
+                         int grid, cudaStream_t s, int dev) {
+  const int key = (BN == 256 ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
+  switch (key) {
+    case 0: return dispatch_epi<128, 6, 0, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 1: return dispatch_epi<128, 6, 0, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 2: return dispatch_epi<128, 6, 1, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 3: return dispatch_epi<128, 6, 1, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 4: return dispatch_epi<256, 4, 0, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 5: return dispatch_epi<256, 4, 0, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 6: return dispatch_epi<256, 4, 1, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    default: return dispatch_epi<256, 4, 1, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+  }
 }
 
 }  // namespace rgpt
@@ -515,11 +616,13 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
                               int b_mn_major, long long ldb, long long b_bstride, int M, int N, int K, int batch,
                               int epi, int act, float alpha, float beta, void* D, long long ldd, long long d_bstride,
                               void* D2, long long ldd2, long long d2_bstride, const void* C, long long ldc,
-                              long long c_bstride, const float* colscale, int splitk, const float* alpha_dev, void* stream) {
+                              long long c_bstride, const float* colscale, int splitk, const float* alpha_dev,
+                              void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
   if (st) return st;
+  if (dev >= 64) return rgpt_set_error(RGPT_ERR_INTERNAL, "device index %d", dev);
   if (batch < 1) batch = 1;
   if (M < 1 || N < 1 || K < 1)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M, N, K >= 1 (got M=%d N=%d K=%d)", M, N, K);
@@ -539,19 +642,20 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "epilogue input C missing or not 16-byte aligned");
   if (epi == RGPT_EPI_BIAS_SIGMOID_BF16 && colscale == nullptr)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "BIAS_SIGMOID needs the bias vector (colscale)");
-  if (colscale != nullptr && (reinterpret_cast<uintptr_t>(colscale) & 15) != 0)
-    return rgpt_set_error(RGPT_ERR_MISALIGNED, "colscale must be 16-byte aligned");
 
-  const int BN = (N > 128) ? 256 : 128;
+  const int nsm = rgpt_num_sms(dev);
   GemmShape sh;
   sh.M = M;
   sh.N = N;
   sh.K = K;
   sh.batch = batch;
   sh.m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+  // 256-wide tiles unless that leaves most SMs idle (small N or few row tiles)
+  int BN = (N > 128) ? 256 : 128;
+  if (BN == 256 && batch * sh.m_tiles * ((N + 255) / 256) < nsm && batch * sh.m_tiles * ((N + 127) / 128) <= 2 * nsm)
+    BN = 128;
   sh.n_tiles = (N + BN - 1) / BN;
   sh.num_kb = (K + GEMM_BK - 1) / GEMM_BK;
-  const int nsm = rgpt_num_sms(dev);
   const int tiles = batch * sh.m_tiles * sh.n_tiles;
   if (splitk <= 0) {
     splitk = 1;
@@ -568,47 +672,42 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.splitk = (sh.num_kb + sh.kb_per_split - 1) / sh.kb_per_split;  // no empty splits
   sh.num_units = tiles * sh.splitk;
 
-  // Tensor maps. K-major: (inner=K, outer=rows); MN-major: (inner=rows, outer=K).
-  CUtensorMap ta, tb;
+  // Operand maps. K-major: (inner=K, outer=rows); MN-major: (inner=rows, outer=K).
+  CUtensorMap ta, tb, td, td2;
   if (a_mn_major)
-    st = make_tmap_bf16_3d(&ta, A, M, K, batch, lda, a_bstride, 64, GEMM_BK);
+    st = make_tmap_3d(&ta, A, 2, M, K, batch, lda, a_bstride, 64, GEMM_BK);
   else
-    st = make_tmap_bf16_3d(&ta, A, K, M, batch, lda, a_bstride, GEMM_BK, GEMM_BM);
+    st = make_tmap_3d(&ta, A, 2, K, M, batch, lda, a_bstride, GEMM_BK, GEMM_BM);
   if (st) return st;
   if (b_mn_major)
-    st = make_tmap_bf16_3d(&tb, B, N, K, batch, ldb, b_bstride, 64, GEMM_BK);
+    st = make_tmap_3d(&tb, B, 2, N, K, batch, ldb, b_bstride, 64, GEMM_BK);
   else
-    st = make_tmap_bf16_3d(&tb, B, K, N, batch, ldb, b_bstride, GEMM_BK, BN);
+    st = make_tmap_3d(&tb, B, 2, K, N, batch, ldb, b_bstride, GEMM_BK, BN);
   if (st) return st;
+  // Output maps: one 32-row x 128-byte box per epilogue warp and chunk.
+  const int ob = out_f32 ? 4 : 2;
+  const uint32_t obox = out_f32 ? 32 : 64;
+  if ((st = make_tmap_3d(&td, D, ob, N, M, batch, ldd, d_bstride, obox, 32))) return st;
+  const bool has_d2 = (epi == RGPT_EPI_ACT_FWD) || (epi == RGPT_EPI_RESID_F32 && D2 != nullptr);
+  if (has_d2) {
+    if ((st = make_tmap_3d(&td2, D2, ob, N, M, batch, ldd2, d2_bstride, obox, 32))) return st;
+  } else {
+    td2 = td;
+  }
 
   EpiParams ep;
   ep.kind = epi;
   ep.act = act;
   ep.alpha = alpha;
   ep.beta = beta;
-  ep.d = D;
-  ep.ldd = ldd;
-  ep.d_bstride = d_bstride;
-  ep.d2 = D2;
-  ep.ldd2 = ldd2;
-  ep.d2_bstride = d2_bstride;
   ep.c = C;
   ep.ldc = ldc;
   ep.c_bstride = c_bstride;
   ep.colscale = colscale;
   ep.alpha_dev = alpha_dev;
+  ep.has_d2 = has_d2 ? 1 : 0;
 
   const int grid = sh.num_units < nsm ? sh.num_units : nsm;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int key = (BN == 256 ? 4 : 0) | (a_mn_major ? 2 : 0) | (b_mn_major ? 1 : 0);
-  switch (key) {
-    case 0: return launch_gemm<128, 6, 0, 0>(ta, tb, sh, ep, grid, s);
-    case 1: return launch_gemm<128, 6, 0, 1>(ta, tb, sh, ep, grid, s);
-    case 2: return launch_gemm<128, 6, 1, 0>(ta, tb, sh, ep, grid, s);
-    case 3: return launch_gemm<128, 6, 1, 1>(ta, tb, sh, ep, grid, s);
-    case 4: return launch_gemm<256, 4, 0, 0>(ta, tb, sh, ep, grid, s);
-    case 5: return launch_gemm<256, 4, 0, 1>(ta, tb, sh, ep, grid, s);
-    case 6: return launch_gemm<256, 4, 1, 0>(ta, tb, sh, ep, grid, s);
-    default: return launch_gemm<256, 4, 1, 1>(ta, tb, sh, ep, grid, s);
-  }
+  return dispatch_gemm(BN, a_mn_major, b_mn_major, epi, ta, tb, td, td2, sh, ep, grid, s, dev);
 }

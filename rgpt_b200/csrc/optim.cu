@@ -99,11 +99,13 @@ __global__ void ns_scale_kernel(__nv_bfloat16* __restrict__ X, long long x_bstri
   const int b = blockIdx.y;
   const float inv = 1.0f / fmaxf(sqrtf(sumsq[b]), 1e-7f);
   __nv_bfloat16* Xb = X + (long long)b * x_bstride;
-  const long long n = (long long)rows * cols;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / cols, c = i % cols;
-    const long long k = r * ldx + c;
-    Xb[k] = __float2bfloat16(__bfloat162float(Xb[k]) * inv);
+  const int pairs = cols / 2;  // cols is even (the stacks are padded to multiples of 8)
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    __nv_bfloat162* row = reinterpret_cast<__nv_bfloat162*>(Xb + (long long)r * ldx);
+    for (int c = threadIdx.x; c < pairs; c += blockDim.x) {
+      float2 v = __bfloat1622float2(row[c]);
+      row[c] = __floats2bfloat162_rn(v.x * inv, v.y * inv);
+    }
   }
 }
 
@@ -170,9 +172,8 @@ extern "C" int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, 
 
 extern "C" int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, int cols, int n, const float* sumsq,
                              void* stream) {
-  const long long elems = (long long)rows * cols;
-  int gx = (int)((elems + 255) / 256);
-  if (gx > 1024) gx = 1024;
+  if (cols % 2 != 0 || ldx % 2 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_scale needs even cols and ldx");
+  const int gx = rows < 256 ? rows : 256;
   ns_scale_kernel<<<dim3(gx, n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<__nv_bfloat16*>(X), x_bstride, ldx, rows, cols, sumsq);
   return rgpt_check_launch("ns_scale_kernel");

@@ -344,41 +344,39 @@ __global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(const __nv_bfloat16* 
                                                            __nv_bfloat16* __restrict__ qn_out,
                                                            const float* __restrict__ inv_freq, QkNormArgs na,
                                                            int M, int T, int H) {
+  // warps stride over tokens; a warp runs every head of its token (angles shared by all heads)
   const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const long long rows = (long long)M * H;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
   const int d = H * 64;
   const int i0 = 2 * lane;
   const bool second = lane >= 16;
   const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
-  for (long long rh = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rh < rows; rh += warps) {
-    const long long tok = rh / H;
-    const int h = (int)(rh % H);
+  for (int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < M; tok += nwarps) {
     const float t = (float)(tok % T);
     float2 c, sn;
     sincosf(t * f0, &sn.x, &c.x);
     sincosf(t * f1, &sn.y, &c.y);
-    // ---- q
-    float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + h * 64 + i0));
-    if (na.kind != RGPT_NORM_IDENTITY) {
-      const float S = warp_sum(x.x * x.x + x.y * x.y);
-      const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
-      const float2 a = qk_affine2(na, true, i0);
-      x = make_float2(x.x * ns.s * a.x * na.sq, x.y * ns.s * a.y * na.sq);
+    const __nv_bfloat16* src = qkv + (size_t)tok * 3 * d + i0;
+    __nv_bfloat16* dst = qk + (size_t)tok * 2 * d + i0;
+#pragma unroll 2
+    for (int h = 0; h < H; ++h) {
+      float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + h * 64));
+      float2 y = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + d + h * 64));
+      if (na.kind != RGPT_NORM_IDENTITY) {
+        const float Sq = warp_sum(x.x * x.x + x.y * x.y);
+        const float Sk = warp_sum(y.x * y.x + y.y * y.y);
+        const NS2 nq = norm_scale(na.kind, Sq, 64, na.eps, na.alpha);
+        const NS2 nk = norm_scale(na.kind, Sk, 64, na.eps, na.alpha);
+        const float2 aq = qk_affine2(na, true, i0), ak = qk_affine2(na, false, i0);
+        x = make_float2(x.x * nq.s * aq.x * na.sq, x.y * nq.s * aq.y * na.sq);
+        y = make_float2(y.x * nk.s * ak.x * na.sk, y.y * nk.s * ak.y * na.sk);
+      }
+      if (qn_out) *reinterpret_cast<uint32_t*>(qn_out + (size_t)tok * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
+      x = rope_pair(x, c, sn, second, 1);
+      y = rope_pair(y, c, sn, second, 1);
+      *reinterpret_cast<uint32_t*>(dst + h * 64) = pack_bf16x2(x.x, x.y);
+      *reinterpret_cast<uint32_t*>(dst + d + h * 64) = pack_bf16x2(y.x, y.y);
     }
-    if (qn_out) *reinterpret_cast<uint32_t*>(qn_out + tok * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
-    x = rope_pair(x, c, sn, second, 1);
-    *reinterpret_cast<uint32_t*>(qk + tok * 2 * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
-    // ---- k
-    x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + d + h * 64 + i0));
-    if (na.kind != RGPT_NORM_IDENTITY) {
-      const float S = warp_sum(x.x * x.x + x.y * x.y);
-      const NS2 ns = norm_scale(na.kind, S, 64, na.eps, na.alpha);
-      const float2 a = qk_affine2(na, false, i0);
-      x = make_float2(x.x * ns.s * a.x * na.sk, x.y * ns.s * a.y * na.sk);
-    }
-    x = rope_pair(x, c, sn, second, 1);
-    *reinterpret_cast<uint32_t*>(qk + tok * 2 * d + d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
   }
 }
 
@@ -391,85 +389,92 @@ __global__ void __launch_bounds__(256) qkv_prep_bwd_kernel(
     const float* __restrict__ dqn_gate, const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv,
     float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dtq,
     float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M, int T, int H) {
+  __shared__ float red[3][64];  // per-CTA column partials: dbg, dwq, dwk
   const int lane = threadIdx.x & 31;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const long long rows = (long long)M * H;
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
   const int d = H * 64;
   const int i0 = 2 * lane;
   const bool second = lane >= 16;
   const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
+  for (int i = threadIdx.x; i < 3 * 64; i += blockDim.x) (&red[0][0])[i] = 0.f;
+  __syncthreads();
   float2 acc_b = make_float2(0.f, 0.f), acc_wq = make_float2(0.f, 0.f), acc_wk = make_float2(0.f, 0.f);
   float acc_tq = 0.f, acc_tk = 0.f;
-  for (long long rh = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); rh < rows; rh += warps) {
-    const long long tok = rh / H;
-    const int h = (int)(rh % H);
+  for (int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < M; tok += nwarps) {
     const float t = (float)(tok % T);
     float2 c, sn;
     sincosf(t * f0, &sn.x, &c.x);
     sincosf(t * f1, &sn.y, &c.y);
-    const long long col = (long long)h * 64 + i0;
-    // ---- q
-    {
-      float2 g = *reinterpret_cast<const float2*>(dq + tok * d + col);
-      g = rope_pair(g, c, sn, second, -1);
-      if (dqn_gate) {
-        const float2 gg = *reinterpret_cast<const float2*>(dqn_gate + tok * d + col);
-        g.x += gg.x;
-        g.y += gg.y;
+#pragma unroll 2
+    for (int h = 0; h < H; ++h) {
+      const size_t col = (size_t)h * 64 + i0;
+      // ---- q
+      {
+        float2 g = *reinterpret_cast<const float2*>(dq + (size_t)tok * d + col);
+        const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + (size_t)tok * 3 * d + col));
+        g = rope_pair(g, c, sn, second, -1);
+        if (dqn_gate) {
+          const float2 gg = *reinterpret_cast<const float2*>(dqn_gate + (size_t)tok * d + col);
+          g.x += gg.x;
+          g.y += gg.y;
+        }
+        if (dgp) {
+          const float2 gp = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dgp + (size_t)tok * d + col));
+          acc_b.x += gp.x;
+          acc_b.y += gp.y;
+        }
+        NS2 ns{1.f, 0.f};
+        if (na.kind != RGPT_NORM_IDENTITY)
+          ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
+        const float2 a = qk_affine2(na, true, i0);
+        const float ax = a.x * na.sq, ay = a.y * na.sq;
+        const float k2 = 2.0f * ns.ds * warp_sum(ax * g.x * x.x + ay * g.y * x.y);
+        if (na.kind == RGPT_NORM_RMS_AFFINE) {
+          acc_wq.x += g.x * x.x * ns.s * na.sq;
+          acc_wq.y += g.y * x.y * ns.s * na.sq;
+        }
+        if (na.kind == RGPT_NORM_L2_TEMP) acc_tq += (g.x * x.x + g.y * x.y) * ns.s * na.sq;
+        *reinterpret_cast<uint32_t*>(dqkv + (size_t)tok * 3 * d + col) =
+            pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
       }
-      if (dgp) {
-        const float2 gp = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dgp + tok * d + col));
-        acc_b.x += gp.x;
-        acc_b.y += gp.y;
+      // ---- k
+      {
+        float2 g = *reinterpret_cast<const float2*>(dk + (size_t)tok * d + col);
+        const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + (size_t)tok * 3 * d + d + col));
+        g = rope_pair(g, c, sn, second, -1);
+        NS2 ns{1.f, 0.f};
+        if (na.kind != RGPT_NORM_IDENTITY)
+          ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
+        const float2 a = qk_affine2(na, false, i0);
+        const float ax = a.x * na.sk, ay = a.y * na.sk;
+        const float k2 = 2.0f * ns.ds * warp_sum(ax * g.x * x.x + ay * g.y * x.y);
+        if (na.kind == RGPT_NORM_RMS_AFFINE) {
+          acc_wk.x += g.x * x.x * ns.s * na.sk;
+          acc_wk.y += g.y * x.y * ns.s * na.sk;
+        }
+        if (na.kind == RGPT_NORM_L2_TEMP) acc_tk += (g.x * x.x + g.y * x.y) * ns.s * na.sk;
+        *reinterpret_cast<uint32_t*>(dqkv + (size_t)tok * 3 * d + d + col) =
+            pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
       }
-      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + col));
-      NS2 ns{1.f, 0.f};
-      if (na.kind != RGPT_NORM_IDENTITY) ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
-      const float2 a = qk_affine2(na, true, i0);
-      const float ax = a.x * na.sq, ay = a.y * na.sq;
-      const float cc = warp_sum(ax * g.x * x.x + ay * g.y * x.y);
-      const float k2 = 2.0f * ns.ds * cc;
-      if (na.kind == RGPT_NORM_RMS_AFFINE) {
-        acc_wq.x += g.x * x.x * ns.s * na.sq;
-        acc_wq.y += g.y * x.y * ns.s * na.sq;
-      }
-      if (na.kind == RGPT_NORM_L2_TEMP) acc_tq += (g.x * x.x + g.y * x.y) * ns.s * na.sq;
-      *reinterpret_cast<uint32_t*>(dqkv + tok * 3 * d + col) =
-          pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
-    }
-    // ---- k
-    {
-      float2 g = *reinterpret_cast<const float2*>(dk + tok * d + col);
-      g = rope_pair(g, c, sn, second, -1);
-      const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + tok * 3 * d + d + col));
-      NS2 ns{1.f, 0.f};
-      if (na.kind != RGPT_NORM_IDENTITY) ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
-      const float2 a = qk_affine2(na, false, i0);
-      const float ax = a.x * na.sk, ay = a.y * na.sk;
-      const float cc = warp_sum(ax * g.x * x.x + ay * g.y * x.y);
-      const float k2 = 2.0f * ns.ds * cc;
-      if (na.kind == RGPT_NORM_RMS_AFFINE) {
-        acc_wk.x += g.x * x.x * ns.s * na.sk;
-        acc_wk.y += g.y * x.y * ns.s * na.sk;
-      }
-      if (na.kind == RGPT_NORM_L2_TEMP) acc_tk += (g.x * x.x + g.y * x.y) * ns.s * na.sk;
-      *reinterpret_cast<uint32_t*>(dqkv + tok * 3 * d + d + col) =
-          pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
     }
   }
-  // per-column partials: each lane owns columns i0, i0+1 of the 64-wide head
+  // column partials: lanes own columns i0, i0+1; fold the CTA's warps in smem, then one atomic per column
   if (dbg) {
-    atomicAdd(&dbg[i0], acc_b.x);
-    atomicAdd(&dbg[i0 + 1], acc_b.y);
+    atomicAdd(&red[0][i0], acc_b.x);
+    atomicAdd(&red[0][i0 + 1], acc_b.y);
   }
   if (na.kind == RGPT_NORM_RMS_AFFINE) {
-    if (dwq) {
-      atomicAdd(&dwq[i0], acc_wq.x);
-      atomicAdd(&dwq[i0 + 1], acc_wq.y);
-    }
-    if (dwk) {
-      atomicAdd(&dwk[i0], acc_wk.x);
-      atomicAdd(&dwk[i0 + 1], acc_wk.y);
+    atomicAdd(&red[1][i0], acc_wq.x);
+    atomicAdd(&red[1][i0 + 1], acc_wq.y);
+    atomicAdd(&red[2][i0], acc_wk.x);
+    atomicAdd(&red[2][i0 + 1], acc_wk.y);
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    if (dbg) atomicAdd(&dbg[threadIdx.x], red[0][threadIdx.x]);
+    if (na.kind == RGPT_NORM_RMS_AFFINE) {
+      if (dwq) atomicAdd(&dwq[threadIdx.x], red[1][threadIdx.x]);
+      if (dwk) atomicAdd(&dwk[threadIdx.x], red[2][threadIdx.x]);
     }
   }
   if (na.kind == RGPT_NORM_L2_TEMP) {
@@ -809,11 +814,11 @@ static QkNormArgs qk_args(int kind, float eps, float alpha, const float* wq, con
   return a;
 }
 
-static int prep_grid(long long rows) {
+static int prep_grid(long long tokens) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const long long want = (rows + 7) / 8;  // 8 warps per 256-thread CTA
-  const long long cap = (long long)rgpt_num_sms(dev) * 16;
+  const long long want = (tokens + 7) / 8;  // 8 warps (one token each) per 256-thread CTA
+  const long long cap = (long long)rgpt_num_sms(dev) * 4;
   return (int)(want < cap ? want : cap);
 }
 
@@ -823,7 +828,7 @@ extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const floa
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
   if (qk_kind == RGPT_NORM_RMS_AFFINE && (wq == nullptr || wk == nullptr))
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rmsnorm QK norm needs weights");
-  qkv_prep_fwd_kernel<<<prep_grid((long long)M * H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  qkv_prep_fwd_kernel<<<prep_grid(M), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
       reinterpret_cast<__nv_bfloat16*>(qn), inv_freq, qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
   return rgpt_check_launch("qkv_prep_fwd_kernel");
@@ -836,7 +841,7 @@ extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* 
                                  int H, void* stream) {
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
   if (dbg && dgp == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dbg needs dgp");
-  qkv_prep_bwd_kernel<<<prep_grid((long long)M * H), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  qkv_prep_bwd_kernel<<<prep_grid(M), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, dqn_gate, reinterpret_cast<const __nv_bfloat16*>(dgp),
       reinterpret_cast<__nv_bfloat16*>(dqkv), dbg, dwq, dwk, dtq, dtk, inv_freq,
       qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);

@@ -156,30 +156,38 @@ class Muon(torch.optim.Optimizer):
         nesterov = bool(group["nesterov"])
         steps = int(group.get("ns_steps", 5))
         coeffs = tuple(group.get("ns_coeffs", NS_COEFFS))
-        classes: Dict[Tuple[int, int], List[torch.Tensor]] = {}
+        # batch by the shape Newton-Schulz sees (rows <= cols after transposing), so e.g. fc1 [4d, d]
+        # and fc2 [d, 4d] share one stack; prep/apply run per original shape on slices of it
+        classes: Dict[Tuple[int, int], Dict[Tuple[int, int], List[torch.Tensor]]] = {}
         for p in params:
             st = self.state[p]
             if len(st) == 0:
                 st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
             R, C = p.shape[0], p.numel() // p.shape[0]
-            classes.setdefault((R, C), []).append(p)
-        for (R, C), ps in classes.items():
-            grads = [p.grad for p in ps]
-            moms = [self.state[p]["momentum_buffer"] for p in ps]
-            rows = _muon_rows(ps, grads, moms)
-            key = ("muon", gi, R, C, tuple(r[0] for r in rows), tuple(r[1] for r in rows))
+            xr, xc = (C, R) if R > C else (R, C)
+            classes.setdefault((xr, xc), {}).setdefault((R, C), []).append(p)
+        for (xr, xc), subs in classes.items():
+            ordered = [(rc, ps) for rc, ps in sorted(subs.items())]
+            all_ps = [p for _, ps in ordered for p in ps]
+            rows_all = _muon_rows(all_ps, [p.grad for p in all_ps], [self.state[p]["momentum_buffer"] for p in all_ps])
+            key = ("muon", gi, xr, xc, tuple(r[0] for r in rows_all), tuple(r[1] for r in rows_all))
             ent = self._cache.get(key)
             if ent is None:
-                xr, xc = (C, R) if R > C else (R, C)
-                ent = (_table(rows, ps[0].device), _NSWorkspace(len(ps), xr, xc, ps[0].device))
+                dev = all_ps[0].device
+                tables, off = [], 0
+                for (R, C), ps in ordered:
+                    tables.append((R, C, off, len(ps), _table(rows_all[off:off + len(ps)], dev)))
+                    off += len(ps)
+                ent = (tables, _NSWorkspace(len(all_ps), xr, xc, dev))
                 self._cache[key] = ent
-            table, ws = ent
-            n = len(ps)
+            tables, ws = ent
             ws.sumsq.zero_()
-            nv.muon_prep(table, n, R, C, ws.X, beta, nesterov, ws.sumsq)
-            nv.ns_scale(ws.X, ws.xr, ws.xc, n, ws.sumsq)
+            for R, C, off, n, table in tables:
+                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n])
+            nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
             out = newton_schulz_batched(ws, steps, coeffs)
-            nv.muon_apply(table, n, R, C, out, lr, wd, muon_lr, _muon_scale(R, C))
+            for R, C, off, n, table in tables:
+                nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C))
 
     def _adamw_group(self, gi, group, params):
         if not params:
@@ -277,7 +285,7 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, coeffs=NS_COEFFS) -
     ws = _NSWorkspace(n, xr, xc, G.device)
     ws.X[:, :xr, :xc].copy_(Xs.to(torch.bfloat16))
     ws.sumsq.copy_(ws.X.float().pow(2).sum(dim=(1, 2)))
-    nv.ns_scale(ws.X, xr, xc, n, ws.sumsq)
+    nv.ns_scale(ws.X, xr, _pad8(xc), n, ws.sumsq)
     out = newton_schulz_batched(ws, steps, coeffs)[:, :xr, :xc]
     out = out.transpose(1, 2) if transposed else out
     out = out.contiguous()
@@ -299,7 +307,7 @@ def muon_update(grad_2d: torch.Tensor, momentum_2d: torch.Tensor, beta: float = 
     dummy = torch.zeros(R, C, device=dev, dtype=torch.float32)
     table = _table([[dummy.data_ptr(), g.data_ptr(), momentum_2d.data_ptr(), 0]], dev)
     nv.muon_prep(table, 1, R, C, ws.X, beta, nesterov, ws.sumsq)
-    nv.ns_scale(ws.X, xr, xc, 1, ws.sumsq)
+    nv.ns_scale(ws.X, xr, _pad8(xc), 1, ws.sumsq)
     out = newton_schulz_batched(ws, ns_steps)[0, :xr, :xc]
     out = out.t() if R > C else out
     return (out.float() * scale).to(torch.bfloat16)
