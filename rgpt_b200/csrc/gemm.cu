@@ -14,8 +14,8 @@
 //               per column chunk it tcgen05.ld's the fp32 accumulator, applies the
 //               fused epilogue, stages the result in swizzled smem and writes it with
 //               a TMA bulk store (or a TMA bulk reduce-add for accumulating outputs)
-// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue of
-// tile i overlaps the main loop of tile i+1. Tiles are visited in groups of
+// The accumulator is multi-buffered in TMEM (512 / BN buffers of BN columns) so the
+// epilogue of tile i overlaps the main loops of the tiles after it. Tiles are visited in groups of
 // GROUP_M row tiles so that consecutive CTAs share A and B panels in L2.
 //
 // Epilogues fuse what the reference runs as separate torch ops:
@@ -203,7 +203,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                         GemmShape sh, EpiParams ep) {
   using L = GemmSmem<BN, STAGES>;
-  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr int NUM_ACC = 512 / BN;  // TMEM accumulator buffers (2 for 256-wide tiles, 4 for 128-wide)
+  constexpr uint32_t TMEM_COLS = NUM_ACC * BN;
   constexpr uint32_t IDESC = make_idesc_bf16(GEMM_BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
@@ -214,8 +215,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + L::EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
-  uint64_t* tempty_bar = tfull_bar + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* tempty_bar = tfull_bar + NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + NUM_ACC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], 4);
     }
@@ -337,7 +338,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (!ok) break;
         umma_commit(&tfull_bar[acc]);
-        if (++acc == 2) {
+        if (++acc == NUM_ACC) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -502,7 +503,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (++acc == 2) {
+      if (++acc == NUM_ACC) {
         acc = 0;
         acc_phase ^= 1u;
       }
@@ -652,8 +653,9 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
   // 256-wide tiles unless that leaves most SMs idle (small N or few row tiles)
   int BN = (N > 128) ? 256 : 128;
-  if (BN == 256 && batch * sh.m_tiles * ((N + 255) / 256) < nsm && batch * sh.m_tiles * ((N + 127) / 128) <= 2 * nsm)
-    BN = 128;
+  if (BN == 256 && epi != RGPT_EPI_ACCUM_F32 && batch * sh.m_tiles * ((N + 255) / 256) < nsm &&
+      batch * sh.m_tiles * ((N + 127) / 128) <= 2 * nsm)
+    BN = 128;  // accumulating GEMMs keep the wide tile (fewer operand re-reads) and split K instead
   sh.n_tiles = (N + BN - 1) / BN;
   sh.num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   const int tiles = batch * sh.m_tiles * sh.n_tiles;
