@@ -21,9 +21,11 @@
 //          bf16 into 128B-swizzled smem for the P V MMA, O accumulated in registers.
 // Backward CTA = one 128-key tile of one (b, h), looping over query tiles:
 //   S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
-//   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> fp32 atomics).
+//   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> TMA bulk reduce-add).
 #include <cudaTypedefs.h>
 #include <math.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "rgpt.h"
@@ -302,35 +304,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       tmem_ld32(t_lane + s * 64, v[0]);
       tmem_ld32(t_lane + s * 64 + 32, v[1]);
       tmem_wait_ld();
-      float mx = -INFINITY;
+      if (masked) {  // causal mask and keys past T (warp-uniform branch)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int key = kbase + c * 32 + t;
-          float x = __uint_as_float(v[c][t]) * p.scale_log2;
-          if (masked && (key > qrow || key >= p.T)) x = -INFINITY;
-          v[c][t] = __float_as_uint(x);
-          mx = fmaxf(mx, x);
-        }
+          for (int t = 0; t < 32; ++t) {
+            const int key = kbase + c * 32 + t;
+            if (key > qrow || key >= p.T) v[c][t] = __float_as_uint(-INFINITY);
+          }
       }
+      // row max of the raw scores (the scale is positive), four independent chains
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int t = 0; t < 32; ++t) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(v[c][t]));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       tc_fence_before();
       mbar_arrive(&s_empty[s]);  // S is in registers now; the TMEM buffer can be refilled
-      const float m_new = fmaxf(m_run, mx);
-      const float alpha = exp2f(m_run - m_new);
-      float sum = 0.f;
+      const float m_new = fmaxf(m_run, mx * p.scale_log2);
+      const float alpha = ex2_approx(m_run - m_new);
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       uint8_t* pbuf = sP + s * P_TILE_BYTES;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float pv[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          pv[t] = exp2f(__uint_as_float(v[c][t]) - m_new);
-          sum += pv[t];
+          pv[t] = ex2_approx(fmaf(__uint_as_float(v[c][t]), p.scale_log2, -m_new));
+          sum4[t & 3] += pv[t];
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       fence_proxy_async_smem();
       mbar_arrive(&p_full[s]);
       l_run = l_run * alpha + sum;
@@ -447,6 +454,7 @@ struct AttnBwdParams {
 
 constexpr int ATT_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
 constexpr uint32_t DQ_STAGE_BYTES = 32 * 32 * 4;  // one warp's 32 x 32 fp32 dQ tile
+constexpr int BWD_STAT_FLOATS = 128;              // one warp's 64 query LSEs (log2 units) + 64 D values
 
 // Backward CTA = one 128-key tile of one (b, h). The 8 softmax warps come in pairs that
 // share TMEM lane quadrants: warp pair (w, w+4) owns key rows 32*(w%4).. and splits the
@@ -464,7 +472,8 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T  : 2 atoms (queries 0-63, 64-127) x 16 KB
   uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T : 2 atoms x 16 KB
   uint8_t* sDQ = sDS + 2 * TILE_BYTES;    // 8 x 4 KB dQ staging (one per softmax warp)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDQ + 8 * DQ_STAGE_BYTES);
+  float* sStat = reinterpret_cast<float*>(sDQ + 8 * DQ_STAGE_BYTES);  // 8 warps x [64 lse*log2(e) | 64 D]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStat + 8 * BWD_STAT_FLOATS);
   uint64_t* kv_full = bars + 0;
   uint64_t* qd_full = bars + 1;   // [2]
   uint64_t* qd_empty = bars + 3;  // [2]
@@ -595,40 +604,66 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     };
     const float* lse_bh = p.lse + ((long long)b * p.H + h) * p.T;
     const float* D_bh = p.Dvec + ((long long)b * p.H + h) * p.T;
+    float* wstat = sStat + sw * BWD_STAT_FLOATS;
+    // P^T = exp2(S^T * scale*log2(e) - lse*log2(e)) and dS^T/scale = P^T (dP^T - D) for one
+    // 32-query chunk of this warp's key row. Queries past T carry lse = +inf (P = 0); keys past
+    // T need no mask (their K/V rows are zero and their dK/dV rows are never stored).
+    auto softmax_chunk = [&](auto mask_tag, int cc, int c) {
+      constexpr bool MASK = decltype(mask_tag)::value;
+      uint32_t sv[32], dv[32];
+      tmem_ld32(t_lane + 0 + c * 32, sv);
+      tmem_ld32(t_lane + 128 + c * 32, dv);
+      tmem_wait_ld();
+      const float4* l4 = reinterpret_cast<const float4*>(wstat + cc * 32);
+      const float4* d4 = reinterpret_cast<const float4*>(wstat + 64 + cc * 32);
+      float pr[32], ds[32];
+#pragma unroll
+      for (int t4 = 0; t4 < 8; ++t4) {
+        const float4 l = l4[t4], dd = d4[t4];
+        const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {dd.x, dd.y, dd.z, dd.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int t = 4 * t4 + e;
+          float pv = ex2_approx(fmaf(__uint_as_float(sv[t]), p.scale_log2, -la[e]));
+          if constexpr (MASK) pv = (c * 32 + t < r) ? 0.f : pv;  // causal: query before key
+          pr[t] = pv;
+          ds[t] = pv * (__uint_as_float(dv[t]) - da[e]);
+        }
+      }
+      uint8_t* patom = sP + half * TILE_BYTES;
+      uint8_t* datom = sDS + half * TILE_BYTES;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        st_sw128_chunk(patom, r, cc * 4 + t, pr + 8 * t);
+        st_sw128_chunk(datom, r, cc * 4 + t, ds + 8 * t);
+      }
+    };
     for (int i = 0; i < nq; ++i) {
       const int qrow0 = (qt0 + i) * ATT_TILE;
+      {  // this warp's 64 queries: LSE in log2 units and D, staged for broadcast reads
+        const int qa = qrow0 + half * 64 + lane, qb = qa + 32;
+        const float la = qa < p.T ? __ldg(lse_bh + qa) * 1.4426950408889634f : INFINITY;
+        const float lb = qb < p.T ? __ldg(lse_bh + qb) * 1.4426950408889634f : INFINITY;
+        const float da = qa < p.T ? __ldg(D_bh + qa) : 0.f;
+        const float db = qb < p.T ? __ldg(D_bh + qb) : 0.f;
+        __syncwarp();
+        wstat[lane] = la;
+        wstat[32 + lane] = lb;
+        wstat[64 + lane] = da;
+        wstat[96 + lane] = db;
+        __syncwarp();
+      }
       if (!wait_all(sdp_full, i & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool diag = (i == 0);
-#pragma unroll 1
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c = half * 2 + cc;  // 32-column chunk of the 128 queries
-        uint32_t sv[32], dv[32];
-        tmem_ld32(t_lane + 0 + c * 32, sv);
-        tmem_ld32(t_lane + 128 + c * 32, dv);
-        tmem_wait_ld();
-        float pr[32], ds[32];
-#pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const int q = qrow0 + c * 32 + t;
-          // lse / D are the same address for every lane of the warp: one broadcast load each
-          const bool live = q < p.T && key < p.T && !(diag && q < key);
-          const int qc = q < p.T ? q : p.T - 1;
-          float pv = live ? exp2f(__uint_as_float(sv[t]) * p.scale_log2 - __ldg(lse_bh + qc) * 1.4426950408889634f)
-                          : 0.f;
-          pr[t] = pv;
-          ds[t] = pv * (__uint_as_float(dv[t]) - __ldg(D_bh + qc)) * p.scale;
-        }
-        uint8_t* patom = sP + half * TILE_BYTES;
-        uint8_t* datom = sDS + half * TILE_BYTES;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          st_sw128_chunk(patom, r, cc * 4 + t, pr + 8 * t);
-          st_sw128_chunk(datom, r, cc * 4 + t, ds + 8 * t);
-        }
+      if (i == 0) {  // the diagonal tile (query tile == key tile)
+        softmax_chunk(std::true_type{}, 0, half * 2);
+        softmax_chunk(std::true_type{}, 1, half * 2 + 1);
+      } else {
+        softmax_chunk(std::false_type{}, 0, half * 2);
+        softmax_chunk(std::false_type{}, 1, half * 2 + 1);
       }
       tc_fence_before();
       fence_proxy_async_smem();
@@ -648,8 +683,8 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
 #pragma unroll
         for (int j = 0; j < 8; ++j)
           *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]), __uint_as_float(v[4 * j + 2]),
-                          __uint_as_float(v[4 * j + 3]));
+              make_float4(__uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
+                          __uint_as_float(v[4 * j + 2]) * p.scale, __uint_as_float(v[4 * j + 3]) * p.scale);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0 && qrow0 + quarter * 32 < p.T) {  // boxes wholly past T carry only zeros
@@ -685,8 +720,8 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
         float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + half * 32);
 #pragma unroll
         for (int t = 0; t < 8; ++t)
-          dkd[t] = make_float4(__uint_as_float(v[4 * t]), __uint_as_float(v[4 * t + 1]),
-                               __uint_as_float(v[4 * t + 2]), __uint_as_float(v[4 * t + 3]));
+          dkd[t] = make_float4(__uint_as_float(v[4 * t]) * p.scale, __uint_as_float(v[4 * t + 1]) * p.scale,
+                               __uint_as_float(v[4 * t + 2]) * p.scale, __uint_as_float(v[4 * t + 3]) * p.scale);
       }
     }
     tc_fence_before();
@@ -700,7 +735,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
 }
 
 constexpr uint32_t FWD_SMEM = TILE_BYTES + 4 * KV_TILE_BYTES + 2 * P_TILE_BYTES + 256 + 1024;
-constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 256 + 1024;
+constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 8 * BWD_STAT_FLOATS * 4 + 256 + 1024;
 
 }  // namespace rgpt
 

@@ -25,6 +25,8 @@
 #include "common.cuh"
 #include "rgpt.h"
 
+#include <type_traits>
+
 namespace rgpt {
 
 struct NS2 {
@@ -142,8 +144,11 @@ __global__ void rownorm_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* _
 //   dls  += g_out * raw        (optional: layer-scale grad of the branch that produced raw)
 //   dw   += dy * x * s         (RMS_AFFINE weight grad)     dtemp += sum(dy * x * s) (L2_TEMP)
 //   dqw  += dq^T h, dqb += dq  (q_head mode, h = the forward norm output in bf16)
-template <int NV, bool QM>
-__global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dy,
+// NV float4s per lane; QM: q-head mode (dy = dq Wq); DW / DLS: accumulate the norm weight /
+// layer-scale grads. For d <= 512 the residual-grad input row is fetched with x and dy so that
+// its latency overlaps the row reductions.
+template <int NV, bool QM, bool DW, bool DLS>
+__global__ void __launch_bounds__(256, NV <= 4 ? 2 : 1) rownorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ dy,
                                    const float* __restrict__ w, float temp, int kind, float eps, float alpha, int M,
                                    int d, const float* __restrict__ g_in, float* __restrict__ g_out,
                                    __nv_bfloat16* __restrict__ g_bf16, const float* __restrict__ ls,
@@ -154,16 +159,19 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
   extern __shared__ float red[];  // per-CTA column partials: [d] dw, [d] dls, [2d] dqw
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const bool need_dw = (dw != nullptr && kind == RGPT_NORM_RMS_AFFINE);
-  const bool need_dls = (dls != nullptr && raw != nullptr);
+  constexpr bool need_dw = DW;
+  constexpr bool need_dls = DLS;
   constexpr bool qmode = QM;
+  constexpr bool PREF = NV <= 4;
   for (int i = threadIdx.x; i < 4 * d; i += blockDim.x) red[i] = 0.f;
   __syncthreads();
   float dtemp_acc = 0.f, dqb0 = 0.f, dqb1 = 0.f;
   // column partials owned by this lane, accumulated over the rows this warp visits
-  float4 pdw[NV], pdls[NV], pq0[QM ? NV : 1], pq1[QM ? NV : 1];
+  float4 pdw[DW ? NV : 1], pdls[DLS ? NV : 1], pq0[QM ? NV : 1], pq1[QM ? NV : 1];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) pdw[i] = pdls[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < (DW ? NV : 1); ++i) pdw[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < (DLS ? NV : 1); ++i) pdls[i] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int i = 0; i < (QM ? NV : 1); ++i) pq0[i] = pq1[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   auto affine = [&](int i) -> float4 {
@@ -177,7 +185,7 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
 
   for (long long row = (long long)blockIdx.x * warps + wid; row < M; row += (long long)gridDim.x * warps) {
     const float4* xr = reinterpret_cast<const float4*>(x + row * d);
-    float4 xv[NV], dv[NV];
+    float4 xv[NV], dv[NV], gpre[PREF ? NV : 1];
     float S = 0.f;
     float q0 = 0.f, q1 = 0.f;
     if (qmode) {
@@ -196,6 +204,8 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
       } else {
         dv[i] = reinterpret_cast<const float4*>(dy + row * d)[lane + 32 * i];
       }
+      if constexpr (PREF)
+        gpre[i] = g_in ? reinterpret_cast<const float4*>(g_in + row * d)[lane + 32 * i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     S = warp_sum(S);
     const NS2 ns = norm_scale(kind, S, d, eps, alpha);
@@ -214,8 +224,10 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
       const float4 av = affine(i);
       float4 g = make_float4(ns.s * av.x * dv[i].x + k2 * xv[i].x, ns.s * av.y * dv[i].y + k2 * xv[i].y,
                              ns.s * av.z * dv[i].z + k2 * xv[i].z, ns.s * av.w * dv[i].w + k2 * xv[i].w);
-      if (g_in) {
-        float4 gi = reinterpret_cast<const float4*>(g_in + row * d)[lane + 32 * i];
+      if (PREF || g_in) {
+        float4 gi;
+        if constexpr (PREF) gi = gpre[i];
+        else gi = reinterpret_cast<const float4*>(g_in + row * d)[lane + 32 * i];
         g.x += gi.x;
         g.y += gi.y;
         g.z += gi.z;
@@ -227,14 +239,14 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
         reinterpret_cast<uint2*>(g_bf16 + row * d)[lane + 32 * i] =
             make_uint2(pack_bf16x2(g.x * s4.x, g.y * s4.y), pack_bf16x2(g.z * s4.z, g.w * s4.w));
       }
-      if (need_dls) {
+      if constexpr (need_dls) {
         float4 rv = reinterpret_cast<const float4*>(raw + row * d)[lane + 32 * i];
         pdls[i].x += g.x * rv.x;
         pdls[i].y += g.y * rv.y;
         pdls[i].z += g.z * rv.z;
         pdls[i].w += g.w * rv.w;
       }
-      if (need_dw) {
+      if constexpr (need_dw) {
         pdw[i].x += dv[i].x * xv[i].x * ns.s;
         pdw[i].y += dv[i].y * xv[i].y * ns.s;
         pdw[i].z += dv[i].z * xv[i].z * ns.s;
@@ -260,13 +272,13 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int c0 = 4 * (lane + 32 * i);
-    if (need_dw) {
+    if constexpr (need_dw) {
       atomicAdd(&red[c0 + 0], pdw[i].x);
       atomicAdd(&red[c0 + 1], pdw[i].y);
       atomicAdd(&red[c0 + 2], pdw[i].z);
       atomicAdd(&red[c0 + 3], pdw[i].w);
     }
-    if (need_dls) {
+    if constexpr (need_dls) {
       atomicAdd(&red[d + c0 + 0], pdls[i].x);
       atomicAdd(&red[d + c0 + 1], pdls[i].y);
       atomicAdd(&red[d + c0 + 2], pdls[i].z);
@@ -302,9 +314,11 @@ __global__ void rownorm_bwd_kernel(const float* __restrict__ x, const float* __r
 }
 
 // ============================================================================ QKV prep
-// One warp per (token, head) row; lane l holds elements 2l, 2l+1 of the 64-wide head
-// (4-byte loads: a warp moves one contiguous 128-byte row). RoPE partners i and
-// i + 32 live in lanes l and l ^ 16. Forward writes
+// A half-warp per (token, head): lane l handles elements 4*(l%16) .. +3 of head 2*hp + l/16,
+// so a warp moves two contiguous 128-byte head rows and the norm sums are 4-step half-warp
+// reductions. RoPE partners i and i + 32 live in lanes l and l ^ 8. Each warp walks a
+// contiguous run of (token, head pair) units and recomputes the RoPE angles only when the
+// token changes. Forward writes
 //   qk [M, 2d]  roped, normalised q | k (the attention operands, bf16)
 //   qn [M, d]   normalised q before RoPE (bf16), the input of the gate GEMM
 // The G1 gate itself, sigmoid(q_n Wg^T + bg), is a tcgen05 GEMM with a bias+sigmoid
@@ -318,64 +332,141 @@ struct QkNormArgs {
   float sq, sk;     // constant post-scales (asymmetric hyperball: 1.0 / 1.1)
 };
 
-__device__ __forceinline__ float2 qk_affine2(const QkNormArgs& a, bool is_q, int i0) {
+__device__ __forceinline__ float half_warp_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v;
+}
+
+__device__ __forceinline__ float4 ld_bf16x4(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float4 v) {
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+__device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
+__device__ __forceinline__ float4 mul4(float4 a, float4 b) {
+  return make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w);
+}
+
+// per-element affine factor of the QK norm (RMS_AFFINE: 1 + w, L2_TEMP: temp) times the post-scale
+__device__ __forceinline__ float4 qk_affine4(const QkNormArgs& a, bool is_q, int i0) {
+  const float post = is_q ? a.sq : a.sk;
   if (a.kind == RGPT_NORM_RMS_AFFINE) {
-    const float* w = is_q ? a.wq : a.wk;
-    return make_float2(1.0f + w[i0], 1.0f + w[i0 + 1]);
+    const float4 w = *reinterpret_cast<const float4*>((is_q ? a.wq : a.wk) + i0);
+    return make_float4((1.0f + w.x) * post, (1.0f + w.y) * post, (1.0f + w.z) * post, (1.0f + w.w) * post);
   }
-  if (a.kind == RGPT_NORM_L2_TEMP) {
-    const float t = is_q ? a.tq : a.tk;
-    return make_float2(t, t);
-  }
-  return make_float2(1.0f, 1.0f);
+  const float t = (a.kind == RGPT_NORM_L2_TEMP ? (is_q ? a.tq : a.tk) : 1.0f) * post;
+  return make_float4(t, t, t, t);
 }
 
-// rotate-half RoPE on a lane's pair (x0, x1) = elements 2l, 2l+1
-__device__ __forceinline__ float2 rope_pair(float2 x, float2 c, float2 sn, bool second_half, int dir) {
-  const float p0 = __shfl_xor_sync(0xffffffffu, x.x, 16);
-  const float p1 = __shfl_xor_sync(0xffffffffu, x.y, 16);
-  // forward: first half y = x c - partner s; second half y = x c + partner s (dir = +1); backward flips the sign
-  const float sg = (second_half ? 1.0f : -1.0f) * (float)dir;
-  return make_float2(x.x * c.x + sg * p0 * sn.x, x.y * c.y + sg * p1 * sn.y);
+// rotate-half RoPE on a lane's 4 elements; the partners sit in lane ^ 8.
+// forward: first half y = x c - partner s, second half y = x c + partner s (dir = +1);
+// the backward (dir = -1) applies the transposed rotation.
+__device__ __forceinline__ float4 rope4(float4 x, float4 c, float4 sn, bool second_half, float dir) {
+  const float p0 = __shfl_xor_sync(0xffffffffu, x.x, 8), p1 = __shfl_xor_sync(0xffffffffu, x.y, 8);
+  const float p2 = __shfl_xor_sync(0xffffffffu, x.z, 8), p3 = __shfl_xor_sync(0xffffffffu, x.w, 8);
+  const float sg = (second_half ? 1.0f : -1.0f) * dir;
+  return make_float4(x.x * c.x + sg * p0 * sn.x, x.y * c.y + sg * p1 * sn.y, x.z * c.z + sg * p2 * sn.z,
+                     x.w * c.w + sg * p3 * sn.w);
 }
 
-__global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+struct PrepLane {
+  int half, i0;  // head of the pair (0/1) and first element
+  bool second;   // elements in [32, 64)
+  float4 f;      // inverse frequencies of the 4 elements
+};
+
+__device__ __forceinline__ PrepLane prep_lane(const float* inv_freq) {
+  PrepLane L;
+  const int lane = threadIdx.x & 31;
+  L.half = lane >> 4;
+  L.i0 = 4 * (lane & 15);
+  L.second = L.i0 >= 32;
+  const int fi = L.i0 & 31;
+  L.f = make_float4(inv_freq[fi], inv_freq[fi + 1], inv_freq[fi + 2], inv_freq[fi + 3]);
+  return L;
+}
+
+// sin and cos of a RoPE angle x = t * inv_freq (|x| < 65536, enforced on the host through T).
+// Cody-Waite reduction by pi/2 with a three-part split of pi/2 whose first part has 8
+// significant bits (k * C1 is exact for |k| < 2^16), then the hardware sin/cos on |r| <= pi/4
+// (absolute error below 4e-7 there) and the quadrant rotation.
+__device__ __forceinline__ void rope_sincos(float x, float* sn, float* cs) {
+  const float k = rintf(x * 0.636619772f);
+  float r = fmaf(-k, 1.5703125f, x);
+  r = fmaf(-k, 4.83826792e-4f, r);
+  r = fmaf(-k, 2.56328292e-12f, r);
+  const float sr = __sinf(r), cr = __cosf(r);
+  const int q = static_cast<int>(k) & 3;
+  const float s1 = (q & 1) ? cr : sr, c1 = (q & 1) ? sr : cr;
+  *sn = (q & 2) ? -s1 : s1;
+  *cs = ((q + 1) & 2) ? -c1 : c1;
+}
+
+__device__ __forceinline__ void rope_angles(const PrepLane& L, float t, float4& c, float4& sn) {
+  rope_sincos(t * L.f.x, &sn.x, &c.x);
+  rope_sincos(t * L.f.y, &sn.y, &c.y);
+  rope_sincos(t * L.f.z, &sn.z, &c.z);
+  rope_sincos(t * L.f.w, &sn.w, &c.w);
+}
+
+// contiguous run of units for this warp
+__device__ __forceinline__ void prep_units(long long total, long long& u0, long long& u1) {
+  const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+  const long long w = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long per = (total + nwarps - 1) / nwarps;
+  u0 = w * per;
+  u1 = u0 + per < total ? u0 + per : total;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(256, 4) qkv_prep_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
                                                            __nv_bfloat16* __restrict__ qk,
                                                            __nv_bfloat16* __restrict__ qn_out,
                                                            const float* __restrict__ inv_freq, QkNormArgs na,
                                                            int M, int T, int H) {
-  // warps stride over tokens; a warp runs every head of its token (angles shared by all heads)
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const PrepLane L = prep_lane(inv_freq);
   const int d = H * 64;
-  const int i0 = 2 * lane;
-  const bool second = lane >= 16;
-  const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
-  for (int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < M; tok += nwarps) {
-    const float t = (float)(tok % T);
-    float2 c, sn;
-    sincosf(t * f0, &sn.x, &c.x);
-    sincosf(t * f1, &sn.y, &c.y);
-    const __nv_bfloat16* src = qkv + (size_t)tok * 3 * d + i0;
-    __nv_bfloat16* dst = qk + (size_t)tok * 2 * d + i0;
-#pragma unroll 2
-    for (int h = 0; h < H; ++h) {
-      float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + h * 64));
-      float2 y = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + d + h * 64));
-      if (na.kind != RGPT_NORM_IDENTITY) {
-        const float Sq = warp_sum(x.x * x.x + x.y * x.y);
-        const float Sk = warp_sum(y.x * y.x + y.y * y.y);
-        const NS2 nq = norm_scale(na.kind, Sq, 64, na.eps, na.alpha);
-        const NS2 nk = norm_scale(na.kind, Sk, 64, na.eps, na.alpha);
-        const float2 aq = qk_affine2(na, true, i0), ak = qk_affine2(na, false, i0);
-        x = make_float2(x.x * nq.s * aq.x * na.sq, x.y * nq.s * aq.y * na.sq);
-        y = make_float2(y.x * nk.s * ak.x * na.sk, y.y * nk.s * ak.y * na.sk);
-      }
-      if (qn_out) *reinterpret_cast<uint32_t*>(qn_out + (size_t)tok * d + h * 64 + i0) = pack_bf16x2(x.x, x.y);
-      x = rope_pair(x, c, sn, second, 1);
-      y = rope_pair(y, c, sn, second, 1);
-      *reinterpret_cast<uint32_t*>(dst + h * 64) = pack_bf16x2(x.x, x.y);
-      *reinterpret_cast<uint32_t*>(dst + d + h * 64) = pack_bf16x2(y.x, y.y);
+  const int hp_n = (H + 1) >> 1;
+  const float4 aq = qk_affine4(na, true, L.i0), ak = qk_affine4(na, false, L.i0);
+  long long u0, u1;
+  prep_units((long long)M * hp_n, u0, u1);
+  int cur_tok = -1;
+  float4 c = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long u = u0; u < u1; ++u) {
+    const int tok = (int)(u / hp_n);
+    const int h = (int)(u % hp_n) * 2 + L.half;
+    if (tok != cur_tok) {
+      cur_tok = tok;
+      rope_angles(L, (float)(tok % T), c, sn);
+    }
+    const bool live = h < H;
+    const size_t col = (size_t)h * 64 + L.i0;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
+    if (live) {
+      x = ld_bf16x4(qkv + (size_t)tok * 3 * d + col);
+      y = ld_bf16x4(qkv + (size_t)tok * 3 * d + d + col);
+    }
+    if (KIND != RGPT_NORM_IDENTITY) {
+      const NS2 nq = norm_scale(KIND, half_warp_sum(dot4(x, x)), 64, na.eps, na.alpha);
+      const NS2 nk = norm_scale(KIND, half_warp_sum(dot4(y, y)), 64, na.eps, na.alpha);
+      x = mul4(x, make_float4(nq.s * aq.x, nq.s * aq.y, nq.s * aq.z, nq.s * aq.w));
+      y = mul4(y, make_float4(nk.s * ak.x, nk.s * ak.y, nk.s * ak.z, nk.s * ak.w));
+    } else {
+      x = mul4(x, aq);
+      y = mul4(y, ak);
+    }
+    if (qn_out && live) st_bf16x4(qn_out + (size_t)tok * d + col, x);
+    x = rope4(x, c, sn, L.second, 1.0f);
+    y = rope4(y, c, sn, L.second, 1.0f);
+    if (live) {
+      st_bf16x4(qk + (size_t)tok * 2 * d + col, x);
+      st_bf16x4(qk + (size_t)tok * 2 * d + d + col, y);
     }
   }
 }
@@ -384,102 +475,107 @@ __global__ void __launch_bounds__(256) qkv_prep_fwd_kernel(const __nv_bfloat16* 
 // dqn_gate: fp32 [M, d] = dgp Wg (the gate GEMM's contribution to d q_n), may be null;
 // dgp: bf16 [M, d] grad of the gate pre-activation, only summed here into dbg.
 // Writes the q and k column blocks of dqkv (bf16); ACCUMULATES dbg, dwq/dwk, dtq/dtk.
-__global__ void __launch_bounds__(256) qkv_prep_bwd_kernel(
+template <int KIND>
+__global__ void __launch_bounds__(256, 3) qkv_prep_bwd_kernel(
     const __nv_bfloat16* __restrict__ qkv, const float* __restrict__ dq, const float* __restrict__ dk,
     const float* __restrict__ dqn_gate, const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv,
     float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dtq,
     float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M, int T, int H) {
   __shared__ float red[3][64];  // per-CTA column partials: dbg, dwq, dwk
-  const int lane = threadIdx.x & 31;
-  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  const PrepLane L = prep_lane(inv_freq);
   const int d = H * 64;
-  const int i0 = 2 * lane;
-  const bool second = lane >= 16;
-  const float f0 = inv_freq[i0 & 31], f1 = inv_freq[(i0 + 1) & 31];
+  const int hp_n = (H + 1) >> 1;
   for (int i = threadIdx.x; i < 3 * 64; i += blockDim.x) (&red[0][0])[i] = 0.f;
   __syncthreads();
-  float2 acc_b = make_float2(0.f, 0.f), acc_wq = make_float2(0.f, 0.f), acc_wk = make_float2(0.f, 0.f);
+  const float4 aq = qk_affine4(na, true, L.i0), ak = qk_affine4(na, false, L.i0);
+  constexpr bool affine = KIND == RGPT_NORM_RMS_AFFINE, temp = KIND == RGPT_NORM_L2_TEMP;
+  float4 acc_b = make_float4(0.f, 0.f, 0.f, 0.f), acc_wq = acc_b, acc_wk = acc_b;
   float acc_tq = 0.f, acc_tk = 0.f;
-  for (int tok = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); tok < M; tok += nwarps) {
-    const float t = (float)(tok % T);
-    float2 c, sn;
-    sincosf(t * f0, &sn.x, &c.x);
-    sincosf(t * f1, &sn.y, &c.y);
-#pragma unroll 2
-    for (int h = 0; h < H; ++h) {
-      const size_t col = (size_t)h * 64 + i0;
-      // ---- q
-      {
-        float2 g = *reinterpret_cast<const float2*>(dq + (size_t)tok * d + col);
-        const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + (size_t)tok * 3 * d + col));
-        g = rope_pair(g, c, sn, second, -1);
-        if (dqn_gate) {
-          const float2 gg = *reinterpret_cast<const float2*>(dqn_gate + (size_t)tok * d + col);
-          g.x += gg.x;
-          g.y += gg.y;
-        }
-        if (dgp) {
-          const float2 gp = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dgp + (size_t)tok * d + col));
-          acc_b.x += gp.x;
-          acc_b.y += gp.y;
-        }
-        NS2 ns{1.f, 0.f};
-        if (na.kind != RGPT_NORM_IDENTITY)
-          ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
-        const float2 a = qk_affine2(na, true, i0);
-        const float ax = a.x * na.sq, ay = a.y * na.sq;
-        const float k2 = 2.0f * ns.ds * warp_sum(ax * g.x * x.x + ay * g.y * x.y);
-        if (na.kind == RGPT_NORM_RMS_AFFINE) {
-          acc_wq.x += g.x * x.x * ns.s * na.sq;
-          acc_wq.y += g.y * x.y * ns.s * na.sq;
-        }
-        if (na.kind == RGPT_NORM_L2_TEMP) acc_tq += (g.x * x.x + g.y * x.y) * ns.s * na.sq;
-        *reinterpret_cast<uint32_t*>(dqkv + (size_t)tok * 3 * d + col) =
-            pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
-      }
-      // ---- k
-      {
-        float2 g = *reinterpret_cast<const float2*>(dk + (size_t)tok * d + col);
-        const float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(qkv + (size_t)tok * 3 * d + d + col));
-        g = rope_pair(g, c, sn, second, -1);
-        NS2 ns{1.f, 0.f};
-        if (na.kind != RGPT_NORM_IDENTITY)
-          ns = norm_scale(na.kind, warp_sum(x.x * x.x + x.y * x.y), 64, na.eps, na.alpha);
-        const float2 a = qk_affine2(na, false, i0);
-        const float ax = a.x * na.sk, ay = a.y * na.sk;
-        const float k2 = 2.0f * ns.ds * warp_sum(ax * g.x * x.x + ay * g.y * x.y);
-        if (na.kind == RGPT_NORM_RMS_AFFINE) {
-          acc_wk.x += g.x * x.x * ns.s * na.sk;
-          acc_wk.y += g.y * x.y * ns.s * na.sk;
-        }
-        if (na.kind == RGPT_NORM_L2_TEMP) acc_tk += (g.x * x.x + g.y * x.y) * ns.s * na.sk;
-        *reinterpret_cast<uint32_t*>(dqkv + (size_t)tok * 3 * d + d + col) =
-            pack_bf16x2(ns.s * ax * g.x + k2 * x.x, ns.s * ay * g.y + k2 * x.y);
-      }
+  long long u0, u1;
+  prep_units((long long)M * hp_n, u0, u1);
+  int cur_tok = -1;
+  float4 c = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long u = u0; u < u1; ++u) {
+    const int tok = (int)(u / hp_n);
+    const int h = (int)(u % hp_n) * 2 + L.half;
+    if (tok != cur_tok) {
+      cur_tok = tok;
+      rope_angles(L, (float)(tok % T), c, sn);
+    }
+    const bool live = h < H;
+    const size_t col = (size_t)h * 64 + L.i0;
+    const size_t rq = (size_t)tok * 3 * d + col;
+    float4 gq = make_float4(0.f, 0.f, 0.f, 0.f), gk = gq, xq = gq, xk = gq, gg = gq, gp = gq;
+    if (live) {
+      gq = *reinterpret_cast<const float4*>(dq + (size_t)tok * d + col);
+      gk = *reinterpret_cast<const float4*>(dk + (size_t)tok * d + col);
+      xq = ld_bf16x4(qkv + rq);
+      xk = ld_bf16x4(qkv + rq + d);
+      if (dqn_gate) gg = *reinterpret_cast<const float4*>(dqn_gate + (size_t)tok * d + col);
+      if (dgp) gp = ld_bf16x4(dgp + (size_t)tok * d + col);
+    }
+    acc_b.x += gp.x;
+    acc_b.y += gp.y;
+    acc_b.z += gp.z;
+    acc_b.w += gp.w;
+    gq = rope4(gq, c, sn, L.second, -1.0f);
+    gk = rope4(gk, c, sn, L.second, -1.0f);
+    gq = make_float4(gq.x + gg.x, gq.y + gg.y, gq.z + gg.z, gq.w + gg.w);
+    NS2 nq{1.f, 0.f}, nk{1.f, 0.f};
+    if (KIND != RGPT_NORM_IDENTITY) {
+      nq = norm_scale(KIND, half_warp_sum(dot4(xq, xq)), 64, na.eps, na.alpha);
+      nk = norm_scale(KIND, half_warp_sum(dot4(xk, xk)), 64, na.eps, na.alpha);
+    }
+    // y = x * s(S) * a  =>  dx = s a g + 2 s'(S) (sum a g x) x
+    const float4 agq = mul4(aq, gq), agk = mul4(ak, gk);
+    const float k2q = 2.0f * nq.ds * half_warp_sum(dot4(agq, xq));
+    const float k2k = 2.0f * nk.ds * half_warp_sum(dot4(agk, xk));
+    if (affine && live) {
+      const float fq = nq.s * na.sq, fk = nk.s * na.sk;
+      acc_wq = make_float4(acc_wq.x + gq.x * xq.x * fq, acc_wq.y + gq.y * xq.y * fq, acc_wq.z + gq.z * xq.z * fq,
+                           acc_wq.w + gq.w * xq.w * fq);
+      acc_wk = make_float4(acc_wk.x + gk.x * xk.x * fk, acc_wk.y + gk.y * xk.y * fk, acc_wk.z + gk.z * xk.z * fk,
+                           acc_wk.w + gk.w * xk.w * fk);
+    }
+    if (temp && live) {
+      acc_tq += dot4(gq, xq) * nq.s * na.sq;
+      acc_tk += dot4(gk, xk) * nk.s * na.sk;
+    }
+    if (live) {
+      st_bf16x4(dqkv + rq, make_float4(nq.s * agq.x + k2q * xq.x, nq.s * agq.y + k2q * xq.y,
+                                       nq.s * agq.z + k2q * xq.z, nq.s * agq.w + k2q * xq.w));
+      st_bf16x4(dqkv + rq + d, make_float4(nk.s * agk.x + k2k * xk.x, nk.s * agk.y + k2k * xk.y,
+                                           nk.s * agk.z + k2k * xk.z, nk.s * agk.w + k2k * xk.w));
     }
   }
-  // column partials: lanes own columns i0, i0+1; fold the CTA's warps in smem, then one atomic per column
+  // column partials: a lane owns columns i0..i0+3; fold the CTA's lanes in smem, then one atomic per column
   if (dbg) {
-    atomicAdd(&red[0][i0], acc_b.x);
-    atomicAdd(&red[0][i0 + 1], acc_b.y);
+    atomicAdd(&red[0][L.i0 + 0], acc_b.x);
+    atomicAdd(&red[0][L.i0 + 1], acc_b.y);
+    atomicAdd(&red[0][L.i0 + 2], acc_b.z);
+    atomicAdd(&red[0][L.i0 + 3], acc_b.w);
   }
-  if (na.kind == RGPT_NORM_RMS_AFFINE) {
-    atomicAdd(&red[1][i0], acc_wq.x);
-    atomicAdd(&red[1][i0 + 1], acc_wq.y);
-    atomicAdd(&red[2][i0], acc_wk.x);
-    atomicAdd(&red[2][i0 + 1], acc_wk.y);
+  if (affine) {
+    atomicAdd(&red[1][L.i0 + 0], acc_wq.x);
+    atomicAdd(&red[1][L.i0 + 1], acc_wq.y);
+    atomicAdd(&red[1][L.i0 + 2], acc_wq.z);
+    atomicAdd(&red[1][L.i0 + 3], acc_wq.w);
+    atomicAdd(&red[2][L.i0 + 0], acc_wk.x);
+    atomicAdd(&red[2][L.i0 + 1], acc_wk.y);
+    atomicAdd(&red[2][L.i0 + 2], acc_wk.z);
+    atomicAdd(&red[2][L.i0 + 3], acc_wk.w);
   }
   __syncthreads();
   if (threadIdx.x < 64) {
     if (dbg) atomicAdd(&dbg[threadIdx.x], red[0][threadIdx.x]);
-    if (na.kind == RGPT_NORM_RMS_AFFINE) {
+    if (affine) {
       if (dwq) atomicAdd(&dwq[threadIdx.x], red[1][threadIdx.x]);
       if (dwk) atomicAdd(&dwk[threadIdx.x], red[2][threadIdx.x]);
     }
   }
-  if (na.kind == RGPT_NORM_L2_TEMP) {
+  if (temp) {
     const float tq = warp_sum(acc_tq), tk = warp_sum(acc_tk);
-    if (lane == 0) {
+    if ((threadIdx.x & 31) == 0) {
       if (dtq) atomicAdd(dtq, tq);
       if (dtk) atomicAdd(dtk, tk);
     }
@@ -665,6 +761,165 @@ __global__ void __launch_bounds__(512) cross_entropy_kernel(__nv_bfloat16* __res
   }
 }
 
+// Row-in-shared-memory variant for V % 8 == 0 and V * 2 bytes <= CE_SMEM_MAX: one bulk copy
+// brings the row into shared memory (two CTAs per SM, so one row's copy overlaps the other's
+// math), then three passes over shared memory: max + argmax, sum of exp2, and the gradient
+// row written straight to HBM. Logits are read from HBM once and dlogits written once.
+constexpr int CE_THREADS = 512;
+constexpr uint32_t CE_SMEM_MAX = 112 * 1024;
+
+__device__ __forceinline__ void ce_unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 p = unpack_bf16x2(w4[e]);
+    f[2 * e] = p.x;
+    f[2 * e + 1] = p.y;
+  }
+}
+
+__global__ void __launch_bounds__(CE_THREADS, 2)
+    cross_entropy_smem_kernel(__nv_bfloat16* __restrict__ logits, long long ld, int V,
+                              const long long* __restrict__ labels, int ignore_index, float* __restrict__ loss_rows,
+                              int* __restrict__ argmax, const float* __restrict__ scale, int write_grad) {
+  extern __shared__ __align__(128) uint8_t ce_row[];
+  __shared__ uint64_t bar;
+  __shared__ float red_f[CE_THREADS / 32];
+  __shared__ int red_i[CE_THREADS / 32];
+  constexpr float LOG2E = 1.4426950408889634f;
+  const long long row = blockIdx.x;
+  __nv_bfloat16* x = logits + row * ld;
+  const int nvec = V >> 3;
+  const int wid = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, (uint32_t)V * 2u);
+    bulk_load_1d(ce_row, x, (uint32_t)V * 2u, &bar);
+  }
+  const long long label = labels[row];
+  const bool valid = label != ignore_index && label >= 0 && label < V;
+  const float sc = (valid && write_grad) ? scale[0] : 0.f;
+  if (!mbar_wait(&bar, 0, nullptr)) {
+    mbar_wait(&bar, 0, nullptr);  // give the copy a second bound before the CTA retires
+    return;
+  }
+  const uint4* s4 = reinterpret_cast<const uint4*>(ce_row);
+
+  // pass 1: max and first index of the max
+  float m = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
+    float f[8];
+    ce_unpack8(s4[v], f);
+    const float lm = fmaxf(fmaxf(fmaxf(f[0], f[1]), fmaxf(f[2], f[3])), fmaxf(fmaxf(f[4], f[5]), fmaxf(f[6], f[7])));
+    if (lm > m) {
+      int e = 7;
+#pragma unroll
+      for (int k = 6; k >= 0; --k) e = (f[k] == lm) ? k : e;
+      m = lm;
+      besti = v * 8 + e;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (om > m || (om == m && oi < besti)) {
+      m = om;
+      besti = oi;
+    }
+  }
+  if (lane == 0) {
+    red_f[wid] = m;
+    red_i[wid] = besti;
+  }
+  __syncthreads();
+  m = red_f[0];
+  besti = red_i[0];
+#pragma unroll
+  for (int w = 1; w < CE_THREADS / 32; ++w) {
+    const float om = red_f[w];
+    const int oi = red_i[w];
+    if (om > m || (om == m && oi < besti)) {
+      m = om;
+      besti = oi;
+    }
+  }
+  __syncthreads();  // red_f is reused below
+
+  // pass 2: sum of exp(x - m) in base 2
+  const float m2 = m * LOG2E;
+  float s0 = 0.f, s1 = 0.f;
+  for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
+    float f[8];
+    ce_unpack8(s4[v], f);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      s0 += ex2_approx(fmaf(f[e], LOG2E, -m2));
+      s1 += ex2_approx(fmaf(f[e + 1], LOG2E, -m2));
+    }
+  }
+  float sum = warp_sum(s0 + s1);
+  if (lane == 0) red_f[wid] = sum;
+  __syncthreads();
+  sum = 0.f;
+#pragma unroll
+  for (int w = 0; w < CE_THREADS / 32; ++w) sum += red_f[w];
+  const float lse2 = m2 + log2f(sum);
+  if (threadIdx.x == 0) {
+    if (loss_rows) {
+      const float xl = valid ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ce_row)[label]) : 0.f;
+      loss_rows[row] = valid ? lse2 * 0.69314718055994531f - xl : 0.f;
+    }
+    if (argmax) argmax[row] = besti;
+  }
+  if (!write_grad) return;
+
+  // pass 3: dlogits = (softmax - onehot) * scale, overwriting the row in HBM
+  const int label_vec = valid ? (int)(label >> 3) : -1;
+  const int label_e = (int)(label & 7);
+  uint4* xo = reinterpret_cast<uint4*>(x);
+  for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
+    float f[8];
+    ce_unpack8(s4[v], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = ex2_approx(fmaf(f[e], LOG2E, -lse2));
+    if (v == label_vec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e == label_e) f[e] -= 1.f;
+    }
+    xo[v] = make_uint4(pack_bf16x2(f[0] * sc, f[1] * sc), pack_bf16x2(f[2] * sc, f[3] * sc),
+                       pack_bf16x2(f[4] * sc, f[5] * sc), pack_bf16x2(f[6] * sc, f[7] * sc));
+  }
+}
+
+// Launch the per-row cross entropy (shared-memory row when it fits, else the streaming kernel).
+static int launch_cross_entropy_rows(__nv_bfloat16* logits, long long ld, int M, int V, const long long* labels,
+                                     int ignore_index, float* loss_rows, int* argmax, const float* scale,
+                                     int write_grad, cudaStream_t s) {
+  if (V % 8 == 0 && (uint32_t)V * 2u <= CE_SMEM_MAX) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static bool attr[64] = {false};
+    if (dev >= 0 && dev < 64 && !attr[dev]) {
+      if (cudaFuncSetAttribute(cross_entropy_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)CE_SMEM_MAX) != cudaSuccess)
+        return rgpt_check_launch("cross_entropy_smem set smem");
+      attr[dev] = true;
+    }
+    cross_entropy_smem_kernel<<<M, CE_THREADS, (size_t)V * 2, s>>>(logits, ld, V, labels, ignore_index, loss_rows,
+                                                                    argmax, scale, write_grad);
+  } else {
+    cross_entropy_kernel<<<M, 512, 0, s>>>(logits, ld, V, labels, ignore_index, loss_rows, argmax, scale,
+                                           write_grad);
+  }
+  return RGPT_OK;
+}
+
 // sum of loss rows / count -> out[0] (mean CE over valid labels), also adds into accum (optional)
 __global__ void ce_finalize_kernel(const float* __restrict__ loss_rows, int M, const float* __restrict__ count,
                                    float* __restrict__ out) {
@@ -779,23 +1034,32 @@ extern "C" int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w,
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   __nv_bfloat16* gb = reinterpret_cast<__nv_bfloat16*>(g_bf16);
   const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(h);
-#define RN_B(N)                                                                                               \
-  do {                                                                                                        \
-    if (dq)                                                                                                   \
-      rownorm_bwd_kernel<N, true><<<grid, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, \
-                                                           ls, raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);    \
-    else                                                                                                      \
-      rownorm_bwd_kernel<N, false><<<grid, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, \
-                                                            ls, raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);   \
-  } while (0)
+  const bool want_dw = dw != nullptr && kind == RGPT_NORM_RMS_AFFINE, want_dls = dls != nullptr && raw != nullptr;
+  auto launch = [&](auto nv_tag, auto qm_tag, auto dw_tag, auto dls_tag) {
+    constexpr int N = decltype(nv_tag)::value;
+    const int cap2 = rgpt_num_sms(dev) * (N <= 4 ? 2 : 1);
+    rownorm_bwd_kernel<N, decltype(qm_tag)::value, decltype(dw_tag)::value, decltype(dls_tag)::value>
+        <<<grid < cap2 ? grid : cap2, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, ls,
+                                                        raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);
+  };
+  auto with_flags = [&](auto nv_tag) {
+    using T_ = std::true_type;
+    using F_ = std::false_type;
+    if (dq) {
+      if (want_dw) want_dls ? launch(nv_tag, T_{}, T_{}, T_{}) : launch(nv_tag, T_{}, T_{}, F_{});
+      else want_dls ? launch(nv_tag, T_{}, F_{}, T_{}) : launch(nv_tag, T_{}, F_{}, F_{});
+    } else {
+      if (want_dw) want_dls ? launch(nv_tag, F_{}, T_{}, T_{}) : launch(nv_tag, F_{}, T_{}, F_{});
+      else want_dls ? launch(nv_tag, F_{}, F_{}, T_{}) : launch(nv_tag, F_{}, F_{}, F_{});
+    }
+  };
   switch (nv) {
-    case 1: RN_B(1); break;
-    case 2: RN_B(2); break;
-    case 4: RN_B(4); break;
-    case 8: RN_B(8); break;
-    default: RN_B(16); break;
+    case 1: with_flags(std::integral_constant<int, 1>{}); break;
+    case 2: with_flags(std::integral_constant<int, 2>{}); break;
+    case 4: with_flags(std::integral_constant<int, 4>{}); break;
+    case 8: with_flags(std::integral_constant<int, 8>{}); break;
+    default: with_flags(std::integral_constant<int, 16>{}); break;
   }
-#undef RN_B
   return rgpt_check_launch("rownorm_bwd_kernel");
 }
 
@@ -814,11 +1078,27 @@ static QkNormArgs qk_args(int kind, float eps, float alpha, const float* wq, con
   return a;
 }
 
-static int prep_grid(long long tokens) {
+// Calls f(std::integral_constant<int, kind>{}) for a runtime norm kind.
+template <typename F>
+static void dispatch_norm_kind(int kind, F&& f) {
+  switch (kind) {
+    case RGPT_NORM_IDENTITY: f(std::integral_constant<int, RGPT_NORM_IDENTITY>{}); break;
+    case RGPT_NORM_RMS_AFFINE: f(std::integral_constant<int, RGPT_NORM_RMS_AFFINE>{}); break;
+    case RGPT_NORM_RMS: f(std::integral_constant<int, RGPT_NORM_RMS>{}); break;
+    case RGPT_NORM_L2_TEMP: f(std::integral_constant<int, RGPT_NORM_L2_TEMP>{}); break;
+    case RGPT_NORM_L2: f(std::integral_constant<int, RGPT_NORM_L2>{}); break;
+    case RGPT_NORM_ELASTIC: f(std::integral_constant<int, RGPT_NORM_ELASTIC>{}); break;
+    case RGPT_NORM_ELASTICBALL: f(std::integral_constant<int, RGPT_NORM_ELASTICBALL>{}); break;
+    default: f(std::integral_constant<int, RGPT_NORM_HYPERBALL>{}); break;
+  }
+}
+
+static int prep_grid(long long tokens, int H, int ctas_per_sm) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const long long want = (tokens + 7) / 8;  // 8 warps (one token each) per 256-thread CTA
-  const long long cap = (long long)rgpt_num_sms(dev) * 4;
+  const long long units = tokens * ((H + 1) / 2);  // (token, head pair) units, one warp each at a time
+  const long long want = (units + 7) / 8;           // 8 warps per 256-thread CTA
+  const long long cap = (long long)rgpt_num_sms(dev) * ctas_per_sm;
   return (int)(want < cap ? want : cap);
 }
 
@@ -826,11 +1106,19 @@ extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const floa
                                  float alpha, const float* wq, const float* wk, float tq, float tk, float sq, float sk,
                                  int M, int T, int H, void* stream) {
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
+  if (T > 65536) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "RoPE positions are limited to T <= 65536 (got %d)", T);
   if (qk_kind == RGPT_NORM_RMS_AFFINE && (wq == nullptr || wk == nullptr))
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rmsnorm QK norm needs weights");
-  qkv_prep_fwd_kernel<<<prep_grid(M), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
-      reinterpret_cast<__nv_bfloat16*>(qn), inv_freq, qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
+  if (qk_kind < RGPT_NORM_IDENTITY || qk_kind > RGPT_NORM_HYPERBALL)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown QK norm kind %d", qk_kind);
+  const QkNormArgs na = qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk);
+  auto launch = [&](auto kind_tag) {
+    qkv_prep_fwd_kernel<decltype(kind_tag)::value>
+        <<<prep_grid(M, H, 4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+            reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
+            reinterpret_cast<__nv_bfloat16*>(qn), inv_freq, na, M, T, H);
+  };
+  dispatch_norm_kind(qk_kind, launch);
   return rgpt_check_launch("qkv_prep_fwd_kernel");
 }
 
@@ -840,11 +1128,19 @@ extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* 
                                  const float* wq, const float* wk, float tq, float tk, float sq, float sk, int M, int T,
                                  int H, void* stream) {
   if (M % T != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rows (%d) must be a multiple of T (%d)", M, T);
+  if (T > 65536) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "RoPE positions are limited to T <= 65536 (got %d)", T);
   if (dbg && dgp == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dbg needs dgp");
-  qkv_prep_bwd_kernel<<<prep_grid(M), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, dqn_gate, reinterpret_cast<const __nv_bfloat16*>(dgp),
-      reinterpret_cast<__nv_bfloat16*>(dqkv), dbg, dwq, dwk, dtq, dtk, inv_freq,
-      qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk), M, T, H);
+  if (qk_kind < RGPT_NORM_IDENTITY || qk_kind > RGPT_NORM_HYPERBALL)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown QK norm kind %d", qk_kind);
+  const QkNormArgs na = qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk);
+  auto launch = [&](auto kind_tag) {
+    qkv_prep_bwd_kernel<decltype(kind_tag)::value>
+        <<<prep_grid(M, H, 3), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+            reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, dqn_gate,
+            reinterpret_cast<const __nv_bfloat16*>(dgp), reinterpret_cast<__nv_bfloat16*>(dqkv), dbg, dwq, dwk, dtq,
+            dtk, inv_freq, na, M, T, H);
+  };
+  dispatch_norm_kind(qk_kind, launch);
   return rgpt_check_launch("qkv_prep_bwd_kernel");
 }
 
@@ -877,8 +1173,9 @@ extern "C" int rgpt_cross_entropy(void* logits, long long ld, int M, int V, cons
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "scale_buf (2 floats) required for loss / grad");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (scale_buf) ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
-  cross_entropy_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, labels, ignore_index,
-                                         loss_rows, argmax, scale_buf, write_grad);
+  int st = launch_cross_entropy_rows(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, labels, ignore_index,
+                                     loss_rows, argmax, scale_buf, write_grad, s);
+  if (st) return st;
   if (loss_out && loss_rows) ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
   return rgpt_check_launch("cross_entropy_kernel");
 }
@@ -941,8 +1238,9 @@ extern "C" int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int
   float* scale_buf = scratch + RGPT_CE_NOALLOC_MAX_ROWS;  // {grad_scale/count, count}, rewritten by this call
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
-  cross_entropy_kernel<<<M, 512, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(logits), ld, V, labels, ignore_index,
-                                         loss_rows, argmax, scale_buf, write_grad);
+  if ((st = launch_cross_entropy_rows(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, labels, ignore_index,
+                                      loss_rows, argmax, scale_buf, write_grad, s)))
+    return st;
   ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
   return rgpt_check_launch("cross_entropy_noalloc");
 }
