@@ -14,11 +14,12 @@
 // one head, with rows past T zero-filled.
 //
 // Forward CTA (192 threads) = one 128-query tile of one (b, h):
-//   warp 0 TMA (Q once, then K/V tiles in a 2-deep ring)
-//   warp 1 TMEM alloc + tcgen05.mma: S = Q K^T into a double-buffered TMEM S,
-//          then O_j = P_j V_j into a double-buffered TMEM O
+//   warp 0 TMA (Q once, then 64-key K and V tiles in separate 3-deep rings)
+//   warp 1 TMEM alloc + tcgen05.mma: S = Q K^T into a double-buffered TMEM S, one
+//          tile ahead; O += P_j V_j accumulated in TMEM
 //   warps 2-5: one thread per query row: online softmax on S (tcgen05.ld), P as
-//          bf16 into 128B-swizzled smem for the P V MMA, O accumulated in registers.
+//          bf16 into 128B-swizzled smem for the P V MMA; O rescaled in TMEM only
+//          when a row max grows by more than 2^8.
 // Backward CTA = one 128-key tile of one (b, h), looping over query tiles:
 //   S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
 //   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> TMA bulk reduce-add).
@@ -134,30 +135,37 @@ struct AttnFwdParams {
 };
 
 constexpr int FWD_KT = 64;                                  // keys per tile in the forward
+constexpr int FWD_KV_STAGES = 3;                            // K and V rings (separate barriers)
 constexpr uint32_t KV_TILE_BYTES = FWD_KT * ATT_D * 2;      // 8 KB
 constexpr uint32_t P_TILE_BYTES = ATT_TILE * FWD_KT * 2;    // 16 KB: [128 queries x 64 keys] bf16
+constexpr float FWD_RESCALE_LOG2 = 8.0f;                    // rescale O only when a row max grows by > 2^8
 
-// Forward CTA: 128 queries of one (b, h), 64-key tiles. 256 TMEM columns and ~80 KB of smem
-// let two CTAs share an SM, so one CTA's softmax overlaps the other's tensor-core work.
+// Forward CTA: 128 queries of one (b, h), 64-key tiles, two CTAs per SM (256 TMEM columns and
+// ~97 KB of smem each) so one CTA's softmax overlaps the other's tensor-core work.
+// MMA order: S(0), then per tile j: S(j+1), O += P(j) V(j); the softmax of tile j+1 thus
+// overlaps P(j) V(j). O accumulates in TMEM. The running row max used for P is only raised
+// when the tile max exceeds it by more than 2^8 (P then stays below 2^8, well inside bf16);
+// that rare rescale multiplies O in TMEM after the previous P V has landed.
 __global__ void __launch_bounds__(ATT_THREADS, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                        // 16 KB
-  uint8_t* sK = sQ + TILE_BYTES;             // 2 x 8 KB
-  uint8_t* sV = sK + 2 * KV_TILE_BYTES;      // 2 x 8 KB
-  uint8_t* sP = sV + 2 * KV_TILE_BYTES;      // 2 x 16 KB
+  uint8_t* sQ = smem;                                    // 16 KB
+  uint8_t* sK = sQ + TILE_BYTES;                         // FWD_KV_STAGES x 8 KB
+  uint8_t* sV = sK + FWD_KV_STAGES * KV_TILE_BYTES;      // FWD_KV_STAGES x 8 KB
+  uint8_t* sP = sV + FWD_KV_STAGES * KV_TILE_BYTES;      // 2 x 16 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_TILE_BYTES);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;    // [2]
-  uint64_t* o_full = bars + 11;   // [2]
-  uint64_t* o_empty = bars + 13;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 1;                        // [FWD_KV_STAGES]
+  uint64_t* k_empty = k_full + FWD_KV_STAGES;         // [FWD_KV_STAGES]
+  uint64_t* v_full = k_empty + FWD_KV_STAGES;         // [FWD_KV_STAGES]
+  uint64_t* v_empty = v_full + FWD_KV_STAGES;         // [FWD_KV_STAGES]
+  uint64_t* s_full = v_empty + FWD_KV_STAGES;         // [2]
+  uint64_t* s_empty = s_full + 2;                     // [2]
+  uint64_t* p_full = s_empty + 2;                     // [2]
+  uint64_t* pv_done = p_full + 2;                     // [2] P V of the tile using P buffer i has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -170,14 +178,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    for (int i = 0; i < FWD_KV_STAGES; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+      mbar_init(&pv_done[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -190,26 +201,38 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S0 [0,64) S1 [64,128) O0 [128,192) O1 [192,256)
+  constexpr uint32_t O_COL = 128;  // TMEM columns: S0 [0,64) S1 [64,128) O [128,192)
 
   if (warp == 0) {
     if (lane == 0) {
       bool ok = true;
       mbar_arrive_expect_tx(q_full, TILE_BYTES);
       tma_load_4d(sQ, &tmQ, q_full, 0, h, q0, b);
+      int issued_k = 0, issued_v = 0;
       for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag)) {
+        const int st = j % FWD_KV_STAGES;
+        const uint32_t ph = ((j / FWD_KV_STAGES) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[st], ph, abort_flag)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_TILE_BYTES);
-        tma_load_4d(sK + s * KV_TILE_BYTES, &tmK, &kv_full[s], 0, h, j * FWD_KT, b);
-        tma_load_4d(sV + s * KV_TILE_BYTES, &tmV, &kv_full[s], 0, h, j * FWD_KT, b);
+        mbar_arrive_expect_tx(&k_full[st], KV_TILE_BYTES);
+        tma_load_4d(sK + st * KV_TILE_BYTES, &tmK, &k_full[st], 0, h, j * FWD_KT, b);
+        ++issued_k;
+        if (!mbar_wait(&v_empty[st], ph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&v_full[st], KV_TILE_BYTES);
+        tma_load_4d(sV + st * KV_TILE_BYTES, &tmV, &v_full[st], 0, h, j * FWD_KT, b);
+        ++issued_v;
       }
-      if (!ok) {
+      if (!ok) {  // let the copies already issued land before the CTA retires
         mbar_wait(q_full, 0, nullptr);
-        for (int s = 0; s < 2; ++s) mbar_wait(&kv_full[s], 0, nullptr);
+        for (int j = max(0, issued_k - FWD_KV_STAGES); j < issued_k; ++j)
+          mbar_wait(&k_full[j % FWD_KV_STAGES], (j / FWD_KV_STAGES) & 1, nullptr);
+        for (int j = max(0, issued_v - FWD_KV_STAGES); j < issued_v; ++j)
+          mbar_wait(&v_full[j % FWD_KV_STAGES], (j / FWD_KV_STAGES) & 1, nullptr);
       }
     }
     __syncwarp();
@@ -219,42 +242,40 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       constexpr uint32_t IDESC_O = make_idesc_bf16(128, 64, 0, 1);
       bool ok = mbar_wait(q_full, 0, abort_flag);
       const uint32_t q_addr = smem_u32(sQ);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&p_full[s], ph, abort_flag)) return false;
-        if (!mbar_wait(&o_empty[s], ph ^ 1, abort_flag)) return false;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % FWD_KV_STAGES, sb = j & 1;
+        if (!mbar_wait(&k_full[st], (j / FWD_KV_STAGES) & 1, abort_flag)) return false;
+        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + s * P_TILE_BYTES);
-        const uint32_t v_addr = smem_u32(sV + s * KV_TILE_BYTES);
+        const uint32_t k_addr = smem_u32(sK + st * KV_TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < FWD_KT / 16; ++kk) {
-          const uint64_t adesc = make_sw128_desc(p_addr + kk * 32, 16, 1024);
-          const uint64_t bdesc = make_sw128_desc(v_addr + kk * 2048, KV_TILE_BYTES, 1024);
-          umma_bf16(tmem + 128 + s * 64, adesc, bdesc, IDESC_O, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&o_full[s]);
-        umma_commit(&kv_empty[s]);
+        for (int kk = 0; kk < ATT_D / 16; ++kk)
+          umma_bf16(tmem + sb * 64, make_sw128_desc(q_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(k_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[sb]);
+        umma_commit(&k_empty[st]);
         return true;
       };
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&kv_full[s], ph, abort_flag) || !mbar_wait(&s_empty[s], ph ^ 1, abort_flag)) {
-          ok = false;
-          break;
-        }
+      auto issue_pv = [&](int j) -> bool {
+        const int st = j % FWD_KV_STAGES, pb = j & 1;
+        if (!mbar_wait(&p_full[pb], (j >> 1) & 1, abort_flag)) return false;
+        if (!mbar_wait(&v_full[st], (j / FWD_KV_STAGES) & 1, abort_flag)) return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * KV_TILE_BYTES);
+        const uint32_t p_addr = smem_u32(sP + pb * P_TILE_BYTES);
+        const uint32_t v_addr = smem_u32(sV + st * KV_TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          umma_bf16(tmem + s * 64, make_sw128_desc(q_addr + kk * 32, 16, 1024),
-                    make_sw128_desc(k_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[s]);
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
+        for (int kk = 0; kk < FWD_KT / 16; ++kk)
+          umma_bf16(tmem + O_COL, make_sw128_desc(p_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(v_addr + kk * 2048, KV_TILE_BYTES, 1024), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[pb]);
+        umma_commit(&v_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv && !issue_s(j + 1)) ok = false;
+        if (ok && !issue_pv(j)) ok = false;
       }
-      if (ok) issue_pv(nkv - 1);
     }
     __syncwarp();
   } else {
@@ -263,10 +284,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     const int r = quarter * 32 + lane;
     const int qrow = q0 + r;
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
-    float o_acc[ATT_D];
-#pragma unroll
-    for (int i = 0; i < ATT_D; ++i) o_acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
 
     auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
@@ -274,26 +292,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       if (lane == 0) v = mbar_wait(bar, ph, abort_flag) ? 1 : 0;
       return __shfl_sync(0xffffffffu, v, 0) != 0;
     };
-    auto accumulate_o = [&](int i, float alpha) -> bool {
-      const int s = i & 1;
-      if (!wait_all(&o_full[s], (i >> 1) & 1)) return false;
-      tc_fence_after();
-      uint32_t v[32];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        tmem_ld32(t_lane + 128 + s * 64 + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 32; ++t) o_acc[c * 32 + t] = o_acc[c * 32 + t] * alpha + __uint_as_float(v[t]);
-      }
-      tc_fence_before();
-      mbar_arrive(&o_empty[s]);
-      return true;
-    };
 
     for (int j = 0; j < nkv; ++j) {
-      const int s = j & 1;
-      if (!wait_all(&s_full[s], (j >> 1) & 1)) {
+      const int sb = j & 1;
+      if (!wait_all(&s_full[sb], (j >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -301,9 +303,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       const int kbase = j * FWD_KT;
       const bool masked = (kbase + FWD_KT > q0) || (kbase + FWD_KT > p.T);  // tiles on the diagonal / past T
       uint32_t v[2][32];
-      tmem_ld32(t_lane + s * 64, v[0]);
-      tmem_ld32(t_lane + s * 64 + 32, v[1]);
+      tmem_ld32(t_lane + sb * 64, v[0]);
+      tmem_ld32(t_lane + sb * 64 + 32, v[1]);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);  // S is in registers now; the TMEM buffer can be refilled
       if (masked) {  // causal mask and keys past T (warp-uniform branch)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
@@ -319,72 +323,102 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int t = 0; t < 32; ++t) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(v[c][t]));
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      tc_fence_before();
-      mbar_arrive(&s_empty[s]);  // S is in registers now; the TMEM buffer can be refilled
-      const float m_new = fmaxf(m_run, mx * p.scale_log2);
-      const float alpha = ex2_approx(m_run - m_new);
+      const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
+      // raise the running max only when P would otherwise exceed 2^8 (always on the first tile)
+      const bool raise = mt > m_run + FWD_RESCALE_LOG2;
+      float alpha = 1.f;
+      if (raise) {
+        alpha = ex2_approx(m_run - mt);  // 0 on the first tile
+        m_run = mt;
+        l_run *= alpha;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, raise)) {
+        // O holds P V of tiles < j: wait for the last of them, then scale the raised rows
+        if (!wait_all(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + O_COL + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+          tmem_st32(t_lane + O_COL + c * 32, o);
+        }
+        tmem_wait_st();
+      }
+      // the P buffer was last read by P V of tile j - 2
+      if (j >= 2 && !wait_all(&pv_done[sb], ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint8_t* pbuf = sP + s * P_TILE_BYTES;
+      uint8_t* pbuf = sP + sb * P_TILE_BYTES;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float pv[32];
 #pragma unroll
         for (int t = 0; t < 32; ++t) {
-          pv[t] = ex2_approx(fmaf(__uint_as_float(v[c][t]), p.scale_log2, -m_new));
+          pv[t] = ex2_approx(fmaf(__uint_as_float(v[c][t]), p.scale_log2, -m_run));
           sum4[t & 3] += pv[t];
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       fence_proxy_async_smem();
-      mbar_arrive(&p_full[s]);
-      l_run = l_run * alpha + sum;
-      m_run = m_new;
-      if (j >= 1 && !accumulate_o(j - 1, alpha_prev)) {
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
+      tc_fence_before();
+      mbar_arrive(&p_full[sb]);
     }
-    if (ok) ok = accumulate_o(nkv - 1, alpha_prev);
-    if (ok && qrow < p.T) {
-      const float inv_l = 1.0f / l_run;
-      const long long row = (long long)b * p.T + qrow;
-      __nv_bfloat16* orow = p.o + row * p.d + h * ATT_D;
-      float ov[ATT_D];
+    // every P V has landed once the last one has (in-order tensor pipe)
+    if (ok) ok = wait_all(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1);
+    if (ok) {
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld32(t_lane + O_COL, o[0]);
+      tmem_ld32(t_lane + O_COL + 32, o[1]);
+      tmem_wait_ld();
+      if (qrow < p.T) {
+        const float inv_l = 1.0f / l_run;
+        const long long row = (long long)b * p.T + qrow;
+        __nv_bfloat16* orow = p.o + row * p.d + h * ATT_D;
+        float ov[ATT_D];
 #pragma unroll
-      for (int i = 0; i < ATT_D; ++i) ov[i] = o_acc[i] * inv_l;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 w;
-        w.x = pack_bf16x2(ov[8 * c + 0], ov[8 * c + 1]);
-        w.y = pack_bf16x2(ov[8 * c + 2], ov[8 * c + 3]);
-        w.z = pack_bf16x2(ov[8 * c + 4], ov[8 * c + 5]);
-        w.w = pack_bf16x2(ov[8 * c + 6], ov[8 * c + 7]);
-        reinterpret_cast<uint4*>(orow)[c] = w;
-      }
-      if (p.og != nullptr) {
-        const uint4* grow = reinterpret_cast<const uint4*>(p.gate + row * p.d + h * ATT_D);
-        uint4* ogrow = reinterpret_cast<uint4*>(p.og + row * p.d + h * ATT_D);
+        for (int i = 0; i < ATT_D; ++i) ov[i] = __uint_as_float(o[i >> 5][i & 31]) * inv_l;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          uint4 g = grow[c];
-          uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-          uint32_t ow[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 gf = unpack_bf16x2(gw[e]);
-            // gate the bf16-rounded o, as the reference multiplies the stored attention output
-            ow[e] = pack_bf16x2(bf16_round(ov[8 * c + 2 * e]) * gf.x, bf16_round(ov[8 * c + 2 * e + 1]) * gf.y);
-          }
-          ogrow[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          uint4 w;
+          w.x = pack_bf16x2(ov[8 * c + 0], ov[8 * c + 1]);
+          w.y = pack_bf16x2(ov[8 * c + 2], ov[8 * c + 3]);
+          w.z = pack_bf16x2(ov[8 * c + 4], ov[8 * c + 5]);
+          w.w = pack_bf16x2(ov[8 * c + 6], ov[8 * c + 7]);
+          reinterpret_cast<uint4*>(orow)[c] = w;
         }
+        if (p.og != nullptr) {
+          const uint4* grow = reinterpret_cast<const uint4*>(p.gate + row * p.d + h * ATT_D);
+          uint4* ogrow = reinterpret_cast<uint4*>(p.og + row * p.d + h * ATT_D);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4 g = grow[c];
+            uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+            uint32_t ow[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float2 gf = unpack_bf16x2(gw[e]);
+              // gate the bf16-rounded o, as the reference multiplies the stored attention output
+              ow[e] = pack_bf16x2(bf16_round(ov[8 * c + 2 * e]) * gf.x, bf16_round(ov[8 * c + 2 * e + 1]) * gf.y);
+            }
+            ogrow[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          }
+        }
+        // natural-log LSE of the scaled scores
+        p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
       }
-      // natural-log LSE of the scaled scores
-      p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
     }
+    tc_fence_before();
   }
 
   __syncthreads();
@@ -734,7 +768,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   }
 }
 
-constexpr uint32_t FWD_SMEM = TILE_BYTES + 4 * KV_TILE_BYTES + 2 * P_TILE_BYTES + 256 + 1024;
+constexpr uint32_t FWD_SMEM = TILE_BYTES + 2 * FWD_KV_STAGES * KV_TILE_BYTES + 2 * P_TILE_BYTES + 256 + 1024;
 constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 8 * BWD_STAT_FLOATS * 4 + 256 + 1024;
 
 }  // namespace rgpt
