@@ -7,13 +7,17 @@
 // forward projections are K-major/K-major, dX = dY*W uses an MN-major B, and
 // dW = dY^T*X uses MN-major A and B, so no operand is ever transposed in HBM.
 //
-// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+// CTA layout (64 + 32 * GEMM_EPI_WARPS threads, one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: 128-byte-swizzled tiles into a STAGES-deep smem ring
 //   warp 1      allocates TMEM, issues tcgen05.mma (one elected thread), commits
-//   warps 2..5  epilogue: each warp owns 32 accumulator rows (one TMEM lane quadrant);
-//               per column chunk it tcgen05.ld's the fp32 accumulator, applies the
-//               fused epilogue, stages the result in swizzled smem and writes it with
-//               a TMA bulk store (or a TMA bulk reduce-add for accumulating outputs)
+//   warps 2..   epilogue: warp w owns TMEM lane quadrant w % 4 (32 accumulator rows) and,
+//               with 8 epilogue warps, half of the tile's columns; per column chunk it
+//               tcgen05.ld's the fp32 accumulator, applies the fused epilogue, stages the
+//               result in swizzled smem and writes it with a TMA bulk store (or a TMA
+//               bulk reduce-add for accumulating outputs)
+// Large GEMMs run on CTA pairs (a cluster of two SMs): one cta_group::2 MMA computes a
+// 256 x 256 tile from 128 rows of A and 128 rows of B staged in each SM's shared memory,
+// which halves the B operand's shared-memory and L2 traffic per SM.
 // The accumulator is multi-buffered in TMEM (512 / BN buffers of BN columns) so the
 // epilogue of tile i overlaps the main loops of the tiles after it. Tiles are visited in groups of
 // GROUP_M row tiles so that consecutive CTAs share A and B panels in L2.
@@ -52,16 +56,17 @@ struct EpiParams {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
+constexpr int GEMM_EPI_WARPS = 4;  // 4: one per TMEM lane quadrant; 8: two per quadrant, splitting the columns
+constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GROUP_M = 8;
 constexpr uint32_t EPI_STAGE_BYTES = 4096;  // one warp's 32 rows x 128 bytes
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct GemmSmem {
-  static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;
-  static constexpr uint32_t B_BYTES = BN * GEMM_BK * 2;
+  static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;              // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;  // a CTA pair splits B's rows
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t EPI_BYTES = 4 * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
+  static constexpr uint32_t EPI_BYTES = GEMM_EPI_WARPS * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
   static constexpr uint32_t BAR_BYTES = 256;
   static constexpr uint32_t TOTAL = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
 };
@@ -197,15 +202,19 @@ __device__ __forceinline__ void act_bwd32_rt(int act, float* v, const uint4* c) 
   }
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
+// PAIR: a cluster of two CTAs computes 256 x BN tiles with cta_group::2 MMAs issued by the
+// even CTA; each CTA loads its 128 rows of A and BN/2 rows of B, and writes its 128 output rows.
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
                         GemmShape sh, EpiParams ep) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, PAIR>;
   constexpr int NUM_ACC = 512 / BN;  // TMEM accumulator buffers (2 for 256-wide tiles, 4 for 128-wide)
   constexpr uint32_t TMEM_COLS = NUM_ACC * BN;
-  constexpr uint32_t IDESC = make_idesc_bf16(GEMM_BM, BN, A_MN, B_MN);
+  constexpr int TILE_M = PAIR ? 2 * GEMM_BM : GEMM_BM;
+  constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B this CTA loads
+  constexpr uint32_t IDESC = make_idesc_bf16(TILE_M, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -221,6 +230,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;  // 0 = the CTA that issues the pair's MMAs
+  const int first_unit = PAIR ? (int)cluster_id_x() : (int)blockIdx.x;
+  const int unit_step = PAIR ? (int)cluster_count_x() : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -229,7 +241,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);
+      mbar_init(&tempty_bar[a], PAIR ? 2 * GEMM_EPI_WARPS : GEMM_EPI_WARPS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -240,13 +252,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch_desc(&tmD);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // barriers of the pair's MMA-issuing CTA, as shared::cluster addresses
+  const uint32_t full_bar0 = PAIR ? mapa_shared(smem_u32(full_bar), 0) : smem_u32(full_bar);
+  const uint32_t tempty_bar0 = PAIR ? mapa_shared(smem_u32(tempty_bar), 0) : smem_u32(tempty_bar);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -254,37 +275,50 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < sh.num_units && ok; u += gridDim.x) {
+      for (int u = first_unit; u < sh.num_units && ok; u += unit_step) {
         int b, mt, nt, ks;
         decode_unit(u, sh, b, mt, nt, ks);
         const int kb0 = ks * sh.kb_per_split;
         const int kb1 = min(kb0 + sh.kb_per_split, sh.num_kb);
+        // MN-major operands arrive as 64-wide sub-boxes; a sub-box lying wholly past M (or N)
+        // is not loaded: its smem only feeds output rows/columns the epilogue never stores.
+        auto a_subs = [&](int rk) {
+          return A_MN ? max(0, min(GEMM_BM / 64, (sh.M - mt * TILE_M - rk * GEMM_BM + 63) / 64)) : 1;
+        };
+        auto b_subs = [&](int rk) {
+          return B_MN ? max(0, min(B_ROWS / 64, (sh.N - nt * BN - rk * B_ROWS + 63) / 64)) : 1;
+        };
+        auto stage_bytes = [&](int rk) -> uint32_t {
+          return (A_MN ? a_subs(rk) * (64 * GEMM_BK * 2) : L::A_BYTES) +
+                 (B_MN ? b_subs(rk) * (64 * GEMM_BK * 2) : L::B_BYTES);
+        };
+        const int a_sub = a_subs(rank), b_sub = b_subs(rank);
+        const int a_row = mt * TILE_M + rank * GEMM_BM, b_row = nt * BN + rank * B_ROWS;
+        const uint32_t expect = PAIR ? stage_bytes(0) + stage_bytes(1) : stage_bytes(0);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          // MN-major operands arrive as 64-wide sub-boxes; a sub-box lying wholly past M (or N)
-          // is not loaded: its smem only feeds output rows/columns the epilogue never stores.
-          const int a_sub = A_MN ? min(GEMM_BM / 64, (sh.M - mt * GEMM_BM + 63) / 64) : 1;
-          const int b_sub = B_MN ? min(BN / 64, (sh.N - nt * BN + 63) / 64) : 1;
-          const uint32_t bytes = (A_MN ? a_sub * (64 * GEMM_BK * 2) : L::A_BYTES) +
-                                 (B_MN ? b_sub * (64 * GEMM_BK * 2) : L::B_BYTES);
-          mbar_arrive_expect_tx(&full_bar[stage], bytes);
+          // the pair's barrier lives in CTA 0, which posts the byte count of both CTAs' loads
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], expect);
           const int k0 = kb * GEMM_BK;
           uint8_t* a_dst = sA + stage * L::A_BYTES;
           uint8_t* b_dst = sB + stage * L::B_BYTES;
+          const uint32_t fb = full_bar0 + stage * 8;
+          auto load = [&](uint8_t* dst, const CUtensorMap* map, int c0, int c1) {
+            if constexpr (PAIR) tma_load_3d_pair(dst, map, fb, c0, c1, b);
+            else tma_load_3d(dst, map, &full_bar[stage], c0, c1, b);
+          };
           if (A_MN) {
-            for (int i = 0; i < a_sub; ++i)
-              tma_load_3d(a_dst + i * (64 * GEMM_BK * 2), &tmA, &full_bar[stage], mt * GEMM_BM + i * 64, k0, b);
+            for (int i = 0; i < a_sub; ++i) load(a_dst + i * (64 * GEMM_BK * 2), &tmA, a_row + i * 64, k0);
           } else {
-            tma_load_3d(a_dst, &tmA, &full_bar[stage], k0, mt * GEMM_BM, b);
+            load(a_dst, &tmA, k0, a_row);
           }
           if (B_MN) {
-            for (int i = 0; i < b_sub; ++i)
-              tma_load_3d(b_dst + i * (64 * GEMM_BK * 2), &tmB, &full_bar[stage], nt * BN + i * 64, k0, b);
+            for (int i = 0; i < b_sub; ++i) load(b_dst + i * (64 * GEMM_BK * 2), &tmB, b_row + i * 64, k0);
           } else {
-            tma_load_3d(b_dst, &tmB, &full_bar[stage], k0, nt * BN, b);
+            load(b_dst, &tmB, k0, b_row);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -292,21 +326,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       }
-      if (!ok) {
-        // Drain: wait (bounded) for every load already issued into the ring.
+      if (!ok && rank == 0) {
+        // Drain: wait (bounded) for every load already issued into the ring (the pair's loads
+        // all complete on CTA 0's barriers; the final cluster barrier keeps CTA 1 alive meanwhile).
         for (int s = 0; s < STAGES; ++s) mbar_wait(&full_bar[s], phase, nullptr);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < sh.num_units && ok; u += gridDim.x) {
+      // completion signals go to both CTAs of a pair (same smem offsets)
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(bar), 0));
+          umma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (int u = first_unit; u < sh.num_units && ok; u += unit_step) {
         int b, mt, nt, ks;
         decode_unit(u, sh, b, mt, nt, ks);
         const int kb0 = ks * sh.kb_per_split;
@@ -328,16 +372,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                         : make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = B_MN ? make_sw128_desc(b_addr + kk * 2048, 64 * GEMM_BK * 2, 1024)
                                         : make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else umma_bf16(d_tmem, adesc, bdesc, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&empty_bar[stage]);
+          commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
+        commit(&tfull_bar[acc]);
         if (++acc == NUM_ACC) {
           acc = 0;
           acc_phase ^= 1u;
@@ -347,7 +392,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int quarter = warp & 3;  // TMEM lane quadrant this warp may access
+    const int quarter = warp & 3;          // TMEM lane quadrant this warp may access
+    const int col_half = (warp - 2) >> 2;  // which part of the tile's columns this warp writes
+    constexpr int COLS = BN * 4 / GEMM_EPI_WARPS;
     uint8_t* buf0 = sEpi + (warp - 2) * 2 * EPI_STAGE_BYTES;
     uint8_t* buf1 = buf0 + EPI_STAGE_BYTES;
     int which = 0;
@@ -356,16 +403,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     constexpr bool reads_c = (EPI == RGPT_EPI_ACT_BWD || EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_RESID_F32);
     const bool dual = (EPI == RGPT_EPI_ACT_FWD) || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
     const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
+    const bool scaled = alpha != 1.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int u = blockIdx.x; u < sh.num_units; u += gridDim.x) {
+    for (int u = first_unit; u < sh.num_units; u += unit_step) {
       int b, mt, nt, ks;
       decode_unit(u, sh, b, mt, nt, ks);
-      const int row0 = mt * GEMM_BM + quarter * 32;  // first output row of this warp
+      const int row0 = mt * TILE_M + rank * GEMM_BM + quarter * 32;  // first output row of this warp
       const int gm = row0 + lane;
       const bool rows_live = row0 < sh.M;
       uint4 pf[8];  // epilogue input prefetch (first chunk issued while the MMAs still run)
-      if constexpr (reads_c) load_c_chunk<bf16_out ? 2 : 4>(ep, sh, b, row0, nt * BN, lane, pf);
+      if constexpr (reads_c) load_c_chunk<bf16_out ? 2 : 4>(ep, sh, b, row0, nt * BN + col_half * COLS, lane, pf);
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -388,17 +436,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             if constexpr (reads_c) bounce_c_chunk(s0, lane, pf, cc);
           }
           if constexpr (reads_c) {
-            if (c0 + 64 < BN) load_c_chunk<2>(ep, sh, b, row0, gn0 + 64, lane, pf);  // next chunk in flight
+            if (c0 + 64 < (col_half + 1) * COLS) load_c_chunk<2>(ep, sh, b, row0, gn0 + 64, lane, pf);  // next chunk
           }
+          uint32_t rr[2][32];
+          tmem_ld32(t_row + c0, rr[0]);  // both 32-column halves in flight, one wait
+          tmem_ld32(t_row + c0 + 32, rr[1]);
+          tmem_wait_ld();
 #pragma unroll
           for (int hf = 0; hf < 2; ++hf) {  // two 32-column halves of the 64-column box
-            uint32_t r[32];
-            tmem_ld32(t_row + c0 + hf * 32, r);
-            tmem_wait_ld();
             if (!live) continue;
             float v[32];
+            if (scaled) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rr[hf][j]) * alpha;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rr[hf][j]);
+            }
             if constexpr (EPI == RGPT_EPI_ACT_BWD) {
               act_bwd32_rt(ep.act, v, &cc[hf * 4]);
             } else if constexpr (EPI == RGPT_EPI_POLY_BF16) {
@@ -418,7 +472,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               for (int j = 0; j < 32; ++j) {
                 const int col = gn0 + hf * 32 + j;
                 const float bias = (col < sh.N) ? __ldg(ep.colscale + col) : 0.f;
-                v[j] = 1.0f / (1.0f + expf(-(v[j] + bias)));
+                v[j] = rcp_approx(1.0f + ex2_approx(-(v[j] + bias) * 1.4426950408889634f));
               }
             }
 #pragma unroll
@@ -446,7 +500,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!dual) which ^= 1;
         };
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) chunk_bf16(c0);
+        for (int c0 = col_half * COLS; c0 < (col_half + 1) * COLS; c0 += 64) chunk_bf16(c0);
       } else {
         constexpr bool resid = EPI == RGPT_EPI_RESID_F32;
         auto chunk_f32 = [&](int c0) {
@@ -457,13 +511,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tmem_wait_ld();
           if (!live) {
             if constexpr (resid) {
-              if (c0 + 32 < BN) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);
+              if (c0 + 32 < (col_half + 1) * COLS) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);
             }
             return;
           }
           float v[32];
+          if (scaled) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          }
           uint8_t* s0 = which ? buf1 : buf0;
           uint8_t* s1 = which ? buf0 : buf1;
           if (lane == 0) {
@@ -474,7 +533,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if constexpr (resid) {
             uint4 cc[8];
             bounce_c_chunk(s0, lane, pf, cc);
-            if (c0 + 32 < BN) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);  // next chunk in flight
+            if (c0 + 32 < (col_half + 1) * COLS) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);  // next chunk
             if (ep.has_d2) stage_f32x32(s1, lane, v);  // raw branch output
             const float* cs = reinterpret_cast<const float*>(cc);
 #pragma unroll
@@ -498,11 +557,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!dual) which ^= 1;
         };
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) chunk_f32(c0);
+        for (int c0 = col_half * COLS; c0 < (col_half + 1) * COLS; c0 += 32) chunk_f32(c0);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(tempty_bar0 + acc * 8);
+        else mbar_arrive(&tempty_bar[acc]);
+      }
       if (++acc == NUM_ACC) {
         acc = 0;
         acc_phase ^= 1u;
@@ -513,9 +575,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still works
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -561,51 +625,98 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_
   return make_tmap_3d(map, ptr, 2, inner, outer, batch, ld_elems, bstride_elems, box_inner, box_outer);
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN, int EPI>
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
-                       const GemmShape& sh, const EpiParams& ep, int grid, cudaStream_t stream, int dev) {
-  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI>;
-  constexpr uint32_t smem = GemmSmem<BN, STAGES>::TOTAL;
+                       const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
+  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
+  constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR>::TOTAL;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr_set[64] = {false};
+  static int max_clusters[64] = {0};
   if (!attr_set[dev]) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return rgpt_check_launch("gemm set smem attribute");
+    if (PAIR) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(2 * rgpt_num_sms(dev), 1, 1);
+      q.blockDim = dim3(GEMM_THREADS, 1, 1);
+      q.dynamicSmemBytes = smem;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1)
+        return rgpt_set_error(RGPT_ERR_INTERNAL, "no CTA pair fits on this GPU (%s)",
+                              cudaGetErrorString(cudaGetLastError()));
+      max_clusters[dev] = n;
+    }
     attr_set[dev] = true;
   }
-  kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, sh, ep);
+  if constexpr (PAIR) {
+    const int clusters = sh.num_units < max_clusters[dev] ? sh.num_units : max_clusters[dev];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, ta, tb, td, td2, sh, ep);
+  } else {
+    const int nsm = rgpt_num_sms(dev);
+    const int grid = sh.num_units < nsm ? sh.num_units : nsm;
+    kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, sh, ep);
+  }
   return rgpt_check_launch("gemm_bf16_tc_kernel");
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN>
+template <int BN, int STAGES, int A_MN, int B_MN, bool PAIR>
 static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                        const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep, int grid, cudaStream_t s,
-                        int dev) {
+                        const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep, cudaStream_t s, int dev) {
+#define RGPT_GEMM_EPI_CASE(E) \
+  case E: return launch_gemm<BN, STAGES, A_MN, B_MN, E, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   switch (epi) {
-    case RGPT_EPI_STORE_BF16: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_STORE_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_STORE_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_STORE_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_ACCUM_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACCUM_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_ACT_FWD: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_ACT_BWD: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_RESID_F32: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_RESID_F32>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    case RGPT_EPI_POLY_BF16: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_POLY_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
-    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16>(ta, tb, td, td2, sh, ep, grid, s, dev);
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_BF16)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_F32)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_ACCUM_F32)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_ACT_FWD)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_ACT_BWD)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
+    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   }
+#undef RGPT_GEMM_EPI_CASE
 }
 
-static int dispatch_gemm(int BN, int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+// Tile configurations: 128 x 128 (6 stages), 128 x 256 (4 stages), and the CTA pair's
+// 256 x 256 (6 stages of 128 x 64 A + 128 x 64 B per CTA).
+static int dispatch_gemm(int BN, bool pair, int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
                          const CUtensorMap& td, const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep,
-                         int grid, cudaStream_t s, int dev) {
-  const int key = (BN == 256 ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
+                         cudaStream_t s, int dev) {
+  const int key = (pair ? 8 : 0) | (BN == 256 ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
   switch (key) {
-    case 0: return dispatch_epi<128, 6, 0, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 1: return dispatch_epi<128, 6, 0, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 2: return dispatch_epi<128, 6, 1, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 3: return dispatch_epi<128, 6, 1, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 4: return dispatch_epi<256, 4, 0, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 5: return dispatch_epi<256, 4, 0, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    case 6: return dispatch_epi<256, 4, 1, 0>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
-    default: return dispatch_epi<256, 4, 1, 1>(epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+    case 0: return dispatch_epi<128, 6, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 1: return dispatch_epi<128, 6, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 2: return dispatch_epi<128, 6, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 3: return dispatch_epi<128, 6, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 4: return dispatch_epi<256, 4, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 5: return dispatch_epi<256, 4, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 6: return dispatch_epi<256, 4, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 7: return dispatch_epi<256, 4, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 12: return dispatch_epi<256, 6, 0, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 13: return dispatch_epi<256, 6, 0, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 14: return dispatch_epi<256, 6, 1, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 15: return dispatch_epi<256, 6, 1, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    default: return rgpt_set_error(RGPT_ERR_INTERNAL, "no GEMM configuration for key %d", key);
   }
 }
 
@@ -650,19 +761,31 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.N = N;
   sh.K = K;
   sh.batch = batch;
-  sh.m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
   // 256-wide tiles unless that leaves most SMs idle (small N or few row tiles)
+  const int m128 = (M + GEMM_BM - 1) / GEMM_BM;
   int BN = (N > 128) ? 256 : 128;
-  if (BN == 256 && epi != RGPT_EPI_ACCUM_F32 && batch * sh.m_tiles * ((N + 255) / 256) < nsm &&
-      batch * sh.m_tiles * ((N + 127) / 128) <= 2 * nsm)
+  if (BN == 256 && epi != RGPT_EPI_ACCUM_F32 && batch * m128 * ((N + 255) / 256) < nsm &&
+      batch * m128 * ((N + 127) / 128) <= 2 * nsm)
     BN = 128;  // accumulating GEMMs keep the wide tile (fewer operand re-reads) and split K instead
-  sh.n_tiles = (N + BN - 1) / BN;
   sh.num_kb = (K + GEMM_BK - 1) / GEMM_BK;
+  // CTA pairs (256 x 256 tiles, half the B traffic per SM) pay off once the main loop is long
+  // (K >= 1024) and there is a wave of pair tiles, or for plain stores with very many tiles
+  // (a vocabulary-sized output); long-K accumulating GEMMs split K to fill the GPU anyway.
+  // Short-K GEMMs with few tiles stay on single-CTA tiles, whose shorter signalling chain
+  // finishes each tile sooner.
+  const long long pair_tiles = (long long)batch * ((M + 255) / 256) * ((N + 255) / 256);
+  const bool plain_store = epi == RGPT_EPI_STORE_BF16 || epi == RGPT_EPI_STORE_F32;
+  const bool pair = BN == 256 && M > GEMM_BM &&
+                    ((pair_tiles >= nsm / 2 && (sh.num_kb >= 16 || (plain_store && pair_tiles >= 8LL * nsm))) ||
+                     (epi == RGPT_EPI_ACCUM_F32 && sh.num_kb >= 32));
+  const int units_per_wave = pair ? nsm / 2 : nsm;
+  sh.m_tiles = pair ? (M + 255) / 256 : m128;
+  sh.n_tiles = (N + BN - 1) / BN;
   const int tiles = batch * sh.m_tiles * sh.n_tiles;
   if (splitk <= 0) {
     splitk = 1;
-    if (epi == RGPT_EPI_ACCUM_F32 && tiles < nsm) {
-      splitk = (nsm + tiles - 1) / tiles;
+    if (epi == RGPT_EPI_ACCUM_F32 && tiles < units_per_wave) {
+      splitk = (units_per_wave + tiles - 1) / tiles;
       int max_split = sh.num_kb / 4 > 0 ? sh.num_kb / 4 : 1;  // keep >= 4 k-blocks per split
       if (splitk > max_split) splitk = max_split;
     }
@@ -684,7 +807,7 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   if (b_mn_major)
     st = make_tmap_3d(&tb, B, 2, N, K, batch, ldb, b_bstride, 64, GEMM_BK);
   else
-    st = make_tmap_3d(&tb, B, 2, K, N, batch, ldb, b_bstride, GEMM_BK, BN);
+    st = make_tmap_3d(&tb, B, 2, K, N, batch, ldb, b_bstride, GEMM_BK, pair ? BN / 2 : BN);
   if (st) return st;
   // Output maps: one 32-row x 128-byte box per epilogue warp and chunk.
   const int ob = out_f32 ? 4 : 2;
@@ -709,7 +832,6 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   ep.alpha_dev = alpha_dev;
   ep.has_d2 = has_d2 ? 1 : 0;
 
-  const int grid = sh.num_units < nsm ? sh.num_units : nsm;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return dispatch_gemm(BN, a_mn_major, b_mn_major, epi, ta, tb, td, td2, sh, ep, grid, s, dev);
+  return dispatch_gemm(BN, pair, a_mn_major, b_mn_major, epi, ta, tb, td, td2, sh, ep, s, dev);
 }

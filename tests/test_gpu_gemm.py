@@ -166,3 +166,49 @@ def test_gemm_rejects_misaligned_leading_dim(cuda):
     w = torch.randn(128, 99, device=cuda).bfloat16()
     with pytest.raises(RuntimeError, match="16 bytes"):
         nv.gemm(a, w, out)
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_cta_pair_ragged(cuda, a_mn, b_mn):
+    # Large enough for the CTA-pair (256 x 256) tiles; M, N and K are not tile multiples, and
+    # the last row tile leaves the second CTA of its pair without any valid row.
+    M, N, K = 4160, 2104, 1096
+    g = torch.Generator(device=cuda).manual_seed(11)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    b = torch.randn(N, K, device=cuda, generator=g).bfloat16()
+    A = a.t().contiguous().t() if a_mn else a
+    B = b.t().contiguous().t() if b_mn else b
+    ref = a.float() @ b.float().t()
+    out = torch.empty(M, N + 8, device=cuda, dtype=torch.bfloat16)[:, :N]  # padded leading dim
+    nv.gemm(A, B, out)
+    assert rel_err(out, ref) < 1e-2
+    out32 = torch.empty(M, N, device=cuda, dtype=torch.float32)
+    nv.gemm(A, B, out32, epi=nv.EPI_STORE_F32, alpha=0.25)
+    assert rel_err(out32, 0.25 * ref) < 1e-4
+    pre = torch.empty(M, N + 8, device=cuda, dtype=torch.bfloat16)[:, :N]
+    post = torch.empty(M, N + 8, device=cuda, dtype=torch.bfloat16)[:, :N]
+    nv.gemm(A, B, pre, epi=nv.EPI_ACT_FWD, act=nv.act_id("squared_relu"), out2=post)
+    assert rel_err(post, torch.relu(ref) ** 2) < 2e-2
+    x = torch.randn(M, N, device=cuda, generator=g)
+    res = torch.empty_like(x)
+    nv.gemm(A, B, res, epi=nv.EPI_RESID_F32, c=x)
+    assert rel_err(res, x + ref) < 1e-5
+
+
+def test_gemm_cta_pair_batched_poly_and_accum(cuda):
+    # Newton-Schulz-sized batched product on CTA pairs, and a long-K weight-gradient GEMM
+    nb, R, C = 16, 1024, 2048
+    g = torch.Generator(device=cuda).manual_seed(12)
+    X = (torch.randn(nb, R, C, device=cuda, generator=g) * 0.05).bfloat16()
+    S = torch.randn(nb, R, R, device=cuda, generator=g)
+    Bm = ((S + S.transpose(1, 2)) * 0.05).bfloat16()
+    out = torch.empty_like(X)
+    nv.gemm(Bm, X.transpose(1, 2), out, epi=nv.EPI_POLY_BF16, alpha=1.0, beta=-4.775, c=X)
+    assert rel_err(out, -4.775 * X.float() + Bm.float() @ X.float()) < 1e-2
+    T, Nout, Kin = 16384, 1536, 512
+    dy = torch.randn(T, Nout, device=cuda, generator=g).bfloat16()
+    xin = torch.randn(T, Kin, device=cuda, generator=g).bfloat16()
+    dw = torch.randn(Nout, Kin, device=cuda, generator=g)
+    ref = dw + dy.float().t() @ xin.float()
+    nv.gemm(dy.t(), xin.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
+    assert rel_err(dw, ref) < 1e-4
