@@ -783,11 +783,21 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.n_tiles = (N + BN - 1) / BN;
   const int tiles = batch * sh.m_tiles * sh.n_tiles;
   if (splitk <= 0) {
+    // Split K (accumulating epilogue only) to minimise waves x (k-blocks per unit + the
+    // tile's reduce-add epilogue, worth about 8 k-blocks), keeping >= 4 k-blocks per split;
+    // fewer splits win ties (fewer reduce-adds).
     splitk = 1;
-    if (epi == RGPT_EPI_ACCUM_F32 && tiles < units_per_wave) {
-      splitk = (units_per_wave + tiles - 1) / tiles;
-      int max_split = sh.num_kb / 4 > 0 ? sh.num_kb / 4 : 1;  // keep >= 4 k-blocks per split
-      if (splitk > max_split) splitk = max_split;
+    if (epi == RGPT_EPI_ACCUM_F32) {
+      long long best = -1;
+      const int max_split = sh.num_kb / 4 > 0 ? (sh.num_kb / 4 < 64 ? sh.num_kb / 4 : 64) : 1;
+      for (int s = 1; s <= max_split; ++s) {
+        const long long waves = ((long long)tiles * s + units_per_wave - 1) / units_per_wave;
+        const long long cost = waves * ((sh.num_kb + s - 1) / s + 8);
+        if (best < 0 || cost < best) {
+          best = cost;
+          splitk = s;
+        }
+      }
     }
   }
   if (splitk > 1 && epi != RGPT_EPI_ACCUM_F32)
