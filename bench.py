@@ -53,6 +53,10 @@ WORKLOADS = {
                               d_model=1024, use_layer_scale=False), B=16, T=1024, accum=1),
 }
 OPT = dict(lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)  # conf/training/default.yaml
+# Measured DRAM traffic (read + write) per tcgen05 GEMM launch, averaged over the 168 GEMM
+# launches of one gpt-small step: ncu dram__bytes_read.sum + dram__bytes_write.sum
+# (profiles/gemm_gpt_small_step_dram.md). Workloads without a capture report null.
+GEMM_TRAFFIC = {"gpt-small": 83.47e6}
 
 
 def flops_per_token(cfg, T):
@@ -249,7 +253,9 @@ def run_ours(args, wl):
                      "peak_source": peaks["source"] + " (sustained bf16: kernels timed inside a long step)",
                      "launches_per_step": len(ev) // args.steps,
                      "gemm_share_of_step": round(gemm_ms / args.steps / ms, 3),
-                     "traffic": None},
+                     "traffic": GEMM_TRAFFIC.get(args.workload),
+                     "traffic_unit": "bytes per launch: DRAM read + write of all GEMM launches of one step / "
+                                     "launches, from one ncu capture (profiles/gemm_gpt_small_step_dram.md)"},
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
