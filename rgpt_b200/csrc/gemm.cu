@@ -61,14 +61,23 @@ constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GROUP_M = 8;
 constexpr uint32_t EPI_STAGE_BYTES = 4096;  // one warp's 32 rows x 128 bytes
 
-template <int BN, int STAGES, bool PAIR = false>
+constexpr int C_DEPTH = 3;  // epilogue input (C) chunks in flight per epilogue warp
+
+__host__ __device__ constexpr bool epi_reads_c(int epi) {
+  return epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32;
+}
+
+template <int BN, int STAGES, bool PAIR = false, bool CIN = false>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;              // this CTA's 128 rows of A
   static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;  // a CTA pair splits B's rows
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr uint32_t EPI_BYTES = GEMM_EPI_WARPS * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
-  static constexpr uint32_t BAR_BYTES = 256;
-  static constexpr uint32_t TOTAL = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+  // per-warp ring of TMA-loaded epilogue-input chunks (32 rows x 128 bytes each)
+  static constexpr uint32_t C_BYTES = CIN ? GEMM_EPI_WARPS * C_DEPTH * EPI_STAGE_BYTES : 0;
+  static constexpr uint32_t BAR_BYTES = 512;
+  static constexpr uint32_t TOTAL =
+      STAGES * STAGE_BYTES + EPI_BYTES + C_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
 };
 
 __device__ __forceinline__ void decode_unit(int u, const GemmShape& sh, int& b, int& mt, int& nt, int& ks) {
@@ -120,50 +129,6 @@ __device__ __forceinline__ void stage_bf16x64(uint8_t* buf, int lane, const floa
                    pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
 }
 
-// Epilogue input C: a warp's 32 rows x 128 bytes per chunk (64 bf16 or 32 fp32 columns).
-// The warp loads it coalesced (each instruction covers 4 full 128-byte rows), keeps it in
-// registers as the prefetch for the next chunk, and later bounces it through its swizzled
-// staging buffer to get one row per thread. Rows >= M and columns >= N read as zero.
-template <int EB>  // element bytes: 2 (bf16) or 4 (fp32)
-__device__ __forceinline__ void load_c_chunk(const EpiParams& ep, const GemmShape& sh, int b, int row0, int gn0,
-                                             int lane, uint4 (&pf)[8]) {
-  constexpr int PER = 16 / EB;  // elements per 16-byte piece
-  const int piece = lane & 7;
-  const int col = gn0 + piece * PER;
-  const char* base = reinterpret_cast<const char*>(ep.c) + ((long long)b * ep.c_bstride) * EB;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int row = row0 + 4 * i + (lane >> 3);
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (row < sh.M && col < sh.N) {
-      const char* p = base + ((long long)row * ep.ldc + col) * EB;
-      if (col + PER <= sh.N) {
-        v = *reinterpret_cast<const uint4*>(p);
-      } else {
-        uint32_t w[4] = {0, 0, 0, 0};
-        for (int e = 0; e < PER && col + e < sh.N; ++e) {
-          if (EB == 2)
-            reinterpret_cast<uint16_t*>(w)[e] = reinterpret_cast<const uint16_t*>(p)[e];
-          else
-            w[e] = reinterpret_cast<const uint32_t*>(p)[e];
-        }
-        v = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    }
-    pf[i] = v;
-  }
-}
-// pf (coalesced layout) -> staging buffer -> cc (row `lane`, 8 pieces). Caller guarantees the
-// buffer is free; leaves it free again (reads complete before the trailing __syncwarp).
-__device__ __forceinline__ void bounce_c_chunk(uint8_t* buf, int lane, const uint4 (&pf)[8], uint4 (&cc)[8]) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(stage_ptr(buf, 4 * i + (lane >> 3), lane & 7)) = pf[i];
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(buf, lane, j));
-  __syncwarp();
-}
-
 // Activation applied to 32 values: forward (ACT_FWD) or derivative times v (ACT_BWD, c = pre).
 template <int ACT>
 __device__ __forceinline__ void act_fwd32(float* v) {
@@ -208,8 +173,9 @@ template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
-                        GemmShape sh, EpiParams ep) {
-  using L = GemmSmem<BN, STAGES, PAIR>;
+                        const __grid_constant__ CUtensorMap tmC, GemmShape sh, EpiParams ep) {
+  constexpr bool reads_c = epi_reads_c(EPI);
+  using L = GemmSmem<BN, STAGES, PAIR, reads_c>;
   constexpr int NUM_ACC = 512 / BN;  // TMEM accumulator buffers (2 for 256-wide tiles, 4 for 128-wide)
   constexpr uint32_t TMEM_COLS = NUM_ACC * BN;
   constexpr int TILE_M = PAIR ? 2 * GEMM_BM : GEMM_BM;
@@ -221,11 +187,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::A_BYTES;
   uint8_t* sEpi = sB + STAGES * L::B_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + L::EPI_BYTES);
+  uint8_t* sC = sEpi + L::EPI_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sC + L::C_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + NUM_ACC;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + NUM_ACC);
+  uint64_t* cfull_bar = tempty_bar + NUM_ACC;  // [GEMM_EPI_WARPS * C_DEPTH]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cfull_bar + GEMM_EPI_WARPS * C_DEPTH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -239,6 +207,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
+    for (int i = 0; i < GEMM_EPI_WARPS * C_DEPTH; ++i) mbar_init(&cfull_bar[i], 1);
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull_bar[a], 1);
       mbar_init(&tempty_bar[a], PAIR ? 2 * GEMM_EPI_WARPS : GEMM_EPI_WARPS);
@@ -250,6 +219,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmD);
+    if constexpr (reads_c) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -400,20 +370,71 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     int which = 0;
     constexpr bool bf16_out = (EPI == RGPT_EPI_STORE_BF16 || EPI == RGPT_EPI_ACT_FWD || EPI == RGPT_EPI_ACT_BWD ||
                                EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_BIAS_SIGMOID_BF16);
-    constexpr bool reads_c = (EPI == RGPT_EPI_ACT_BWD || EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_RESID_F32);
     const bool dual = (EPI == RGPT_EPI_ACT_FWD) || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
     const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
     const bool scaled = alpha != 1.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
+    // Epilogue input C arrives by TMA: 32-row x 128-byte chunks into a per-warp C_DEPTH ring,
+    // issued C_DEPTH chunks ahead (the first ones while the tile's MMAs still run). A warp's
+    // live chunks (inside M and N) are a prefix of its columns; only those are loaded.
+    constexpr int CW = bf16_out ? 64 : 32;  // columns per chunk
+    uint8_t* cring = sC + (warp - 2) * C_DEPTH * EPI_STAGE_BYTES;
+    uint64_t* cbar = cfull_bar + (warp - 2) * C_DEPTH;
+    uint32_t c_issued = 0, c_used = 0;
+    bool c_ok = true;
+    int c_next = 0, c_live = 0, c_b = 0, c_row0 = 0, c_col0 = 0;  // this tile's C chunk queue
+    auto c_issue = [&]() {  // lane 0: load the tile's next live chunk into the ring
+      if (c_next < c_live) {
+        uint64_t* bar = &cbar[c_issued % C_DEPTH];
+        mbar_arrive_expect_tx(bar, EPI_STAGE_BYTES);
+        tma_load_3d(cring + (c_issued % C_DEPTH) * EPI_STAGE_BYTES, &tmC, bar, c_col0 + c_next * CW, c_row0, c_b);
+        ++c_issued;
+        ++c_next;
+      }
+    };
+    auto c_get = [&](uint4 (&cc)[8]) {  // this row's 128 bytes of the oldest chunk, then refill
+      int okc = 1;
+      if (lane == 0) okc = mbar_wait(&cbar[c_used % C_DEPTH], (c_used / C_DEPTH) & 1u, abort_flag) ? 1 : 0;
+      okc = __shfl_sync(0xffffffffu, okc, 0);
+      if (!okc) {
+        c_ok = false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cc[j] = make_uint4(0, 0, 0, 0);
+        return;
+      }
+      const uint8_t* buf = cring + (c_used % C_DEPTH) * EPI_STAGE_BYTES;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(const_cast<uint8_t*>(buf), lane, j));
+      ++c_used;
+      __syncwarp();
+      if (lane == 0) {
+        fence_proxy_async_smem();  // our reads of the buffer come before the next TMA write into it
+        c_issue();
+      } else if (c_next < c_live) {
+        ++c_issued;  // keep every lane's queue counters in step with lane 0
+        ++c_next;
+      }
+    };
     for (int u = first_unit; u < sh.num_units; u += unit_step) {
       int b, mt, nt, ks;
       decode_unit(u, sh, b, mt, nt, ks);
       const int row0 = mt * TILE_M + rank * GEMM_BM + quarter * 32;  // first output row of this warp
-      const int gm = row0 + lane;
       const bool rows_live = row0 < sh.M;
-      uint4 pf[8];  // epilogue input prefetch (first chunk issued while the MMAs still run)
-      if constexpr (reads_c) load_c_chunk<bf16_out ? 2 : 4>(ep, sh, b, row0, nt * BN + col_half * COLS, lane, pf);
+      if constexpr (reads_c) {
+        c_b = b;
+        c_row0 = row0;
+        c_col0 = nt * BN + col_half * COLS;
+        c_next = 0;
+        c_live = rows_live ? max(0, min(COLS / CW, (sh.N - c_col0 + CW - 1) / CW)) : 0;
+        const int first = min(C_DEPTH, c_live);
+        if (lane == 0) {
+          for (int j = 0; j < first; ++j) c_issue();
+        } else {
+          c_issued += first;
+          c_next = first;
+        }
+      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -433,10 +454,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               else bulk_wait_read_1();  // the store issued from this buffer two chunks ago has read it
             }
             __syncwarp();
-            if constexpr (reads_c) bounce_c_chunk(s0, lane, pf, cc);
-          }
-          if constexpr (reads_c) {
-            if (c0 + 64 < (col_half + 1) * COLS) load_c_chunk<2>(ep, sh, b, row0, gn0 + 64, lane, pf);  // next chunk
+            if constexpr (reads_c) c_get(cc);
           }
           uint32_t rr[2][32];
           tmem_ld32(t_row + c0, rr[0]);  // both 32-column halves in flight, one wait
@@ -509,12 +527,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           uint32_t r[32];
           tmem_ld32(t_row + c0, r);
           tmem_wait_ld();
-          if (!live) {
-            if constexpr (resid) {
-              if (c0 + 32 < (col_half + 1) * COLS) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);
-            }
-            return;
-          }
+          if (!live) return;
           float v[32];
           if (scaled) {
 #pragma unroll
@@ -532,8 +545,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           __syncwarp();
           if constexpr (resid) {
             uint4 cc[8];
-            bounce_c_chunk(s0, lane, pf, cc);
-            if (c0 + 32 < (col_half + 1) * COLS) load_c_chunk<4>(ep, sh, b, row0, gn0 + 32, lane, pf);  // next chunk
+            c_get(cc);
             if (ep.has_d2) stage_f32x32(s1, lane, v);  // raw branch output
             const float* cs = reinterpret_cast<const float*>(cc);
 #pragma unroll
@@ -569,6 +581,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
+      if (!c_ok) break;
+    }
+    if constexpr (reads_c) {  // C loads still in flight (only after a timed-out wait) land before exit
+      if (lane == 0)
+        for (; c_used < c_issued; ++c_used) mbar_wait(&cbar[c_used % C_DEPTH], (c_used / C_DEPTH) & 1u, nullptr);
+      __syncwarp();
     }
     if (lane == 0) bulk_wait_all();  // every bulk store has landed before the CTA retires
     __syncwarp();
@@ -625,11 +643,14 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_
   return make_tmap_3d(map, ptr, 2, inner, outer, batch, ld_elems, bstride_elems, box_inner, box_outer);
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR>
+template <int BN, int STAGES_IN, int A_MN, int B_MN, int EPI, bool PAIR>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
-                       const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
+                       const CUtensorMap& tc, const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
+  // epilogues that read C give up operand stages for their per-warp C ring
+  constexpr bool CIN = epi_reads_c(EPI);
+  constexpr int STAGES = !CIN ? STAGES_IN : (BN == 256 && !PAIR ? 3 : 4);
   auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
-  constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR>::TOTAL;
+  constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR, CIN>::TOTAL;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr_set[64] = {false};
   static int max_clusters[64] = {0};
@@ -670,20 +691,21 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kern, ta, tb, td, td2, sh, ep);
+    cudaLaunchKernelEx(&cfg, kern, ta, tb, td, td2, tc, sh, ep);
   } else {
     const int nsm = rgpt_num_sms(dev);
     const int grid = sh.num_units < nsm ? sh.num_units : nsm;
-    kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, sh, ep);
+    kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, tc, sh, ep);
   }
   return rgpt_check_launch("gemm_bf16_tc_kernel");
 }
 
 template <int BN, int STAGES, int A_MN, int B_MN, bool PAIR>
 static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                        const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep, cudaStream_t s, int dev) {
+                        const CUtensorMap& td2, const CUtensorMap& tc, const GemmShape& sh, const EpiParams& ep,
+                        cudaStream_t s, int dev) {
 #define RGPT_GEMM_EPI_CASE(E) \
-  case E: return launch_gemm<BN, STAGES, A_MN, B_MN, E, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
+  case E: return launch_gemm<BN, STAGES, A_MN, B_MN, E, PAIR>(ta, tb, td, td2, tc, sh, ep, s, dev);
   switch (epi) {
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_BF16)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_F32)
@@ -692,7 +714,7 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
     RGPT_GEMM_EPI_CASE(RGPT_EPI_ACT_BWD)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
-    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
+    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, tc, sh, ep, s, dev);
   }
 #undef RGPT_GEMM_EPI_CASE
 }
@@ -700,22 +722,22 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
 // Tile configurations: 128 x 128 (6 stages), 128 x 256 (4 stages), and the CTA pair's
 // 256 x 256 (6 stages of 128 x 64 A + 128 x 64 B per CTA).
 static int dispatch_gemm(int BN, bool pair, int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                         const CUtensorMap& td, const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep,
-                         cudaStream_t s, int dev) {
+                         const CUtensorMap& td, const CUtensorMap& td2, const CUtensorMap& tc, const GemmShape& sh,
+                         const EpiParams& ep, cudaStream_t s, int dev) {
   const int key = (pair ? 8 : 0) | (BN == 256 ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
   switch (key) {
-    case 0: return dispatch_epi<128, 6, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 1: return dispatch_epi<128, 6, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 2: return dispatch_epi<128, 6, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 3: return dispatch_epi<128, 6, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 4: return dispatch_epi<256, 4, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 5: return dispatch_epi<256, 4, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 6: return dispatch_epi<256, 4, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 7: return dispatch_epi<256, 4, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 12: return dispatch_epi<256, 6, 0, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 13: return dispatch_epi<256, 6, 0, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 14: return dispatch_epi<256, 6, 1, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
-    case 15: return dispatch_epi<256, 6, 1, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 0: return dispatch_epi<128, 6, 0, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 1: return dispatch_epi<128, 6, 0, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 2: return dispatch_epi<128, 6, 1, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 3: return dispatch_epi<128, 6, 1, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 4: return dispatch_epi<256, 4, 0, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 5: return dispatch_epi<256, 4, 0, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 6: return dispatch_epi<256, 4, 1, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 7: return dispatch_epi<256, 4, 1, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 12: return dispatch_epi<256, 6, 0, 0, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 13: return dispatch_epi<256, 6, 0, 1, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 14: return dispatch_epi<256, 6, 1, 0, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 15: return dispatch_epi<256, 6, 1, 1, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
     default: return rgpt_set_error(RGPT_ERR_INTERNAL, "no GEMM configuration for key %d", key);
   }
 }
@@ -830,6 +852,14 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
     td2 = td;
   }
 
+  // epilogue input C: the same 32-row x 128-byte boxes as the output (bf16 C for ACT_BWD / POLY,
+  // fp32 for RESID)
+  CUtensorMap tc = td;
+  if (epi_reads_c(epi)) {
+    const int cb = (epi == RGPT_EPI_RESID_F32) ? 4 : 2;
+    if ((st = make_tmap_3d(&tc, C, cb, N, M, batch, ldc, c_bstride, cb == 4 ? 32 : 64, 32))) return st;
+  }
+
   EpiParams ep;
   ep.kind = epi;
   ep.act = act;
@@ -843,5 +873,5 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   ep.has_d2 = has_d2 ? 1 : 0;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return dispatch_gemm(BN, pair, a_mn_major, b_mn_major, epi, ta, tb, td, td2, sh, ep, s, dev);
+  return dispatch_gemm(BN, pair, a_mn_major, b_mn_major, epi, ta, tb, td, td2, tc, sh, ep, s, dev);
 }
