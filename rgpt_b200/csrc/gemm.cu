@@ -148,28 +148,7 @@ __device__ __forceinline__ void act_bwd32(float* v, const uint4* c) {
     }
   }
 }
-__device__ __forceinline__ void act_fwd32_rt(int act, float* v) {
-  switch (act) {
-    case ACT_SQRELU: act_fwd32<ACT_SQRELU>(v); break;
-    case ACT_GELU: act_fwd32<ACT_GELU>(v); break;
-    case ACT_SILU: act_fwd32<ACT_SILU>(v); break;
-    case ACT_MISH: act_fwd32<ACT_MISH>(v); break;
-    default: break;
-  }
-}
-__device__ __forceinline__ void act_bwd32_rt(int act, float* v, const uint4* c) {
-  switch (act) {
-    case ACT_SQRELU: act_bwd32<ACT_SQRELU>(v, c); break;
-    case ACT_GELU: act_bwd32<ACT_GELU>(v, c); break;
-    case ACT_SILU: act_bwd32<ACT_SILU>(v, c); break;
-    case ACT_MISH: act_bwd32<ACT_MISH>(v, c); break;
-    default: break;
-  }
-}
-
-// PAIR: a cluster of two CTAs computes 256 x BN tiles with cta_group::2 MMAs issued by the
-// even CTA; each CTA loads its 128 rows of A and BN/2 rows of B, and writes its 128 output rows.
-template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR>
+template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR, int ACT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
@@ -375,22 +354,38 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const bool scaled = alpha != 1.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // Epilogue input C arrives by TMA: 32-row x 128-byte chunks into a per-warp C_DEPTH ring,
-    // issued C_DEPTH chunks ahead (the first ones while the tile's MMAs still run). A warp's
-    // live chunks (inside M and N) are a prefix of its columns; only those are loaded.
+    // Epilogue input C arrives by TMA: 32-row x 128-byte chunks into a per-warp C_DEPTH ring.
+    // Lane 0 keeps up to C_DEPTH chunks in flight, running ahead across tile boundaries, so the
+    // next tile's first chunks load while this tile is being written. A warp's live chunks
+    // (inside M and N) are a prefix of its columns; only those are loaded and consumed.
     constexpr int CW = bf16_out ? 64 : 32;  // columns per chunk
     uint8_t* cring = sC + (warp - 2) * C_DEPTH * EPI_STAGE_BYTES;
     uint64_t* cbar = cfull_bar + (warp - 2) * C_DEPTH;
     uint32_t c_issued = 0, c_used = 0;
     bool c_ok = true;
-    int c_next = 0, c_live = 0, c_b = 0, c_row0 = 0, c_col0 = 0;  // this tile's C chunk queue
-    auto c_issue = [&]() {  // lane 0: load the tile's next live chunk into the ring
-      if (c_next < c_live) {
+    int iu = first_unit, ic = 0, ilive = -1;  // lane 0's issue cursor (unit, chunk, live chunks of unit)
+    auto tile_origin = [&](int uu, int& b_, int& r0, int& col0) {
+      int mt_, nt_, ks_;
+      decode_unit(uu, sh, b_, mt_, nt_, ks_);
+      r0 = mt_ * TILE_M + rank * GEMM_BM + quarter * 32;
+      col0 = nt_ * BN + col_half * COLS;
+    };
+    auto c_fill = [&]() {
+      while (c_issued - c_used < (uint32_t)C_DEPTH && iu < sh.num_units) {
+        int b_, r0, col0;
+        tile_origin(iu, b_, r0, col0);
+        if (ilive < 0) ilive = r0 < sh.M ? max(0, min(COLS / CW, (sh.N - col0 + CW - 1) / CW)) : 0;
+        if (ic >= ilive) {
+          iu += unit_step;
+          ic = 0;
+          ilive = -1;
+          continue;
+        }
         uint64_t* bar = &cbar[c_issued % C_DEPTH];
         mbar_arrive_expect_tx(bar, EPI_STAGE_BYTES);
-        tma_load_3d(cring + (c_issued % C_DEPTH) * EPI_STAGE_BYTES, &tmC, bar, c_col0 + c_next * CW, c_row0, c_b);
+        tma_load_3d(cring + (c_issued % C_DEPTH) * EPI_STAGE_BYTES, &tmC, bar, col0 + ic * CW, r0, b_);
         ++c_issued;
-        ++c_next;
+        ++ic;
       }
     };
     auto c_get = [&](uint4 (&cc)[8]) {  // this row's 128 bytes of the oldest chunk, then refill
@@ -403,38 +398,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int j = 0; j < 8; ++j) cc[j] = make_uint4(0, 0, 0, 0);
         return;
       }
-      const uint8_t* buf = cring + (c_used % C_DEPTH) * EPI_STAGE_BYTES;
+      uint8_t* buf = cring + (c_used % C_DEPTH) * EPI_STAGE_BYTES;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(const_cast<uint8_t*>(buf), lane, j));
+      for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(buf, lane, j));
       ++c_used;
       __syncwarp();
       if (lane == 0) {
         fence_proxy_async_smem();  // our reads of the buffer come before the next TMA write into it
-        c_issue();
-      } else if (c_next < c_live) {
-        ++c_issued;  // keep every lane's queue counters in step with lane 0
-        ++c_next;
+        c_fill();
       }
     };
+    if constexpr (reads_c) {
+      if (lane == 0) c_fill();
+    }
     for (int u = first_unit; u < sh.num_units; u += unit_step) {
       int b, mt, nt, ks;
       decode_unit(u, sh, b, mt, nt, ks);
       const int row0 = mt * TILE_M + rank * GEMM_BM + quarter * 32;  // first output row of this warp
       const bool rows_live = row0 < sh.M;
-      if constexpr (reads_c) {
-        c_b = b;
-        c_row0 = row0;
-        c_col0 = nt * BN + col_half * COLS;
-        c_next = 0;
-        c_live = rows_live ? max(0, min(COLS / CW, (sh.N - c_col0 + CW - 1) / CW)) : 0;
-        const int first = min(C_DEPTH, c_live);
-        if (lane == 0) {
-          for (int j = 0; j < first; ++j) c_issue();
-        } else {
-          c_issued += first;
-          c_next = first;
-        }
-      }
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -472,7 +453,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rr[hf][j]);
             }
             if constexpr (EPI == RGPT_EPI_ACT_BWD) {
-              act_bwd32_rt(ep.act, v, &cc[hf * 4]);
+              act_bwd32<ACT>(v, &cc[hf * 4]);
             } else if constexpr (EPI == RGPT_EPI_POLY_BF16) {
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
@@ -499,7 +480,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                   make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
                              pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
             if constexpr (EPI == RGPT_EPI_ACT_FWD) {
-              act_fwd32_rt(ep.act, v);
+              act_fwd32<ACT>(v);
 #pragma unroll
               for (int j = 0; j < 4; ++j)
                 *reinterpret_cast<uint4*>(stage_ptr(s1, lane, hf * 4 + j)) =
@@ -643,13 +624,13 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_
   return make_tmap_3d(map, ptr, 2, inner, outer, batch, ld_elems, bstride_elems, box_inner, box_outer);
 }
 
-template <int BN, int STAGES_IN, int A_MN, int B_MN, int EPI, bool PAIR>
+template <int BN, int STAGES_IN, int A_MN, int B_MN, int EPI, bool PAIR, int ACT = ACT_NONE>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
                        const CUtensorMap& tc, const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
   // epilogues that read C give up operand stages for their per-warp C ring
   constexpr bool CIN = epi_reads_c(EPI);
   constexpr int STAGES = !CIN ? STAGES_IN : (BN == 256 && !PAIR ? 3 : 4);
-  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR>;
+  auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR, ACT>;
   constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR, CIN>::TOTAL;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr_set[64] = {false};
@@ -710,8 +691,27 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_BF16)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_ACCUM_F32)
-    RGPT_GEMM_EPI_CASE(RGPT_EPI_ACT_FWD)
-    RGPT_GEMM_EPI_CASE(RGPT_EPI_ACT_BWD)
+    case RGPT_EPI_ACT_FWD:
+    case RGPT_EPI_ACT_BWD: {
+      // the activation is a compile-time parameter of the epilogue
+      const bool fwd = epi == RGPT_EPI_ACT_FWD;
+#define RGPT_GEMM_ACT_CASE(A)                                                                                      \
+  case A:                                                                                                          \
+    return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, A>(ta, tb, td, td2, tc, sh, ep, s, dev) \
+               : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, A>(ta, tb, td, td2, tc, sh, ep, s, dev);
+      switch (ep.act) {
+        RGPT_GEMM_ACT_CASE(ACT_SQRELU)
+        RGPT_GEMM_ACT_CASE(ACT_GELU)
+        RGPT_GEMM_ACT_CASE(ACT_SILU)
+        RGPT_GEMM_ACT_CASE(ACT_MISH)
+        default:
+          return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, ACT_NONE>(ta, tb, td, td2, tc, sh,
+                                                                                          ep, s, dev)
+                     : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, ACT_NONE>(ta, tb, td, td2, tc, sh,
+                                                                                          ep, s, dev);
+      }
+#undef RGPT_GEMM_ACT_CASE
+    }
     RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
     default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, tc, sh, ep, s, dev);
