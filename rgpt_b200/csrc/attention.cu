@@ -20,9 +20,10 @@
 //   warps 2-5: one thread per query row: online softmax on S (tcgen05.ld), P as
 //          bf16 into 128B-swizzled smem for the P V MMA; O rescaled in TMEM only
 //          when a row max grows by more than 2^8.
-// Backward CTA = one 128-key tile of one (b, h), looping over query tiles:
-//   S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
+// Backward CTA = one 128-key tile of one (b, h), looping over query tiles in 64-query
+//   halves: S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
 //   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> TMA bulk reduce-add).
+//   Two softmax warpgroups take alternate halves, overlapping the MMAs of the other half.
 #include <cudaTypedefs.h>
 #include <math.h>
 
@@ -490,9 +491,16 @@ constexpr int ATT_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue 
 constexpr uint32_t DQ_STAGE_BYTES = 32 * 32 * 4;  // one warp's 32 x 32 fp32 dQ tile
 constexpr int BWD_STAT_FLOATS = 128;              // one warp's 64 query LSEs (log2 units) + 64 D values
 
-// Backward CTA = one 128-key tile of one (b, h). The 8 softmax warps come in pairs that
-// share TMEM lane quadrants: warp pair (w, w+4) owns key rows 32*(w%4).. and splits the
-// 128 query columns of P^T/dS^T (and later the 64 head columns of dQ/dK/dV) in halves.
+// Backward CTA = one 128-key tile of one (b, h), looping over the query tiles that see
+// these keys, each split into two 64-query halves. Softmax warpgroup g (warps 2-5: g = 0,
+// warps 6-9: g = 1) handles half g of every query tile, so the two halves are computed
+// concurrently, and the MMA warp issues the next tile's S/dP half as soon as a warpgroup has
+// handed over this tile's P/dS half:
+//   tensor pipe: SD(0,0) SD(0,1) VK(0,0) SD(1,0) VK(0,1) SD(1,1) Q(0) VK(1,0) SD(2,0) ...
+//   SD(t,g): S^T and dP^T of half g (TMEM buffer g), VK(t,g): dV += P^T dO, dK += dS^T Q on
+//   half g, Q(t): dQ = dS K for the whole tile (reads both halves' dS).
+// A warpgroup stores its next P/dS half only after Q of the previous tile has completed (it
+// reads both dS halves), and writes that tile's dQ (TMEM -> TMA bulk reduce-add) right after.
 __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -501,21 +509,21 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                     // 16 KB
   uint8_t* sV = sK + TILE_BYTES;          // 16 KB
-  uint8_t* sQ = sV + TILE_BYTES;          // 2 x 16 KB
+  uint8_t* sQ = sV + TILE_BYTES;          // 2 x 16 KB (query-tile ring)
   uint8_t* sDO = sQ + 2 * TILE_BYTES;     // 2 x 16 KB
-  uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T  : 2 atoms (queries 0-63, 64-127) x 16 KB
-  uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T : 2 atoms x 16 KB
+  uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T : 2 atoms (query half 0, 1) x 16 KB
+  uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T: 2 atoms x 16 KB
   uint8_t* sDQ = sDS + 2 * TILE_BYTES;    // 8 x 4 KB dQ staging (one per softmax warp)
   float* sStat = reinterpret_cast<float*>(sDQ + 8 * DQ_STAGE_BYTES);  // 8 warps x [64 lse*log2(e) | 64 D]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStat + 8 * BWD_STAT_FLOATS);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_full = bars + 1;   // [2] query-tile ring
   uint64_t* qd_empty = bars + 3;  // [2]
-  uint64_t* sdp_full = bars + 5;
-  uint64_t* ds_ready = bars + 6;  // P^T, dS^T written, S^T/dP^T TMEM read
-  uint64_t* dq_full = bars + 7;
-  uint64_t* dq_empty = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* sdp_full = bars + 5;  // [2] S^T/dP^T of half g in TMEM buffer g
+  uint64_t* ds_ready = bars + 7;  // [2] P^T/dS^T of half g in smem (and its S/dP read)
+  uint64_t* dq_full = bars + 9;
+  uint64_t* dq_empty = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -531,9 +539,9 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&ds_ready[i], 128);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(ds_ready, 256);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 256);
     *abort_flag = 0;
@@ -548,7 +556,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S^T [0,128) dP^T [128,256) dV [256,320) dK [320,384) dQ [384,448)
+  // TMEM columns: half g: S^T [128g, 128g+64) dP^T [128g+64, 128g+128); dV [256,320) dK [320,384) dQ [384,448)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -575,57 +583,89 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = make_idesc_bf16(128, 128, 0, 0);   // K Q^T, V dO^T
-      constexpr uint32_t IDESC_KV = make_idesc_bf16(128, 64, 0, 1);   // P^T dO, dS^T Q  (B MN-major)
+      constexpr uint32_t IDESC_S = make_idesc_bf16(128, 64, 0, 0);    // K Q_g^T, V dO_g^T (64 queries)
+      constexpr uint32_t IDESC_KV = make_idesc_bf16(128, 64, 0, 1);   // P_g^T dO_g, dS_g^T Q_g (B MN-major)
       constexpr uint32_t IDESC_Q = make_idesc_bf16(128, 64, 1, 1);    // dS K (A, B MN-major)
       bool ok = mbar_wait(kv_full, 0, abort_flag);
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      const uint32_t p_addr = smem_u32(sP), ds_addr = smem_u32(sDS);
-      for (int i = 0; i < nq && ok; ++i) {
-        const int s = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!mbar_wait(&qd_full[s], ph, abort_flag)) {
-          ok = false;
-          break;
-        }
-        // S^T / dP^T TMEM is free: the softmax threads read it before arriving on ds_ready(i-1),
-        // which this thread waited on in the previous iteration.
-        tc_fence_after();
-        const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES), do_addr = smem_u32(sDO + s * TILE_BYTES);
+      const uint32_t ds_addr = smem_u32(sDS);
+      // S^T and dP^T of half g of query tile t into TMEM buffer g
+      auto issue_sd = [&](int t, int g) {
+        const int s = t & 1;
+        const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES) + g * 8192;
+        const uint32_t do_addr = smem_u32(sDO + s * TILE_BYTES) + g * 8192;
 #pragma unroll
         for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          umma_bf16(tmem + 0, make_sw128_desc(k_addr + kk * 32, 16, 1024), make_sw128_desc(q_addr + kk * 32, 16, 1024),
-                    IDESC_S, kk > 0 ? 1u : 0u);
-          umma_bf16(tmem + 128, make_sw128_desc(v_addr + kk * 32, 16, 1024),
+          umma_bf16(tmem + g * 128, make_sw128_desc(k_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          umma_bf16(tmem + g * 128 + 64, make_sw128_desc(v_addr + kk * 32, 16, 1024),
                     make_sw128_desc(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
         }
-        umma_commit(sdp_full);
-        if (!mbar_wait(ds_ready, i & 1, abort_flag) || !mbar_wait(dq_empty, (i & 1) ^ 1, abort_flag)) {
+        umma_commit(&sdp_full[g]);
+      };
+      // dV += P_g^T dO_g ; dK += dS_g^T Q_g  (64 queries of half g as the K dimension)
+      auto issue_vk = [&](int t, int g) {
+        const int s = t & 1;
+        const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES) + g * 8192;
+        const uint32_t do_addr = smem_u32(sDO + s * TILE_BYTES) + g * 8192;
+        const uint32_t p_addr = smem_u32(sP + g * TILE_BYTES), dsg_addr = smem_u32(sDS + g * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t acc = (t > 0 || g > 0 || kk > 0) ? 1u : 0u;
+          umma_bf16(tmem + 256, make_sw128_desc(p_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(do_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, acc);
+          umma_bf16(tmem + 320, make_sw128_desc(dsg_addr + kk * 32, 16, 1024),
+                    make_sw128_desc(q_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, acc);
+        }
+      };
+      // dQ = dS K over the whole tile: A = dS^T atoms read MN-major (rows = keys), B = K MN-major
+      auto issue_q = [&]() {
+#pragma unroll
+        for (int kk = 0; kk < ATT_TILE / 16; ++kk)
+          umma_bf16(tmem + 384, make_sw128_desc(ds_addr + kk * 2048, TILE_BYTES, 1024),
+                    make_sw128_desc(k_addr + kk * 2048, TILE_BYTES, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+      };
+      if (ok && nq > 0) {
+        ok = mbar_wait(&qd_full[0], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          issue_sd(0, 0);
+          issue_sd(0, 1);
+        }
+      }
+      for (int t = 0; t < nq && ok; ++t) {
+        for (int g = 0; g < 2 && ok; ++g) {
+          if (!mbar_wait(&ds_ready[g], t & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_vk(t, g);
+          if (g == 1) umma_commit(&qd_empty[t & 1]);  // the last reader of this tile's Q / dO
+          if (t + 1 < nq) {
+            if (g == 0 && !mbar_wait(&qd_full[(t + 1) & 1], ((t + 1) >> 1) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_sd(t + 1, g);  // buffer g was read before ds_ready[g] arrived
+          }
+        }
+        if (!ok) break;
+        if (t > 0 && !mbar_wait(dq_empty, (t - 1) & 1, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < ATT_TILE / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * TILE_BYTES + (kk & 3) * 32;  // K-major over queries
-          // dV += P^T dO ; dK += dS^T Q   (B operands: the same smem tiles, read MN-major)
-          umma_bf16(tmem + 256, make_sw128_desc(p_addr + a_off, 16, 1024),
-                    make_sw128_desc(do_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
-          umma_bf16(tmem + 320, make_sw128_desc(ds_addr + a_off, 16, 1024),
-                    make_sw128_desc(q_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, (i > 0 || kk > 0) ? 1u : 0u);
-          // dQ = dS K : A = dS^T read MN-major (rows = keys), B = K read MN-major
-          umma_bf16(tmem + 384, make_sw128_desc(ds_addr + kk * 2048, TILE_BYTES, 1024),
-                    make_sw128_desc(k_addr + kk * 2048, TILE_BYTES, 1024), IDESC_Q, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(dq_full);
-        umma_commit(&qd_empty[s]);
+        issue_q();
       }
     }
     __syncwarp();
   } else {
     const int sw = warp - 2;            // 0..7
     const int quarter = warp & 3;       // TMEM lane quadrant
-    const int half = sw >> 2;           // which half of the columns this warp handles
+    const int g = sw >> 2;              // softmax warpgroup = query half it handles
     const int r = quarter * 32 + lane;  // key row (S^T / dP^T / dV / dK) and query row (dQ)
     const int key = k0 + r;
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -639,43 +679,70 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     const float* lse_bh = p.lse + ((long long)b * p.H + h) * p.T;
     const float* D_bh = p.Dvec + ((long long)b * p.H + h) * p.T;
     float* wstat = sStat + sw * BWD_STAT_FLOATS;
-    // P^T = exp2(S^T * scale*log2(e) - lse*log2(e)) and dS^T/scale = P^T (dP^T - D) for one
-    // 32-query chunk of this warp's key row. Queries past T carry lse = +inf (P = 0); keys past
-    // T need no mask (their K/V rows are zero and their dK/dV rows are never stored).
-    auto softmax_chunk = [&](auto mask_tag, int cc, int c) {
+    uint8_t* patom = sP + g * TILE_BYTES;
+    uint8_t* datom = sDS + g * TILE_BYTES;
+    // P^T = exp2(S^T * scale*log2(e) - lse*log2(e)) and dS^T/scale = P^T (dP^T - D) for 32
+    // queries (chunk cc of this half) of this thread's key row, in registers. Queries past T
+    // carry lse = +inf (P = 0); keys past T need no mask (their K/V rows are zero and their
+    // dK/dV rows are never stored).
+    auto softmax_chunk = [&](auto mask_tag, int cc, uint4 (&pk)[4], uint4 (&dk)[4]) {
       constexpr bool MASK = decltype(mask_tag)::value;
       uint32_t sv[32], dv[32];
-      tmem_ld32(t_lane + 0 + c * 32, sv);
-      tmem_ld32(t_lane + 128 + c * 32, dv);
+      tmem_ld32(t_lane + g * 128 + cc * 32, sv);
+      tmem_ld32(t_lane + g * 128 + 64 + cc * 32, dv);
       tmem_wait_ld();
       const float4* l4 = reinterpret_cast<const float4*>(wstat + cc * 32);
       const float4* d4 = reinterpret_cast<const float4*>(wstat + 64 + cc * 32);
-      float pr[32], ds[32];
+      float pr[8], ds[8];
 #pragma unroll
       for (int t4 = 0; t4 < 8; ++t4) {
         const float4 l = l4[t4], dd = d4[t4];
         const float la[4] = {l.x, l.y, l.z, l.w}, da[4] = {dd.x, dd.y, dd.z, dd.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int t = 4 * t4 + e;
-          float pv = ex2_approx(fmaf(__uint_as_float(sv[t]), p.scale_log2, -la[e]));
-          if constexpr (MASK) pv = (c * 32 + t < r) ? 0.f : pv;  // causal: query before key
-          pr[t] = pv;
-          ds[t] = pv * (__uint_as_float(dv[t]) - da[e]);
+          const int t_ = 4 * t4 + e;
+          float pv = ex2_approx(fmaf(__uint_as_float(sv[t_]), p.scale_log2, -la[e]));
+          if constexpr (MASK) pv = (g * 64 + cc * 32 + t_ < r) ? 0.f : pv;  // causal: query before key
+          pr[t_ & 7] = pv;
+          ds[t_ & 7] = pv * (__uint_as_float(dv[t_]) - da[e]);
+        }
+        if (t4 & 1) {  // 8 values -> one 16-byte chunk of bf16
+          pk[t4 >> 1] = make_uint4(pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]), pack_bf16x2(pr[4], pr[5]),
+                                   pack_bf16x2(pr[6], pr[7]));
+          dk[t4 >> 1] = make_uint4(pack_bf16x2(ds[0], ds[1]), pack_bf16x2(ds[2], ds[3]), pack_bf16x2(ds[4], ds[5]),
+                                   pack_bf16x2(ds[6], ds[7]));
         }
       }
-      uint8_t* patom = sP + half * TILE_BYTES;
-      uint8_t* datom = sDS + half * TILE_BYTES;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        st_sw128_chunk(patom, r, cc * 4 + t, pr + 8 * t);
-        st_sw128_chunk(datom, r, cc * 4 + t, ds + 8 * t);
-      }
     };
-    for (int i = 0; i < nq; ++i) {
+    // dQ rows of tile i (TMEM lane = query row), this warp's 32 of the 64 head columns
+    auto dq_out = [&](int i) -> bool {
+      if (!wait_all(dq_full, i & 1)) return false;
+      tc_fence_after();
+      const int qrow0 = (qt0 + i) * ATT_TILE;
+      uint32_t v[32];
+      tmem_ld32(t_lane + 384 + g * 32, v);
+      tmem_wait_ld();
+      if (lane == 0) bulk_wait_read0();  // the previous bulk reduce has finished reading the stage
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(__uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
+                        __uint_as_float(v[4 * j + 2]) * p.scale, __uint_as_float(v[4 * j + 3]) * p.scale);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && qrow0 + quarter * 32 < p.T) {  // boxes wholly past T carry only zeros
+        tma_reduce_add_4d(&tmDQ, stage, g * 32, h, qrow0 + quarter * 32, b);
+        bulk_commit();
+      }
+      tc_fence_before();
+      mbar_arrive(dq_empty);
+      return true;
+    };
+    for (int i = 0; i < nq && ok; ++i) {
       const int qrow0 = (qt0 + i) * ATT_TILE;
       {  // this warp's 64 queries: LSE in log2 units and D, staged for broadcast reads
-        const int qa = qrow0 + half * 64 + lane, qb = qa + 32;
+        const int qa = qrow0 + g * 64 + lane, qb = qa + 32;
         const float la = qa < p.T ? __ldg(lse_bh + qa) * 1.4426950408889634f : INFINITY;
         const float lb = qb < p.T ? __ldg(lse_bh + qb) * 1.4426950408889634f : INFINITY;
         const float da = qa < p.T ? __ldg(D_bh + qa) : 0.f;
@@ -687,60 +754,50 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
         wstat[96 + lane] = db;
         __syncwarp();
       }
-      if (!wait_all(sdp_full, i & 1)) {
+      if (!wait_all(&sdp_full[g], i & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      uint4 pk[2][4], dk[2][4];  // P^T / dS^T as bf16, 16-byte chunks of this key row
       if (i == 0) {  // the diagonal tile (query tile == key tile)
-        softmax_chunk(std::true_type{}, 0, half * 2);
-        softmax_chunk(std::true_type{}, 1, half * 2 + 1);
+        softmax_chunk(std::true_type{}, 0, pk[0], dk[0]);
+        softmax_chunk(std::true_type{}, 1, pk[1], dk[1]);
       } else {
-        softmax_chunk(std::false_type{}, 0, half * 2);
-        softmax_chunk(std::false_type{}, 1, half * 2 + 1);
+        softmax_chunk(std::false_type{}, 0, pk[0], dk[0]);
+        softmax_chunk(std::false_type{}, 1, pk[1], dk[1]);
       }
+      // dQ of the previous tile reads both dS halves: it must have completed before we overwrite
+      if (i > 0 && !dq_out(i - 1)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int ch = cc * 4 + t;
+          *reinterpret_cast<uint4*>(patom + r * 128 + ((ch ^ (r & 7)) << 4)) = pk[cc][t];
+          *reinterpret_cast<uint4*>(datom + r * 128 + ((ch ^ (r & 7)) << 4)) = dk[cc][t];
+        }
       tc_fence_before();
       fence_proxy_async_smem();
-      mbar_arrive(ds_ready);
-      if (!wait_all(dq_full, i & 1)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      // dQ rows (TMEM lane r = query row qrow0 + r), this warp's 32 of the 64 head columns
-      {
-        uint32_t v[32];
-        tmem_ld32(t_lane + 384 + half * 32, v);
-        tmem_wait_ld();
-        if (lane == 0) bulk_wait_read0();  // the previous bulk reduce has finished reading the stage
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
-              make_float4(__uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
-                          __uint_as_float(v[4 * j + 2]) * p.scale, __uint_as_float(v[4 * j + 3]) * p.scale);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && qrow0 + quarter * 32 < p.T) {  // boxes wholly past T carry only zeros
-          tma_reduce_add_4d(&tmDQ, stage, half * 32, h, qrow0 + quarter * 32, b);
-          bulk_commit();
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(dq_empty);
+      mbar_arrive(&ds_ready[g]);
     }
+    if (ok && nq > 0) ok = dq_out(nq - 1);
     if (lane == 0) bulk_wait0();  // every dQ reduce has landed before the CTA retires
     __syncwarp();
-    // dK, dV rows (key-major) once every query tile has been folded in. Every lane runs the
+    // dK, dV rows (key-major) once every query tile has been folded in: dq_full of the last tile
+    // means every earlier MMA (in-order tensor pipe) has completed. Every lane runs the
     // warp-collective TMEM loads; only the stores are predicated on the row being inside T.
     if (ok) {
       const bool valid = key < p.T;
       const long long row = (long long)b * p.T + (valid ? key : 0);
       uint32_t v[32];
-      tmem_ld32(t_lane + 256 + half * 32, v);
+      tmem_ld32(t_lane + 256 + g * 32, v);
       tmem_wait_ld();
       if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + half * 32);
+        uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + g * 32);
 #pragma unroll
         for (int t = 0; t < 4; ++t)
           dst[t] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
@@ -748,10 +805,10 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
                               pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
                               pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
       }
-      tmem_ld32(t_lane + 320 + half * 32, v);
+      tmem_ld32(t_lane + 320 + g * 32, v);
       tmem_wait_ld();
       if (valid) {
-        float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + half * 32);
+        float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + g * 32);
 #pragma unroll
         for (int t = 0; t < 8; ++t)
           dkd[t] = make_float4(__uint_as_float(v[4 * t]) * p.scale, __uint_as_float(v[4 * t + 1]) * p.scale,
