@@ -21,8 +21,9 @@
 //          bf16 into 128B-swizzled smem for the P V MMA; O rescaled in TMEM only
 //          when a row max grows by more than 2^8.
 // Backward CTA = one 128-key tile of one (b, h), looping over query tiles in 64-query
-//   halves: S^T = K Q^T, dP^T = V dO^T (TMEM); P^T and dS^T into smem; then
-//   dV += P^T dO, dK += dS^T Q (TMEM-resident), dQ = dS K (TMEM -> TMA bulk reduce-add).
+//   halves: S^T = K Q^T, dP^T = V dO^T (TMEM, K and V read from TMEM); P^T and dS^T into TMEM
+//   (dS^T also into smem); then dV += P^T dO, dK += dS^T Q (TMEM-resident, A from TMEM),
+//   dQ = dS K (TMEM -> TMA bulk reduce-add).
 //   Two softmax warpgroups take alternate halves, overlapping the MMAs of the other half.
 #include <cudaTypedefs.h>
 #include <math.h>
@@ -511,8 +512,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   uint8_t* sV = sK + TILE_BYTES;          // 16 KB
   uint8_t* sQ = sV + TILE_BYTES;          // 2 x 16 KB (query-tile ring)
   uint8_t* sDO = sQ + 2 * TILE_BYTES;     // 2 x 16 KB
-  uint8_t* sP = sDO + 2 * TILE_BYTES;     // P^T : 2 atoms (query half 0, 1) x 16 KB
-  uint8_t* sDS = sP + 2 * TILE_BYTES;     // dS^T: 2 atoms x 16 KB
+  uint8_t* sDS = sDO + 2 * TILE_BYTES;    // dS^T: 2 atoms (query half 0, 1) x 16 KB (P^T lives in TMEM)
   uint8_t* sDQ = sDS + 2 * TILE_BYTES;    // 8 x 4 KB dQ staging (one per softmax warp)
   float* sStat = reinterpret_cast<float*>(sDQ + 8 * DQ_STAGE_BYTES);  // 8 warps x [64 lse*log2(e) | 64 D]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sStat + 8 * BWD_STAT_FLOATS);
@@ -523,6 +523,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   uint64_t* ds_ready = bars + 7;  // [2] P^T/dS^T of half g in smem (and its S/dP read)
   uint64_t* dq_full = bars + 9;
   uint64_t* dq_empty = bars + 10;
+  uint64_t* kv_tmem = bars + 11;  // K and V copied into TMEM (the A operands of S^T / dP^T)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -544,6 +545,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     }
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 256);
+    mbar_init(kv_tmem, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -556,7 +558,10 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: half g: S^T [128g, 128g+64) dP^T [128g+64, 128g+128); dV [256,320) dK [320,384) dQ [384,448)
+  // TMEM columns: half g: S^T [128g, 128g+64) dP^T [128g+64, 128g+128), overwritten after the softmax by
+  // P^T [128g, 128g+32) and dS^T [128g+32, 128g+64) as packed bf16 pairs; dV [256,320) dK [320,384)
+  // dQ [384,448); K [448,480) and V [480,512) as packed bf16 pairs (A operands read from TMEM).
+  constexpr uint32_t KA_COL = 448, VA_COL = 480;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -586,8 +591,8 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
       constexpr uint32_t IDESC_S = make_idesc_bf16(128, 64, 0, 0);    // K Q_g^T, V dO_g^T (64 queries)
       constexpr uint32_t IDESC_KV = make_idesc_bf16(128, 64, 0, 1);   // P_g^T dO_g, dS_g^T Q_g (B MN-major)
       constexpr uint32_t IDESC_Q = make_idesc_bf16(128, 64, 1, 1);    // dS K (A, B MN-major)
-      bool ok = mbar_wait(kv_full, 0, abort_flag);
-      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      bool ok = mbar_wait(kv_full, 0, abort_flag) && mbar_wait(kv_tmem, 0, abort_flag);
+      const uint32_t k_addr = smem_u32(sK);
       const uint32_t ds_addr = smem_u32(sDS);
       // S^T and dP^T of half g of query tile t into TMEM buffer g
       auto issue_sd = [&](int t, int g) {
@@ -595,11 +600,11 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
         const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES) + g * 8192;
         const uint32_t do_addr = smem_u32(sDO + s * TILE_BYTES) + g * 8192;
 #pragma unroll
-        for (int kk = 0; kk < ATT_D / 16; ++kk) {
-          umma_bf16(tmem + g * 128, make_sw128_desc(k_addr + kk * 32, 16, 1024),
-                    make_sw128_desc(q_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-          umma_bf16(tmem + g * 128 + 64, make_sw128_desc(v_addr + kk * 32, 16, 1024),
-                    make_sw128_desc(do_addr + kk * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < ATT_D / 16; ++kk) {  // A = K / V rows from TMEM, 8 columns per 16 head dims
+          umma_bf16_ts(tmem + g * 128, tmem + KA_COL + kk * 8, make_sw128_desc(q_addr + kk * 32, 16, 1024), IDESC_S,
+                       kk > 0 ? 1u : 0u);
+          umma_bf16_ts(tmem + g * 128 + 64, tmem + VA_COL + kk * 8, make_sw128_desc(do_addr + kk * 32, 16, 1024),
+                       IDESC_S, kk > 0 ? 1u : 0u);
         }
         umma_commit(&sdp_full[g]);
       };
@@ -608,14 +613,13 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
         const int s = t & 1;
         const uint32_t q_addr = smem_u32(sQ + s * TILE_BYTES) + g * 8192;
         const uint32_t do_addr = smem_u32(sDO + s * TILE_BYTES) + g * 8192;
-        const uint32_t p_addr = smem_u32(sP + g * TILE_BYTES), dsg_addr = smem_u32(sDS + g * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
+        for (int kk = 0; kk < 4; ++kk) {  // A = P^T / dS^T of half g from TMEM, 8 columns per 16 queries
           const uint32_t acc = (t > 0 || g > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16(tmem + 256, make_sw128_desc(p_addr + kk * 32, 16, 1024),
-                    make_sw128_desc(do_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, acc);
-          umma_bf16(tmem + 320, make_sw128_desc(dsg_addr + kk * 32, 16, 1024),
-                    make_sw128_desc(q_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, acc);
+          umma_bf16_ts(tmem + 256, tmem + g * 128 + kk * 8, make_sw128_desc(do_addr + kk * 2048, TILE_BYTES, 1024),
+                       IDESC_KV, acc);
+          umma_bf16_ts(tmem + 320, tmem + g * 128 + 32 + kk * 8,
+                       make_sw128_desc(q_addr + kk * 2048, TILE_BYTES, 1024), IDESC_KV, acc);
         }
       };
       // dQ = dS K over the whole tile: A = dS^T atoms read MN-major (rows = keys), B = K MN-major
@@ -679,8 +683,28 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     const float* lse_bh = p.lse + ((long long)b * p.H + h) * p.T;
     const float* D_bh = p.Dvec + ((long long)b * p.H + h) * p.T;
     float* wstat = sStat + sw * BWD_STAT_FLOATS;
-    uint8_t* patom = sP + g * TILE_BYTES;
     uint8_t* datom = sDS + g * TILE_BYTES;
+    if (g == 0) {  // K and V rows (this thread's key row r) into TMEM as packed bf16 pairs
+      ok = wait_all(kv_full, 0);
+      if (ok) {
+        uint32_t w[32];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v4 = *reinterpret_cast<const uint4*>(sK + r * 128 + ((j ^ (r & 7)) << 4));
+          w[4 * j] = v4.x, w[4 * j + 1] = v4.y, w[4 * j + 2] = v4.z, w[4 * j + 3] = v4.w;
+        }
+        tmem_st32(t_lane + KA_COL, w);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v4 = *reinterpret_cast<const uint4*>(sV + r * 128 + ((j ^ (r & 7)) << 4));
+          w[4 * j] = v4.x, w[4 * j + 1] = v4.y, w[4 * j + 2] = v4.z, w[4 * j + 3] = v4.w;
+        }
+        tmem_st32(t_lane + VA_COL, w);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      mbar_arrive(kv_tmem);
+    }
     // P^T = exp2(S^T * scale*log2(e) - lse*log2(e)) and dS^T/scale = P^T (dP^T - D) for 32
     // queries (chunk cc of this half) of this thread's key row, in registers. Queries past T
     // carry lse = +inf (P = 0); keys past T need no mask (their K/V rows are zero and their
@@ -772,14 +796,29 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
         ok = false;
         break;
       }
+      // P^T and dS^T of this key row into TMEM (A operands of dV / dK); dS^T also into smem for dQ
+      {
+        uint32_t pw[32], dw[32];
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint4 a = pk[cc][t], d4 = dk[cc][t];
+            const int o = cc * 16 + t * 4;
+            pw[o] = a.x, pw[o + 1] = a.y, pw[o + 2] = a.z, pw[o + 3] = a.w;
+            dw[o] = d4.x, dw[o + 1] = d4.y, dw[o + 2] = d4.z, dw[o + 3] = d4.w;
+          }
+        tmem_st32(t_lane + g * 128, pw);
+        tmem_st32(t_lane + g * 128 + 32, dw);
+      }
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc)
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int ch = cc * 4 + t;
-          *reinterpret_cast<uint4*>(patom + r * 128 + ((ch ^ (r & 7)) << 4)) = pk[cc][t];
           *reinterpret_cast<uint4*>(datom + r * 128 + ((ch ^ (r & 7)) << 4)) = dk[cc][t];
         }
+      tmem_wait_st();
       tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&ds_ready[g]);
@@ -826,7 +865,7 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
 }
 
 constexpr uint32_t FWD_SMEM = TILE_BYTES + 2 * FWD_KV_STAGES * KV_TILE_BYTES + 2 * P_TILE_BYTES + 256 + 1024;
-constexpr uint32_t BWD_SMEM = 10 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 8 * BWD_STAT_FLOATS * 4 + 256 + 1024;
+constexpr uint32_t BWD_SMEM = 8 * TILE_BYTES + 8 * DQ_STAGE_BYTES + 8 * BWD_STAT_FLOATS * 4 + 256 + 1024;
 
 }  // namespace rgpt
 
