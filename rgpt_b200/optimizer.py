@@ -92,6 +92,32 @@ def newton_schulz_batched(ws: _NSWorkspace, steps: int, coeffs=NS_COEFFS) -> tor
     return X
 
 
+class _NSView:
+    """The NS buffers of matrices [s, e) of a shape-class workspace (contiguous along the batch)."""
+
+    def __init__(self, ws: _NSWorkspace, s: int, e: int):
+        self.n, self.xr, self.xc = e - s, ws.xr, ws.xc
+        self.X, self.X2, self.A, self.B = ws.X[s:e], ws.X2[s:e], ws.A[s:e], ws.B[s:e]
+        self.sumsq = ws.sumsq[s:e]
+
+
+def assign_ns_owners(shapes: List[Tuple[int, int]], world: int) -> List[int]:
+    """Owner rank of each Muon matrix's Newton-Schulz iteration, balanced by NS FLOPs.
+
+    `shapes` are the (rows, cols) each matrix has after the rows <= cols transpose. Greedy
+    longest-processing-time assignment (heaviest matrices first, to the least loaded rank, lowest
+    rank on ties); deterministic, so every rank computes the same assignment."""
+    cost = [2 * r * r * c * 2 + 2 * r ** 3 for r, c in shapes]
+    order = sorted(range(len(shapes)), key=lambda i: (-cost[i], i))
+    load = [0] * world
+    owner = [0] * len(shapes)
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        owner[i] = r
+        load[r] += cost[i]
+    return owner
+
+
 def _muon_rows(params, grads, moms) -> List[List[int]]:
     rows = []
     for p, g, m in zip(params, grads, moms):
@@ -228,20 +254,115 @@ class Muon(torch.optim.Optimizer):
 class DistMuon(Muon):
     """Data-parallel Muon (optimizer.py:278-415).
 
-    The reference relies on DDP to all-reduce gradients and then repeats the
-    whole update on every rank. Here gradients are averaged across ranks by
-    this optimizer (the model is not wrapped in DDP), so the update is the
-    same as the reference's on DDP-averaged gradients."""
+    The reference relies on DDP to all-reduce gradients and then repeats the whole update on
+    every rank. Here gradients are averaged across ranks by this optimizer (the model is not
+    wrapped in DDP): one fp32 all-reduce of the flat gradient arena per step. The momentum and
+    AdamW updates then run on every rank as in the reference, but each Muon matrix's
+    Newton-Schulz iteration runs on one owner rank only (balanced by NS FLOPs) and the bf16
+    results are all-gathered, so every rank applies identical updates while doing 1/N of the
+    NS work. `shard_ns=False` repeats the full NS on every rank instead."""
 
-    def __init__(self, params, *args, process_group=None, **kwargs):
+    def __init__(self, params, *args, process_group=None, shard_ns: bool = True, **kwargs):
         super().__init__(params, *args, **kwargs)
         self.process_group = process_group
+        self.shard_ns = shard_ns
 
     @torch.no_grad()
     def step(self, closure: Optional[Any] = None):
-        if dist.is_available() and dist.is_initialized() and dist.get_world_size(self.process_group) > 1:
-            self._average_grads()
-        return super().step(closure)
+        world = dist.get_world_size(self.process_group) if dist.is_available() and dist.is_initialized() else 1
+        if world <= 1:
+            return super().step(closure)
+        self._average_grads()
+        if not self.shard_ns:
+            return super().step(closure)
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        rank = dist.get_rank(self.process_group)
+        for gi, group in enumerate(self.param_groups):
+            if group.get("use_muon", False):
+                self._muon_group_sharded(gi, group, [p for p in group["params"] if p.grad is not None], rank, world)
+            else:
+                self._adamw_group(gi, group, [p for p in group["params"] if p.grad is not None])
+        return loss
+
+    def _muon_group_sharded(self, gi, group, params, rank: int, world: int):
+        if not params:
+            return
+        lr = float(group["lr"])
+        wd = float(group["weight_decay"])
+        muon_lr = lr * float(group["muon_lr_multiplier"])
+        beta = float(group["momentum"])
+        nesterov = bool(group["nesterov"])
+        steps = int(group.get("ns_steps", 5))
+        coeffs = tuple(group.get("ns_coeffs", NS_COEFFS))
+        for p in params:
+            st = self.state[p]
+            if len(st) == 0:
+                st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+        rows_all = _muon_rows(params, [p.grad for p in params], [self.state[p]["momentum_buffer"] for p in params])
+        key = ("muon_sharded", gi, world, rank, tuple(tuple(r) for r in rows_all))
+        plan = self._cache.get(key)
+        if plan is None:
+            plan = self._plan_sharded(params, rows_all, world)
+            self._cache[key] = plan
+        for (xr, xc), cls in plan.items():
+            ws = cls["ws"]
+            ws.sumsq.zero_()
+            # momentum (and the NS input) for every matrix: the momentum state stays replicated
+            for R, C, owner, off, n, table in cls["segments"]:
+                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n])
+            s, e = cls["blocks"][rank]
+            send = cls["send"]
+            if e > s:
+                view = _NSView(ws, s, e)
+                nv.ns_scale(view.X, xr, _pad8(xc), view.n, view.sumsq)
+                out = newton_schulz_batched(view, steps, coeffs)
+                send[:e - s].copy_(out)
+            dist.all_gather_into_tensor(cls["gathered"], send, group=self.process_group)
+            maxc = cls["maxc"]
+            for R, C, owner, off, n, table in cls["segments"]:
+                g0 = owner * maxc + (off - cls["blocks"][owner][0])
+                nv.muon_apply(table, n, R, C, cls["gathered"][g0:g0 + n], lr, wd, muon_lr, _muon_scale(R, C))
+
+    def _plan_sharded(self, params, rows_all, world):
+        """Per shape class: matrices ordered by (owner, original shape), one prep/apply table per
+        (owner, shape) run, each owner's matrices contiguous, and the all-gather buffers."""
+        dev = params[0].device
+        shapes = []
+        for p in params:
+            R, C = p.shape[0], p.numel() // p.shape[0]
+            shapes.append((R, C, (C, R) if R > C else (R, C)))
+        owners = assign_ns_owners([sh[2] for sh in shapes], world)
+        by_class: Dict[Tuple[int, int], List[int]] = {}
+        for i, sh in enumerate(shapes):
+            by_class.setdefault(sh[2], []).append(i)
+        plan = {}
+        for (xr, xc), idx in sorted(by_class.items()):
+            idx = sorted(idx, key=lambda i: (owners[i], shapes[i][0], shapes[i][1], i))
+            segments, blocks, off = [], [], 0
+            for r in range(world):
+                start = off
+                mine = [i for i in idx if owners[i] == r]
+                j = 0
+                while j < len(mine):
+                    R, C = shapes[mine[j]][0], shapes[mine[j]][1]
+                    k = j
+                    while k < len(mine) and (shapes[mine[k]][0], shapes[mine[k]][1]) == (R, C):
+                        k += 1
+                    run = mine[j:k]
+                    segments.append((R, C, r, off, len(run), _table([rows_all[i] for i in run], dev)))
+                    off += len(run)
+                    j = k
+                blocks.append((start, off))
+            maxc = max(max(e - s for s, e in blocks), 1)
+            ws = _NSWorkspace(len(idx), xr, xc, dev)
+            rp, cp = _pad8(xr), _pad8(xc)
+            plan[(xr, xc)] = dict(ws=ws, segments=segments, blocks=blocks, maxc=maxc,
+                                  send=torch.zeros(maxc, rp, cp, device=dev, dtype=torch.bfloat16),
+                                  gathered=torch.zeros(world * maxc, rp, cp, device=dev, dtype=torch.bfloat16))
+        return plan
 
     def _average_grads(self):
         ws = dist.get_world_size(self.process_group)

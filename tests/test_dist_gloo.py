@@ -61,3 +61,17 @@ def test_distmuon_averages_grads_over_two_gloo_ranks():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results == {0: True, 1: True}
+
+
+def test_ns_owner_assignment_is_balanced_and_deterministic():
+    from rgpt_b200.optimizer import assign_ns_owners
+
+    # gpt-small Muon matrices as NS sees them: 4 x [512,512] and 2 x [512,2048] per layer, gate [64,64]
+    shapes = ([(512, 512)] * 4 + [(512, 2048)] * 2 + [(64, 64)]) * 8
+    cost = [2 * r * r * c * 2 + 2 * r ** 3 for r, c in shapes]
+    for world in (1, 2, 4, 8):
+        own = assign_ns_owners(shapes, world)
+        assert own == assign_ns_owners(shapes, world)
+        assert set(own) == set(range(world))
+        load = [sum(c for c, o in zip(cost, own) if o == r) for r in range(world)]
+        assert max(load) <= 1.01 * min(load)
