@@ -28,6 +28,8 @@ from __future__ import annotations
 import math
 import warnings
 
+from typing import Dict, List
+
 import torch
 
 from .. import native as nv
@@ -154,12 +156,23 @@ class Engine:
         self.grad_arena = torch.zeros(total, device=dev, dtype=torch.float32)
         off = 0
         self.grads = {}
+        # gradient buckets, in the order the backward finishes them: the parameters after the
+        # layers (ln_f, lm_head, ...), each layer from the last to the first, then the embedding
+        spans: Dict[str, List[int]] = {}
         for name, p in named:
             g = self.grad_arena[off:off + p.numel()].view_as(p)
             p.grad = g
             p._rgpt_grad_arena = self.grad_arena
             self.grads[name] = g
+            parts = name.split(".")
+            key = f"layer{parts[1]}" if parts[0] == "layers" else ("pre" if not any(k.startswith("layer") for k in spans)
+                                                                       else "post")
+            sp = spans.setdefault(key, [off, off])
+            if sp[1] != off:
+                raise RuntimeError(f"gradient bucket {key} is not contiguous in the arena")
+            sp[1] = off + p.numel()
             off += p.numel()
+        self.grad_buckets = spans
         # bf16 shadows: fused QKV per layer, out, fc1, fc2, lm_head
         d = self.d
         self.shadow_src = []  # (param, shadow view, version)
@@ -380,6 +393,14 @@ class Engine:
         tval = float(temp) if temp is not None else 1.0
         halting = self._halting_active
         need_gb_now = not halting
+        # A data-parallel optimizer may hook the arena to reduce each gradient bucket as soon as the
+        # backward has finished it (overlapping the collective with the rest of the backward). Buckets
+        # are final after one pass only without recurrence reuse or halting heads.
+        sync = getattr(self.grad_arena, "_rgpt_sync", None)
+        if sync is not None and (self.n_recur != 1 or halting):
+            sync = None
+        if sync is not None:
+            sync.begin(self.grad_arena)
         nv.rownorm_bwd(A.x[napp], A.dy32, kind, eps, A.g, w=w, temp=tval, alpha=alpha, g_in=None,
                        g_bf16=A.gb if need_gb_now else None,
                        ls=last_blk.ff_layer_scale if (self.ls and need_gb_now) else None,
@@ -389,6 +410,8 @@ class Engine:
         if halting:
             if alpha_dev is not None:
                 A.dq.mul_(alpha_dev)
+        if sync is not None and "post" in self.grad_buckets:
+            sync.ready(self.grad_arena, *self.grad_buckets["post"])
         app = napp
         for r in reversed(range(self.n_recur)):
             if halting:
@@ -410,10 +433,16 @@ class Engine:
                 # from the complete gradient, so the layer must not emit them first
                 defer = halting and boundary
                 self._layer_bwd(m.layers[li], li, self.layer_w[li], A, app, first or cut or defer)
+                if sync is not None:
+                    sync.ready(self.grad_arena, *self.grad_buckets[f"layer{li}"])
                 if cut:
                     A.g.zero_()
                     A.gb.zero_()
         nv.embedding_bwd(self._ids, A.g, G["embs.weight"])
+        if sync is not None:
+            if "pre" in self.grad_buckets:
+                sync.ready(self.grad_arena, *self.grad_buckets["pre"])
+            sync.end(self.grad_arena)
 
     def _pname(self, blk, attr):
         idx = list(self.model.layers).index(blk)

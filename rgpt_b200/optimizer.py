@@ -262,10 +262,27 @@ class DistMuon(Muon):
     results are all-gathered, so every rank applies identical updates while doing 1/N of the
     NS work. `shard_ns=False` repeats the full NS on every rank instead."""
 
-    def __init__(self, params, *args, process_group=None, shard_ns: bool = True, **kwargs):
+    def __init__(self, params, *args, process_group=None, shard_ns: bool = True, overlap_grad_sync: bool = True,
+                 **kwargs):
         super().__init__(params, *args, **kwargs)
         self.process_group = process_group
         self.shard_ns = shard_ns
+        self.overlap_grad_sync = overlap_grad_sync
+        self._pending: List[Any] = []    # async all-reduces launched during the backward
+        self._synced: Dict[int, bool] = {}  # arena id -> every bucket reduced in the latest backward
+
+    # -- gradient-bucket hooks called by the native backward (see Engine.backward) --
+    def begin(self, arena):
+        self._synced[id(arena)] = False
+
+    def ready(self, arena, start: int, end: int):
+        # the collective waits for the kernels already queued on the current stream, then runs
+        # alongside the rest of the backward; AVG averages over the ranks like the reference's DDP
+        self._pending.append(dist.all_reduce(arena[start:end], op=dist.ReduceOp.AVG, group=self.process_group,
+                                             async_op=True))
+
+    def end(self, arena):
+        self._synced[id(arena)] = True
 
     @torch.no_grad()
     def step(self, closure: Optional[Any] = None):
@@ -366,6 +383,10 @@ class DistMuon(Muon):
 
     def _average_grads(self):
         ws = dist.get_world_size(self.process_group)
+        for w in self._pending:
+            w.wait()
+        self._pending = []
+        nccl = dist.get_backend(self.process_group) == "nccl"
         arenas, loose = {}, []
         for group in self.param_groups:
             for p in group["params"]:
@@ -376,7 +397,11 @@ class DistMuon(Muon):
                     arenas[id(a)] = a
                 else:
                     loose.append(p.grad)
-        for a in arenas.values():
+        for key, a in arenas.items():
+            if self._synced.pop(key, False):
+                continue  # every bucket was averaged during the backward
+            if nccl and self.overlap_grad_sync:
+                a._rgpt_sync = self  # later backwards reduce bucket by bucket
             dist.all_reduce(a, op=dist.ReduceOp.SUM, group=self.process_group)
             a.mul_(1.0 / ws)
         for g in loose:

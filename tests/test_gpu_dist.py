@@ -90,3 +90,84 @@ def test_distmuon_sharded_ns_matches_replicated_on_two_gpus():
         assert err < 1e-6, (rank, err)
         assert same == 0.0, (rank, same)
         assert moved > 1e-3, (rank, moved)  # the update did something
+
+
+def _train_worker(rank: int, world: int, port: int, q) -> None:
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from rgpt_b200.model import GPT
+        from rgpt_b200.optimizer import DistMuon, trainer_param_groups
+
+        cfg = dict(name="gpt", n_layers=2, n_recur=1, detach_recur=False, cal_halt_loss=False, n_heads=2,
+                   d_model=128, vocab_size=384, max_seq_len=256, dropout=0.0, norm_type="rmsnorm", norm_eps=1e-5,
+                   qk_normtype="f_rmsnorm", activation_type="squared_relu", g1_gate=True, use_layer_scale=True,
+                   pad_token_id=-100, tie_word_embeddings=False)
+        g = torch.Generator().manual_seed(10 + rank)  # each rank trains on its own batches
+        batches = [torch.randint(0, 384, (2, 129), generator=g).to(dev) for _ in range(3)]
+        torch.manual_seed(0)
+        model = GPT(**cfg).to(dev)
+        opt = DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
+
+        def backward(ids):
+            total, _, _ = model.forward_loss(ids[:, :-1], ids[:, 1:].contiguous())
+            total.backward()
+
+        backward(batches[0])  # step 1 averages the whole arena at step time and installs the bucket hooks
+        opt.step()
+        opt.zero_grad()
+        arena = next(model.parameters())._rgpt_grad_arena
+        hooked = getattr(arena, "_rgpt_sync", None) is opt
+        backward(batches[1])  # buckets averaged during the backward
+        opt._average_grads()
+        a_hooks = arena.clone()
+        opt.zero_grad()
+        arena._rgpt_sync = None
+        backward(batches[1])  # same parameters and batch, one all-reduce of the arena afterwards
+        opt._average_grads()
+        a_step = arena.clone()
+        arena._rgpt_sync = opt
+        err = ((a_hooks - a_step).norm() / a_step.norm()).item()
+        opt.step()  # a full hooked step keeps every rank's parameters identical
+        opt.zero_grad()
+        backward(batches[2])
+        opt.step()
+        torch.cuda.synchronize()
+        ref = [p.detach().clone() for p in model.parameters()]
+        for t in ref:
+            dist.broadcast(t, 0)
+        same = max((p - r).abs().max().item() for p, r in zip(model.parameters(), ref))
+        q.put((rank, hooked, err, same))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_distmuon_overlapped_bucket_sync_matches_step_time_allreduce():
+    # Gradient buckets averaged during the backward (one async all-reduce per bucket, issued as the
+    # backward finishes it) equal one all-reduce of the whole arena after the backward, from the
+    # same parameters and batch (tolerance 1e-5 relative: the backward's fp32 atomics and split-K
+    # reduce-adds sum in a run-to-run varying order), and every rank ends with the same parameters.
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_train_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, hooked, err, same in res:
+        assert hooked, rank
+        assert err < 1e-5, (rank, err)
+        assert same == 0.0, (rank, same)
