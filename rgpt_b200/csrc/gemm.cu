@@ -783,12 +783,13 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.N = N;
   sh.K = K;
   sh.batch = batch;
-  // 256-wide tiles unless that leaves most SMs idle (small N or few row tiles)
+  // 256-wide tiles unless at most half the SMs would get one. A 128 x 128 x 16 MMA costs nearly
+  // as much issue time as a 128 x 256 x 16 one (measured ~125 vs ~135 SM cycles), so halving the
+  // tile only pays when both widths fit in one wave. Accumulating GEMMs keep the wide tile (fewer
+  // operand re-reads) and split K instead.
   const int m128 = (M + GEMM_BM - 1) / GEMM_BM;
   int BN = (N > 128) ? 256 : 128;
-  if (BN == 256 && epi != RGPT_EPI_ACCUM_F32 && batch * m128 * ((N + 255) / 256) < nsm &&
-      batch * m128 * ((N + 127) / 128) <= 2 * nsm)
-    BN = 128;  // accumulating GEMMs keep the wide tile (fewer operand re-reads) and split K instead
+  if (BN == 256 && epi != RGPT_EPI_ACCUM_F32 && 2LL * batch * m128 * ((N + 255) / 256) <= nsm) BN = 128;
   sh.num_kb = (K + GEMM_BK - 1) / GEMM_BK;
   // CTA pairs (256 x 256 tiles, half the B traffic per SM) pay off once the main loop is long
   // (K >= 1024) and there is a wave of pair tiles, or for plain stores with very many tiles
