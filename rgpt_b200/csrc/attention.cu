@@ -172,8 +172,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + ATT_TILE - 1) / ATT_TILE;
-  const int qt = n_qt - 1 - blockIdx.x;  // heaviest (longest causal row) tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // one linear grid, heaviest query tiles (longest causal rows) of every (b, h) first, so the
+  // last CTAs to start are the shortest ones
+  const int bh = blockIdx.x % (p.H * p.B);
+  const int qt = n_qt - 1 - (int)(blockIdx.x / (p.H * p.B));
+  const int h = bh % p.H, b = bh / p.H;
   const int q0 = qt * ATT_TILE;
   const int last_key = min(q0 + ATT_TILE - 1, p.T - 1);
   const int nkv = last_key / FWD_KT + 1;
@@ -528,8 +531,10 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kt = blockIdx.x;  // heaviest key tiles (most query tiles) have the lowest index
-  const int h = blockIdx.y, b = blockIdx.z;
+  // one linear grid, heaviest key tiles (most query tiles: lowest index) of every (b, h) first
+  const int bh = blockIdx.x % (p.H * p.B);
+  const int kt = (int)(blockIdx.x / (p.H * p.B));
+  const int h = bh % p.H, b = bh / p.H;
   const int k0 = kt * ATT_TILE;
   const int n_qt = (p.T + ATT_TILE - 1) / ATT_TILE;
   const int qt0 = kt;  // query tiles qt >= kt see these keys
@@ -909,7 +914,7 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
       return rgpt_check_launch("attn_fwd set smem");
     attr[dev] = true;
   }
-  dim3 grid((T + ATT_TILE - 1) / ATT_TILE, H, B);
+  const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
   attn_fwd_kernel<<<grid, ATT_THREADS, FWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   return rgpt_check_launch("attn_fwd_kernel");
 }
@@ -967,7 +972,7 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
       return rgpt_check_launch("attn_bwd set smem");
     attr[dev] = true;
   }
-  dim3 grid((T + ATT_TILE - 1) / ATT_TILE, H, B);
+  const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
   attn_bwd_kernel<<<grid, ATT_BWD_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, tdq, p);
   return rgpt_check_launch("attn_bwd_kernel");
 }
