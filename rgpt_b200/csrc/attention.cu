@@ -102,6 +102,13 @@ __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const 
       "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2,
+                                             int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -150,7 +157,9 @@ constexpr float FWD_RESCALE_LOG2 = 8.0f;                    // rescale O only wh
 // that rare rescale multiplies O in TMEM after the previous P V has landed.
 __global__ void __launch_bounds__(ATT_THREADS, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, AttnFwdParams p) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
+                    const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmOG,
+                    AttnFwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                                    // 16 KB
@@ -167,7 +176,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   uint64_t* s_empty = s_full + 2;                     // [2]
   uint64_t* p_full = s_empty + 2;                     // [2]
   uint64_t* pv_done = p_full + 2;                     // [2] P V of the tile using P buffer i has landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* g_full = pv_done + 2;                     // gate tile landed in sQ (after the last S)
+  uint64_t* q_free = g_full + 1;                      // the last S MMA (last reader of Q) has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -195,6 +206,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       mbar_init(&p_full[i], 128);
       mbar_init(&pv_done[i], 1);
     }
+    mbar_init(g_full, 1);
+    mbar_init(q_free, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -231,6 +244,16 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         mbar_arrive_expect_tx(&v_full[st], KV_TILE_BYTES);
         tma_load_4d(sV + st * KV_TILE_BYTES, &tmV, &v_full[st], 0, h, j * FWD_KT, b);
         ++issued_v;
+      }
+      // the gate tile reuses sQ once the last S MMA (the last reader of Q) has completed
+      if (ok && p.og != nullptr) {
+        if (mbar_wait(q_free, 0, abort_flag)) {
+          mbar_arrive_expect_tx(g_full, TILE_BYTES);
+          tma_load_4d(sQ, &tmG, g_full, 0, h, q0, b);
+          mbar_wait(g_full, 0, nullptr);  // the copy lands before this thread moves on
+        } else {
+          ok = false;
+        }
       }
       if (!ok) {  // let the copies already issued land before the CTA retires
         mbar_wait(q_full, 0, nullptr);
@@ -279,8 +302,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkv && ok; ++j) {
         if (j + 1 < nkv && !issue_s(j + 1)) ok = false;
+        if (ok && j + 1 == nkv - 1) umma_commit(q_free);  // after the last S
         if (ok && !issue_pv(j)) ok = false;
       }
+      if (ok && nkv == 1) umma_commit(q_free);
     }
     __syncwarp();
   } else {
@@ -381,47 +406,52 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     // every P V has landed once the last one has (in-order tensor pipe)
     if (ok) ok = wait_all(&pv_done[(nkv - 1) & 1], ((nkv - 1) >> 1) & 1);
     if (ok) {
+      // O / l as bf16 (and og = bf16(o) * gate) staged in the free P buffers as 128B-swizzled rows,
+      // then written by TMA bulk stores, one 32-row box per warp (rows past T are clipped)
       tc_fence_after();
       uint32_t o[2][32];
       tmem_ld32(t_lane + O_COL, o[0]);
       tmem_ld32(t_lane + O_COL + 32, o[1]);
       tmem_wait_ld();
-      if (qrow < p.T) {
-        const float inv_l = 1.0f / l_run;
-        const long long row = (long long)b * p.T + qrow;
-        __nv_bfloat16* orow = p.o + row * p.d + h * ATT_D;
-        float ov[ATT_D];
+      const float inv_l = 1.0f / l_run;
+      float ov[ATT_D];
 #pragma unroll
-        for (int i = 0; i < ATT_D; ++i) ov[i] = __uint_as_float(o[i >> 5][i & 31]) * inv_l;
+      for (int i = 0; i < ATT_D; ++i) ov[i] = __uint_as_float(o[i >> 5][i & 31]) * inv_l;
+      uint8_t* so = sP;                 // o tile  [128 x 64] bf16
+      uint8_t* sog = sP + P_TILE_BYTES;  // og tile [128 x 64] bf16
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 w;
-          w.x = pack_bf16x2(ov[8 * c + 0], ov[8 * c + 1]);
-          w.y = pack_bf16x2(ov[8 * c + 2], ov[8 * c + 3]);
-          w.z = pack_bf16x2(ov[8 * c + 4], ov[8 * c + 5]);
-          w.w = pack_bf16x2(ov[8 * c + 6], ov[8 * c + 7]);
-          reinterpret_cast<uint4*>(orow)[c] = w;
-        }
-        if (p.og != nullptr) {
-          const uint4* grow = reinterpret_cast<const uint4*>(p.gate + row * p.d + h * ATT_D);
-          uint4* ogrow = reinterpret_cast<uint4*>(p.og + row * p.d + h * ATT_D);
+      for (int c = 0; c < 8; ++c) st_sw128_chunk(so, r, c, ov + 8 * c);
+      const bool gated = p.og != nullptr;
+      if (gated) {
+        if (!wait_all(g_full, 0)) ok = false;
+        if (ok) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            uint4 g = grow[c];
-            uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-            uint32_t ow[4];
+            const uint4 g = *reinterpret_cast<const uint4*>(sQ + r * 128 + ((c ^ (r & 7)) << 4));
+            const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+            float gv[8];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              float2 gf = unpack_bf16x2(gw[e]);
+              const float2 gf = unpack_bf16x2(gw[e]);
               // gate the bf16-rounded o, as the reference multiplies the stored attention output
-              ow[e] = pack_bf16x2(bf16_round(ov[8 * c + 2 * e]) * gf.x, bf16_round(ov[8 * c + 2 * e + 1]) * gf.y);
+              gv[2 * e] = bf16_round(ov[8 * c + 2 * e]) * gf.x;
+              gv[2 * e + 1] = bf16_round(ov[8 * c + 2 * e + 1]) * gf.y;
             }
-            ogrow[c] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            st_sw128_chunk(sog, r, c, gv);
           }
         }
-        // natural-log LSE of the scaled scores
-        p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
       }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (ok && lane == 0 && q0 + quarter * 32 < p.T) {
+        tma_store_4d(&tmO, so + quarter * 32 * 128, 0, h, q0 + quarter * 32, b);
+        if (gated) tma_store_4d(&tmOG, sog + quarter * 32 * 128, 0, h, q0 + quarter * 32, b);
+        bulk_commit();
+      }
+      // natural-log LSE of the scaled scores
+      if (qrow < p.T) p.lse[((long long)b * p.H + h) * p.T + qrow] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+      if (lane == 0) bulk_wait0();  // the stores have read the staging tiles before the CTA retires
+      __syncwarp();
     }
     tc_fence_before();
   }
@@ -898,6 +928,15 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
   if ((st = make_head_map(&tq, qkb, H, T, B, 2LL * d))) return st;
   if ((st = make_head_map(&tk, qkb + d, H, T, B, 2LL * d, FWD_KT))) return st;
   if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d, FWD_KT))) return st;
+  // gate (read) and the outputs o / og (written): 4-D maps with 128-row (gate) / 32-row (stores) boxes
+  CUtensorMap tg, to, tog;
+  if ((st = make_head_map(&to, o, H, T, B, (long long)d, 32))) return st;
+  tog = to;
+  tg = to;
+  if (og != nullptr) {
+    if ((st = make_head_map(&tog, og, H, T, B, (long long)d, 32))) return st;
+    if ((st = make_head_map(&tg, gate, H, T, B, (long long)d))) return st;
+  }
   AttnFwdParams p;
   p.B = B;
   p.T = T;
@@ -915,7 +954,7 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
     attr[dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  attn_fwd_kernel<<<grid, ATT_THREADS, FWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+  attn_fwd_kernel<<<grid, ATT_THREADS, FWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tg, to, tog, p);
   return rgpt_check_launch("attn_fwd_kernel");
 }
 
