@@ -92,6 +92,24 @@ static int make_head_map_f32(CUtensorMap* map, const float* base, int H, int T, 
   return RGPT_OK;
 }
 
+// bf16 (64, H, T, B) view with 32-row x 32-column boxes and no swizzle (64-byte smem rows): the
+// target of the per-warp dV bulk stores.
+static int make_head_map_bf16_32(CUtensorMap* map, const void* base, int H, int T, int B, long long row_stride) {
+  auto enc = att_encode_fn();
+  if (enc == nullptr) return rgpt_set_error(RGPT_ERR_INTERNAL, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_stride * 2) % 16 != 0)
+    return rgpt_set_error(RGPT_ERR_MISALIGNED, "dv base/row stride not 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)ATT_D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ATT_D * 2, (cuuint64_t)row_stride * 2, (cuuint64_t)T * row_stride * 2};
+  cuuint32_t box[4] = {32, 1, 32, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return rgpt_set_error(RGPT_ERR_INTERNAL, "dv tensor map encode failed (%d)", (int)r);
+  return RGPT_OK;
+}
+
 // Bulk add of a 32 x 32 fp32 smem tile into global memory through a tensor map (rows past the
 // tensor's extent are skipped by the hardware). Coordinates are never negative here.
 __device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2,
@@ -538,7 +556,8 @@ constexpr int BWD_STAT_FLOATS = 128;              // one warp's 64 query LSEs (l
 __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const __grid_constant__ CUtensorMap tmDQ, AttnBwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const __grid_constant__ CUtensorMap tmDK,
+                    const __grid_constant__ CUtensorMap tmDV, AttnBwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;                     // 16 KB
@@ -706,7 +725,6 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     const int quarter = warp & 3;       // TMEM lane quadrant
     const int g = sw >> 2;              // softmax warpgroup = query half it handles
     const int r = quarter * 32 + lane;  // key row (S^T / dP^T / dV / dK) and query row (dQ)
-    const int key = k0 + r;
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     uint8_t* stage = sDQ + sw * DQ_STAGE_BYTES;
     bool ok = true;
@@ -861,33 +879,38 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     if (ok && nq > 0) ok = dq_out(nq - 1);
     if (lane == 0) bulk_wait0();  // every dQ reduce has landed before the CTA retires
     __syncwarp();
-    // dK, dV rows (key-major) once every query tile has been folded in: dq_full of the last tile
-    // means every earlier MMA (in-order tensor pipe) has completed. Every lane runs the
-    // warp-collective TMEM loads; only the stores are predicated on the row being inside T.
+    // dK, dV (key-major) once every query tile has been folded in: dq_full of the last tile means
+    // every earlier MMA (in-order tensor pipe) has completed. This warp's 32 key rows x 32 head
+    // columns are staged (dK fp32 in its dQ stage, dV bf16 in the now idle dS area) and written by
+    // TMA bulk stores; rows past T are clipped by the hardware.
     if (ok) {
-      const bool valid = key < p.T;
-      const long long row = (long long)b * p.T + (valid ? key : 0);
       uint32_t v[32];
-      tmem_ld32(t_lane + 256 + g * 32, v);
-      tmem_wait_ld();
-      if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(p.dv + row * p.dv_stride + h * ATT_D + g * 32);
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          dst[t] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
-                              pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
-                              pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
-                              pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
-      }
       tmem_ld32(t_lane + 320 + g * 32, v);
       tmem_wait_ld();
-      if (valid) {
-        float4* dkd = reinterpret_cast<float4*>(p.dk + row * p.dk_stride + h * ATT_D + g * 32);
 #pragma unroll
-        for (int t = 0; t < 8; ++t)
-          dkd[t] = make_float4(__uint_as_float(v[4 * t]) * p.scale, __uint_as_float(v[4 * t + 1]) * p.scale,
-                               __uint_as_float(v[4 * t + 2]) * p.scale, __uint_as_float(v[4 * t + 3]) * p.scale);
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(__uint_as_float(v[4 * j]) * p.scale, __uint_as_float(v[4 * j + 1]) * p.scale,
+                        __uint_as_float(v[4 * j + 2]) * p.scale, __uint_as_float(v[4 * j + 3]) * p.scale);
+      tmem_ld32(t_lane + 256 + g * 32, v);
+      tmem_wait_ld();
+      uint8_t* dv_stage = sDS + sw * 2048;  // 32 rows x 64 bytes, unswizzled
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        *reinterpret_cast<uint4*>(dv_stage + lane * 64 + t * 16) =
+            make_uint4(pack_bf16x2(__uint_as_float(v[8 * t]), __uint_as_float(v[8 * t + 1])),
+                       pack_bf16x2(__uint_as_float(v[8 * t + 2]), __uint_as_float(v[8 * t + 3])),
+                       pack_bf16x2(__uint_as_float(v[8 * t + 4]), __uint_as_float(v[8 * t + 5])),
+                       pack_bf16x2(__uint_as_float(v[8 * t + 6]), __uint_as_float(v[8 * t + 7])));
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && k0 + quarter * 32 < p.T) {
+        tma_store_4d(&tmDK, stage, g * 32, h, k0 + quarter * 32, b);
+        tma_store_4d(&tmDV, dv_stage, g * 32, h, k0 + quarter * 32, b);
+        bulk_commit();
+        bulk_wait0();
       }
+      __syncwarp();
     }
     tc_fence_before();
   }
@@ -992,6 +1015,9 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
   if ((st = make_head_map(&tv, qkvb + 2 * d, H, T, B, 3LL * d))) return st;
   if ((st = make_head_map(&tdo, dout, H, T, B, (long long)d))) return st;
   if ((st = make_head_map_f32(&tdq, dq, H, T, B, (long long)d))) return st;
+  CUtensorMap tdk, tdv;
+  if ((st = make_head_map_f32(&tdk, dk, H, T, B, dk_stride))) return st;
+  if ((st = make_head_map_bf16_32(&tdv, dv, H, T, B, dv_stride))) return st;
   AttnBwdParams p;
   p.B = B;
   p.T = T;
@@ -1012,6 +1038,6 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
     attr[dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  attn_bwd_kernel<<<grid, ATT_BWD_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, tdq, p);
+  attn_bwd_kernel<<<grid, ATT_BWD_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
   return rgpt_check_launch("attn_bwd_kernel");
 }
