@@ -11,7 +11,9 @@ step (d_model 512, 8 heads, 8 layers, squared-ReLU FFN, RMSNorm pre-norm,
 f_rmsnorm QK norm, RoPE, G1 gate, vocab 50304, seq 1024, micro-batch 16,
 Muon for 2-D weights + AdamW) on synthetic uniform token ids with
 random-init weights. Multi-GPU runs (torchrun) are weak-scaling data parallel:
-16 sequences per GPU, gradients averaged over NCCL by DistMuon.
+16 sequences per GPU, gradients averaged over NCCL by DistMuon. On one GPU the
+step is replayed as one CUDA graph (rgpt_b200.graph.GraphedTrainStep; --eager
+issues every kernel from Python instead); multi-GPU steps run eagerly.
 
 Printed (rank 0, one JSON line): value = whole-job tokens/s with inputs resident
 in HBM; e2e = tokens/s through the public API with the token ids copied from
@@ -156,14 +158,23 @@ def run_ours(args, wl):
     ids_dev = torch.empty_like(dev_batches[0])
     inv_accum = 1.0 / accum
 
-    def step(ids):
-        opt.zero_grad(set_to_none=True)
-        total = None
-        for a in range(accum):
-            total, _, _ = model.forward_loss(ids[a, :, :-1], ids[a, :, 1:])
-            (total * inv_accum).backward()
-        opt.step()
-        return total
+    graphed = None
+    if world == 1 and not args.eager:
+        # the whole step as one CUDA graph; 2 eager warm-up steps build the optimizer state first
+        from rgpt_b200.graph import GraphedTrainStep
+
+        graphed = GraphedTrainStep(model, opt, B, T, accum, warmup=2)
+        step, step_eager = graphed, graphed.eager
+    else:
+        def step(ids):
+            opt.zero_grad(set_to_none=True)
+            total = None
+            for a in range(accum):
+                total, _, _ = model.forward_loss(ids[a, :, :-1], ids[a, :, 1:])
+                (total * inv_accum).backward()
+            opt.step()
+            return total
+        step_eager = step
 
     def barrier():
         if dist is not None:
@@ -206,8 +217,11 @@ def run_ours(args, wl):
     barrier()
     e0.record()
     for i in range(args.steps):
-        ids_dev.copy_(host[i % n_batches], non_blocking=True)
-        total = step(ids_dev)
+        if graphed is not None:
+            total = step(host[i % n_batches])  # H2D copy into the graph's static id buffer
+        else:
+            ids_dev.copy_(host[i % n_batches], non_blocking=True)
+            total = step(ids_dev)
         loss_host[i:i + 1].copy_(total.detach().reshape(1), non_blocking=True)
     e1.record()
     barrier()
@@ -217,7 +231,7 @@ def run_ours(args, wl):
     nv.gemm_events = []
     barrier()
     for i in range(args.steps):
-        step(dev_batches[i % n_batches])
+        step_eager(dev_batches[i % n_batches])  # launch by launch, so each GEMM gets its own events
     barrier()
     ev, nv.gemm_events = nv.gemm_events, None
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in ev)
@@ -240,6 +254,7 @@ def run_ours(args, wl):
                    "vocab": cfg["vocab_size"], "seq_len": T, "micro_batch": B, "grad_accum": accum,
                    "global_batch": B * accum * world, "parallelism": f"dp{world}",
                    "optimizer": "Muon (5 NS steps) + AdamW", "dropout": 0.0,
+                   "launch": "one CUDA graph replay per step" if graphed is not None else "eager",
                    "l2": "no flush: each step's working set (activations + weights) is several GB, far above "
                          "the 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": host[0].numel() * 8,
@@ -338,6 +353,7 @@ def main():
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gpt-small")
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="issue every kernel from Python (no CUDA graph)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         log("note: warm-up raised to 3 steps")

@@ -76,9 +76,10 @@ int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bst
  * model/attention.py:56-61 (forward) and their autograd backward. */
 int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse,
                   int B, int T, int H, int d, void* stream);
-/* dout = dog*gate; dgate_pre = dog*o*gate*(1-gate); Dvec = rowsum(dout*o). gate may be null (ungated). */
+/* dout = dog*gate; dgate_pre = dog*o*gate*(1-gate); Dvec = rowsum(dout*o). gate may be null (ungated).
+ * dq_zero (optional, [B*T, d] fp32, 16-byte aligned) is zeroed: the dq accumulator of rgpt_attn_bwd. */
 int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,
-                       float* Dvec, int B, int T, int H, int d, void* stream);
+                       float* Dvec, float* dq_zero, int B, int T, int H, int d, void* stream);
 /* dq [B*T, d] fp32 is ACCUMULATED (caller zeroes it); dk fp32 and dv bf16 are written with row strides. */
 int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, const float* lse, const float* Dvec,
                   float* dq, float* dk, long long dk_stride, void* dv, long long dv_stride,
@@ -158,19 +159,26 @@ typedef struct RgptAdamwTensor {
 typedef struct RgptMuonTensor {
   float* param; const float* grad; unsigned short* mom; unsigned short* shadow;
 } RgptMuonTensor;
+/* Per-step scalars read from DEVICE memory instead of the by-value arguments when the `hp` pointer
+ * of an optimizer entry point is non-null (so that a captured CUDA graph of the step sees each
+ * step's learning rate and bias corrections). Layout, 8 floats per parameter group:
+ *   AdamW group: {lr, wd, beta1, beta2, eps, 1/(1-beta1^step), 1/sqrt(1-beta2^step), 0}
+ *   Muon group:  {beta, 1 - lr*wd, -muon_lr, 0, ...}                                        */
+#define RGPT_HP_FLOATS 8
 /* foreach_adamw_step (optimizer.py:80-116) over a device table of tensors split into chunks
  * (chunk_tensor[i], chunk_start[i]); shadow (bf16 copy of p) optional per tensor. */
 int rgpt_adamw(const RgptAdamwTensor* table, const int* chunk_tensor, const long long* chunk_start, int n_chunks,
-               int chunk_elems, float lr, float wd, float beta1, float beta2, float eps, int step, void* stream);
+               int chunk_elems, float lr, float wd, float beta1, float beta2, float eps, int step, const float* hp,
+               void* stream);
 /* muon_update's momentum/Nesterov/transposition (optimizer.py:51-69, :23-26) for n same-shape [R, C]
  * matrices into the bf16 NS stack X (zero-padded, leading dim ldx); sumsq[n] ACCUMULATES ||X||_F^2. */
 int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, void* X, long long x_bstride, int ldx,
-                   float beta, int nesterov, float* sumsq, void* stream);
+                   float beta, int nesterov, float* sumsq, const float* hp, void* stream);
 /* X /= max(||X||_F, 1e-7) per matrix (optimizer.py:31-32). */
 int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, int cols, int n, const float* sumsq, void* stream);
 /* p = p*(1 - lr*wd) - muon_lr * bf16(X*scale) (optimizer.py:209-227); shadow = bf16(p). */
 int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C, const void* X, long long x_bstride, int ldx,
-                    float lr, float wd, float muon_lr, float scale, void* stream);
+                    float lr, float wd, float muon_lr, float scale, const float* hp, void* stream);
 
 #ifdef __cplusplus
 }

@@ -485,8 +485,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 // do = dog * gate; dgate_pre = dog * o * gate * (1 - gate); D = rowsum(do * o)   (8 threads per (token, head))
 __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dog, const __nv_bfloat16* __restrict__ o,
                                      const __nv_bfloat16* __restrict__ gate, __nv_bfloat16* __restrict__ dout,
-                                     __nv_bfloat16* __restrict__ dgate_pre, float* __restrict__ Dvec, int B, int T,
-                                     int H, int d) {
+                                     __nv_bfloat16* __restrict__ dgate_pre, float* __restrict__ Dvec,
+                                     float* __restrict__ dq_zero, int B, int T, int H, int d) {
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long rowhead = gid >> 3;  // (token, head) index
   const int part = gid & 7;
@@ -516,6 +516,11 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dog, cons
     }
     *reinterpret_cast<uint4*>(dout + off) = make_uint4(do4[0], do4[1], do4[2], do4[3]);
     if (gate) *reinterpret_cast<uint4*>(dgate_pre + off) = make_uint4(dg4[0], dg4[1], dg4[2], dg4[3]);
+    if (dq_zero) {  // the attention backward accumulates dQ into this [B*T, d] fp32 buffer
+      float4* z = reinterpret_cast<float4*>(dq_zero + off);
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   dsum += __shfl_xor_sync(0xffffffffu, dsum, 1);
   dsum += __shfl_xor_sync(0xffffffffu, dsum, 2);
@@ -982,9 +987,11 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
 }
 
 extern "C" int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,
-                                  float* Dvec, int B, int T, int H, int d, void* stream) {
+                                  float* Dvec, float* dq_zero, int B, int T, int H, int d, void* stream) {
   int st = check_attn_args(B, T, H, d);
   if (st) return st;
+  if (reinterpret_cast<uintptr_t>(dq_zero) & 15)
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dq_zero must be 16-byte aligned");
   if (gate != nullptr && dgate_pre == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gate needs dgate_pre");
   const long long threads = (long long)B * T * H * 8;
   const int block = 256;
@@ -992,7 +999,7 @@ extern "C" int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* ga
   attn_bwd_prep_kernel<<<(unsigned)grid, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const __nv_bfloat16*>(dog), reinterpret_cast<const __nv_bfloat16*>(o),
       reinterpret_cast<const __nv_bfloat16*>(gate), reinterpret_cast<__nv_bfloat16*>(dout),
-      reinterpret_cast<__nv_bfloat16*>(dgate_pre), Dvec, B, T, H, d);
+      reinterpret_cast<__nv_bfloat16*>(dgate_pre), Dvec, dq_zero, B, T, H, d);
   return rgpt_check_launch("attn_bwd_prep_kernel");
 }
 

@@ -25,7 +25,11 @@ __device__ __forceinline__ float lerpf_torch(float a, float b, float w) {
 
 __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int* __restrict__ chunk_tensor,
                              const long long* __restrict__ chunk_start, int chunk_elems, float lr, float wd,
-                             float beta1, float beta2, float eps, float inv_bc1, float inv_sqrt_bc2) {
+                             float beta1, float beta2, float eps, float inv_bc1, float inv_sqrt_bc2,
+                             const float* __restrict__ hp) {
+  if (hp != nullptr) {  // this step's scalars from the device block (layout in rgpt.h)
+    lr = hp[0], wd = hp[1], beta1 = hp[2], beta2 = hp[3], eps = hp[4], inv_bc1 = hp[5], inv_sqrt_bc2 = hp[6];
+  }
   const int c = blockIdx.x;
   const RgptAdamwTensor t = tab[chunk_tensor[c]];
   const long long start = chunk_start[c];
@@ -47,44 +51,131 @@ __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int*
 }
 
 // ---------------------------------------------------------------------------- Muon
-// One CTA per 32x32 tile of one matrix. grid = (tiles_c, tiles_r, n_matrices).
-__global__ void muon_prep_kernel(const RgptMuonTensor* __restrict__ tab, int R, int C, int transpose,
-                                 __nv_bfloat16* __restrict__ X, long long x_bstride, int ldx, float beta,
-                                 int nesterov, float* __restrict__ sumsq) {
-  __shared__ float tile[32][33];
-  const RgptMuonTensor t = tab[blockIdx.z];
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8 threads
-  float ss = 0.f;
-  for (int rr = ty; rr < 32; rr += 8) {
-    const int r = r0 + rr, c = c0 + tx;
-    float x = 0.f;
-    if (r < R && c < C) {
-      const long long i = (long long)r * C + c;
-      const float gb = __bfloat162float(__float2bfloat16(t.grad[i]));  // grad.to(bf16)
-      const float m_old = __bfloat162float(__ushort_as_bfloat16(t.mom[i]));
-      const float m_new = __bfloat162float(__float2bfloat16(lerpf_torch(m_old, gb, 1.0f - beta)));
-      t.mom[i] = __bfloat16_as_ushort(__float2bfloat16(m_new));
-      x = nesterov ? __bfloat162float(__float2bfloat16(lerpf_torch(gb, m_new, beta))) : m_new;
-      ss += x * x;
-    }
-    tile[rr][tx] = x;
+// One CTA per 64x64 tile of one matrix; grid = (tiles_c, tiles_r, n_matrices). Each thread owns
+// groups of 8 consecutive columns of one row (16-byte bf16 / 2x16-byte fp32 accesses). The
+// transposed NS stack (R > C) is written through a shared tile of bf16 pairs: a thread then owns
+// 8 consecutive rows of two columns, i.e. 16 contiguous bytes of two rows of X. Groups that run
+// past the matrix edge, or tensors that are not 16-byte aligned, take the same path with scalar
+// accesses, so the arithmetic (and the result) does not depend on alignment.
+constexpr int MUON_TILE = 64;
+constexpr int MUON_LDW = MUON_TILE / 2 + 1;  // 32-bit words per shared row: 32 bf16 pairs + 1 pad
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+__device__ __forceinline__ void load8_f32(const float* p, bool vec, int n, float* v) {
+  if (vec) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = k < n ? p[k] : 0.f;
   }
-  __syncthreads();
-  __nv_bfloat16* Xb = X + (long long)blockIdx.z * x_bstride;
-  for (int rr = ty; rr < 32; rr += 8) {
-    if (!transpose) {
-      const int r = r0 + rr, c = c0 + tx;
-      if (r < R && c < C) Xb[(long long)r * ldx + c] = __float2bfloat16(tile[rr][tx]);
+}
+__device__ __forceinline__ void store8_f32(float* p, bool vec, int n, const float* v) {
+  if (vec) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < n) p[k] = v[k];
+  }
+}
+__device__ __forceinline__ void load8_bf16(const unsigned short* p, bool vec, int n, float* v) {
+  if (vec) {
+    const uint4 w = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(w4[j]);
+      v[2 * j] = f.x, v[2 * j + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = k < n ? __bfloat162float(__ushort_as_bfloat16(p[k])) : 0.f;
+  }
+}
+__device__ __forceinline__ void store8_bf16(unsigned short* p, bool vec, int n, const float* v) {
+  if (vec) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                              pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (k < n) p[k] = __bfloat16_as_ushort(__float2bfloat16(v[k]));
+  }
+}
+
+__global__ void __launch_bounds__(256) muon_prep_kernel(const RgptMuonTensor* __restrict__ tab, int R, int C,
+                                                        int transpose, unsigned short* __restrict__ X,
+                                                        long long x_bstride, int ldx, float beta, int nesterov,
+                                                        float* __restrict__ sumsq, const float* __restrict__ hp) {
+  if (hp != nullptr) beta = hp[0];
+  __shared__ uint32_t tile[MUON_TILE][MUON_LDW];
+  __shared__ float red[8];
+  const RgptMuonTensor t = tab[blockIdx.z];
+  const int r0 = blockIdx.y * MUON_TILE, c0 = blockIdx.x * MUON_TILE;
+  unsigned short* Xb = X + (long long)blockIdx.z * x_bstride;
+  const bool src_vec = (C % 8 == 0) && aligned16(t.grad) && aligned16(t.mom);
+  const bool x_vec = (ldx % 8 == 0) && (x_bstride % 8 == 0) && aligned16(X);
+  const int cg = threadIdx.x & 7;
+  float ss = 0.f;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int rr = pass * 32 + (threadIdx.x >> 3);
+    const int r = r0 + rr, c = c0 + cg * 8;
+    const int n = r < R ? min(8, C - c) : 0;  // valid elements of this group (<= 0: none)
+    float x[8];
+    if (n > 0) {
+      const long long i = (long long)r * C + c;
+      const bool vec = src_vec && n == 8;
+      float g[8], m[8];
+      load8_f32(t.grad + i, vec, n, g);
+      load8_bf16(t.mom + i, vec, n, m);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float gb = __bfloat162float(__float2bfloat16(g[k]));  // grad.to(bf16)
+        const float m_new = __bfloat162float(__float2bfloat16(lerpf_torch(m[k], gb, 1.0f - beta)));
+        m[k] = m_new;
+        x[k] = k < n ? (nesterov ? __bfloat162float(__float2bfloat16(lerpf_torch(gb, m_new, beta))) : m_new) : 0.f;
+        ss += x[k] * x[k];
+      }
+      store8_bf16(t.mom + i, vec, n, m);
+      if (!transpose) store8_bf16(Xb + (long long)r * ldx + c, x_vec && n == 8, n, x);
     } else {
-      // X[c][r] = g[r][c]: thread tx walks r (contiguous in X's row c)
-      const int c = c0 + rr, r = r0 + tx;
-      if (r < R && c < C) Xb[(long long)c * ldx + r] = __float2bfloat16(tile[tx][rr]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] = 0.f;
+    }
+    if (transpose) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tile[rr][cg * 4 + j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+    }
+  }
+  if (transpose) {
+    __syncthreads();
+    // X[c][r] = g[r][c]: this thread writes rows r0+8rg..+7 of columns c0+2cp and c0+2cp+1
+    const int rg = threadIdx.x & 7, cp = threadIdx.x >> 3;
+    uint32_t w[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[k] = tile[rg * 8 + k][cp];
+    const int r = r0 + rg * 8;
+    const int n = min(8, R - r);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + 2 * cp + h;
+      if (c < C && n > 0) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float2 f = unpack_bf16x2(w[k]);
+          v[k] = h ? f.y : f.x;
+        }
+        store8_bf16(Xb + (long long)c * ldx + r, x_vec && n == 8, n, v);
+      }
     }
   }
   ss = warp_sum(ss);
-  __shared__ float red[8];
-  if (tx == 0) red[ty] = ss;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x == 0) {
     float s = 0.f;
@@ -92,52 +183,99 @@ __global__ void muon_prep_kernel(const RgptMuonTensor* __restrict__ tab, int R, 
     atomicAdd(&sumsq[blockIdx.z], s);
   }
 }
-
 // X = bf16(X / max(sqrt(sumsq), 1e-7)) over the valid [rows, cols] block of each matrix.
 __global__ void ns_scale_kernel(__nv_bfloat16* __restrict__ X, long long x_bstride, int ldx, int rows, int cols,
                                 const float* __restrict__ sumsq) {
   const int b = blockIdx.y;
   const float inv = 1.0f / fmaxf(sqrtf(sumsq[b]), 1e-7f);
   __nv_bfloat16* Xb = X + (long long)b * x_bstride;
-  const int pairs = cols / 2;  // cols is even (the stacks are padded to multiples of 8)
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
-    __nv_bfloat162* row = reinterpret_cast<__nv_bfloat162*>(Xb + (long long)r * ldx);
-    for (int c = threadIdx.x; c < pairs; c += blockDim.x) {
-      float2 v = __bfloat1622float2(row[c]);
-      row[c] = __floats2bfloat162_rn(v.x * inv, v.y * inv);
+  const bool vec = (cols % 8 == 0) && (ldx % 8 == 0) && (x_bstride % 8 == 0) && aligned16(X);
+  if (vec) {
+    const int octs = cols / 8;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+      uint4* row = reinterpret_cast<uint4*>(Xb + (long long)r * ldx);
+      for (int c = threadIdx.x; c < octs; c += blockDim.x) {
+        uint4 w = row[c];
+        uint32_t* w4 = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 v = unpack_bf16x2(w4[j]);
+          w4[j] = pack_bf16x2(v.x * inv, v.y * inv);
+        }
+        row[c] = w;
+      }
     }
+    return;
+  }
+  // any width, stride or alignment: one 2-byte element per access
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    __nv_bfloat16* row = Xb + (long long)r * ldx;
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) row[c] = __float2bfloat16(__bfloat162float(row[c]) * inv);
   }
 }
 
-__global__ void muon_apply_kernel(const RgptMuonTensor* __restrict__ tab, int R, int C, int transpose,
-                                  const __nv_bfloat16* __restrict__ X, long long x_bstride, int ldx, float decay,
-                                  float neg_lr, float scale) {
-  __shared__ float tile[32][33];
+__global__ void __launch_bounds__(256) muon_apply_kernel(const RgptMuonTensor* __restrict__ tab, int R, int C,
+                                                         int transpose, const unsigned short* __restrict__ X,
+                                                         long long x_bstride, int ldx, float decay, float neg_lr,
+                                                         float scale, const float* __restrict__ hp) {
+  if (hp != nullptr) decay = hp[1], neg_lr = hp[2];
+  __shared__ uint32_t tile[MUON_TILE][MUON_LDW];
   const RgptMuonTensor t = tab[blockIdx.z];
-  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const __nv_bfloat16* Xb = X + (long long)blockIdx.z * x_bstride;
-  for (int rr = ty; rr < 32; rr += 8) {
-    if (!transpose) {
-      const int r = r0 + rr, c = c0 + tx;
-      tile[rr][tx] = (r < R && c < C) ? __bfloat162float(Xb[(long long)r * ldx + c]) : 0.f;
-    } else {
-      const int c = c0 + rr, r = r0 + tx;
-      tile[tx][rr] = (r < R && c < C) ? __bfloat162float(Xb[(long long)c * ldx + r]) : 0.f;
+  const int r0 = blockIdx.y * MUON_TILE, c0 = blockIdx.x * MUON_TILE;
+  const unsigned short* Xb = X + (long long)blockIdx.z * x_bstride;
+  const bool x_vec = (ldx % 8 == 0) && (x_bstride % 8 == 0) && aligned16(X);
+  const bool dst_vec = (C % 8 == 0) && aligned16(t.param) && (t.shadow == nullptr || aligned16(t.shadow));
+  if (transpose) {
+    // gather X[c][r0+8rg..+7] for columns c0+2cp, c0+2cp+1 into the shared [r][c] tile
+    const int rg = threadIdx.x & 7, cp = threadIdx.x >> 3;
+    const int r = r0 + rg * 8;
+    const int n = min(8, R - r);
+    float v[2][8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + 2 * cp + h;
+      if (c < C && n > 0) {
+        load8_bf16(Xb + (long long)c * ldx + r, x_vec && n == 8, n, v[h]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[h][k] = 0.f;
+      }
     }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tile[rg * 8 + k][cp] = pack_bf16x2(v[0][k], v[1][k]);
+    __syncthreads();
   }
-  __syncthreads();
-  for (int rr = ty; rr < 32; rr += 8) {
-    const int r = r0 + rr, c = c0 + tx;
-    if (r < R && c < C) {
-      const long long i = (long long)r * C + c;
-      const float u = __bfloat162float(__float2bfloat16(tile[rr][tx] * scale));  // upd.mul_(scale) in bf16
-      float p = t.param[i];
-      if (decay != 1.0f) p *= decay;
-      p += neg_lr * u;
-      t.param[i] = p;
-      if (t.shadow) t.shadow[i] = __bfloat16_as_ushort(__float2bfloat16(p));
+  const int cg = threadIdx.x & 7;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    const int rr = pass * 32 + (threadIdx.x >> 3);
+    const int r = r0 + rr, c = c0 + cg * 8;
+    const int n = r < R ? min(8, C - c) : 0;
+    if (n <= 0) continue;
+    float u[8];
+    if (transpose) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(tile[rr][cg * 4 + j]);
+        u[2 * j] = f.x, u[2 * j + 1] = f.y;
+      }
+    } else {
+      load8_bf16(Xb + (long long)r * ldx + c, x_vec && n == 8, n, u);
     }
+    const long long i = (long long)r * C + c;
+    const bool vec = dst_vec && n == 8;
+    float p[8];
+    load8_f32(t.param + i, vec, n, p);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float uk = __bfloat162float(__float2bfloat16(u[k] * scale));  // upd.mul_(scale) in bf16
+      float pk = p[k];
+      if (decay != 1.0f) pk *= decay;
+      pk += neg_lr * uk;
+      p[k] = pk;
+    }
+    store8_f32(t.param + i, vec, n, p);
+    if (t.shadow) store8_bf16(t.shadow + i, vec, n, p);
   }
 }
 
@@ -147,32 +285,35 @@ using namespace rgpt;
 
 extern "C" int rgpt_adamw(const RgptAdamwTensor* table, const int* chunk_tensor, const long long* chunk_start,
                           int n_chunks, int chunk_elems, float lr, float wd, float beta1, float beta2, float eps,
-                          int step, void* stream) {
+                          int step, const float* hp, void* stream) {
   if (n_chunks <= 0) return RGPT_OK;
-  if (step < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "adamw step must be >= 1");
-  const double bc1 = 1.0 - pow((double)beta1, (double)step);
-  const double bc2 = 1.0 - pow((double)beta2, (double)step);
+  float inv_bc1 = 0.f, inv_sqrt_bc2 = 0.f;
+  if (hp == nullptr) {  // else the bias corrections come from the device block
+    if (step < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "adamw step must be >= 1");
+    const double bc1 = 1.0 - pow((double)beta1, (double)step);
+    const double bc2 = 1.0 - pow((double)beta2, (double)step);
+    inv_bc1 = (float)(1.0 / bc1);
+    inv_sqrt_bc2 = (float)(1.0 / sqrt(bc2));
+  }
   adamw_kernel<<<n_chunks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      table, chunk_tensor, chunk_start, chunk_elems, lr, wd, beta1, beta2, eps, (float)(1.0 / bc1),
-      (float)(1.0 / sqrt(bc2)));
+      table, chunk_tensor, chunk_start, chunk_elems, lr, wd, beta1, beta2, eps, inv_bc1, inv_sqrt_bc2, hp);
   return rgpt_check_launch("adamw_kernel");
 }
 
 extern "C" int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, void* X, long long x_bstride, int ldx,
-                              float beta, int nesterov, float* sumsq, void* stream) {
+                              float beta, int nesterov, float* sumsq, const float* hp, void* stream) {
   const int transpose = R > C ? 1 : 0;
-  const int xr = transpose ? C : R, xc = transpose ? R : C;
+  const int xc = transpose ? R : C;
   if (ldx < xc) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "NS stack too narrow (ldx %d < %d)", ldx, xc);
-  (void)xr;
-  dim3 grid((C + 31) / 32, (R + 31) / 32, n);
+  dim3 grid((C + MUON_TILE - 1) / MUON_TILE, (R + MUON_TILE - 1) / MUON_TILE, n);
   muon_prep_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      table, R, C, transpose, reinterpret_cast<__nv_bfloat16*>(X), x_bstride, ldx, beta, nesterov, sumsq);
+      table, R, C, transpose, reinterpret_cast<unsigned short*>(X), x_bstride, ldx, beta, nesterov, sumsq, hp);
   return rgpt_check_launch("muon_prep_kernel");
 }
 
 extern "C" int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, int cols, int n, const float* sumsq,
                              void* stream) {
-  if (cols % 2 != 0 || ldx % 2 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_scale needs even cols and ldx");
+  if (ldx < cols) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_scale: ldx %d < cols %d", ldx, cols);
   const int gx = rows < 256 ? rows : 256;
   ns_scale_kernel<<<dim3(gx, n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<__nv_bfloat16*>(X), x_bstride, ldx, rows, cols, sumsq);
@@ -180,11 +321,12 @@ extern "C" int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, in
 }
 
 extern "C" int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C, const void* X, long long x_bstride,
-                               int ldx, float lr, float wd, float muon_lr, float scale, void* stream) {
+                               int ldx, float lr, float wd, float muon_lr, float scale, const float* hp,
+                               void* stream) {
   const int transpose = R > C ? 1 : 0;
-  dim3 grid((C + 31) / 32, (R + 31) / 32, n);
+  dim3 grid((C + MUON_TILE - 1) / MUON_TILE, (R + MUON_TILE - 1) / MUON_TILE, n);
   muon_apply_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      table, R, C, transpose, reinterpret_cast<const __nv_bfloat16*>(X), x_bstride, ldx, 1.0f - lr * wd, -muon_lr,
-      scale);
+      table, R, C, transpose, reinterpret_cast<const unsigned short*>(X), x_bstride, ldx, 1.0f - lr * wd, -muon_lr,
+      scale, hp);
   return rgpt_check_launch("muon_apply_kernel");
 }

@@ -468,8 +468,8 @@ class Engine:
         at = blk.attn
         nv.gemm(A.gb, W["wo"].t(), A.dog)
         nv.gemm(A.gb.t(), A.og[app].t(), G[pre + "attn.out_proj.weight"], epi=nv.EPI_ACCUM_F32, splitk=0)
-        nv.attn_bwd_prep(A.dog, A.o[app], A.gate[app], A.do, A.dgp if self.g1 else None, A.D, B, T, H)
-        A.dqa.zero_()
+        nv.attn_bwd_prep(A.dog, A.o[app], A.gate[app], A.do, A.dgp if self.g1 else None, A.D, B, T, H,
+                         dq_zero=A.dqa)
         nv.attn_bwd(A.qk[app], A.qkv[app], A.do, A.lse[app], A.D, A.dqa, A.dka, A.dqkv[:, 2 * d:], B, T, H)
         qs = self._qk_spec(at)
         qn = pre + "attn.qk_norm."

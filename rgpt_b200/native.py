@@ -121,11 +121,16 @@ def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: 
 
 
 def attn_bwd_prep(dog: torch.Tensor, o: torch.Tensor, gate: torch.Tensor | None, do: torch.Tensor,
-                  dgate_pre: torch.Tensor | None, D: torch.Tensor, B: int, T: int, H: int) -> None:
-    """do = dog*gate, dgate_pre = dog*o*gate*(1-gate), D = rowsum(do*o) per (token, head)."""
+                  dgate_pre: torch.Tensor | None, D: torch.Tensor, B: int, T: int, H: int,
+                  dq_zero: torch.Tensor | None = None) -> None:
+    """do = dog*gate, dgate_pre = dog*o*gate*(1-gate), D = rowsum(do*o) per (token, head);
+    dq_zero (the fp32 [B*T, d] dq accumulator of attn_bwd), when given, is zeroed in the same pass."""
     d = H * 64
-    _lib.call("rgpt_attn_bwd_prep", ptr(dog), ptr(o), ptr(gate), ptr(do), ptr(dgate_pre), ptr(D), B, T, H, d,
-              _lib.stream_ptr(o.device))
+    if dq_zero is not None and (dq_zero.dtype != torch.float32 or not dq_zero.is_contiguous()
+                                or dq_zero.numel() != B * T * d):
+        raise RuntimeError("attn_bwd_prep: dq_zero must be a contiguous fp32 [B*T, d] tensor")
+    _lib.call("rgpt_attn_bwd_prep", ptr(dog), ptr(o), ptr(gate), ptr(do), ptr(dgate_pre), ptr(D), ptr(dq_zero),
+              B, T, H, d, _lib.stream_ptr(o.device))
 
 
 def attn_bwd(qk: torch.Tensor, qkv: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, D: torch.Tensor,
@@ -211,21 +216,27 @@ def halt_losses(q: torch.Tensor, argmax: torch.Tensor, labels: torch.Tensor, dq:
 
 
 # ----------------------------------------------------------------------------- optimizer
+# hp: optional device pointer (int) to a parameter group's block of RGPT_HP_FLOATS scalars; when
+# given, the kernels read this step's lr / betas / bias corrections from it instead of the arguments.
+HP_FLOATS = 8
+
+
 def adamw(table: torch.Tensor, chunk_tensor: torch.Tensor, chunk_start: torch.Tensor, chunk_elems: int,
-          lr: float, wd: float, beta1: float, beta2: float, eps: float, step: int) -> None:
+          lr: float, wd: float, beta1: float, beta2: float, eps: float, step: int, hp: int | None = None) -> None:
     _lib.call("rgpt_adamw", ptr(table), ptr(chunk_tensor), ptr(chunk_start), chunk_tensor.numel(), chunk_elems,
-              float(lr), float(wd), float(beta1), float(beta2), float(eps), int(step), _lib.stream_ptr(table.device))
+              float(lr), float(wd), float(beta1), float(beta2), float(eps), int(step), hp,
+              _lib.stream_ptr(table.device))
 
 
-def muon_prep(table, n, R, C, X, beta, nesterov, sumsq) -> None:
+def muon_prep(table, n, R, C, X, beta, nesterov, sumsq, hp: int | None = None) -> None:
     _lib.call("rgpt_muon_prep", ptr(table), n, R, C, ptr(X), X.stride(0), X.stride(1), float(beta), int(nesterov),
-              ptr(sumsq), _lib.stream_ptr(X.device))
+              ptr(sumsq), hp, _lib.stream_ptr(X.device))
 
 
 def ns_scale(X, rows, cols, n, sumsq) -> None:
     _lib.call("rgpt_ns_scale", ptr(X), X.stride(0), X.stride(1), rows, cols, n, ptr(sumsq), _lib.stream_ptr(X.device))
 
 
-def muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale) -> None:
+def muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale, hp: int | None = None) -> None:
     _lib.call("rgpt_muon_apply", ptr(table), n, R, C, ptr(X), X.stride(0), X.stride(1), float(lr), float(wd),
-              float(muon_lr), float(scale), _lib.stream_ptr(X.device))
+              float(muon_lr), float(scale), hp, _lib.stream_ptr(X.device))

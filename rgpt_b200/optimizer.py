@@ -21,6 +21,7 @@ from __future__ import annotations
 import math
 from typing import Any, Dict, List, Optional, Tuple
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -28,6 +29,7 @@ from . import native as nv
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)  # optimizer.py:19
 _ADAM_CHUNK = 16384
+_HP_RING = 4  # pinned host slots for the per-step scalars (copies in flight before a slot is reused)
 
 
 def _muon_scale(m: int, n: int) -> float:
@@ -138,6 +140,65 @@ class Muon(torch.optim.Optimizer):
                         ns_steps=ns_steps, ns_coeffs=tuple(ns_coeffs))
         super().__init__(params, defaults)
         self._cache: Dict[Any, Any] = {}
+        self._hp_dev: Optional[torch.Tensor] = None
+
+    # ------------------------------------------------------------------ device scalars
+    def use_device_hparams(self) -> None:
+        """Make the update kernels read each step's scalars (learning rates, momentum, betas, AdamW
+        bias corrections) from a device block that stage_device_hparams() refills, instead of
+        kernel arguments. A captured CUDA graph of the step needs this: its kernel arguments are
+        frozen at capture, the block's contents are not. Call stage_device_hparams() before
+        every step from then on."""
+        if self._hp_dev is not None:
+            return
+        dev = next(p.device for g in self.param_groups for p in g["params"])
+        n = len(self.param_groups) * nv.HP_FLOATS
+        self._hp_dev = torch.zeros(n, device=dev, dtype=torch.float32)
+        self._hp_host = [torch.zeros(n, dtype=torch.float32).pin_memory() for _ in range(_HP_RING)]
+        self._hp_done: List[Optional[torch.cuda.Event]] = [None] * _HP_RING
+        self._hp_slot = 0
+
+    def stage_device_hparams(self) -> None:
+        """Compute the next step's per-group scalars on the host (advancing the AdamW step
+        counters) and enqueue their copy into the device block on the current stream. The values
+        are rounded exactly as the by-value path rounds them, so both paths update identically."""
+        if self._hp_dev is None:
+            raise RuntimeError("stage_device_hparams() needs use_device_hparams() first")
+        slot = self._hp_slot
+        if self._hp_done[slot] is not None:
+            self._hp_done[slot].synchronize()  # the copy that last read this pinned slot has run
+        buf = self._hp_host[slot]
+        v = buf.numpy()
+        v[:] = 0.0
+        f32 = np.float32
+        for gi, group in enumerate(self.param_groups):
+            o = gi * nv.HP_FLOATS
+            lr, wd = float(group["lr"]), float(group["weight_decay"])
+            if group.get("use_muon", False):
+                muon_lr = lr * float(group["muon_lr_multiplier"])
+                v[o] = f32(group["momentum"])
+                v[o + 1] = f32(1.0) - f32(lr) * f32(wd)  # rgpt_muon_apply's float 1 - lr*wd
+                v[o + 2] = -f32(muon_lr)
+            else:
+                beta1, beta2 = group["adam_betas"]
+                step_i = int(group.get("_adam_step", 0)) + 1
+                group["_adam_step"] = step_i
+                b1, b2 = float(f32(beta1)), float(f32(beta2))
+                bc1 = 1.0 - b1 ** step_i  # rgpt_adamw: double pow of the float betas
+                bc2 = 1.0 - b2 ** step_i
+                v[o:o + 7] = [f32(lr), f32(wd), f32(b1), f32(b2), f32(group["adam_eps"]), f32(1.0 / bc1),
+                              f32(1.0 / math.sqrt(bc2))]
+        self._hp_dev.copy_(buf, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self._hp_done[slot] = ev
+        self._hp_slot = (slot + 1) % _HP_RING
+
+    def _hp(self, gi: int) -> Optional[int]:
+        """Device address of group gi's scalar block, or None on the by-value path."""
+        if self._hp_dev is None:
+            return None
+        return self._hp_dev.data_ptr() + gi * nv.HP_FLOATS * 4
 
     # ------------------------------------------------------------------ grads
     @torch.no_grad()
@@ -209,11 +270,12 @@ class Muon(torch.optim.Optimizer):
             tables, ws = ent
             ws.sumsq.zero_()
             for R, C, off, n, table in tables:
-                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n])
+                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n],
+                             hp=self._hp(gi))
             nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
             out = newton_schulz_batched(ws, steps, coeffs)
             for R, C, off, n, table in tables:
-                nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C))
+                nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C), hp=self._hp(gi))
 
     def _adamw_group(self, gi, group, params):
         if not params:
@@ -222,8 +284,10 @@ class Muon(torch.optim.Optimizer):
         wd = float(group["weight_decay"])
         beta1, beta2 = group["adam_betas"]
         eps = float(group["adam_eps"])
-        step_i = int(group.get("_adam_step", 0)) + 1
-        group["_adam_step"] = step_i
+        step_i = int(group.get("_adam_step", 0))
+        if self._hp_dev is None:  # else stage_device_hparams() advanced it
+            step_i += 1
+            group["_adam_step"] = step_i
         for p in params:
             st = self.state[p]
             if len(st) == 0:
@@ -248,7 +312,7 @@ class Muon(torch.optim.Optimizer):
                    torch.tensor(cs, dtype=torch.int64).to(dev))
             self._cache[key] = ent
         table, ct, cs = ent
-        nv.adamw(table, ct, cs, _ADAM_CHUNK, lr, wd, float(beta1), float(beta2), eps, step_i)
+        nv.adamw(table, ct, cs, _ADAM_CHUNK, lr, wd, float(beta1), float(beta2), eps, step_i, hp=self._hp(gi))
 
 
 class DistMuon(Muon):
@@ -329,7 +393,8 @@ class DistMuon(Muon):
             ws.sumsq.zero_()
             # momentum (and the NS input) for every matrix: the momentum state stays replicated
             for R, C, owner, off, n, table in cls["segments"]:
-                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n])
+                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n],
+                             hp=self._hp(gi))
             s, e = cls["blocks"][rank]
             send = cls["send"]
             if e > s:
@@ -341,7 +406,8 @@ class DistMuon(Muon):
             maxc = cls["maxc"]
             for R, C, owner, off, n, table in cls["segments"]:
                 g0 = owner * maxc + (off - cls["blocks"][owner][0])
-                nv.muon_apply(table, n, R, C, cls["gathered"][g0:g0 + n], lr, wd, muon_lr, _muon_scale(R, C))
+                nv.muon_apply(table, n, R, C, cls["gathered"][g0:g0 + n], lr, wd, muon_lr, _muon_scale(R, C),
+                              hp=self._hp(gi))
 
     def _plan_sharded(self, params, rows_all, world):
         """Per shape class: matrices ordered by (owner, original shape), one prep/apply table per

@@ -11,7 +11,9 @@ sizes (16 x 1024 tokens, d_model 512, 8 heads, FFN 2048, vocabulary 50304):
   4. causal attention forward   (B 16, T 1024, H 8, head dim 64)
   5. causal attention backward  (same sizes; after its bf16-gate prep kernel)
   6. cross entropy with the gradient written in place (4096 rows x 50304)
-Device memory stays under 1 GB, so a multi-pass profiler capture saves and restores little.
+  7. lm_head forward GEMM  logits = h Wlm^T  (4096 x 50304, K = 512; CTA pairs, bf16 store)
+  8. G1 gate GEMM          gate = sigmoid(q_n Wg^T + bg)  (131072 x 64, K = 64; bias+sigmoid epilogue)
+Device memory stays under 2 GB, so a multi-pass profiler capture saves and restores little.
 """
 import torch
 
@@ -55,6 +57,14 @@ def main() -> None:
     labels = torch.randint(0, V, (Mc,), device=dev, generator=g)
     rows = torch.empty(Mc, device=dev); sb = torch.empty(4, device=dev); lo = torch.empty(1, device=dev)
     nv.cross_entropy(logits, labels, loss_rows=rows, scale_buf=sb, loss_out=lo, write_grad=True)
+    # 7 lm_head forward into bf16 logits (the same 4096 x 50304 buffer)
+    h, wlm = rb(Mc, d), rb(V, d)
+    nv.gemm(h, wlm, logits)
+    # 8 G1 gate of every (token, head): [M*H, 64] x [64, 64]^T, bias + sigmoid epilogue
+    qn, wg = rb(M * H, 64), rb(64, 64)
+    bg = torch.randn(64, device=dev, generator=g)
+    gate_out = torch.empty(M * H, 64, device=dev, dtype=torch.bfloat16)
+    nv.gemm(qn, wg, gate_out, epi=nv.EPI_BIAS_SIGMOID_BF16, colscale=bg)
     torch.cuda.synchronize()
     print("rgpt_b200.prof: ok")
 

@@ -61,8 +61,8 @@ def test_attention_fwd_bwd(cuda, B, T, H):
     do = torch.empty_like(o)
     dgp = torch.empty_like(o)
     D = torch.empty(B, H, T, device=cuda, dtype=torch.float32)
-    nv.attn_bwd_prep(dog, o, gate, do, dgp, D, B, T, H)
-    dq = torch.zeros(B * T, d, device=cuda, dtype=torch.float32)
+    dq = torch.full((B * T, d), 7.0, device=cuda, dtype=torch.float32)  # zeroed by the prep pass
+    nv.attn_bwd_prep(dog, o, gate, do, dgp, D, B, T, H, dq_zero=dq)
     dk = torch.empty(B * T, d, device=cuda, dtype=torch.float32)
     dqkv = torch.zeros(B * T, 3 * d, device=cuda, dtype=torch.bfloat16)
     nv.attn_bwd(qk, qkv, do, lse, D, dq, dk, dqkv[:, 2 * d:], B, T, H)

@@ -71,3 +71,70 @@ def test_muon_update_functional_matches_oracle(cuda):
         ur = O.muon_update(G, mr, 0.95, 5, True, O.muon_scale(96, 32))
         assert rel(u.float(), ur.float()) < 5e-2
         assert rel(m.float(), mr.float()) < 1e-2
+
+
+def _buf(shape, dtype, dev, misalign):
+    """A contiguous tensor whose storage starts 0 or 1 element past a 256-byte boundary."""
+    n = 1
+    for s in shape:
+        n *= s
+    flat = torch.zeros(n + 1, dtype=dtype, device=dev)
+    return flat[1:].view(*shape) if misalign else flat[:n].view(*shape)
+
+
+@pytest.mark.parametrize("shape", [(100, 37), (37, 100), (136, 72), (72, 200), (64, 64), (3, 520), (200, 8)])
+def test_muon_prep_apply_kernels_match_torch_and_paths_agree(cuda, shape):
+    """muon_prep / ns_scale / muon_apply element by element (optimizer.py:51-69, :199-227): the
+    16-byte vector path (aligned tensors, widths multiple of 8) and the scalar path (tensors one
+    element off alignment) agree, and both follow the torch op sequence."""
+    from rgpt_b200 import native as nv
+    from rgpt_b200.optimizer import _pad8, _table
+    R, C = shape
+    n = 2
+    beta, lr, wd, muon_lr, scale = 0.95, 6e-4, 0.1, 0.02, 1.7
+    gen = torch.Generator().manual_seed(R * 1000 + C)
+    grad = torch.randn(n, R, C, generator=gen) * 1e-2
+    mom0 = (torch.randn(n, R, C, generator=gen) * 1e-2).to(torch.bfloat16)
+    par0 = torch.randn(n, R, C, generator=gen) * 0.02
+    tr = R > C
+    xr, xc = (C, R) if tr else (R, C)
+    outs = []
+    for mis in (False, True):
+        g, m, p, sh = (_buf((n, R, C), dt, cuda, mis) for dt in (torch.float32, torch.bfloat16, torch.float32,
+                                                                  torch.bfloat16))
+        g.copy_(grad)
+        m.copy_(mom0)
+        p.copy_(par0)
+        X = _buf((n, _pad8(xr), _pad8(xc)), torch.bfloat16, cuda, mis)
+        ss = torch.zeros(n, device=cuda)
+        table = _table([[p[i].data_ptr(), g[i].data_ptr(), m[i].data_ptr(), sh[i].data_ptr()] for i in range(n)],
+                       cuda)
+        nv.muon_prep(table, n, R, C, X, beta, True, ss)
+        Xp = X.clone()
+        nv.ns_scale(X, xr, _pad8(xc), n, ss)
+        nv.muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale)
+        torch.cuda.synchronize()
+        outs.append([t.cpu() for t in (m, Xp, X, ss, p, sh)])
+    # momentum and the unscaled stack are bit-identical; the norm is summed with float atomics in
+    # no fixed order, so what depends on it agrees to rounding
+    for i, (a, b) in enumerate(zip(*outs)):
+        if i < 2:
+            assert torch.equal(a, b)
+        else:
+            torch.testing.assert_close(a.float(), b.float(), rtol=1e-5, atol=1e-7)
+    m, Xp, X, ss, p, sh = outs[0]
+    # torch op sequence on the CPU (float opmath, bf16 storage)
+    gb = grad.to(torch.bfloat16)
+    m_ref = mom0.clone()
+    m_ref.lerp_(gb, 1 - beta)
+    x_ref = gb.lerp(m_ref, beta)
+    xs = x_ref.transpose(1, 2) if tr else x_ref
+    assert (m.float() - m_ref.float()).abs().max() <= 2 ** -8 * m_ref.float().abs().max()
+    assert (Xp[:, :xr, :xc].float() - xs.float()).abs().max() <= 2 ** -8 * xs.float().abs().max()
+    assert Xp[:, xr:, :].abs().sum() == 0 and Xp[:, :, xc:].abs().sum() == 0  # padding stays zero
+    torch.testing.assert_close(ss, xs.float().pow(2).sum(dim=(1, 2)), rtol=1e-4, atol=0)
+    u = X[:, :xr, :xc].float()
+    u = u.transpose(1, 2) if tr else u
+    p_ref = par0 * (1 - lr * wd) - muon_lr * (u * scale).to(torch.bfloat16).float()
+    torch.testing.assert_close(p, p_ref, rtol=1e-6, atol=1e-8)
+    assert torch.equal(sh, p.to(torch.bfloat16))
