@@ -237,6 +237,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // every operand and output lives in memory the previous kernels use
+  griddep_launch();
   constexpr uint32_t O_COL = 128;  // TMEM columns: S0 [0,64) S1 [64,128) O [128,192)
 
   if (warp == 0) {
@@ -487,6 +489,8 @@ __global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dog, cons
                                      const __nv_bfloat16* __restrict__ gate, __nv_bfloat16* __restrict__ dout,
                                      __nv_bfloat16* __restrict__ dgate_pre, float* __restrict__ Dvec,
                                      float* __restrict__ dq_zero, int B, int T, int H, int d) {
+  griddep_wait();
+  griddep_launch();
   const long long gid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long rowhead = gid >> 3;  // (token, head) index
   const int part = gid & 7;
@@ -617,6 +621,8 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  griddep_wait();  // every operand and output lives in memory the previous kernels use
+  griddep_launch();
   // TMEM columns: half g: S^T [128g, 128g+64) dP^T [128g+64, 128g+128), overwritten after the softmax by
   // P^T [128g, 128g+32) and dS^T [128g+32, 128g+64) as packed bf16 pairs; dV [256,320) dK [320,384)
   // dQ [384,448); K [448,480) and V [480,512) as packed bf16 pairs (A operands read from TMEM).
@@ -982,7 +988,7 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
     attr[dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  attn_fwd_kernel<<<grid, ATT_THREADS, FWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tg, to, tog, p);
+  launch_pdl(attn_fwd_kernel, dim3(grid), dim3(ATT_THREADS), FWD_SMEM, reinterpret_cast<cudaStream_t>(stream), 1, tq, tk, tv, tg, to, tog, p);
   return rgpt_check_launch("attn_fwd_kernel");
 }
 
@@ -996,7 +1002,7 @@ extern "C" int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* ga
   const long long threads = (long long)B * T * H * 8;
   const int block = 256;
   const long long grid = (threads + block - 1) / block;
-  attn_bwd_prep_kernel<<<(unsigned)grid, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(attn_bwd_prep_kernel, dim3((unsigned)grid), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       reinterpret_cast<const __nv_bfloat16*>(dog), reinterpret_cast<const __nv_bfloat16*>(o),
       reinterpret_cast<const __nv_bfloat16*>(gate), reinterpret_cast<__nv_bfloat16*>(dout),
       reinterpret_cast<__nv_bfloat16*>(dgate_pre), Dvec, dq_zero, B, T, H, d);
@@ -1045,6 +1051,6 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
     attr[dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  attn_bwd_kernel<<<grid, ATT_BWD_THREADS, BWD_SMEM, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, tdo, tdq, tdk, tdv, p);
+  launch_pdl(attn_bwd_kernel, dim3(grid), dim3(ATT_BWD_THREADS), BWD_SMEM, reinterpret_cast<cudaStream_t>(stream), 1, tq, tk, tv, tdo, tdq, tdk, tdv, p);
   return rgpt_check_launch("attn_bwd_kernel");
 }

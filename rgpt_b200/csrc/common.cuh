@@ -38,6 +38,18 @@ __device__ __forceinline__ void record_device_error(int code) {
   atomicCAS(&g_rgpt_device_error, 0, code);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of this library is launched with programmatic stream serialization allowed
+// (launch_pdl below): it may be scheduled while the previous kernel of the stream is still
+// running, once every CTA of that kernel has triggered (griddep_launch) or exited. Its prologue
+// (barrier init, TMEM alloc, descriptor prefetch) then overlaps the previous kernel's tail.
+// Before its first global-memory access, EVERY thread calls griddep_wait(), which returns once
+// the previous kernel has completed and its writes are visible. Kernels with many short CTAs
+// trigger right after the wait; the persistent GEMM triggers once its last loads are issued, so
+// the next kernel's waiting CTAs do not sit beside it for its whole run.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(
@@ -376,5 +388,42 @@ enum RgptStatus {
 
 int rgpt_set_error(int code, const char* fmt, ...);
 int rgpt_check_launch(const char* what);
+
+// Host: launch `kernel` on `stream` with programmatic dependent launch allowed (and a 1-D cluster
+// of `cluster_x` CTAs when > 1). The kernel must call griddep_wait() before touching memory that
+// earlier work in the stream writes or reads. While the stream is being captured into a CUDA graph
+// the launch is an ordinary one (griddep_wait() then returns at once): a replayed graph already
+// starts each kernel node right behind the previous one, and programmatic edges measured slower.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  int n = 0;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    (void)cudaGetLastError();  // an unanswerable query leaves no error behind for the launch check
+    cap = cudaStreamCaptureStatusActive;  // and takes the ordinary launch
+  }
+  if (cap == cudaStreamCaptureStatusNone) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = cluster_x;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 int rgpt_check_device(int device);  // verifies sm_100 and caches SM count
 int rgpt_num_sms(int device);

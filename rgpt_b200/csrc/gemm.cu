@@ -214,6 +214,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // operands, C and the output come from / go to the previous kernels' memory
   // barriers of the pair's MMA-issuing CTA, as shared::cluster addresses
   const uint32_t full_bar0 = PAIR ? mapa_shared(smem_u32(full_bar), 0) : smem_u32(full_bar);
   const uint32_t tempty_bar0 = PAIR ? mapa_shared(smem_u32(tempty_bar), 0) : smem_u32(tempty_bar);
@@ -275,6 +276,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       }
+      griddep_launch();  // every load of this CTA is issued: the next kernel may start filling SMs
       if (!ok && rank == 0) {
         // Drain: wait (bounded) for every load already issued into the ring (the pair's loads
         // all complete on CTA 0's barriers; the final cluster barrier keeps CTA 1 alive meanwhile).
@@ -660,23 +662,11 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   }
   if constexpr (PAIR) {
     const int clusters = sh.num_units < max_clusters[dev] ? sh.num_units : max_clusters[dev];
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(GEMM_THREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, kern, ta, tb, td, td2, tc, sh, ep);
+    launch_pdl(kern, dim3(2 * clusters), dim3(GEMM_THREADS), smem, stream, 2, ta, tb, td, td2, tc, sh, ep);
   } else {
     const int nsm = rgpt_num_sms(dev);
     const int grid = sh.num_units < nsm ? sh.num_units : nsm;
-    kern<<<grid, GEMM_THREADS, smem, stream>>>(ta, tb, td, td2, tc, sh, ep);
+    launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), smem, stream, 1, ta, tb, td, td2, tc, sh, ep);
   }
   return rgpt_check_launch("gemm_bf16_tc_kernel");
 }

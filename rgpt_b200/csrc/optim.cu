@@ -18,15 +18,20 @@
 namespace rgpt {
 
 // ---------------------------------------------------------------------------- AdamW
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 __device__ __forceinline__ float lerpf_torch(float a, float b, float w) {
-  // torch's lerp: a + w (b - a) for w < 0.5, else b - (b - a)(1 - w)
-  return (w < 0.5f) ? a + w * (b - a) : b - (b - a) * (1.0f - w);
+  // torch's lerp: a + w (b - a) for w < 0.5, else b - (b - a)(1 - w), each as one fused step
+  const float d = b - a;
+  return (w < 0.5f) ? fmaf(w, d, a) : fmaf(-d, 1.0f - w, b);
 }
 
 __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int* __restrict__ chunk_tensor,
                              const long long* __restrict__ chunk_start, int chunk_elems, float lr, float wd,
                              float beta1, float beta2, float eps, float inv_bc1, float inv_sqrt_bc2,
                              const float* __restrict__ hp) {
+  griddep_wait();
+  griddep_launch();
   if (hp != nullptr) {  // this step's scalars from the device block (layout in rgpt.h)
     lr = hp[0], wd = hp[1], beta1 = hp[2], beta2 = hp[3], eps = hp[4], inv_bc1 = hp[5], inv_sqrt_bc2 = hp[6];
   }
@@ -35,16 +40,42 @@ __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int*
   const long long start = chunk_start[c];
   const long long end = min(start + (long long)chunk_elems, t.n);
   const float decay = 1.0f - lr * wd;
-  for (long long i = start + threadIdx.x; i < end; i += blockDim.x) {
-    float p = t.p[i];
-    const float g = t.g[i];
-    if (wd != 0.f) p *= decay;
-    const float m = lerpf_torch(t.m[i], g, 1.0f - beta1);
-    const float v = lerpf_torch(t.v[i], g * g, 1.0f - beta2);
+  // Every rounding spelled out (torch's op order: p*decay, lerps, sqrt(v)*c + eps, m/denom*c,
+  // p - lr*u as one fused step), so no expression has two products the compiler could pick
+  // between for contraction: the vector and scalar paths give identical bits.
+  auto update = [&](float& p, float g, float& m, float& v) {
+    if (wd != 0.f) p = __fmul_rn(p, decay);
+    m = lerpf_torch(m, g, 1.0f - beta1);
+    v = lerpf_torch(v, __fmul_rn(g, g), 1.0f - beta2);
+    const float denom = __fadd_rn(__fmul_rn(sqrtf(v), inv_sqrt_bc2), eps);
+    p = fmaf(-lr, __fmul_rn(__fdiv_rn(m, denom), inv_bc1), p);
+  };
+  long long i = start;
+  // 16-byte accesses over the aligned body of the chunk (chunk starts are multiples of 4)
+  if (aligned16(t.p) && aligned16(t.g) && aligned16(t.m) && aligned16(t.v) &&
+      (reinterpret_cast<uintptr_t>(t.shadow) & 7) == 0 && (start & 3) == 0) {
+    const long long end4 = start + ((end - start) & ~3ll);
+    for (long long j = start + 4ll * threadIdx.x; j < end4; j += 4ll * blockDim.x) {
+      float4 p = *reinterpret_cast<const float4*>(t.p + j);
+      const float4 g = *reinterpret_cast<const float4*>(t.g + j);
+      float4 m = *reinterpret_cast<const float4*>(t.m + j);
+      float4 v = *reinterpret_cast<const float4*>(t.v + j);
+      update(p.x, g.x, m.x, v.x);
+      update(p.y, g.y, m.y, v.y);
+      update(p.z, g.z, m.z, v.z);
+      update(p.w, g.w, m.w, v.w);
+      *reinterpret_cast<float4*>(t.m + j) = m;
+      *reinterpret_cast<float4*>(t.v + j) = v;
+      *reinterpret_cast<float4*>(t.p + j) = p;
+      if (t.shadow) *reinterpret_cast<uint2*>(t.shadow + j) = make_uint2(pack_bf16x2(p.x, p.y), pack_bf16x2(p.z, p.w));
+    }
+    i = end4;
+  }
+  for (i += threadIdx.x; i < end; i += blockDim.x) {
+    float p = t.p[i], m = t.m[i], v = t.v[i];
+    update(p, t.g[i], m, v);
     t.m[i] = m;
     t.v[i] = v;
-    const float denom = sqrtf(v) * inv_sqrt_bc2 + eps;
-    p = p - lr * ((m / denom) * inv_bc1);
     t.p[i] = p;
     if (t.shadow) t.shadow[i] = __bfloat16_as_ushort(__float2bfloat16(p));
   }
@@ -60,7 +91,6 @@ __global__ void adamw_kernel(const RgptAdamwTensor* __restrict__ tab, const int*
 constexpr int MUON_TILE = 64;
 constexpr int MUON_LDW = MUON_TILE / 2 + 1;  // 32-bit words per shared row: 32 bf16 pairs + 1 pad
 
-__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 __device__ __forceinline__ void load8_f32(const float* p, bool vec, int n, float* v) {
   if (vec) {
@@ -110,6 +140,8 @@ __global__ void __launch_bounds__(256) muon_prep_kernel(const RgptMuonTensor* __
                                                         int transpose, unsigned short* __restrict__ X,
                                                         long long x_bstride, int ldx, float beta, int nesterov,
                                                         float* __restrict__ sumsq, const float* __restrict__ hp) {
+  griddep_wait();
+  griddep_launch();
   if (hp != nullptr) beta = hp[0];
   __shared__ uint32_t tile[MUON_TILE][MUON_LDW];
   __shared__ float red[8];
@@ -186,6 +218,8 @@ __global__ void __launch_bounds__(256) muon_prep_kernel(const RgptMuonTensor* __
 // X = bf16(X / max(sqrt(sumsq), 1e-7)) over the valid [rows, cols] block of each matrix.
 __global__ void ns_scale_kernel(__nv_bfloat16* __restrict__ X, long long x_bstride, int ldx, int rows, int cols,
                                 const float* __restrict__ sumsq) {
+  griddep_wait();
+  griddep_launch();
   const int b = blockIdx.y;
   const float inv = 1.0f / fmaxf(sqrtf(sumsq[b]), 1e-7f);
   __nv_bfloat16* Xb = X + (long long)b * x_bstride;
@@ -218,6 +252,8 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const RgptMuonTensor* _
                                                          int transpose, const unsigned short* __restrict__ X,
                                                          long long x_bstride, int ldx, float decay, float neg_lr,
                                                          float scale, const float* __restrict__ hp) {
+  griddep_wait();
+  griddep_launch();
   if (hp != nullptr) decay = hp[1], neg_lr = hp[2];
   __shared__ uint32_t tile[MUON_TILE][MUON_LDW];
   const RgptMuonTensor t = tab[blockIdx.z];
@@ -270,9 +306,8 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const RgptMuonTensor* _
     for (int k = 0; k < 8; ++k) {
       const float uk = __bfloat162float(__float2bfloat16(u[k] * scale));  // upd.mul_(scale) in bf16
       float pk = p[k];
-      if (decay != 1.0f) pk *= decay;
-      pk += neg_lr * uk;
-      p[k] = pk;
+      if (decay != 1.0f) pk = __fmul_rn(pk, decay);
+      p[k] = fmaf(neg_lr, uk, pk);
     }
     store8_f32(t.param + i, vec, n, p);
     if (t.shadow) store8_bf16(t.shadow + i, vec, n, p);
@@ -295,7 +330,7 @@ extern "C" int rgpt_adamw(const RgptAdamwTensor* table, const int* chunk_tensor,
     inv_bc1 = (float)(1.0 / bc1);
     inv_sqrt_bc2 = (float)(1.0 / sqrt(bc2));
   }
-  adamw_kernel<<<n_chunks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(adamw_kernel, dim3(n_chunks), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       table, chunk_tensor, chunk_start, chunk_elems, lr, wd, beta1, beta2, eps, inv_bc1, inv_sqrt_bc2, hp);
   return rgpt_check_launch("adamw_kernel");
 }
@@ -306,7 +341,7 @@ extern "C" int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, 
   const int xc = transpose ? R : C;
   if (ldx < xc) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "NS stack too narrow (ldx %d < %d)", ldx, xc);
   dim3 grid((C + MUON_TILE - 1) / MUON_TILE, (R + MUON_TILE - 1) / MUON_TILE, n);
-  muon_prep_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(muon_prep_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       table, R, C, transpose, reinterpret_cast<unsigned short*>(X), x_bstride, ldx, beta, nesterov, sumsq, hp);
   return rgpt_check_launch("muon_prep_kernel");
 }
@@ -315,7 +350,7 @@ extern "C" int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, in
                              void* stream) {
   if (ldx < cols) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_scale: ldx %d < cols %d", ldx, cols);
   const int gx = rows < 256 ? rows : 256;
-  ns_scale_kernel<<<dim3(gx, n), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(ns_scale_kernel, dim3(dim3(gx, n)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       reinterpret_cast<__nv_bfloat16*>(X), x_bstride, ldx, rows, cols, sumsq);
   return rgpt_check_launch("ns_scale_kernel");
 }
@@ -325,7 +360,7 @@ extern "C" int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C,
                                void* stream) {
   const int transpose = R > C ? 1 : 0;
   dim3 grid((C + MUON_TILE - 1) / MUON_TILE, (R + MUON_TILE - 1) / MUON_TILE, n);
-  muon_apply_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(muon_apply_kernel, dim3(grid), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       table, R, C, transpose, reinterpret_cast<const unsigned short*>(X), x_bstride, ldx, 1.0f - lr * wd, -muon_lr,
       scale, hp);
   return rgpt_check_launch("muon_apply_kernel");

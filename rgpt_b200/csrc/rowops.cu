@@ -89,6 +89,8 @@ __global__ void rownorm_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* _
                                    const float* __restrict__ w, float temp, int kind, float eps, float alpha, int M,
                                    int d, const float* __restrict__ qw, const float* __restrict__ qb,
                                    float* __restrict__ qout) {
+  griddep_wait();
+  griddep_launch();
   const int warps = blockDim.x >> 5;
   const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -156,6 +158,8 @@ __global__ void __launch_bounds__(256, NV <= 4 ? 2 : 1) rownorm_bwd_kernel(const
                                    float* __restrict__ dtemp, const float* __restrict__ dq,
                                    const float* __restrict__ qw, const __nv_bfloat16* __restrict__ h,
                                    float* __restrict__ dqw, float* __restrict__ dqb) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ float red[];  // per-CTA column partials: [d] dw, [d] dls, [2d] dqw
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -430,6 +434,8 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_kernel(const __nv_bfloat1
                                                            __nv_bfloat16* __restrict__ qn_out,
                                                            const float* __restrict__ inv_freq, QkNormArgs na,
                                                            int M, int T, int H) {
+  griddep_wait();
+  griddep_launch();
   const PrepLane L = prep_lane(inv_freq);
   const int d = H * 64;
   const int hp_n = (H + 1) >> 1;
@@ -481,6 +487,8 @@ __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_kernel(
     const float* __restrict__ dqn_gate, const __nv_bfloat16* __restrict__ dgp, __nv_bfloat16* __restrict__ dqkv,
     float* __restrict__ dbg, float* __restrict__ dwq, float* __restrict__ dwk, float* __restrict__ dtq,
     float* __restrict__ dtk, const float* __restrict__ inv_freq, QkNormArgs na, int M, int T, int H) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float red[3][64];  // per-CTA column partials: dbg, dwq, dwk
   const PrepLane L = prep_lane(inv_freq);
   const int d = H * 64;
@@ -585,6 +593,8 @@ __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_kernel(
 // ============================================================================ embedding
 __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const float* __restrict__ emb,
                                      float* __restrict__ x, int M, int d, int V, int* __restrict__ err) {
+  griddep_wait();
+  griddep_launch();
   const int warps = blockDim.x >> 5;
   const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -602,6 +612,8 @@ __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const fl
 
 __global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const float* __restrict__ dx,
                                      float* __restrict__ demb, int M, int d, int V) {
+  griddep_wait();
+  griddep_launch();
   const int warps = blockDim.x >> 5;
   const long long row = (long long)blockIdx.x * warps + (threadIdx.x >> 5);
   if (row >= M) return;
@@ -617,6 +629,8 @@ __global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const fl
 // count valid labels; scale_out = grad_scale / count
 __global__ void ce_count_kernel(const long long* __restrict__ labels, int M, int ignore_index, float grad_scale,
                                 float* __restrict__ scale_out, float* __restrict__ count_out) {
+  griddep_wait();
+  griddep_launch();
   __shared__ int s[32];
   int c = 0;
   for (int i = threadIdx.x; i < M; i += blockDim.x) c += (labels[i] != ignore_index) ? 1 : 0;
@@ -638,6 +652,8 @@ __global__ void __launch_bounds__(512) cross_entropy_kernel(__nv_bfloat16* __res
                                                             const long long* __restrict__ labels, int ignore_index,
                                                             float* __restrict__ loss_rows, int* __restrict__ argmax,
                                                             const float* __restrict__ scale, int write_grad) {
+  griddep_wait();
+  griddep_launch();
   const long long row = blockIdx.x;
   __nv_bfloat16* x = logits + row * ld;
   const int nvec = V / 8;
@@ -782,6 +798,8 @@ __global__ void __launch_bounds__(CE_THREADS, 2)
     cross_entropy_smem_kernel(__nv_bfloat16* __restrict__ logits, long long ld, int V,
                               const long long* __restrict__ labels, int ignore_index, float* __restrict__ loss_rows,
                               int* __restrict__ argmax, const float* __restrict__ scale, int write_grad) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ __align__(128) uint8_t ce_row[];
   __shared__ uint64_t bar;
   __shared__ float red_f[CE_THREADS / 32];
@@ -911,10 +929,10 @@ static int launch_cross_entropy_rows(__nv_bfloat16* logits, long long ld, int M,
         return rgpt_check_launch("cross_entropy_smem set smem");
       attr[dev] = true;
     }
-    cross_entropy_smem_kernel<<<M, CE_THREADS, (size_t)V * 2, s>>>(logits, ld, V, labels, ignore_index, loss_rows,
+    launch_pdl(cross_entropy_smem_kernel, dim3(M), dim3(CE_THREADS), (size_t)V * 2, s, 1, logits, ld, V, labels, ignore_index, loss_rows,
                                                                     argmax, scale, write_grad);
   } else {
-    cross_entropy_kernel<<<M, 512, 0, s>>>(logits, ld, V, labels, ignore_index, loss_rows, argmax, scale,
+    launch_pdl(cross_entropy_kernel, dim3(M), dim3(512), 0, s, 1, logits, ld, V, labels, ignore_index, loss_rows, argmax, scale,
                                            write_grad);
   }
   return RGPT_OK;
@@ -923,6 +941,8 @@ static int launch_cross_entropy_rows(__nv_bfloat16* logits, long long ld, int M,
 // sum of loss rows / count -> out[0] (mean CE over valid labels), also adds into accum (optional)
 __global__ void ce_finalize_kernel(const float* __restrict__ loss_rows, int M, const float* __restrict__ count,
                                    float* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   __shared__ float s[32];
   float a = 0.f;
   for (int i = threadIdx.x; i < M; i += blockDim.x) a += loss_rows[i];
@@ -949,6 +969,8 @@ __device__ __forceinline__ float bce_logits(float x, float y) {
 __global__ void halt_losses_kernel(const float* __restrict__ q, const int* __restrict__ argmax,
                                    const long long* __restrict__ labels, int R, int M, float grad_scale,
                                    float* __restrict__ dq, float* __restrict__ losses) {
+  griddep_wait();
+  griddep_launch();
   const int m = blockIdx.x * blockDim.x + threadIdx.x;
   float lh = 0.f, lc = 0.f;
   if (m < M) {
@@ -1002,7 +1024,7 @@ extern "C" int rgpt_rownorm_fwd(const float* x, void* y, float* stat, const floa
   const int grid = (M + rows_per - 1) / rows_per;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   __nv_bfloat16* yb = reinterpret_cast<__nv_bfloat16*>(y);
-#define RN_F(N) rownorm_fwd_kernel<N><<<grid, block, 0, s>>>(x, yb, stat, w, temp, kind, eps, alpha, M, d, qw, qb, qout)
+#define RN_F(N) launch_pdl(rownorm_fwd_kernel<N>, dim3(grid), dim3(block), 0, s, 1, x, yb, stat, w, temp, kind, eps, alpha, M, d, qw, qb, qout)
   switch (nv) {
     case 1: RN_F(1); break;
     case 2: RN_F(2); break;
@@ -1038,8 +1060,7 @@ extern "C" int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w,
   auto launch = [&](auto nv_tag, auto qm_tag, auto dw_tag, auto dls_tag) {
     constexpr int N = decltype(nv_tag)::value;
     const int cap2 = rgpt_num_sms(dev) * (N <= 4 ? 2 : 1);
-    rownorm_bwd_kernel<N, decltype(qm_tag)::value, decltype(dw_tag)::value, decltype(dls_tag)::value>
-        <<<grid < cap2 ? grid : cap2, block, smem, s>>>(x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, ls,
+    launch_pdl(rownorm_bwd_kernel<N, decltype(qm_tag)::value, decltype(dw_tag)::value, decltype(dls_tag)::value>, dim3(grid < cap2 ? grid : cap2), dim3(block), smem, s, 1, x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, ls,
                                                         raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);
   };
   auto with_flags = [&](auto nv_tag) {
@@ -1113,8 +1134,7 @@ extern "C" int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const floa
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown QK norm kind %d", qk_kind);
   const QkNormArgs na = qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk);
   auto launch = [&](auto kind_tag) {
-    qkv_prep_fwd_kernel<decltype(kind_tag)::value>
-        <<<prep_grid(M, H, 4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    launch_pdl(qkv_prep_fwd_kernel<decltype(kind_tag)::value>, dim3(prep_grid(M, H, 4)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
             reinterpret_cast<const __nv_bfloat16*>(qkv), reinterpret_cast<__nv_bfloat16*>(qk),
             reinterpret_cast<__nv_bfloat16*>(qn), inv_freq, na, M, T, H);
   };
@@ -1134,8 +1154,7 @@ extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* 
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown QK norm kind %d", qk_kind);
   const QkNormArgs na = qk_args(qk_kind, eps, alpha, wq, wk, tq, tk, sq, sk);
   auto launch = [&](auto kind_tag) {
-    qkv_prep_bwd_kernel<decltype(kind_tag)::value>
-        <<<prep_grid(M, H, 3), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    launch_pdl(qkv_prep_bwd_kernel<decltype(kind_tag)::value>, dim3(prep_grid(M, H, 3)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
             reinterpret_cast<const __nv_bfloat16*>(qkv), dq, dk, dqn_gate,
             reinterpret_cast<const __nv_bfloat16*>(dgp), reinterpret_cast<__nv_bfloat16*>(dqkv), dbg, dwq, dwk, dtq,
             dtk, inv_freq, na, M, T, H);
@@ -1150,7 +1169,7 @@ extern "C" int rgpt_embedding_fwd(const long long* ids, const float* emb, float*
   const int block = 256, rows_per = block / 32;
   int* err = nullptr;
   cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_rgpt_device_error);
-  embedding_fwd_kernel<<<(M + rows_per - 1) / rows_per, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(embedding_fwd_kernel, dim3((M + rows_per - 1) / rows_per), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       ids, emb, x, M, d, V, err);
   return rgpt_check_launch("embedding_fwd_kernel");
 }
@@ -1159,7 +1178,7 @@ extern "C" int rgpt_embedding_bwd(const long long* ids, const float* dx, float* 
                                   void* stream) {
   if (d % 4 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "embedding dim must be a multiple of 4");
   const int block = 256, rows_per = block / 32;
-  embedding_bwd_kernel<<<(M + rows_per - 1) / rows_per, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(embedding_bwd_kernel, dim3((M + rows_per - 1) / rows_per), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       ids, dx, demb, M, d, V);
   return rgpt_check_launch("embedding_bwd_kernel");
 }
@@ -1172,18 +1191,18 @@ extern "C" int rgpt_cross_entropy(void* logits, long long ld, int M, int V, cons
   if ((write_grad || loss_out) && scale_buf == nullptr)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "scale_buf (2 floats) required for loss / grad");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (scale_buf) ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
+  if (scale_buf) launch_pdl(ce_count_kernel, dim3(1), dim3(1024), 0, s, 1, labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
   int st = launch_cross_entropy_rows(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, labels, ignore_index,
                                      loss_rows, argmax, scale_buf, write_grad, s);
   if (st) return st;
-  if (loss_out && loss_rows) ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
+  if (loss_out && loss_rows) launch_pdl(ce_finalize_kernel, dim3(1), dim3(1024), 0, s, 1, loss_rows, M, scale_buf + 1, loss_out);
   return rgpt_check_launch("cross_entropy_kernel");
 }
 
 extern "C" int rgpt_halt_losses(const float* q, const int* argmax, const long long* labels, int R, int M,
                                 float grad_scale, float* dq, float* losses, void* stream) {
   const int block = 256;
-  halt_losses_kernel<<<(M + block - 1) / block, block, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  launch_pdl(halt_losses_kernel, dim3((M + block - 1) / block), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
       q, argmax, labels, R, M, grad_scale, dq, losses);
   return rgpt_check_launch("halt_losses_kernel");
 }
@@ -1237,10 +1256,10 @@ extern "C" int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int
   float* loss_rows = scratch;                           // M floats, every one rewritten by this call
   float* scale_buf = scratch + RGPT_CE_NOALLOC_MAX_ROWS;  // {grad_scale/count, count}, rewritten by this call
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  ce_count_kernel<<<1, 1024, 0, s>>>(labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
+  launch_pdl(ce_count_kernel, dim3(1), dim3(1024), 0, s, 1, labels, M, ignore_index, grad_scale, scale_buf, scale_buf + 1);
   if ((st = launch_cross_entropy_rows(reinterpret_cast<__nv_bfloat16*>(logits), ld, M, V, labels, ignore_index,
                                       loss_rows, argmax, scale_buf, write_grad, s)))
     return st;
-  ce_finalize_kernel<<<1, 1024, 0, s>>>(loss_rows, M, scale_buf + 1, loss_out);
+  launch_pdl(ce_finalize_kernel, dim3(1), dim3(1024), 0, s, 1, loss_rows, M, scale_buf + 1, loss_out);
   return rgpt_check_launch("cross_entropy_noalloc");
 }
