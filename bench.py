@@ -58,7 +58,7 @@ OPT = dict(lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)  # conf/training/
 # Measured DRAM traffic (read + write) per tcgen05 GEMM launch, averaged over the 168 GEMM
 # launches of one gpt-small step: ncu dram__bytes_read.sum + dram__bytes_write.sum
 # (profiles/gemm_gpt_small_step_dram.md). Workloads without a capture report null.
-GEMM_TRAFFIC = {"gpt-small": 83.47e6}
+GEMM_TRAFFIC = {"gpt-small": 84.33e6}
 
 
 def flops_per_token(cfg, T):
