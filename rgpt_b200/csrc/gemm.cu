@@ -7,14 +7,15 @@
 // forward projections are K-major/K-major, dX = dY*W uses an MN-major B, and
 // dW = dY^T*X uses MN-major A and B, so no operand is ever transposed in HBM.
 //
-// CTA layout (64 + 32 * GEMM_EPI_WARPS threads, one CTA per SM, persistent over output tiles):
+// CTA layout (64 + 32 * EW threads, EW = 4 or 8 epilogue warps; one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer: 128-byte-swizzled tiles into a STAGES-deep smem ring
 //   warp 1      allocates TMEM, issues tcgen05.mma (one elected thread), commits
 //   warps 2..   epilogue: warp w owns TMEM lane quadrant w % 4 (32 accumulator rows) and,
 //               with 8 epilogue warps, half of the tile's columns; per column chunk it
-//               tcgen05.ld's the fp32 accumulator, applies the fused epilogue, stages the
-//               result in swizzled smem and writes it with a TMA bulk store (or a TMA
-//               bulk reduce-add for accumulating outputs)
+//               tcgen05.ld's the fp32 accumulator, applies the fused epilogue (an input C
+//               is read by each thread for its own row with 16-byte loads, one chunk ahead),
+//               stages the result in swizzled smem and writes it with a TMA bulk store (or a
+//               TMA bulk reduce-add for accumulating outputs)
 // Large GEMMs run on CTA pairs (a cluster of two SMs): one cta_group::2 MMA computes a
 // 256 x 256 tile from 128 rows of A and 128 rows of B staged in each SM's shared memory,
 // which halves the B operand's shared-memory and L2 traffic per SM.
@@ -56,29 +57,42 @@ struct EpiParams {
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_EPI_WARPS = 4;  // 4: one per TMEM lane quadrant; 8: two per quadrant, splitting the columns
-constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
+// Epilogue warps per CTA (EW): 4 = one per TMEM lane quadrant; 8 = two per quadrant, each taking half
+// of the tile's columns, for the epilogues that read an input C (their per-chunk work is the longest),
+// so that two warps per SM sub-partition hide each other's latency (measured 2-5 % faster there;
+// the two-output activation forward measured slower with 8).
+__host__ __device__ constexpr int gemm_epi_warps(int epi) {
+  return (epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32) ? 8 : 4;
+}
+__host__ __device__ constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr int GROUP_M = 8;
 constexpr uint32_t EPI_STAGE_BYTES = 4096;  // one warp's 32 rows x 128 bytes
-
-constexpr int C_DEPTH = 3;  // epilogue input (C) chunks in flight per epilogue warp
 
 __host__ __device__ constexpr bool epi_reads_c(int epi) {
   return epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32;
 }
+// bytes per element of the epilogue input C: bf16 for ACT_BWD / POLY, fp32 for RESID
+__host__ __device__ constexpr int epi_c_bytes(int epi) { return epi == RGPT_EPI_RESID_F32 ? 4 : 2; }
 
-template <int BN, int STAGES, bool PAIR = false, bool CIN = false>
+template <int BN, int STAGES, bool PAIR, int EW>
 struct GemmSmem {
   static constexpr uint32_t A_BYTES = GEMM_BM * GEMM_BK * 2;              // this CTA's 128 rows of A
   static constexpr uint32_t B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;  // a CTA pair splits B's rows
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t EPI_BYTES = GEMM_EPI_WARPS * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
-  // per-warp ring of TMA-loaded epilogue-input chunks (32 rows x 128 bytes each)
-  static constexpr uint32_t C_BYTES = CIN ? GEMM_EPI_WARPS * C_DEPTH * EPI_STAGE_BYTES : 0;
+  static constexpr uint32_t EPI_BYTES = EW * 2 * EPI_STAGE_BYTES;  // 2 staging buffers per epilogue warp
   static constexpr uint32_t BAR_BYTES = 512;
-  static constexpr uint32_t TOTAL =
-      STAGES * STAGE_BYTES + EPI_BYTES + C_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
+  static constexpr uint32_t TOTAL = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;  // +1024 alignment slack
 };
+
+// 16 bytes of global memory through L1 (the epilogue's C rows: a row's 128-byte chunk is read
+// as 8 such loads, so the line's later 16-byte pieces hit L1).
+__device__ __forceinline__ uint4 ld_global_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
 
 __device__ __forceinline__ void decode_unit(int u, const GemmShape& sh, int& b, int& mt, int& nt, int& ks) {
   ks = u % sh.splitk;
@@ -149,12 +163,13 @@ __device__ __forceinline__ void act_bwd32(float* v, const uint4* c) {
   }
 }
 template <int BN, int STAGES, int A_MN, int B_MN, int EPI, bool PAIR, int ACT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmD2,
-                        const __grid_constant__ CUtensorMap tmC, GemmShape sh, EpiParams ep) {
+                        GemmShape sh, EpiParams ep) {
   constexpr bool reads_c = epi_reads_c(EPI);
-  using L = GemmSmem<BN, STAGES, PAIR, reads_c>;
+  constexpr int EW = gemm_epi_warps(EPI);
+  using L = GemmSmem<BN, STAGES, PAIR, EW>;
   constexpr int NUM_ACC = 512 / BN;  // TMEM accumulator buffers (2 for 256-wide tiles, 4 for 128-wide)
   constexpr uint32_t TMEM_COLS = NUM_ACC * BN;
   constexpr int TILE_M = PAIR ? 2 * GEMM_BM : GEMM_BM;
@@ -166,13 +181,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::A_BYTES;
   uint8_t* sEpi = sB + STAGES * L::B_BYTES;
-  uint8_t* sC = sEpi + L::EPI_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sC + L::C_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + L::EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint64_t* tempty_bar = tfull_bar + NUM_ACC;
-  uint64_t* cfull_bar = tempty_bar + NUM_ACC;  // [GEMM_EPI_WARPS * C_DEPTH]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(cfull_bar + GEMM_EPI_WARPS * C_DEPTH);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + NUM_ACC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -186,10 +199,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int i = 0; i < GEMM_EPI_WARPS * C_DEPTH; ++i) mbar_init(&cfull_bar[i], 1);
     for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], PAIR ? 2 * GEMM_EPI_WARPS : GEMM_EPI_WARPS);
+      mbar_init(&tempty_bar[a], PAIR ? 2 * EW : EW);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -198,7 +210,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmD);
-    if constexpr (reads_c) tma_prefetch_desc(&tmC);
   }
   if (warp == 1) {
     if constexpr (PAIR) {
@@ -345,7 +356,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ------------------------------------------------------------ epilogue warps
     const int quarter = warp & 3;          // TMEM lane quadrant this warp may access
     const int col_half = (warp - 2) >> 2;  // which part of the tile's columns this warp writes
-    constexpr int COLS = BN * 4 / GEMM_EPI_WARPS;
+    constexpr int COLS = BN * 4 / EW;
     uint8_t* buf0 = sEpi + (warp - 2) * 2 * EPI_STAGE_BYTES;
     uint8_t* buf1 = buf0 + EPI_STAGE_BYTES;
     int which = 0;
@@ -356,68 +367,49 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const bool scaled = alpha != 1.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // Epilogue input C arrives by TMA: 32-row x 128-byte chunks into a per-warp C_DEPTH ring.
-    // Lane 0 keeps up to C_DEPTH chunks in flight, running ahead across tile boundaries, so the
-    // next tile's first chunks load while this tile is being written. A warp's live chunks
-    // (inside M and N) are a prefix of its columns; only those are loaded and consumed.
+    // Epilogue input C (bf16 for ACT_BWD / POLY, fp32 for RESID): each thread reads its own output
+    // row's 128 bytes of every column chunk straight from global memory as eight 16-byte loads
+    // (the line's later pieces hit L1). The next chunk's loads are issued before the current chunk
+    // is processed, and a tile's first chunk before the wait for the tile's accumulator, so the
+    // load latency hides behind the MMAs and the previous chunk's math.
     constexpr int CW = bf16_out ? 64 : 32;  // columns per chunk
-    uint8_t* cring = sC + (warp - 2) * C_DEPTH * EPI_STAGE_BYTES;
-    uint64_t* cbar = cfull_bar + (warp - 2) * C_DEPTH;
-    uint32_t c_issued = 0, c_used = 0;
-    bool c_ok = true;
-    int iu = first_unit, ic = 0, ilive = -1;  // lane 0's issue cursor (unit, chunk, live chunks of unit)
-    auto tile_origin = [&](int uu, int& b_, int& r0, int& col0) {
-      int mt_, nt_, ks_;
-      decode_unit(uu, sh, b_, mt_, nt_, ks_);
-      r0 = mt_ * TILE_M + rank * GEMM_BM + quarter * 32;
-      col0 = nt_ * BN + col_half * COLS;
-    };
-    auto c_fill = [&]() {
-      while (c_issued - c_used < (uint32_t)C_DEPTH && iu < sh.num_units) {
-        int b_, r0, col0;
-        tile_origin(iu, b_, r0, col0);
-        if (ilive < 0) ilive = r0 < sh.M ? max(0, min(COLS / CW, (sh.N - col0 + CW - 1) / CW)) : 0;
-        if (ic >= ilive) {
-          iu += unit_step;
-          ic = 0;
-          ilive = -1;
-          continue;
+    constexpr int CE = epi_c_bytes(EPI);   // bytes per C element
+    constexpr int EPV = 16 / CE;           // C elements per 16-byte load
+    auto c_load = [&](int b_, int row, int col, uint4 (&cc)[8]) {
+      const uint8_t* base = reinterpret_cast<const uint8_t*>(ep.c) + ((long long)b_ * ep.c_bstride +
+                                                                     (long long)row * ep.ldc) * CE;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = col + j * EPV;
+        if (row < sh.M && c + EPV <= sh.N) {
+          cc[j] = ld_global_v4(base + (long long)c * CE);
+        } else {
+          // ragged edge (past N inside the last vector, or rows/columns outside the matrix): zeros
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          if (row < sh.M) {
+#pragma unroll
+            for (int i = 0; i < EPV; ++i) {
+              if (c + i < sh.N) {
+                if constexpr (CE == 2)
+                  w[i >> 1] |= (uint32_t)(*reinterpret_cast<const unsigned short*>(base + (long long)(c + i) * 2))
+                               << (16 * (i & 1));
+                else
+                  w[i] = *reinterpret_cast<const uint32_t*>(base + (long long)(c + i) * 4);
+              }
+            }
+          }
+          cc[j] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        uint64_t* bar = &cbar[c_issued % C_DEPTH];
-        mbar_arrive_expect_tx(bar, EPI_STAGE_BYTES);
-        tma_load_3d(cring + (c_issued % C_DEPTH) * EPI_STAGE_BYTES, &tmC, bar, col0 + ic * CW, r0, b_);
-        ++c_issued;
-        ++ic;
       }
     };
-    auto c_get = [&](uint4 (&cc)[8]) {  // this row's 128 bytes of the oldest chunk, then refill
-      int okc = 1;
-      if (lane == 0) okc = mbar_wait(&cbar[c_used % C_DEPTH], (c_used / C_DEPTH) & 1u, abort_flag) ? 1 : 0;
-      okc = __shfl_sync(0xffffffffu, okc, 0);
-      if (!okc) {
-        c_ok = false;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) cc[j] = make_uint4(0, 0, 0, 0);
-        return;
-      }
-      uint8_t* buf = cring + (c_used % C_DEPTH) * EPI_STAGE_BYTES;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cc[j] = *reinterpret_cast<const uint4*>(stage_ptr(buf, lane, j));
-      ++c_used;
-      __syncwarp();
-      if (lane == 0) {
-        fence_proxy_async_smem();  // our reads of the buffer come before the next TMA write into it
-        c_fill();
-      }
-    };
-    if constexpr (reads_c) {
-      if (lane == 0) c_fill();
-    }
     for (int u = first_unit; u < sh.num_units; u += unit_step) {
       int b, mt, nt, ks;
       decode_unit(u, sh, b, mt, nt, ks);
       const int row0 = mt * TILE_M + rank * GEMM_BM + quarter * 32;  // first output row of this warp
       const bool rows_live = row0 < sh.M;
+      const int cbeg = col_half * COLS, cend = cbeg + COLS;  // this warp's columns of the tile
+      uint4 cnext[8];
+      if constexpr (reads_c) c_load(b, row0 + lane, nt * BN + cbeg, cnext);  // ahead of the accumulator
       int ok = 1;
       if (lane == 0) ok = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -425,19 +417,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if constexpr (bf16_out) {
-        auto chunk_bf16 = [&](int c0) {
+        auto chunk_bf16 = [&](int c0, const uint4 (&cc)[8]) {
           const int gn0 = nt * BN + c0;
           const bool live = rows_live && gn0 < sh.N;  // warp-uniform
           uint8_t* s0 = which ? buf1 : buf0;
           uint8_t* s1 = which ? buf0 : buf1;
-          uint4 cc[8];
           if (live) {
             if (lane == 0) {
               if (dual) bulk_wait_read_0();
               else bulk_wait_read_1();  // the store issued from this buffer two chunks ago has read it
             }
             __syncwarp();
-            if constexpr (reads_c) c_get(cc);
           }
           uint32_t rr[2][32];
           tmem_ld32(t_row + c0, rr[0]);  // both 32-column halves in flight, one wait
@@ -501,10 +491,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!dual) which ^= 1;
         };
 #pragma unroll 1
-        for (int c0 = col_half * COLS; c0 < (col_half + 1) * COLS; c0 += 64) chunk_bf16(c0);
+        for (int c0 = cbeg; c0 < cend; c0 += CW) {
+          uint4 cc[8];
+          if constexpr (reads_c) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cc[j] = cnext[j];
+            if (c0 + CW < cend) c_load(b, row0 + lane, nt * BN + c0 + CW, cnext);
+          }
+          chunk_bf16(c0, cc);
+        }
       } else {
         constexpr bool resid = EPI == RGPT_EPI_RESID_F32;
-        auto chunk_f32 = [&](int c0) {
+        auto chunk_f32 = [&](int c0, const uint4 (&cc)[8]) {
           const int gn0 = nt * BN + c0;
           const bool live = rows_live && gn0 < sh.N;
           uint32_t r[32];
@@ -527,8 +525,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           __syncwarp();
           if constexpr (resid) {
-            uint4 cc[8];
-            c_get(cc);
             if (ep.has_d2) stage_f32x32(s1, lane, v);  // raw branch output
             const float* cs = reinterpret_cast<const float*>(cc);
 #pragma unroll
@@ -552,7 +548,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (!dual) which ^= 1;
         };
 #pragma unroll 1
-        for (int c0 = col_half * COLS; c0 < (col_half + 1) * COLS; c0 += 32) chunk_f32(c0);
+        for (int c0 = cbeg; c0 < cend; c0 += CW) {
+          uint4 cc[8];
+          if constexpr (reads_c) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cc[j] = cnext[j];
+            if (c0 + CW < cend) c_load(b, row0 + lane, nt * BN + c0 + CW, cnext);
+          }
+          chunk_f32(c0, cc);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -564,12 +568,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         acc = 0;
         acc_phase ^= 1u;
       }
-      if (!c_ok) break;
-    }
-    if constexpr (reads_c) {  // C loads still in flight (only after a timed-out wait) land before exit
-      if (lane == 0)
-        for (; c_used < c_issued; ++c_used) mbar_wait(&cbar[c_used % C_DEPTH], (c_used / C_DEPTH) & 1u, nullptr);
-      __syncwarp();
     }
     if (lane == 0) bulk_wait_all();  // every bulk store has landed before the CTA retires
     __syncwarp();
@@ -626,14 +624,22 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_
   return make_tmap_3d(map, ptr, 2, inner, outer, batch, ld_elems, bstride_elems, box_inner, box_outer);
 }
 
+// Operand stages that fit beside EW warps' staging buffers (at most `want`).
+template <int BN, bool PAIR, int EW>
+constexpr int gemm_fit_stages(int want) {
+  using L1 = GemmSmem<BN, 1, PAIR, EW>;
+  const int fit = (int)((232448u - L1::EPI_BYTES - L1::BAR_BYTES - 1024u) / L1::STAGE_BYTES);
+  return fit < want ? fit : want;
+}
+
 template <int BN, int STAGES_IN, int A_MN, int B_MN, int EPI, bool PAIR, int ACT = ACT_NONE>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& td2,
-                       const CUtensorMap& tc, const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
-  // epilogues that read C give up operand stages for their per-warp C ring
-  constexpr bool CIN = epi_reads_c(EPI);
-  constexpr int STAGES = !CIN ? STAGES_IN : (BN == 256 && !PAIR ? 3 : 4);
+                       const GemmShape& sh, const EpiParams& ep, cudaStream_t stream, int dev) {
+  constexpr int EW = gemm_epi_warps(EPI);
+  constexpr int STAGES = gemm_fit_stages<BN, PAIR, EW>(STAGES_IN);
+  constexpr int THREADS = gemm_threads(EW);
   auto kern = gemm_bf16_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, PAIR, ACT>;
-  constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR, CIN>::TOTAL;
+  constexpr uint32_t smem = GemmSmem<BN, STAGES, PAIR, EW>::TOTAL;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the per-CTA limit");
   static bool attr_set[64] = {false};
   static int max_clusters[64] = {0};
@@ -643,7 +649,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     if (PAIR) {
       cudaLaunchConfig_t q = {};
       q.gridDim = dim3(2 * rgpt_num_sms(dev), 1, 1);
-      q.blockDim = dim3(GEMM_THREADS, 1, 1);
+      q.blockDim = dim3(THREADS, 1, 1);
       q.dynamicSmemBytes = smem;
       cudaLaunchAttribute qa[1];
       qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -662,21 +668,21 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
   }
   if constexpr (PAIR) {
     const int clusters = sh.num_units < max_clusters[dev] ? sh.num_units : max_clusters[dev];
-    launch_pdl(kern, dim3(2 * clusters), dim3(GEMM_THREADS), smem, stream, 2, ta, tb, td, td2, tc, sh, ep);
+    launch_pdl(kern, dim3(2 * clusters), dim3(THREADS), smem, stream, 2, ta, tb, td, td2, sh, ep);
   } else {
     const int nsm = rgpt_num_sms(dev);
     const int grid = sh.num_units < nsm ? sh.num_units : nsm;
-    launch_pdl(kern, dim3(grid), dim3(GEMM_THREADS), smem, stream, 1, ta, tb, td, td2, tc, sh, ep);
+    launch_pdl(kern, dim3(grid), dim3(THREADS), smem, stream, 1, ta, tb, td, td2, sh, ep);
   }
   return rgpt_check_launch("gemm_bf16_tc_kernel");
 }
 
 template <int BN, int STAGES, int A_MN, int B_MN, bool PAIR>
 static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-                        const CUtensorMap& td2, const CUtensorMap& tc, const GemmShape& sh, const EpiParams& ep,
+                        const CUtensorMap& td2, const GemmShape& sh, const EpiParams& ep,
                         cudaStream_t s, int dev) {
 #define RGPT_GEMM_EPI_CASE(E) \
-  case E: return launch_gemm<BN, STAGES, A_MN, B_MN, E, PAIR>(ta, tb, td, td2, tc, sh, ep, s, dev);
+  case E: return launch_gemm<BN, STAGES, A_MN, B_MN, E, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   switch (epi) {
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_BF16)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_STORE_F32)
@@ -687,24 +693,24 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
       const bool fwd = epi == RGPT_EPI_ACT_FWD;
 #define RGPT_GEMM_ACT_CASE(A)                                                                                      \
   case A:                                                                                                          \
-    return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, A>(ta, tb, td, td2, tc, sh, ep, s, dev) \
-               : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, A>(ta, tb, td, td2, tc, sh, ep, s, dev);
+    return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, A>(ta, tb, td, td2, sh, ep, s, dev) \
+               : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, A>(ta, tb, td, td2, sh, ep, s, dev);
       switch (ep.act) {
         RGPT_GEMM_ACT_CASE(ACT_SQRELU)
         RGPT_GEMM_ACT_CASE(ACT_GELU)
         RGPT_GEMM_ACT_CASE(ACT_SILU)
         RGPT_GEMM_ACT_CASE(ACT_MISH)
         default:
-          return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, ACT_NONE>(ta, tb, td, td2, tc, sh,
+          return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, ACT_NONE>(ta, tb, td, td2, sh,
                                                                                           ep, s, dev)
-                     : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, ACT_NONE>(ta, tb, td, td2, tc, sh,
+                     : launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_BWD, PAIR, ACT_NONE>(ta, tb, td, td2, sh,
                                                                                           ep, s, dev);
       }
 #undef RGPT_GEMM_ACT_CASE
     }
     RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
-    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, tc, sh, ep, s, dev);
+    default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   }
 #undef RGPT_GEMM_EPI_CASE
 }
@@ -712,22 +718,22 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
 // Tile configurations: 128 x 128 (6 stages), 128 x 256 (4 stages), and the CTA pair's
 // 256 x 256 (6 stages of 128 x 64 A + 128 x 64 B per CTA).
 static int dispatch_gemm(int BN, bool pair, int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
-                         const CUtensorMap& td, const CUtensorMap& td2, const CUtensorMap& tc, const GemmShape& sh,
+                         const CUtensorMap& td, const CUtensorMap& td2, const GemmShape& sh,
                          const EpiParams& ep, cudaStream_t s, int dev) {
   const int key = (pair ? 8 : 0) | (BN == 256 ? 4 : 0) | (a_mn ? 2 : 0) | (b_mn ? 1 : 0);
   switch (key) {
-    case 0: return dispatch_epi<128, 6, 0, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 1: return dispatch_epi<128, 6, 0, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 2: return dispatch_epi<128, 6, 1, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 3: return dispatch_epi<128, 6, 1, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 4: return dispatch_epi<256, 4, 0, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 5: return dispatch_epi<256, 4, 0, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 6: return dispatch_epi<256, 4, 1, 0, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 7: return dispatch_epi<256, 4, 1, 1, false>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 12: return dispatch_epi<256, 6, 0, 0, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 13: return dispatch_epi<256, 6, 0, 1, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 14: return dispatch_epi<256, 6, 1, 0, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
-    case 15: return dispatch_epi<256, 6, 1, 1, true>(epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+    case 0: return dispatch_epi<128, 6, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 1: return dispatch_epi<128, 6, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 2: return dispatch_epi<128, 6, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 3: return dispatch_epi<128, 6, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 4: return dispatch_epi<256, 4, 0, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 5: return dispatch_epi<256, 4, 0, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 6: return dispatch_epi<256, 4, 1, 0, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 7: return dispatch_epi<256, 4, 1, 1, false>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 12: return dispatch_epi<256, 6, 0, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 13: return dispatch_epi<256, 6, 0, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 14: return dispatch_epi<256, 6, 1, 0, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
+    case 15: return dispatch_epi<256, 6, 1, 1, true>(epi, ta, tb, td, td2, sh, ep, s, dev);
     default: return rgpt_set_error(RGPT_ERR_INTERNAL, "no GEMM configuration for key %d", key);
   }
 }
@@ -843,12 +849,13 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
     td2 = td;
   }
 
-  // epilogue input C: the same 32-row x 128-byte boxes as the output (bf16 C for ACT_BWD / POLY,
-  // fp32 for RESID)
-  CUtensorMap tc = td;
+  // epilogue input C (bf16 for ACT_BWD / POLY, fp32 for RESID) is read with 16-byte loads
   if (epi_reads_c(epi)) {
-    const int cb = (epi == RGPT_EPI_RESID_F32) ? 4 : 2;
-    if ((st = make_tmap_3d(&tc, C, cb, N, M, batch, ldc, c_bstride, cb == 4 ? 32 : 64, 32))) return st;
+    const long long cb = epi_c_bytes(epi);
+    if (C == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "epilogue %d needs its input C", epi);
+    if (ldc < N) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ldc (%lld) < N (%d)", ldc, N);
+    if ((reinterpret_cast<uintptr_t>(C) & 15) != 0 || (ldc * cb) % 16 != 0 || (batch > 1 && (c_bstride * cb) % 16 != 0))
+      return rgpt_set_error(RGPT_ERR_MISALIGNED, "C must be 16-byte aligned with 16-byte row and batch strides");
   }
 
   EpiParams ep;
@@ -864,5 +871,5 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   ep.has_d2 = has_d2 ? 1 : 0;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return dispatch_gemm(BN, pair, a_mn_major, b_mn_major, epi, ta, tb, td, td2, tc, sh, ep, s, dev);
+  return dispatch_gemm(BN, pair, a_mn_major, b_mn_major, epi, ta, tb, td, td2, sh, ep, s, dev);
 }

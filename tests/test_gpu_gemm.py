@@ -212,3 +212,28 @@ def test_gemm_cta_pair_batched_poly_and_accum(cuda):
     ref = dw + dy.float().t() @ xin.float()
     nv.gemm(dy.t(), xin.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
     assert rel_err(dw, ref) < 1e-4
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 1003, 200), (4160, 2043, 1096)])
+def test_gemm_c_epilogues_ragged_edges(cuda, M, N, K):
+    # Epilogues that read an input C (activation backward, residual add, Newton-Schulz polynomial)
+    # with ragged M, N not a multiple of the 16-byte vector, and padded leading dimensions; the
+    # second shape runs on CTA pairs.
+    g = torch.Generator(device=cuda).manual_seed(13)
+    a = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    ref = a.float() @ w.float().t()
+    ldb = (N + 7) // 8 * 8 + 8  # bf16 leading dims: multiples of 8 elements (16 bytes)
+    ldf = (N + 3) // 4 * 4 + 4  # fp32 leading dims: multiples of 4
+    pre = torch.randn(M, ldb, device=cuda, generator=g).bfloat16()[:, :N]
+    dpre = torch.full((M, ldb), 7.0, device=cuda, dtype=torch.bfloat16)[:, :N]
+    nv.gemm(a, w, dpre, epi=nv.EPI_ACT_BWD, act=nv.act_id("squared_relu"), c=pre)
+    assert rel_err(dpre, ref * ref_act_grad("squared_relu", pre.float())) < 2e-2
+    x = torch.randn(M, ldf, device=cuda, generator=g)[:, :N]
+    res = torch.full((M, ldf), 7.0, device=cuda)[:, :N]
+    nv.gemm(a, w, res, epi=nv.EPI_RESID_F32, c=x)
+    assert rel_err(res, x + ref) < 1e-5
+    c = torch.randn(M, ldb, device=cuda, generator=g).bfloat16()[:, :N]
+    out = torch.full((M, ldb), 7.0, device=cuda, dtype=torch.bfloat16)[:, :N]
+    nv.gemm(a, w, out, epi=nv.EPI_POLY_BF16, alpha=0.5, beta=-1.5, c=c)
+    assert rel_err(out, 0.5 * ref - 1.5 * c.float()) < 1e-2
