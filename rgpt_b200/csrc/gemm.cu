@@ -779,9 +779,11 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   sh.N = N;
   sh.K = K;
   sh.batch = batch;
-  // 256-wide tiles unless at most half the SMs would get one. A 128 x 128 x 16 MMA costs nearly
-  // as much issue time as a 128 x 256 x 16 one (measured ~125 vs ~135 SM cycles), so halving the
-  // tile only pays when both widths fit in one wave. Accumulating GEMMs keep the wide tile (fewer
+  // 256-wide tiles unless at most half the SMs would get one. Both widths run the tensor pipe at
+  // full rate (a 128 x N x 16 MMA takes 64 SM cycles at N = 128 and 128 at N = 256; only N = 64
+  // falls short at ~55), but a 128 x 128 tile moves 64 bytes of operands from L2 per 1024 FLOP
+  // against 48 for 128 x 256, and measured 15-40 % slower on the step's GEMMs; halving the tile
+  // only pays when both widths fit in one wave. Accumulating GEMMs keep the wide tile (fewer
   // operand re-reads) and split K instead.
   const int m128 = (M + GEMM_BM - 1) / GEMM_BM;
   int BN = (N > 128) ? 256 : 128;
