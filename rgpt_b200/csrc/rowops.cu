@@ -22,6 +22,8 @@
 // Backward: dx = s (a.dy) + 2 s'(S) (sum a.dy.x) x.
 #include <math.h>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "rgpt.h"
 
@@ -779,10 +781,46 @@ __global__ void __launch_bounds__(512) cross_entropy_kernel(__nv_bfloat16* __res
 
 // Row-in-shared-memory variant for V % 8 == 0 and V * 2 bytes <= CE_SMEM_MAX: one bulk copy
 // brings the row into shared memory (two CTAs per SM, so one row's copy overlaps the other's
-// math), then three passes over shared memory: max + argmax, sum of exp2, and the gradient
-// row written straight to HBM. Logits are read from HBM once and dlogits written once.
+// math), then three passes over shared memory: max + argmax (packed bf16 compares), the sum of
+// e = exp2((x - max) log2 e) with e written back in place as fp16, and the gradient e * scale / sum
+// (minus scale at the label) written straight to HBM. Logits are read from HBM once, dlogits written
+// once, and each logit costs one exp2 (the gradient's softmax carries e's fp16 rounding, <= 2^-11
+// relative, before its bf16 rounding).
 constexpr int CE_THREADS = 512;
 constexpr uint32_t CE_SMEM_MAX = 112 * 1024;
+
+// Packed fp32 pairs on the FMA pipe (fma/add/mul.rn.f32x2: two IEEE round-to-nearest results per
+// instruction, bit-identical to the scalar fmaf / + / *).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 __device__ __forceinline__ void ce_unpack8(const uint4& u, float (&f)[8]) {
   const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
@@ -826,15 +864,24 @@ __global__ void __launch_bounds__(CE_THREADS, 2)
     return;
   }
   const uint4* s4 = reinterpret_cast<const uint4*>(ce_row);
+  // the label's logit, read before pass 2 overwrites the row with exponentials
+  const float xl = (threadIdx.x == 0 && valid) ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ce_row)[label])
+                                               : 0.f;
 
-  // pass 1: max and first index of the max
+  // pass 1: max (packed bf16 compares; exact) and the first index of the max
   float m = -INFINITY;
   int besti = 0x7fffffff;
   for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
-    float f[8];
-    ce_unpack8(s4[v], f);
-    const float lm = fmaxf(fmaxf(fmaxf(f[0], f[1]), fmaxf(f[2], f[3])), fmaxf(fmaxf(f[4], f[5]), fmaxf(f[6], f[7])));
-    if (lm > m) {
+    const uint4 u = s4[v];
+    const __nv_bfloat162 h01 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&u.x),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    const __nv_bfloat162 h23 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&u.z),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&u.w));
+    const float2 hm = __bfloat1622float2(__hmax2(h01, h23));
+    const float lm = fmaxf(hm.x, hm.y);
+    if (lm > m) {  // strictly greater: the earliest vector holding the max keeps it
+      float f[8];
+      ce_unpack8(u, f);
       int e = 7;
 #pragma unroll
       for (int k = 6; k >= 0; --k) e = (f[k] == lm) ? k : e;
@@ -868,19 +915,33 @@ __global__ void __launch_bounds__(CE_THREADS, 2)
   }
   __syncthreads();  // red_f is reused below
 
-  // pass 2: sum of exp(x - m) in base 2
+  // pass 2: e = exp2((x - m) log2 e), summed, and kept in place as fp16 for pass 3 (e is in (0, 1])
   const float m2 = m * LOG2E;
-  float s0 = 0.f, s1 = 0.f;
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+  uint4* s4w = reinterpret_cast<uint4*>(ce_row);
+  const float2 l2e = make_float2(LOG2E, LOG2E), nm2 = make_float2(-m2, -m2);
   for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
     float f[8];
     ce_unpack8(s4[v], f);
+    float e[8];
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      s0 += ex2_approx(fmaf(f[e], LOG2E, -m2));
-      s1 += ex2_approx(fmaf(f[e + 1], LOG2E, -m2));
+    for (int k = 0; k < 4; ++k) {
+      const float2 t = ffma2(make_float2(f[2 * k], f[2 * k + 1]), l2e, nm2);
+      e[2 * k] = ex2_approx(t.x);
+      e[2 * k + 1] = ex2_approx(t.y);
+    }
+    acc0 = fadd2(acc0, make_float2(e[0], e[1]));
+    acc1 = fadd2(acc1, make_float2(e[2], e[3]));
+    acc0 = fadd2(acc0, make_float2(e[4], e[5]));
+    acc1 = fadd2(acc1, make_float2(e[6], e[7]));
+    if (write_grad) {
+      __half2 h[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(e[2 * k], e[2 * k + 1]);
+      s4w[v] = *reinterpret_cast<const uint4*>(h);
     }
   }
-  float sum = warp_sum(s0 + s1);
+  float sum = warp_sum((acc0.x + acc0.y) + (acc1.x + acc1.y));
   if (lane == 0) red_f[wid] = sum;
   __syncthreads();
   sum = 0.f;
@@ -888,30 +949,33 @@ __global__ void __launch_bounds__(CE_THREADS, 2)
   for (int w = 0; w < CE_THREADS / 32; ++w) sum += red_f[w];
   const float lse2 = m2 + log2f(sum);
   if (threadIdx.x == 0) {
-    if (loss_rows) {
-      const float xl = valid ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(ce_row)[label]) : 0.f;
-      loss_rows[row] = valid ? lse2 * 0.69314718055994531f - xl : 0.f;
-    }
+    if (loss_rows) loss_rows[row] = valid ? lse2 * 0.69314718055994531f - xl : 0.f;
     if (argmax) argmax[row] = besti;
   }
   if (!write_grad) return;
 
-  // pass 3: dlogits = (softmax - onehot) * scale, overwriting the row in HBM
+  // pass 3: dlogits = (softmax - onehot) * scale = e * (scale / sum) - onehot * scale, overwriting the
+  // row in HBM (each thread reads back only the vectors it wrote in pass 2)
   const int label_vec = valid ? (int)(label >> 3) : -1;
   const int label_e = (int)(label & 7);
+  const float k = sc / sum;
+  const float2 k2 = make_float2(k, k);
   uint4* xo = reinterpret_cast<uint4*>(x);
   for (int v = threadIdx.x; v < nvec; v += CE_THREADS) {
-    float f[8];
-    ce_unpack8(s4[v], f);
+    const uint4 u = s4[v];
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+    float2 p[4];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) f[e] = ex2_approx(fmaf(f[e], LOG2E, -lse2));
+    for (int q = 0; q < 4; ++q) p[q] = fmul2(__half22float2(*reinterpret_cast<const __half2*>(&w4[q])), k2);
     if (v == label_vec) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e == label_e) f[e] -= 1.f;
+      for (int q = 0; q < 4; ++q) {
+        if (2 * q == label_e) p[q].x -= sc;
+        if (2 * q + 1 == label_e) p[q].y -= sc;
+      }
     }
-    xo[v] = make_uint4(pack_bf16x2(f[0] * sc, f[1] * sc), pack_bf16x2(f[2] * sc, f[3] * sc),
-                       pack_bf16x2(f[4] * sc, f[5] * sc), pack_bf16x2(f[6] * sc, f[7] * sc));
+    xo[v] = make_uint4(pack_bf16x2(p[0].x, p[0].y), pack_bf16x2(p[1].x, p[1].y), pack_bf16x2(p[2].x, p[2].y),
+                       pack_bf16x2(p[3].x, p[3].y));
   }
 }
 
