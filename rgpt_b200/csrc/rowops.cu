@@ -444,15 +444,17 @@ __global__ void __launch_bounds__(256, 4) qkv_prep_fwd_kernel(const __nv_bfloat1
   const float4 aq = qk_affine4(na, true, L.i0), ak = qk_affine4(na, false, L.i0);
   long long u0, u1;
   prep_units((long long)M * hp_n, u0, u1);
-  int cur_tok = -1;
   float4 c = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (long long u = u0; u < u1; ++u) {
-    const int tok = (int)(u / hp_n);
-    const int h = (int)(u % hp_n) * 2 + L.half;
-    if (tok != cur_tok) {
-      cur_tok = tok;
+  // (token, head pair) of unit u, walked incrementally (no 64-bit division per unit)
+  int tok = (int)(u0 / hp_n), hp = (int)(u0 % hp_n);
+  if (u0 < u1) rope_angles(L, (float)(tok % T), c, sn);
+  for (long long u = u0; u < u1; ++u, ++hp) {
+    if (hp == hp_n) {
+      hp = 0;
+      ++tok;
       rope_angles(L, (float)(tok % T), c, sn);
     }
+    const int h = hp * 2 + L.half;
     const bool live = h < H;
     const size_t col = (size_t)h * 64 + L.i0;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = x;
@@ -503,15 +505,17 @@ __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_kernel(
   float acc_tq = 0.f, acc_tk = 0.f;
   long long u0, u1;
   prep_units((long long)M * hp_n, u0, u1);
-  int cur_tok = -1;
   float4 c = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (long long u = u0; u < u1; ++u) {
-    const int tok = (int)(u / hp_n);
-    const int h = (int)(u % hp_n) * 2 + L.half;
-    if (tok != cur_tok) {
-      cur_tok = tok;
+  // (token, head pair) of unit u, walked incrementally (no 64-bit division per unit)
+  int tok = (int)(u0 / hp_n), hp = (int)(u0 % hp_n);
+  if (u0 < u1) rope_angles(L, (float)(tok % T), c, sn);
+  for (long long u = u0; u < u1; ++u, ++hp) {
+    if (hp == hp_n) {
+      hp = 0;
+      ++tok;
       rope_angles(L, (float)(tok % T), c, sn);
     }
+    const int h = hp * 2 + L.half;
     const bool live = h < H;
     const size_t col = (size_t)h * 64 + L.i0;
     const size_t rq = (size_t)tok * 3 * d + col;
