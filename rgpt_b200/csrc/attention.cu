@@ -367,12 +367,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
             if (key > qrow || key >= p.T) v[c][t] = __float_as_uint(-INFINITY);
           }
       }
-      // row max of the raw scores (the scale is positive), four independent chains
+      // row max of the raw scores (the scale is positive), four independent chains of 3-input max
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int t = 0; t < 32; ++t) mx4[t & 3] = fmaxf(mx4[t & 3], __uint_as_float(v[c][t]));
+        for (int t = 0; t < 32; t += 2)
+          mx4[(t >> 1) & 3] = fmax3(mx4[(t >> 1) & 3], __uint_as_float(v[c][t]), __uint_as_float(v[c][t + 1]));
       const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       // raise the running max only when P would otherwise exceed 2^8 (always on the first tile)
       const bool raise = mt > m_run + FWD_RESCALE_LOG2;
@@ -405,20 +406,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
         ok = false;
         break;
       }
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // P = exp2(s * scale_log2 - m) with the FMAs and the row-sum adds on packed fp32 pairs
+      float2 sum_a = make_float2(0.f, 0.f), sum_b = sum_a;
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m_run, -m_run);
       uint8_t* pbuf = sP + sb * P_TILE_BYTES;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         float pv[32];
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          pv[t] = ex2_approx(fmaf(__uint_as_float(v[c][t]), p.scale_log2, -m_run));
-          sum4[t & 3] += pv[t];
+        for (int t = 0; t < 32; t += 2) {
+          const float2 x = ffma2(make_float2(__uint_as_float(v[c][t]), __uint_as_float(v[c][t + 1])), sc2, nm2);
+          pv[t] = ex2_approx(x.x);
+          pv[t + 1] = ex2_approx(x.y);
+        }
+#pragma unroll
+        for (int t = 0; t < 32; t += 4) {
+          sum_a = fadd2(sum_a, make_float2(pv[t], pv[t + 1]));
+          sum_b = fadd2(sum_b, make_float2(pv[t + 2], pv[t + 3]));
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
       }
-      l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      l_run += (sum_a.x + sum_a.y) + (sum_b.x + sum_b.y);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[sb]);
