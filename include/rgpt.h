@@ -50,7 +50,8 @@ enum RgptEpilogue {
   RGPT_EPI_RESID_F32 = 5,  /* D f32 = C f32 + alpha*acc*colscale[n] (colscale opt.);
                               D2 f32 (optional) = alpha*acc, the unscaled branch output */
   RGPT_EPI_POLY_BF16 = 6,  /* D bf16 = beta*C + alpha*acc, C bf16                   */
-  RGPT_EPI_BIAS_SIGMOID_BF16 = 7 /* D bf16 = sigmoid(alpha*acc + colscale[n]) (G1 gate)   */
+  RGPT_EPI_BIAS_SIGMOID_BF16 = 7, /* D bf16 = sigmoid(alpha*acc + colscale[n]) (G1 gate)  */
+  RGPT_EPI_POLY_F32 = 8    /* D f32  = beta*C + alpha*acc, C f32 (fp32 Newton-Schulz)  */
 };
 enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4 };
 
@@ -176,6 +177,23 @@ int rgpt_muon_prep(const RgptMuonTensor* table, int n, int R, int C, void* X, lo
                    float beta, int nesterov, float* sumsq, const float* hp, void* stream);
 /* X /= max(||X||_F, 1e-7) per matrix (optimizer.py:31-32). */
 int rgpt_ns_scale(void* X, long long x_bstride, int ldx, int rows, int cols, int n, const float* sumsq, void* stream);
+/* Newton-Schulz at fp32 accuracy on the bf16 tensor cores (the fp32 form of
+ * zeropower_via_newtonschulz5, optimizer.py:8-45, with X = G.float()). Each fp32 value x is split as
+ * hi = bf16(x), lo = bf16(x - hi); a product X*Y is then hi*hi + hi*lo + lo*hi (relative error ~2^-17),
+ * computed as ONE bf16 GEMM over K tripled by stacking the operand blocks along K.
+ * Logical source matrix b, element (i, j) = src[b*s_b + i*s_i + j*s_j], rows x cols, fp32 (bf16 if
+ * src_bf16), one of s_i / s_j equal to 1 (so a transposed view reads coalesced).
+ * rgpt_ns_sumsq: sumsq[b] += sum of squares of matrix b (caller zeroes sumsq).
+ * rgpt_ns_split: v = x * s with s = 1/max(sqrt(sumsq[b]), 1e-7) if sumsq != null, else 1;
+ *   xout (optional, fp32, row stride ldo, batch stride o_bstride) = v;
+ *   dst (optional, bf16, row stride ldd, batch stride d_bstride): nblk copies, block k at dst + k*blk_off
+ *   (elements), holding lo(v) if bit k of lo_mask is set, else hi(v). Padding outside rows x cols is
+ *   never written. */
+int rgpt_ns_sumsq(const void* src, int src_bf16, long long s_b, long long s_i, long long s_j, int rows, int cols,
+                  int n, float* sumsq, void* stream);
+int rgpt_ns_split(const void* src, int src_bf16, long long s_b, long long s_i, long long s_j, int rows, int cols,
+                  int n, const float* sumsq, float* xout, long long o_bstride, long long ldo, void* dst,
+                  long long d_bstride, long long ldd, int nblk, long long blk_off, unsigned lo_mask, void* stream);
 /* p = p*(1 - lr*wd) - muon_lr * bf16(X*scale) (optimizer.py:209-227); shadow = bf16(p). */
 int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C, const void* X, long long x_bstride, int ldx,
                     float lr, float wd, float muon_lr, float scale, const float* hp, void* stream);

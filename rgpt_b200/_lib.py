@@ -58,6 +58,9 @@ _SIGNATURES: dict[str, list] = {
                    _c_vp, _c_vp],
     "rgpt_muon_prep": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_int, _c_vp, _c_vp, _c_vp],
     "rgpt_ns_scale": [_c_vp, _c_ll, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp],
+    "rgpt_ns_sumsq": [_c_vp, _c_int, _c_ll, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_vp, _c_vp],
+    "rgpt_ns_split": [_c_vp, _c_int, _c_ll, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_ll, _c_ll,
+                      _c_vp, _c_ll, _c_ll, _c_int, _c_ll, ctypes.c_uint, _c_vp],
     "rgpt_muon_apply": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_float, _c_float,
                         _c_float, _c_vp, _c_vp],
     "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],

@@ -28,6 +28,7 @@
 //   ACT_BWD      dpre = acc * act'(pre)              (model/kernels.py:207-281)
 //   RESID_F32    x_out = x_in + acc * layer_scale    (model/transformer_block.py:43-57)
 //   POLY_BF16    beta*C + alpha*acc                  (optimizer.py:36-41, Newton-Schulz)
+//   POLY_F32     the same in fp32 (C and D fp32)     (fp32 Newton-Schulz on split bf16 operands)
 //   BIAS_SIGMOID sigmoid(acc + bias)                 (model/attention.py:45-48, G1 gate)
 //   ACCUM_F32    grad += acc (bulk reduce-add, so split-K needs no separate reduction)
 #include <cudaTypedefs.h>
@@ -62,17 +63,21 @@ constexpr int GEMM_BK = 64;
 // so that two warps per SM sub-partition hide each other's latency (measured 2-5 % faster there;
 // the two-output activation forward measured slower with 8).
 __host__ __device__ constexpr int gemm_epi_warps(int epi) {
-  return (epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32) ? 8 : 4;
+  return (epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32 ||
+          epi == RGPT_EPI_POLY_F32) ? 8 : 4;
 }
 __host__ __device__ constexpr int gemm_threads(int ew) { return 64 + 32 * ew; }
 constexpr int GROUP_M = 8;
 constexpr uint32_t EPI_STAGE_BYTES = 4096;  // one warp's 32 rows x 128 bytes
 
 __host__ __device__ constexpr bool epi_reads_c(int epi) {
-  return epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32;
+  return epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_POLY_BF16 || epi == RGPT_EPI_RESID_F32 ||
+         epi == RGPT_EPI_POLY_F32;
 }
-// bytes per element of the epilogue input C: bf16 for ACT_BWD / POLY, fp32 for RESID
-__host__ __device__ constexpr int epi_c_bytes(int epi) { return epi == RGPT_EPI_RESID_F32 ? 4 : 2; }
+// bytes per element of the epilogue input C: bf16 for ACT_BWD / POLY_BF16, fp32 for RESID / POLY_F32
+__host__ __device__ constexpr int epi_c_bytes(int epi) {
+  return (epi == RGPT_EPI_RESID_F32 || epi == RGPT_EPI_POLY_F32) ? 4 : 2;
+}
 
 template <int BN, int STAGES, bool PAIR, int EW>
 struct GemmSmem {
@@ -532,6 +537,10 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
               const float sc = (ep.colscale != nullptr && gn0 + j < sh.N) ? __ldg(ep.colscale + gn0 + j) : 1.0f;
               v[j] = cs[j] + v[j] * sc;
             }
+          } else if constexpr (EPI == RGPT_EPI_POLY_F32) {
+            const float* cs = reinterpret_cast<const float*>(cc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = fmaf(ep.beta, cs[j], v[j]);
           }
           stage_f32x32(s0, lane, v);
           fence_proxy_async_smem();
@@ -710,6 +719,7 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
     }
     RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_F32)
     default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   }
 #undef RGPT_GEMM_EPI_CASE
@@ -756,10 +766,11 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
   if (batch < 1) batch = 1;
   if (M < 1 || N < 1 || K < 1)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M, N, K >= 1 (got M=%d N=%d K=%d)", M, N, K);
-  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_BIAS_SIGMOID_BF16)
+  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_POLY_F32)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown epilogue %d", epi);
   if (D == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm output pointer is null");
-  const bool out_f32 = (epi == RGPT_EPI_STORE_F32 || epi == RGPT_EPI_ACCUM_F32 || epi == RGPT_EPI_RESID_F32);
+  const bool out_f32 = (epi == RGPT_EPI_STORE_F32 || epi == RGPT_EPI_ACCUM_F32 || epi == RGPT_EPI_RESID_F32 ||
+                        epi == RGPT_EPI_POLY_F32);
   const int vec = out_f32 ? 4 : 8;
   if (ldd % vec != 0 || (reinterpret_cast<uintptr_t>(D) & 15) != 0)
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "output leading dim / pointer not 16-byte aligned");
@@ -767,7 +778,7 @@ extern "C" int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "ACT_FWD needs an aligned second output");
   if (epi == RGPT_EPI_RESID_F32 && D2 != nullptr && (ldd2 % 4 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "RESID_F32 raw output must be 16-byte aligned");
-  if ((epi == RGPT_EPI_ACT_BWD || epi == RGPT_EPI_RESID_F32 || epi == RGPT_EPI_POLY_BF16) &&
+  if (epi_reads_c(epi) &&
       (C == nullptr || ldc % vec != 0 || (reinterpret_cast<uintptr_t>(C) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "epilogue input C missing or not 16-byte aligned");
   if (epi == RGPT_EPI_BIAS_SIGMOID_BF16 && colscale == nullptr)

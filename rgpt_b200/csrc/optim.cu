@@ -11,6 +11,10 @@
 //   ns_scale    X = bf16(X / max(||X||_F, 1e-7))
 //   (5 iterations of three batched tcgen05 GEMMs: A = X X^T; B = b*A + c*A*A; X = a*X + B*X)
 //   muon_apply  p = p * (1 - lr*wd) - muon_lr * bf16(X * scale) (transposed back); shadow = bf16(p)
+//
+// fp32 Newton-Schulz (zeropower_via_newtonschulz5 with X = G.float(), optimizer.py:8-45):
+//   ns_sumsq    ||X||_F^2 per matrix, reading the unit-stride dimension fastest
+//   ns_split    X / max(||X||_F, 1e-7) (optional), an fp32 copy, and bf16 hi/lo blocks for the GEMMs
 // Tensors are addressed through small device-resident descriptor tables built once by the host.
 #include "common.cuh"
 #include "rgpt.h"
@@ -314,6 +318,90 @@ __global__ void __launch_bounds__(256) muon_apply_kernel(const RgptMuonTensor* _
   }
 }
 
+// ---------------------------------------------------------------------------- fp32 Newton-Schulz
+// Each fp32 value v is carried to the bf16 tensor cores as hi = bf16(v), lo = bf16(v - hi): v - hi is
+// exact in fp32 and |v - hi - lo| <= 2^-18 |v|. A product X Y is hi*hi + hi*lo + lo*hi (the dropped lo*lo
+// is ~2^-18 relative), summed in one GEMM whose K runs over the three stacked operand blocks.
+constexpr int NS_TILE = 32;
+
+__device__ __forceinline__ float ns_load(const void* src, int src_bf16, long long off) {
+  return src_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(src)[off])
+                  : reinterpret_cast<const float*>(src)[off];
+}
+
+// sumsq[b] += sum of squares of matrix b; the unit-stride dimension is walked by consecutive threads.
+__global__ void __launch_bounds__(256) ns_sumsq_kernel(const void* __restrict__ src, int src_bf16, long long s_b,
+                                                       long long s_i, long long s_j, int rows, int cols,
+                                                       float* __restrict__ sumsq) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ float red[8];
+  const int b = blockIdx.y;
+  const bool j_fast = s_j == 1;
+  const int inner = j_fast ? cols : rows, outer = j_fast ? rows : cols;
+  const long long s_in = j_fast ? s_j : s_i, s_out = j_fast ? s_i : s_j;
+  float ss = 0.f;
+  for (int o = blockIdx.x; o < outer; o += gridDim.x) {
+    const long long base = (long long)b * s_b + (long long)o * s_out;
+    for (int in = threadIdx.x; in < inner; in += blockDim.x) {
+      const float v = ns_load(src, src_bf16, base + (long long)in * s_in);
+      ss = fmaf(v, v, ss);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    atomicAdd(&sumsq[b], t);
+  }
+}
+
+// One 32 x 32 tile of matrix blockIdx.z per block of 32 x 8 threads. The tile is read along the
+// source's unit-stride dimension (so a transposed view reads coalesced), turned in shared memory,
+// and written along rows: the fp32 copy and the nblk hi/lo blocks.
+__global__ void __launch_bounds__(256) ns_split_kernel(const void* __restrict__ src, int src_bf16, long long s_b,
+                                                       long long s_i, long long s_j, int rows, int cols,
+                                                       const float* __restrict__ sumsq, float* __restrict__ xout,
+                                                       long long o_bstride, long long ldo,
+                                                       __nv_bfloat16* __restrict__ dst, long long d_bstride,
+                                                       long long ldd, int nblk, long long blk_off,
+                                                       unsigned lo_mask) {
+  griddep_wait();
+  griddep_launch();
+  __shared__ float tile[NS_TILE][NS_TILE + 1];
+  const int b = blockIdx.z, i0 = blockIdx.y * NS_TILE, j0 = blockIdx.x * NS_TILE;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const long long sb = (long long)b * s_b;
+  if (s_i == 1 && s_j != 1) {  // column-major source: consecutive threads walk i
+    for (int c = ty; c < NS_TILE; c += 8) {
+      const int i = i0 + tx, j = j0 + c;
+      tile[tx][c] = (i < rows && j < cols) ? ns_load(src, src_bf16, sb + i + (long long)j * s_j) : 0.f;
+    }
+  } else {
+    for (int r = ty; r < NS_TILE; r += 8) {
+      const int i = i0 + r, j = j0 + tx;
+      tile[r][tx] = (i < rows && j < cols) ? ns_load(src, src_bf16, sb + (long long)i * s_i + (long long)j * s_j)
+                                           : 0.f;
+    }
+  }
+  __syncthreads();
+  const float den = sumsq != nullptr ? fmaxf(sqrtf(sumsq[b]), 1e-7f) : 1.0f;
+  for (int r = ty; r < NS_TILE; r += 8) {
+    const int i = i0 + r, j = j0 + tx;
+    if (i >= rows || j >= cols) continue;
+    const float v = sumsq != nullptr ? __fdiv_rn(tile[r][tx], den) : tile[r][tx];
+    if (xout != nullptr) xout[(long long)b * o_bstride + (long long)i * ldo + j] = v;
+    if (dst != nullptr) {
+      const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+      const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+      __nv_bfloat16* d = dst + (long long)b * d_bstride + (long long)i * ldd + j;
+      for (int k = 0; k < nblk; ++k) d[(long long)k * blk_off] = ((lo_mask >> k) & 1u) ? lo : hi;
+    }
+  }
+}
+
 }  // namespace rgpt
 
 using namespace rgpt;
@@ -364,4 +452,34 @@ extern "C" int rgpt_muon_apply(const RgptMuonTensor* table, int n, int R, int C,
       table, R, C, transpose, reinterpret_cast<const unsigned short*>(X), x_bstride, ldx, 1.0f - lr * wd, -muon_lr,
       scale, hp);
   return rgpt_check_launch("muon_apply_kernel");
+}
+
+extern "C" int rgpt_ns_sumsq(const void* src, int src_bf16, long long s_b, long long s_i, long long s_j, int rows,
+                             int cols, int n, float* sumsq, void* stream) {
+  if (rows < 1 || cols < 1 || n < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_sumsq: empty matrix stack");
+  if (s_i != 1 && s_j != 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_sumsq: source needs a unit stride");
+  if (src == nullptr || sumsq == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_sumsq: null pointer");
+  const int outer = s_j == 1 ? rows : cols;
+  const int gx = outer < 128 ? outer : 128;
+  launch_pdl(ns_sumsq_kernel, dim3(gx, n), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1, src, src_bf16,
+             s_b, s_i, s_j, rows, cols, sumsq);
+  return rgpt_check_launch("ns_sumsq_kernel");
+}
+
+extern "C" int rgpt_ns_split(const void* src, int src_bf16, long long s_b, long long s_i, long long s_j, int rows,
+                             int cols, int n, const float* sumsq, float* xout, long long o_bstride, long long ldo,
+                             void* dst, long long d_bstride, long long ldd, int nblk, long long blk_off,
+                             unsigned lo_mask, void* stream) {
+  if (rows < 1 || cols < 1 || n < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: empty matrix stack");
+  if (src == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: null source");
+  if (s_i != 1 && s_j != 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: source needs a unit stride");
+  if (xout != nullptr && ldo < cols) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: ldo %lld < cols %d", ldo, cols);
+  if (dst != nullptr && (ldd < cols || nblk < 1 || nblk > 32))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: ldd %lld / nblk %d invalid", ldd, nblk);
+  if (rows > 65535 * NS_TILE) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_split: %d rows", rows);
+  dim3 grid((cols + NS_TILE - 1) / NS_TILE, (rows + NS_TILE - 1) / NS_TILE, n);
+  launch_pdl(ns_split_kernel, grid, dim3(NS_TILE, 8), 0, reinterpret_cast<cudaStream_t>(stream), 1, src, src_bf16,
+             s_b, s_i, s_j, rows, cols, sumsq, xout, o_bstride, ldo, reinterpret_cast<__nv_bfloat16*>(dst),
+             d_bstride, ldd, dst != nullptr ? nblk : 0, blk_off, lo_mask);
+  return rgpt_check_launch("ns_split_kernel");
 }

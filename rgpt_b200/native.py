@@ -18,6 +18,7 @@ EPI_ACT_BWD = 4
 EPI_RESID_F32 = 5
 EPI_POLY_BF16 = 6
 EPI_BIAS_SIGMOID_BF16 = 7
+EPI_POLY_F32 = 8
 
 ACTIVATIONS = {"none": 0, "identity": 0, "squared_relu": 1, "gelu": 2, "silu": 3, "mish": 4}
 
@@ -235,6 +236,38 @@ def muon_prep(table, n, R, C, X, beta, nesterov, sumsq, hp: int | None = None) -
 
 def ns_scale(X, rows, cols, n, sumsq) -> None:
     _lib.call("rgpt_ns_scale", ptr(X), X.stride(0), X.stride(1), rows, cols, n, ptr(sumsq), _lib.stream_ptr(X.device))
+
+
+def _ns_src(src: torch.Tensor):
+    """(is_bf16, batch/row/col element strides) of a 3-D [n, rows, cols] source view."""
+    if src.dim() != 3 or src.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("Newton-Schulz source must be a 3-D fp32/bf16 [n, rows, cols] view")
+    return int(src.dtype == torch.bfloat16), src.stride(0), src.stride(1), src.stride(2)
+
+
+def ns_sumsq(src: torch.Tensor, sumsq: torch.Tensor) -> None:
+    """sumsq[b] += ||src[b]||_F^2 (fp32 accumulation)."""
+    bf, sb, si, sj = _ns_src(src)
+    n, rows, cols = src.shape
+    _lib.call("rgpt_ns_sumsq", ptr(src), bf, sb, si, sj, rows, cols, n, ptr(sumsq), _lib.stream_ptr(src.device))
+
+
+def ns_split(src: torch.Tensor, *, sumsq: torch.Tensor | None = None, xout: torch.Tensor | None = None,
+             dst: torch.Tensor | None = None, nblk: int = 0, blk_off: int = 0, lo_mask: int = 0) -> None:
+    """v = src / max(||src||_F, 1e-7) (if sumsq given) -> xout (fp32) and nblk bf16 hi/lo blocks of dst.
+
+    Block k starts blk_off elements after dst's first element and holds bf16(v - bf16(v)) if bit k of
+    lo_mask is set, else bf16(v). dst and xout share src's [n, rows, cols] indexing (their own strides)."""
+    bf, sb, si, sj = _ns_src(src)
+    n, rows, cols = src.shape
+    if xout is not None and (xout.dtype != torch.float32 or xout.stride(2) != 1):
+        raise ValueError("ns_split: xout must be fp32 with unit column stride")
+    if dst is not None and (dst.dtype != torch.bfloat16 or dst.stride(2) != 1):
+        raise ValueError("ns_split: dst must be bf16 with unit column stride")
+    _lib.call("rgpt_ns_split", ptr(src), bf, sb, si, sj, rows, cols, n, ptr(sumsq),
+              ptr(xout), xout.stride(0) if xout is not None else 0, xout.stride(1) if xout is not None else 0,
+              ptr(dst), dst.stride(0) if dst is not None else 0, dst.stride(1) if dst is not None else 0,
+              nblk, blk_off, lo_mask, _lib.stream_ptr(src.device))
 
 
 def muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale, hp: int | None = None) -> None:

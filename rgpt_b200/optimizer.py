@@ -94,6 +94,53 @@ def newton_schulz_batched(ws: _NSWorkspace, steps: int, coeffs=NS_COEFFS) -> tor
     return X
 
 
+class _NSWorkspaceF32:
+    """fp32 Newton-Schulz buffers for n matrices of one shape class (rows <= cols after transpose).
+
+    X, A, Bm hold the fp32 iterates. The bf16 operand stacks carry each fp32 value as hi + lo
+    (hi = bf16(v), lo = bf16(v - hi)), blocks stacked along the GEMM's K so that one bf16 GEMM sums
+    hi*hi + hi*lo + lo*hi:
+      WX  [rp, 4cp] = [Xh | Xh | Xl | Xh]: A-operand columns [0, 3cp), B-operand columns [cp, 4cp)
+      WA  [rp, 4rp] = [Ah | Ah | Al | Ah]: the same pairing for A @ A (A is symmetric)
+      WB  [rp, 3rp] = [Bh | Bh | Bl]     : A operand of B @ X
+      WXr [3rp, cp] = [Xh ; Xl ; Xh]     : B operand of B @ X, read MN-major (K runs down the rows)
+    Padding stays zero, so the padded rows/columns of every product are zero too."""
+
+    def __init__(self, n, xr, xc, device):
+        self.n, self.xr, self.xc = n, xr, xc
+        rp, cp = _pad8(xr), _pad8(xc)
+        self.rp, self.cp = rp, cp
+        f32, bf = dict(device=device, dtype=torch.float32), dict(device=device, dtype=torch.bfloat16)
+        self.X, self.X2 = torch.zeros(n, rp, cp, **f32), torch.zeros(n, rp, cp, **f32)
+        self.A, self.Bm = torch.zeros(n, rp, rp, **f32), torch.zeros(n, rp, rp, **f32)
+        self.WX = torch.zeros(n, rp, 4 * cp, **bf)
+        self.WXr = torch.zeros(n, 3 * rp, cp, **bf)
+        self.WA = torch.zeros(n, rp, 4 * rp, **bf)
+        self.WB = torch.zeros(n, rp, 3 * rp, **bf)
+        self.sumsq = torch.zeros(n, **f32)
+
+
+def newton_schulz_batched_f32(ws: _NSWorkspaceF32, steps: int, coeffs=NS_COEFFS) -> torch.Tensor:
+    """The quintic NS iteration at fp32 accuracy on ws.X (already normalised); returns the result buffer.
+
+    Per step: A = X X^T (fp32 out); B = b*A + c*A@A (POLY_F32); X = a*X + B@X (POLY_F32), each product
+    one tcgen05 bf16 GEMM over K tripled (hi/lo operand blocks), fp32 accumulation."""
+    a, b, c = coeffs
+    xr, xc, rp, cp = ws.xr, ws.xc, ws.rp, ws.cp
+    X, X2 = ws.X, ws.X2
+    for _ in range(steps):
+        nv.ns_split(X[:, :xr, :xc], dst=ws.WX[:, :xr, :xc], nblk=4, blk_off=cp, lo_mask=0b0100)
+        nv.ns_split(X[:, :xr, :xc], dst=ws.WXr[:, :xr, :xc], nblk=3, blk_off=rp * cp, lo_mask=0b010)
+        nv.gemm(ws.WX[:, :, :3 * cp], ws.WX[:, :, cp:], ws.A, epi=nv.EPI_STORE_F32)               # A = X X^T
+        nv.ns_split(ws.A[:, :xr, :xr], dst=ws.WA[:, :xr, :xr], nblk=4, blk_off=rp, lo_mask=0b0100)
+        nv.gemm(ws.WA[:, :, :3 * rp], ws.WA[:, :, rp:], ws.Bm, epi=nv.EPI_POLY_F32, alpha=c, beta=b,
+                c=ws.A)                                                                          # B = b*A + c*A@A
+        nv.ns_split(ws.Bm[:, :xr, :xr], dst=ws.WB[:, :xr, :xr], nblk=3, blk_off=rp, lo_mask=0b100)
+        nv.gemm(ws.WB, ws.WXr.transpose(1, 2), X2, epi=nv.EPI_POLY_F32, alpha=1.0, beta=a, c=X)  # X = a*X + B@X
+        X, X2 = X2, X
+    return X
+
+
 class _NSView:
     """The NS buffers of matrices [s, e) of a shape-class workspace (contiguous along the batch)."""
 
@@ -482,18 +529,30 @@ DistNorMuon = DistMuon
 
 # ---------------------------------------------------------------------- functional API
 @torch.no_grad()
-def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, coeffs=NS_COEFFS) -> torch.Tensor:
+def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, coeffs=NS_COEFFS, precision: str = "bf16") -> torch.Tensor:
     """Native quintic Newton-Schulz orthogonalisation of a 2-D (or batched 3-D) CUDA tensor (optimizer.py:8-45).
 
-    Returns bf16 with G's shape."""
+    precision "bf16" (the reference's): X = bf16(G), bf16 iterates; returns bf16.
+    precision "fp32": X = G.float() and fp32 iterates (bf16 hi/lo operand splitting on the tensor
+    cores, fp32 accumulation); returns fp32. Both return G's shape."""
     if not G.is_cuda:
         raise RuntimeError("zeropower_via_newtonschulz5 runs on CUDA tensors only (no CPU path)")
+    if precision not in ("bf16", "fp32"):
+        raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
     squeeze = G.dim() == 2
     Gb = G.unsqueeze(0) if squeeze else G
     n, R, C = Gb.shape
     transposed = R > C
     Xs = Gb.transpose(1, 2) if transposed else Gb
     xr, xc = Xs.shape[1], Xs.shape[2]
+    if precision == "fp32":
+        src = Xs if Xs.dtype in (torch.float32, torch.bfloat16) else Xs.float()
+        ws = _NSWorkspaceF32(n, xr, xc, G.device)
+        nv.ns_sumsq(src, ws.sumsq)
+        nv.ns_split(src, sumsq=ws.sumsq, xout=ws.X[:, :xr, :xc])
+        out = newton_schulz_batched_f32(ws, steps, coeffs)[:, :xr, :xc]
+        out = (out.transpose(1, 2) if transposed else out).contiguous()
+        return out[0] if squeeze else out
     ws = _NSWorkspace(n, xr, xc, G.device)
     ws.X[:, :xr, :xc].copy_(Xs.to(torch.bfloat16))
     ws.sumsq.copy_(ws.X.float().pow(2).sum(dim=(1, 2)))

@@ -171,3 +171,53 @@ def test_foreach_adamw_vector_and_scalar_paths_match_oracle(cuda):
         outs.append([t.cpu() for t in ps + ms + vs])
     for a, b in zip(*outs):
         assert torch.equal(a, b)
+
+
+def test_zeropower_fp32_within_1e3_of_fp32_restatement(cuda):
+    """fp32 Newton-Schulz (hi/lo bf16 operand split, fp32 accumulation) vs the fp32 restatement of
+    optimizer.py:8-45: relative Frobenius error below 1e-3, the bar set for polar_express in fp32.
+    The first case is the single-matrix Muon workload: G [2048, 512] ~ N(0, 1) * 1e-2, seed 0."""
+    torch.manual_seed(0)
+    cases = [torch.randn(2048, 512) * 1e-2]
+    g = torch.Generator().manual_seed(11)
+    cases += [torch.randn(*s, generator=g) * 1e-2 for s in [(512, 2048), (512, 512), (64, 64), (96, 40), (33, 130)]]
+    for G in cases:
+        ours = zeropower_via_newtonschulz5(G.to(cuda), 5, precision="fp32")
+        assert ours.dtype == torch.float32 and ours.shape == G.shape
+        ref32 = O.zeropower_ns5(G, 5, dtype=torch.float32)
+        err = rel(ours, ref32)
+        assert err < 1e-3, (tuple(G.shape), err)
+    # batched 3-D input, and a bf16 input (X = G.float() is exact)
+    Gb = torch.randn(3, 128, 384, generator=g) * 1e-2
+    ours = zeropower_via_newtonschulz5(Gb.to(cuda), 5, precision="fp32")
+    for i in range(3):
+        assert rel(ours[i], O.zeropower_ns5(Gb[i], 5, dtype=torch.float32)) < 1e-3
+    Gh = (torch.randn(256, 96, generator=g) * 1e-2).bfloat16()
+    ours = zeropower_via_newtonschulz5(Gh.to(cuda), 5, precision="fp32")
+    assert rel(ours, O.zeropower_ns5(Gh, 5, dtype=torch.float32)) < 1e-3
+
+
+def test_ns_split_hi_lo_blocks_and_transposed_source(cuda):
+    """ns_split: hi = bf16(v), lo = bf16(v - hi) placed by lo_mask; a column-major (transposed) source
+    reads the same logical matrix; padding is left untouched; sumsq scaling divides by the norm."""
+    from rgpt_b200 import native as nv
+    g = torch.Generator().manual_seed(3)
+    G = torch.randn(2, 70, 45, generator=g)
+    src = G.to(cuda).transpose(1, 2)                  # logical [2, 45, 70], unit stride on rows
+    sumsq = torch.zeros(2, device=cuda)
+    nv.ns_sumsq(src, sumsq)
+    ref_ss = G.pow(2).sum(dim=(1, 2))
+    assert torch.allclose(sumsq.cpu(), ref_ss, rtol=1e-5)
+    X = torch.full((2, 48, 72), 7.0, device=cuda)
+    W = torch.full((2, 48, 3 * 72), 9.0, device=cuda, dtype=torch.bfloat16)
+    nv.ns_split(src, sumsq=sumsq, xout=X[:, :45, :70], dst=W[:, :45, :70], nblk=3, blk_off=72, lo_mask=0b010)
+    v = G.transpose(1, 2) / ref_ss.sqrt().view(2, 1, 1)
+    assert torch.allclose(X[:, :45, :70].cpu(), v, rtol=1e-5, atol=0)
+    hi = X[:, :45, :70].bfloat16()
+    lo = (X[:, :45, :70] - hi.float()).bfloat16()
+    assert torch.equal(W[:, :45, 0:70], hi) and torch.equal(W[:, :45, 144:214], hi)
+    assert torch.equal(W[:, :45, 72:142], lo)
+    recon = W[:, :45, 0:70].double() + W[:, :45, 72:142].double()
+    assert ((recon - X[:, :45, :70].double()).abs() <= X[:, :45, :70].double().abs() * 2.0 ** -17).all()
+    assert (X[:, 45:, :] == 7.0).all() and (X[:, :, 70:] == 7.0).all()      # padding untouched
+    assert (W[:, 45:, :] == 9.0).all() and (W[:, :45, 70:72] == 9.0).all()
