@@ -147,7 +147,9 @@ def run_ours(args, wl):
 
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    cfg, B, T, accum = wl["cfg"], wl["B"], wl["T"], wl["accum"]
+    cfg, B, T, accum = dict(wl["cfg"]), wl["B"], wl["T"], wl["accum"]
+    if args.dropout is not None:
+        cfg["dropout"] = args.dropout
     torch.manual_seed(1234)
     model = GPT(**cfg).to(dev).train()
     opt = (DistMuon if world > 1 else Muon)(trainer_param_groups(model), **OPT)
@@ -253,7 +255,7 @@ def run_ours(args, wl):
                    "n_layers": cfg["n_layers"], "n_recur": cfg.get("n_recur", 1), "n_heads": cfg["n_heads"],
                    "vocab": cfg["vocab_size"], "seq_len": T, "micro_batch": B, "grad_accum": accum,
                    "global_batch": B * accum * world, "parallelism": f"dp{world}",
-                   "optimizer": "Muon (5 NS steps) + AdamW", "dropout": 0.0,
+                   "optimizer": "Muon (5 NS steps) + AdamW", "dropout": cfg["dropout"],
                    "launch": "one CUDA graph replay per step" if graphed is not None else "eager",
                    "l2": "no flush: each step's working set (activations + weights) is several GB, far above "
                          "the 126 MB L2"},
@@ -354,6 +356,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=30.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="issue every kernel from Python (no CUDA graph)")
+    ap.add_argument("--dropout", type=float, default=None,
+                    help="dropout rate of the embedding, attention probabilities and residual branches "
+                         "(default: the workload's)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         log("note: warm-up raised to 3 steps")

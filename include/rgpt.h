@@ -67,16 +67,35 @@ int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bst
                    void* D2, long long ldd2, long long d2_bstride,
                    const void* C, long long ldc, long long c_bstride,
                    const float* colscale, int splitk, const float* alpha_dev, void* stream);
+/* RGPT_DROPOUT. rgpt_gemm_bf16 with the residual-branch dropout of model/transformer_block.py:45,52 fused
+ * into the RESID_F32 epilogue (batch 1 only): the branch output alpha*acc*colscale becomes
+ * alpha*acc*keep/(1-drop_p) (D2 stores that dropped branch output), keep drawn for (row, column) from
+ * Philox4x32-10 block (column/8, row, drop_site, 0) under key (*drop_seed low, high 32 bits), element
+ * column%8 = 16-bit half (column%2) of word (column%8)/2, kept iff >= round(drop_p*65536); the bits go to
+ * drop_mask[row*drop_ldm + column/32]. */
+int rgpt_gemm_bf16_dropout(const void* A, int a_mn_major, long long lda, long long a_bstride,
+                           const void* B, int b_mn_major, long long ldb, long long b_bstride,
+                           int M, int N, int K, int batch, int epi, int act, float alpha, float beta,
+                           void* D, long long ldd, long long d_bstride, void* D2, long long ldd2, long long d2_bstride,
+                           const void* C, long long ldc, long long c_bstride, const float* colscale, int splitk,
+                           const float* alpha_dev, void* drop_mask, long long drop_ldm, const void* drop_seed,
+                           unsigned drop_site, float drop_p, void* stream);
 
 
 /* ------------------------------------------------------------------ attention
  * Causal softmax attention, head_dim 64, scale 1/8, token-major operands:
  *   qk  [B*T, 2d] bf16 (q heads | k heads, after QK norm + RoPE), qkv [B*T, 3d] bf16 (v = cols [2d,3d)),
  *   gate/o/og/dout/dgate_pre [B*T, d] bf16, lse/Dvec [B, H, T] fp32.
- * Replaces F.scaled_dot_product_attention(is_causal=True) and the G1 gate multiply,
- * model/attention.py:56-61 (forward) and their autograd backward. */
+ * Replaces F.scaled_dot_product_attention(is_causal=True, dropout_p) and the G1 gate multiply,
+ * model/attention.py:56-61 (forward) and their autograd backward.
+ * Dropout (drop_mask != null and drop_p > 0): the forward draws the keep bit of (query q, key k) of head
+ * bh = b*H + h from Philox4x32-10 block (k/8, q, drop_site, bh) under key (*drop_seed low, high 32 bits)
+ * -- 16-bit uniform (k%8 picks word (k%8)/2, half k%2) >= round(p*65536) -- scales the kept
+ * probabilities by 1/(1-p) and stores the bits in drop_mask [B*H][ceil(T/32)][T] (word = 32 queries of
+ * one key); the backward reads them back. See RGPT_DROPOUT below for the other sites. */
 int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse,
-                  int B, int T, int H, int d, void* stream);
+                  int B, int T, int H, int d, unsigned* drop_mask, const unsigned long long* drop_seed,
+                  unsigned drop_site, float drop_p, void* stream);
 /* dout = dog*gate; dgate_pre = dog*o*gate*(1-gate); Dvec = rowsum(dout*o). gate may be null (ungated).
  * dq_zero (optional, [B*T, d] fp32, 16-byte aligned) is zeroed: the dq accumulator of rgpt_attn_bwd. */
 int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,
@@ -84,7 +103,7 @@ int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* d
 /* dq [B*T, d] fp32 is ACCUMULATED (caller zeroes it); dk fp32 and dv bf16 are written with row strides. */
 int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, const float* lse, const float* Dvec,
                   float* dq, float* dk, long long dk_stride, void* dv, long long dv_stride,
-                  int B, int T, int H, int d, void* stream);
+                  int B, int T, int H, int d, const unsigned* drop_mask, float drop_p, void* stream);
 
 /* ------------------------------------------------------------------ norms
  * y = x * s(sum x^2) * affine over rows of length d. Kinds follow model/norm.py. */
@@ -104,12 +123,13 @@ enum RgptNormKind {
 int rgpt_rownorm_fwd(const float* x, void* y, float* stat, const float* w, float temp, int kind, float eps,
                      float alpha, int M, int d, const float* qw, const float* qb, float* qout, void* stream);
 /* Norm backward fused with the residual-gradient add (model/transformer_block.py:43-57):
- *   g_out = g_in + dx; g_bf16 = bf16(g_out * ls); dls += sum_rows g_out*raw; dw += sum_rows dy*x*s.
+ *   g_out = g_in + dx; g_bf16 = bf16(g_out * ls * z); dls += sum_rows g_out*raw; dw += sum_rows dy*x*s,
+ *   z = keep/(1-drop_p) from the branch's dropout mask [M, d/32] (drop_mask null: z = 1).
  * q_head mode (dq != null): dy = dq @ qw, plus dqw += dq^T h, dqb += sum dq. Optional pointers may be null. */
 int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w, float temp, int kind, float eps, float alpha,
                      int M, int d, const float* g_in, float* g_out, void* g_bf16, const float* ls,
                      const float* raw, float* dls, float* dw, float* dtemp, const float* dq, const float* qw,
-                     const void* h, float* dqw, float* dqb, void* stream);
+                     const void* h, float* dqw, float* dqb, const unsigned* drop_mask, float drop_p, void* stream);
 
 /* ------------------------------------------------------------------ QKV prep
  * Per (token, head): QK norm (QKNorm, model/norm.py:182-204) and RoPE (model/rope.py:38-57).
@@ -128,9 +148,14 @@ int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const f
                       float sq, float sk, int M, int T, int H, void* stream);
 
 /* ------------------------------------------------------------------ embedding / loss
- * nn.Embedding forward (model/gpt.py:95) and its backward (dx rows ACCUMULATED into demb). */
-int rgpt_embedding_fwd(const long long* ids, const float* emb, float* x, int M, int d, int V, void* stream);
-int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M, int d, int V, void* stream);
+ * nn.Embedding forward (model/gpt.py:95) and its backward (dx rows ACCUMULATED into demb), with the
+ * embedding dropout of model/gpt.py:96 when drop_mask != null (d % 128 == 0): keep bits of (row, column)
+ * from Philox block (column/8, row, drop_site, 0), stored in drop_mask [M, d/32] and read back by the
+ * backward. */
+int rgpt_embedding_fwd(const long long* ids, const float* emb, float* x, int M, int d, int V, unsigned* drop_mask,
+                       const unsigned long long* drop_seed, unsigned drop_site, float drop_p, void* stream);
+int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M, int d, int V,
+                       const unsigned* drop_mask, float drop_p, void* stream);
 /* Cross entropy over bf16 logits rows (F.cross_entropy with ignore_index, trainer.py:148) plus the
  * row argmax (model/gpt.py:119-120). scale_buf[2] = {grad_scale/count, count}; loss_out = mean loss.
  * write_grad: logits are overwritten in place by bf16 (softmax - onehot) * grad_scale / count. */

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import math
 
+import numpy as np
 import torch
 import torch.nn.functional as F
 
@@ -183,16 +184,74 @@ def rope_apply(q, k, cos, sin):
 # --------------------------------------------------------------------------
 # Attention — model/attention.py:35-64
 # --------------------------------------------------------------------------
-def causal_attention(q, k, v, scale):
-    """softmax(q k^T * scale + causal mask) v, q/k/v [B, H, T, D] (F.scaled_dot_product_attention, is_causal)."""
+# --------------------------------------------------------------------------
+# Dropout masks — nn.Dropout / SDPA dropout_p (model/gpt.py:96, model/transformer_block.py:45,52,
+# model/attention.py:57). torch draws its own Philox stream, which no other implementation can
+# reproduce bit for bit; the native kernels draw theirs from Philox4x32-10 with the counter layout
+# below, and this restatement regenerates exactly those masks so that a dropout step can be checked
+# element by element. Philox4x32-10: Salmon, Moraes, Dror and Shaw, SC 2011 (checked against the
+# published known-answer vectors in tests/test_oracle_golden.py).
+# --------------------------------------------------------------------------
+_U32 = np.uint64(0xFFFFFFFF)
+EMB_DROP_SITE = 0xFFFFFF
+
+
+def philox4x32_10(c0, c1, c2, c3, k0, k1):
+    """Vectorised Philox4x32-10 over uint32 counter arrays; returns the four output words (uint32)."""
+    c = [np.asarray(x, dtype=np.uint64) for x in np.broadcast_arrays(c0, c1, c2, c3)]
+    k0, k1 = np.uint64(k0), np.uint64(k1)
+    for _ in range(10):
+        p0 = np.uint64(0xD2511F53) * c[0]
+        p1 = np.uint64(0xCD9E8D57) * c[2]
+        c = [(p1 >> np.uint64(32)) ^ c[1] ^ k0, p1 & _U32, (p0 >> np.uint64(32)) ^ c[3] ^ k1, p0 & _U32]
+        k0 = (k0 + np.uint64(0x9E3779B9)) & _U32
+        k1 = (k1 + np.uint64(0xBB67AE85)) & _U32
+    return [x.astype(np.uint32) for x in c]
+
+
+def drop_thresh(p):
+    """Keep iff a 16-bit uniform >= round(p * 65536)."""
+    return int(round(p * 65536.0))
+
+
+def keep_mask(seed, site, sub, rows, cols, p):
+    """Keep mask [rows, cols] (bool): element (r, c) is 16-bit half (c & 1) of word (c >> 1) & 3 of
+    Philox block (c >> 3, r, site, sub) under key (seed low 32 bits, seed high 32 bits)."""
+    cb = (cols + 7) // 8
+    r = np.arange(rows, dtype=np.uint64)[:, None]
+    b = np.arange(cb, dtype=np.uint64)[None, :]
+    w = philox4x32_10(b, r, np.uint64(site), np.uint64(sub), seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF)
+    w = np.stack(w, axis=-1)                                   # [rows, cb, 4]
+    halves = np.stack([w & 0xFFFF, w >> 16], axis=-1)          # [rows, cb, 4, 2]
+    u16 = halves.reshape(rows, cb * 8)[:, :cols]
+    return torch.from_numpy(u16 >= drop_thresh(p))
+
+
+def resid_drop_mask(seed, site, M, d, p):
+    """Residual-branch / embedding mask over [M, d] (rows = tokens), sub-stream 0."""
+    return keep_mask(seed, site, 0, M, d, p)
+
+
+def attn_drop_mask(seed, site, B, H, T, p):
+    """Attention-probability mask [B, H, T(query), T(key)]: head bh = b*H + h is sub-stream bh."""
+    return torch.stack([keep_mask(seed, site, bh, T, T, p) for bh in range(B * H)]).view(B, H, T, T)
+
+
+def causal_attention(q, k, v, scale, keep=None, p=0.0):
+    """softmax(q k^T * scale + causal mask) v, q/k/v [B, H, T, D] (F.scaled_dot_product_attention, is_causal).
+
+    keep: optional [B, H, T, T] dropout mask applied to the probabilities (scaled by 1/(1-p))."""
     T = q.shape[-2]
     s = (q @ k.transpose(-2, -1)) * scale
     mask = torch.ones(T, T, dtype=torch.bool).triu(1)
     s = s.masked_fill(mask, float("-inf"))
-    return torch.softmax(s, dim=-1) @ v
+    pr = torch.softmax(s, dim=-1)
+    if keep is not None:
+        pr = pr * keep.to(pr.dtype) * (1.0 / (1.0 - p))
+    return pr @ v
 
 
-def attention_forward(x, params, prefix, cfg):
+def attention_forward(x, params, prefix, cfg, drop=None):
     B, T, d = x.shape
     H = cfg["n_heads"]
     Dh = d // H
@@ -209,40 +268,65 @@ def attention_forward(x, params, prefix, cfg):
     q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     cos, sin = rope_tables(T, Dh, 10000.0, q.dtype)
     q, k = rope_apply(q, k, cos, sin)
-    o = causal_attention(q, k, v, 1.0 / math.sqrt(Dh))
+    keep = None
+    if drop is not None:
+        keep = attn_drop_mask(drop["seed"], drop["site"] + 2, B, H, T, drop["p"])
+    o = causal_attention(q, k, v, 1.0 / math.sqrt(Dh), keep, drop["p"] if drop else 0.0)
     if gate is not None:
         o = o * gate
     o = o.transpose(1, 2).reshape(B, T, d)
     return o @ params[prefix + ".out_proj.weight"].t()
 
 
-def block_forward(x, params, prefix, cfg):
-    """Pre-norm block with optional layer scale, dropout off (model/transformer_block.py:43-57)."""
+def _dropped(y, drop, site):
+    """nn.Dropout with the native kernels' mask of `site` over the rows of y [B, T, d]."""
+    if drop is None:
+        return y
+    B, T, d = y.shape
+    keep = resid_drop_mask(drop["seed"], site, B * T, d, drop["p"]).view(B, T, d)
+    return y * keep.to(y.dtype) * (1.0 / (1.0 - drop["p"]))
+
+
+def block_forward(x, params, prefix, cfg, drop=None):
+    """Pre-norm block with optional layer scale (model/transformer_block.py:43-57).
+
+    drop: None (dropout off) or {"p", "seed", "site"}: branch masks at sites site+0 (attention
+    output) and site+1 (FFN output), the attention-probability mask at site+2."""
     d = cfg["d_model"]
     nt, eps = cfg["norm_type"], cfg["norm_eps"]
-    a = attention_forward(norm_apply(nt, x, params, prefix + ".attn_norm", eps, d), params, prefix + ".attn", cfg)
+    a = attention_forward(norm_apply(nt, x, params, prefix + ".attn_norm", eps, d), params, prefix + ".attn", cfg,
+                          drop)
+    a = _dropped(a, drop, drop["site"] if drop else 0)
     h = x + (a * params[prefix + ".attn_layer_scale"] if cfg.get("use_layer_scale") else a)
     hn = norm_apply(nt, h, params, prefix + ".ff_norm", eps, d)
     B, T, _ = hn.shape
     f, _, _ = linear_act_forward(hn.reshape(-1, d), params[prefix + ".ff.fc1.weight"],
                                  params[prefix + ".ff.fc2.weight"].t(), cfg["activation_type"])
-    f = f.view(B, T, d)
+    f = _dropped(f.view(B, T, d), drop, drop["site"] + 1 if drop else 0)
     return h + (f * params[prefix + ".ff_layer_scale"] if cfg.get("use_layer_scale") else f)
 
 
-def gpt_forward(params, input_ids, cfg, labels=None, training=True):
-    """GPT.forward (model/gpt.py:92-143) with dropout off.
+def gpt_forward(params, input_ids, cfg, labels=None, training=True, drop_seed=None):
+    """GPT.forward (model/gpt.py:92-143).
 
+    Dropout is off unless drop_seed is given (with training and cfg["dropout"] > 0): then the
+    embedding output uses site EMB_DROP_SITE and layer application `app` (recurrence i, layer li,
+    app = i * n_layers + li) sites 4 * app + {0, 1, 2}, the masks of the native kernels.
     Returns (final_logits, accum_halt_loss, all_step_q, target_q_continues)."""
     d = cfg["d_model"]
     nt, eps = cfg["norm_type"], cfg["norm_eps"]
+    p = cfg.get("dropout", 0.0)
+    use_drop = training and drop_seed is not None and p > 0
     x = params["embs.weight"][input_ids]
+    if use_drop:
+        x = _dropped(x, {"p": p, "seed": drop_seed}, EMB_DROP_SITE)
     n_recur = cfg.get("n_recur", 1)
     all_q = []
     halt = torch.zeros(())
     for i in range(n_recur):
         for li in range(cfg["n_layers"]):
-            x = block_forward(x, params, f"layers.{li}", cfg)
+            drop = {"p": p, "seed": drop_seed, "site": 4 * (i * cfg["n_layers"] + li)} if use_drop else None
+            x = block_forward(x, params, f"layers.{li}", cfg, drop)
         if cfg.get("cal_halt_loss") and labels is not None:
             h = norm_apply(nt, x, params, "ln_f", eps, d)
             cur_q = h @ params["q_head.weight"].t() + params["q_head.bias"]

@@ -37,18 +37,25 @@ _SIGNATURES: dict[str, list] = {
         _c_vp, _c_ll, _c_ll,  # C, ldc, c_bstride
         _c_vp, _c_int, _c_vp, _c_vp,  # colscale, splitk, alpha_dev, stream
     ],
+    "rgpt_gemm_bf16_dropout": [
+        _c_vp, _c_int, _c_ll, _c_ll, _c_vp, _c_int, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_int,
+        _c_int, _c_int, _c_float, _c_float, _c_vp, _c_ll, _c_ll, _c_vp, _c_ll, _c_ll, _c_vp, _c_ll, _c_ll,
+        _c_vp, _c_int, _c_vp,  # colscale, splitk, alpha_dev
+        _c_vp, _c_ll, _c_vp, ctypes.c_uint, _c_float,  # drop_mask, drop_ldm, drop_seed, drop_site, drop_p
+        _c_vp,
+    ],
     "rgpt_rownorm_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
                          _c_vp, _c_vp, _c_vp, _c_vp],
     "rgpt_rownorm_bwd": [_c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
                          _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
-                         _c_vp, _c_vp],
+                         _c_vp, _c_vp, _c_float, _c_vp],
     "rgpt_qkv_prep_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float,
                           _c_float, _c_float, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_qkv_prep_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp,
                           _c_int, _c_float, _c_float, _c_vp, _c_vp, _c_float, _c_float, _c_float, _c_float,
                           _c_int, _c_int, _c_int, _c_vp],
-    "rgpt_embedding_fwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
-    "rgpt_embedding_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_embedding_fwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, ctypes.c_uint, _c_float, _c_vp],
+    "rgpt_embedding_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_vp, _c_float, _c_vp],
     "rgpt_cross_entropy": [_c_vp, _c_ll, _c_int, _c_int, _c_vp, _c_int, _c_float, _c_vp, _c_vp, _c_vp, _c_vp,
                            _c_int, _c_vp],
     "rgpt_cross_entropy_noalloc": [_c_vp, _c_ll, _c_int, _c_int, _c_vp, _c_int, _c_float, _c_vp, _c_vp, _c_int,
@@ -63,10 +70,11 @@ _SIGNATURES: dict[str, list] = {
                       _c_vp, _c_ll, _c_ll, _c_int, _c_ll, ctypes.c_uint, _c_vp],
     "rgpt_muon_apply": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_float, _c_float,
                         _c_float, _c_vp, _c_vp],
-    "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
+                      _c_vp, _c_vp, ctypes.c_uint, _c_float, _c_vp],
     "rgpt_attn_bwd_prep": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_attn_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_ll, _c_vp, _c_ll,
-                      _c_int, _c_int, _c_int, _c_int, _c_vp],
+                      _c_int, _c_int, _c_int, _c_int, _c_vp, _c_float, _c_vp],
 }
 
 _lock = threading.Lock()

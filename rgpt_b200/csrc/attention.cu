@@ -159,6 +159,13 @@ struct AttnFwdParams {
   __nv_bfloat16* og; // [B*T, d] (gated) or null
   const __nv_bfloat16* gate;  // [B*T, d] or null
   float* lse;        // [B, H, T] natural-log LSE of the scaled scores
+  // dropout of the attention probabilities (SDPA dropout_p, model/attention.py:57), DROP kernels only:
+  // keep bit of (query q, key k) of head bh from Philox block (k / 8, q, site, bh), written to
+  // drop_mask[(bh * ceil(T/32) + q / 32) * T + k] bit q % 32 (one word per key and 32 queries)
+  uint32_t* drop_mask;
+  const unsigned long long* drop_seed;
+  uint32_t drop_site, drop_thresh;
+  float drop_scale;
 };
 
 constexpr int FWD_KT = 64;                                  // keys per tile in the forward
@@ -173,6 +180,7 @@ constexpr float FWD_RESCALE_LOG2 = 8.0f;                    // rescale O only wh
 // overlaps P(j) V(j). O accumulates in TMEM. The running row max used for P is only raised
 // when the tile max exceeds it by more than 2^8 (P then stays below 2^8, well inside bf16);
 // that rare rescale multiplies O in TMEM after the previous P V has landed.
+template <bool DROP>
 __global__ void __launch_bounds__(ATT_THREADS, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmG,
@@ -336,6 +344,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    uint32_t rk0 = 0, rk1 = 0;
+    if constexpr (DROP) {
+      const unsigned long long sd = *p.drop_seed;
+      rk0 = (uint32_t)sd;
+      rk1 = (uint32_t)(sd >> 32);
+    }
 
     auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
       int v = 1;
@@ -424,6 +438,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
           sum_a = fadd2(sum_a, make_float2(pv[t], pv[t + 1]));
           sum_b = fadd2(sum_b, make_float2(pv[t + 2], pv[t + 3]));
         }
+        if constexpr (DROP) {
+          // the row sum keeps every probability; P V sees only the kept ones (1/(1-p) is applied to O)
+          const int key0 = kbase + c * 32;
+          const uint32_t keep = keep32((uint32_t)key0, (uint32_t)qrow, p.drop_site, (uint32_t)bh, rk0, rk1,
+                                       p.drop_thresh);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) pv[t] = ((keep >> t) & 1u) ? pv[t] : 0.f;
+          // lane t gets key key0 + t's bits over this warp's 32 queries: one coalesced 128-byte store
+          const uint32_t kw = warp_transpose_bits(keep, lane);
+          const int qb = (q0 >> 5) + quarter;
+          if (key0 + lane < p.T && qb * 32 < p.T)
+            p.drop_mask[((long long)bh * ((p.T + 31) >> 5) + qb) * p.T + key0 + lane] = kw;
+        }
 #pragma unroll
         for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
       }
@@ -442,7 +469,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       tmem_ld32(t_lane + O_COL, o[0]);
       tmem_ld32(t_lane + O_COL + 32, o[1]);
       tmem_wait_ld();
-      const float inv_l = 1.0f / l_run;
+      const float inv_l = (DROP ? p.drop_scale : 1.0f) / l_run;
       float ov[ATT_D];
 #pragma unroll
       for (int i = 0; i < ATT_D; ++i) ov[i] = __uint_as_float(o[i >> 5][i & 31]) * inv_l;
@@ -555,6 +582,8 @@ struct AttnBwdParams {
   long long dk_stride;
   __nv_bfloat16* dv; // [B*T, dv_stride] bf16
   long long dv_stride;
+  const uint32_t* drop_mask;  // DROP kernels: the forward's attention-probability keep bits
+  float drop_scale;           // 1 / (1 - p)
 };
 
 constexpr int ATT_BWD_THREADS = 320;  // TMA warp, MMA warp, 8 softmax/epilogue warps
@@ -571,6 +600,7 @@ constexpr int BWD_STAT_FLOATS = 128;              // one warp's 64 query LSEs (l
 //   half g, Q(t): dQ = dS K for the whole tile (reads both halves' dS).
 // A warpgroup stores its next P/dS half only after Q of the previous tile has completed (it
 // reads both dS halves), and writes that tile's dQ (TMEM -> TMA bulk reduce-add) right after.
+template <bool DROP>
 __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -782,7 +812,9 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
     // queries (chunk cc of this half) of this thread's key row, in registers. Queries past T
     // carry lse = +inf (P = 0); keys past T need no mask (their K/V rows are zero and their
     // dK/dV rows are never stored).
-    auto softmax_chunk = [&](auto mask_tag, int cc, uint4 (&pk)[4], uint4 (&dk)[4]) {
+    // With dropout (keep bits kw over the chunk's 32 queries, z = kept / (1-p)): P~ = P z feeds dV and
+    // dS = P (z dP~ - D), dP~ = dO V^T being what the dP^T MMA computed.
+    auto softmax_chunk = [&](auto mask_tag, int cc, uint4 (&pk)[4], uint4 (&dk)[4], uint32_t kw) {
       constexpr bool MASK = decltype(mask_tag)::value;
       uint32_t sv[32], dv[32];
       tmem_ld32(t_lane + g * 128 + cc * 32, sv);
@@ -800,8 +832,14 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
           const int t_ = 4 * t4 + e;
           float pv = ex2_approx(fmaf(__uint_as_float(sv[t_]), p.scale_log2, -la[e]));
           if constexpr (MASK) pv = (g * 64 + cc * 32 + t_ < r) ? 0.f : pv;  // causal: query before key
-          pr[t_ & 7] = pv;
-          ds[t_ & 7] = pv * (__uint_as_float(dv[t_]) - da[e]);
+          if constexpr (DROP) {
+            const float z = ((kw >> t_) & 1u) ? p.drop_scale : 0.f;
+            pr[t_ & 7] = pv * z;
+            ds[t_ & 7] = pv * fmaf(__uint_as_float(dv[t_]), z, -da[e]);
+          } else {
+            pr[t_ & 7] = pv;
+            ds[t_ & 7] = pv * (__uint_as_float(dv[t_]) - da[e]);
+          }
         }
         if (t4 & 1) {  // 8 values -> one 16-byte chunk of bf16
           pk[t4 >> 1] = make_uint4(pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[2], pr[3]), pack_bf16x2(pr[4], pr[5]),
@@ -836,8 +874,16 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
       mbar_arrive(dq_empty);
       return true;
     };
+    const int key = k0 + r;
     for (int i = 0; i < nq && ok; ++i) {
       const int qrow0 = (qt0 + i) * ATT_TILE;
+      uint32_t kw0 = 0, kw1 = 0;  // dropout keep bits of this key over the half's two 32-query chunks
+      if constexpr (DROP) {
+        const int qb = (qrow0 + g * 64) >> 5, nqb = (p.T + 31) >> 5;
+        const uint32_t* mrow = p.drop_mask + ((long long)bh * nqb + qb) * p.T + key;
+        if (key < p.T && qb < nqb) kw0 = __ldg(mrow);
+        if (key < p.T && qb + 1 < nqb) kw1 = __ldg(mrow + p.T);
+      }
       {  // this warp's 64 queries: LSE in log2 units and D, staged for broadcast reads
         const int qa = qrow0 + g * 64 + lane, qb = qa + 32;
         const float la = qa < p.T ? __ldg(lse_bh + qa) * 1.4426950408889634f : INFINITY;
@@ -858,11 +904,11 @@ __global__ void __launch_bounds__(ATT_BWD_THREADS, 1)
       tc_fence_after();
       uint4 pk[2][4], dk[2][4];  // P^T / dS^T as bf16, 16-byte chunks of this key row
       if (i == 0) {  // the diagonal tile (query tile == key tile)
-        softmax_chunk(std::true_type{}, 0, pk[0], dk[0]);
-        softmax_chunk(std::true_type{}, 1, pk[1], dk[1]);
+        softmax_chunk(std::true_type{}, 0, pk[0], dk[0], kw0);
+        softmax_chunk(std::true_type{}, 1, pk[1], dk[1], kw1);
       } else {
-        softmax_chunk(std::false_type{}, 0, pk[0], dk[0]);
-        softmax_chunk(std::false_type{}, 1, pk[1], dk[1]);
+        softmax_chunk(std::false_type{}, 0, pk[0], dk[0], kw0);
+        softmax_chunk(std::false_type{}, 1, pk[1], dk[1], kw1);
       }
       // dQ of the previous tile reads both dS halves: it must have completed before we overwrite
       if (i > 0 && !dq_out(i - 1)) {
@@ -957,7 +1003,8 @@ static int check_attn_args(int B, int T, int H, int d) {
 }
 
 extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse, int B,
-                             int T, int H, int d, void* stream) {
+                             int T, int H, int d, unsigned* drop_mask, const unsigned long long* drop_seed,
+                             unsigned drop_site, float drop_p, void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
@@ -990,14 +1037,28 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
   p.og = reinterpret_cast<__nv_bfloat16*>(og);
   p.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
   p.lse = lse;
-  static bool attr[64] = {false};
-  if (!attr[dev]) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM) != cudaSuccess)
-      return rgpt_check_launch("attn_fwd set smem");
-    attr[dev] = true;
+  const bool drop = drop_mask != nullptr && drop_p > 0.0f;
+  if (drop && (!(drop_p < 1.0f) || drop_seed == nullptr))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout needs p in [0, 1) and a device seed");
+  p.drop_mask = drop ? reinterpret_cast<uint32_t*>(drop_mask) : nullptr;
+  p.drop_seed = drop_seed;
+  p.drop_site = drop_site;
+  p.drop_thresh = drop ? (uint32_t)lrintf(drop_p * 65536.0f) : 0u;
+  p.drop_scale = drop ? (float)(1.0 / (1.0 - (double)drop_p)) : 1.0f;
+  static bool attr[2][64] = {{false}};
+  if (!attr[drop][dev]) {
+    const cudaError_t e =
+        drop ? cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM)
+             : cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM);
+    if (e != cudaSuccess) return rgpt_check_launch("attn_fwd set smem");
+    attr[drop][dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  launch_pdl(attn_fwd_kernel, dim3(grid), dim3(ATT_THREADS), FWD_SMEM, reinterpret_cast<cudaStream_t>(stream), 1, tq, tk, tv, tg, to, tog, p);
+  cudaStream_t st_ = reinterpret_cast<cudaStream_t>(stream);
+  if (drop)
+    launch_pdl(attn_fwd_kernel<true>, dim3(grid), dim3(ATT_THREADS), FWD_SMEM, st_, 1, tq, tk, tv, tg, to, tog, p);
+  else
+    launch_pdl(attn_fwd_kernel<false>, dim3(grid), dim3(ATT_THREADS), FWD_SMEM, st_, 1, tq, tk, tv, tg, to, tog, p);
   return rgpt_check_launch("attn_fwd_kernel");
 }
 
@@ -1020,7 +1081,7 @@ extern "C" int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* ga
 
 extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, const float* lse, const float* Dvec,
                              float* dq, float* dk, long long dk_stride, void* dv, long long dv_stride, int B, int T,
-                             int H, int d, void* stream) {
+                             int H, int d, const unsigned* drop_mask, float drop_p, void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
@@ -1053,13 +1114,25 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
   p.dk_stride = dk_stride;
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
   p.dv_stride = dv_stride;
-  static bool attr[64] = {false};
-  if (!attr[dev]) {
-    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM) != cudaSuccess)
-      return rgpt_check_launch("attn_bwd set smem");
-    attr[dev] = true;
+  const bool drop = drop_mask != nullptr && drop_p > 0.0f;
+  if (drop && !(drop_p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout needs p in [0, 1)");
+  p.drop_mask = drop ? reinterpret_cast<const uint32_t*>(drop_mask) : nullptr;
+  p.drop_scale = drop ? (float)(1.0 / (1.0 - (double)drop_p)) : 1.0f;
+  static bool attr[2][64] = {{false}};
+  if (!attr[drop][dev]) {
+    const cudaError_t e =
+        drop ? cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM)
+             : cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM);
+    if (e != cudaSuccess) return rgpt_check_launch("attn_bwd set smem");
+    attr[drop][dev] = true;
   }
   const dim3 grid((unsigned)(((T + ATT_TILE - 1) / ATT_TILE) * H * B));
-  launch_pdl(attn_bwd_kernel, dim3(grid), dim3(ATT_BWD_THREADS), BWD_SMEM, reinterpret_cast<cudaStream_t>(stream), 1, tq, tk, tv, tdo, tdq, tdk, tdv, p);
+  cudaStream_t st_ = reinterpret_cast<cudaStream_t>(stream);
+  if (drop)
+    launch_pdl(attn_bwd_kernel<true>, dim3(grid), dim3(ATT_BWD_THREADS), BWD_SMEM, st_, 1, tq, tk, tv, tdo, tdq, tdk,
+               tdv, p);
+  else
+    launch_pdl(attn_bwd_kernel<false>, dim3(grid), dim3(ATT_BWD_THREADS), BWD_SMEM, st_, 1, tq, tk, tv, tdo, tdq,
+               tdk, tdv, p);
   return rgpt_check_launch("attn_bwd_kernel");
 }

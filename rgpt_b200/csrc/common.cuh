@@ -412,6 +412,54 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- dropout
+// Philox4x32-10 (Salmon, Moraes, Dror and Shaw, "Parallel Random Numbers: As Easy as 1, 2, 3",
+// SC 2011): a counter-based generator, so every dropout bit is a pure function of
+// (seed, site, position) and forward / backward / tests can agree on it without shared state.
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+// Eight keep bits from one Philox block: element e uses the 16-bit half (e & 1) of word e >> 1
+// (low half first) and is kept iff that value >= thresh, thresh = round(p * 65536).
+__device__ __forceinline__ uint32_t keep8(uint4 r, uint32_t thresh) {
+  const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+  uint32_t bits = 0;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) bits |= (((w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu) >= thresh ? 1u : 0u) << e;
+  return bits;
+}
+// Keep bits of 32 consecutive positions pos0 .. pos0 + 31 (pos0 a multiple of 8) of row `row`:
+// block i uses counter (pos0 / 8 + i, row, site, sub).
+__device__ __forceinline__ uint32_t keep32(uint32_t pos0, uint32_t row, uint32_t site, uint32_t sub, uint32_t k0,
+                                           uint32_t k1, uint32_t thresh) {
+  uint32_t w = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w |= keep8(philox4x32_10(make_uint4((pos0 >> 3) + i, row, site, sub), k0, k1), thresh) << (8 * i);
+  return w;
+}
+// 32 x 32 bit-matrix transpose across a warp: lane i holds row i (bit j = M[i][j]); returns
+// column `lane` (bit i = M[i][lane]). Five exchange steps of halving block size.
+__device__ __forceinline__ uint32_t warp_transpose_bits(uint32_t x, int lane) {
+  const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const int s = 16 >> k;
+    const uint32_t m = masks[k];
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, s);
+    x = (lane & s) ? ((x & ~m) | ((y & ~m) >> s)) : ((x & m) | ((y & m) << s));
+  }
+  return x;
+}
+
 }  // namespace rgpt
 
 // ---------------------------------------------------------------- host-side error plumbing

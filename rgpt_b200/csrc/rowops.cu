@@ -159,7 +159,8 @@ __global__ void __launch_bounds__(256, NV <= 4 ? 2 : 1) rownorm_bwd_kernel(const
                                    const float* __restrict__ raw, float* __restrict__ dls, float* __restrict__ dw,
                                    float* __restrict__ dtemp, const float* __restrict__ dq,
                                    const float* __restrict__ qw, const __nv_bfloat16* __restrict__ h,
-                                   float* __restrict__ dqw, float* __restrict__ dqb) {
+                                   float* __restrict__ dqw, float* __restrict__ dqb,
+                                   const uint32_t* __restrict__ drop_mask, float drop_scale) {
   griddep_wait();
   griddep_launch();
   extern __shared__ float red[];  // per-CTA column partials: [d] dw, [d] dls, [2d] dqw
@@ -242,6 +243,14 @@ __global__ void __launch_bounds__(256, NV <= 4 ? 2 : 1) rownorm_bwd_kernel(const
       reinterpret_cast<float4*>(g_out + row * d)[lane + 32 * i] = g;
       if (g_bf16) {
         float4 s4 = ls ? reinterpret_cast<const float4*>(ls)[lane + 32 * i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        if (drop_mask != nullptr) {  // the branch output was dropped: its gradient takes the same mask
+          const int col = 4 * (lane + 32 * i);
+          const uint32_t bits = (__ldg(drop_mask + row * (d >> 5) + (col >> 5)) >> (col & 31)) & 0xFu;
+          s4.x = (bits & 1u) ? s4.x * drop_scale : 0.f;
+          s4.y = (bits & 2u) ? s4.y * drop_scale : 0.f;
+          s4.z = (bits & 4u) ? s4.z * drop_scale : 0.f;
+          s4.w = (bits & 8u) ? s4.w * drop_scale : 0.f;
+        }
         reinterpret_cast<uint2*>(g_bf16 + row * d)[lane + 32 * i] =
             make_uint2(pack_bf16x2(g.x * s4.x, g.y * s4.y), pack_bf16x2(g.z * s4.z, g.w * s4.w));
       }
@@ -597,8 +606,12 @@ __global__ void __launch_bounds__(256, 3) qkv_prep_bwd_kernel(
 }
 
 // ============================================================================ embedding
+// x = emb[ids] (model/gpt.py:95), then nn.Dropout (model/gpt.py:96) when drop_mask != null: keep bits
+// of (row, column) from Philox block (column / 8, row, site, 0), written to drop_mask [M, d / 32].
 __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const float* __restrict__ emb,
-                                     float* __restrict__ x, int M, int d, int V, int* __restrict__ err) {
+                                     float* __restrict__ x, int M, int d, int V, int* __restrict__ err,
+                                     uint32_t* __restrict__ drop_mask, const unsigned long long* __restrict__ seed,
+                                     uint32_t site, uint32_t thresh, float scale) {
   griddep_wait();
   griddep_launch();
   const int warps = blockDim.x >> 5;
@@ -607,17 +620,40 @@ __global__ void embedding_fwd_kernel(const long long* __restrict__ ids, const fl
   const long long id = ids[row];
   const int lane = threadIdx.x & 31;
   float4* dst = reinterpret_cast<float4*>(x + row * d);
-  if (id < 0 || id >= V) {
-    if (lane == 0) atomicCAS(err, 0, RGPT_DEVERR_BAD_ARGS);
-    for (int c = lane; c < d / 4; c += 32) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    return;
+  const bool bad = id < 0 || id >= V;
+  if (bad && lane == 0) atomicCAS(err, 0, RGPT_DEVERR_BAD_ARGS);
+  const float4* src = reinterpret_cast<const float4*>(emb + (bad ? 0 : id) * d);
+  uint32_t k0 = 0, k1 = 0;
+  if (drop_mask != nullptr) {
+    const unsigned long long sd = *seed;
+    k0 = (uint32_t)sd;
+    k1 = (uint32_t)(sd >> 32);
   }
-  const float4* src = reinterpret_cast<const float4*>(emb + id * d);
-  for (int c = lane; c < d / 4; c += 32) dst[c] = src[c];
+  for (int c0 = 0; c0 < d / 4; c0 += 32) {  // warp-uniform trip count (d % 128 == 0 with dropout)
+    const int c = c0 + lane;
+    float4 v = (c < d / 4 && !bad) ? src[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (drop_mask != nullptr) {
+      // this lane's 4 columns are half of Philox block c / 2; groups of 8 lanes share one mask word
+      const uint32_t k8 = keep8(philox4x32_10(make_uint4((uint32_t)(c >> 1), (uint32_t)row, site, 0u), k0, k1),
+                                thresh);
+      const uint32_t b4 = (k8 >> (4 * (c & 1))) & 0xFu;
+      v.x = (b4 & 1u) ? v.x * scale : 0.f;
+      v.y = (b4 & 2u) ? v.y * scale : 0.f;
+      v.z = (b4 & 4u) ? v.z * scale : 0.f;
+      v.w = (b4 & 8u) ? v.w * scale : 0.f;
+      uint32_t word = b4 << (4 * (lane & 7));
+      word |= __shfl_xor_sync(0xffffffffu, word, 1);
+      word |= __shfl_xor_sync(0xffffffffu, word, 2);
+      word |= __shfl_xor_sync(0xffffffffu, word, 4);
+      if ((lane & 7) == 0 && c < d / 4) drop_mask[row * (d >> 5) + (c >> 3)] = word;
+    }
+    if (c < d / 4) dst[c] = v;
+  }
 }
 
 __global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const float* __restrict__ dx,
-                                     float* __restrict__ demb, int M, int d, int V) {
+                                     float* __restrict__ demb, int M, int d, int V,
+                                     const uint32_t* __restrict__ drop_mask, float scale) {
   griddep_wait();
   griddep_launch();
   const int warps = blockDim.x >> 5;
@@ -628,7 +664,17 @@ __global__ void embedding_bwd_kernel(const long long* __restrict__ ids, const fl
   const int lane = threadIdx.x & 31;
   const float4* src = reinterpret_cast<const float4*>(dx + row * d);
   float4* dst = reinterpret_cast<float4*>(demb + id * d);
-  for (int c = lane; c < d / 4; c += 32) atomicAdd(dst + c, src[c]);
+  for (int c = lane; c < d / 4; c += 32) {
+    float4 g = src[c];
+    if (drop_mask != nullptr) {  // the forward's dropout mask of this row
+      const uint32_t b4 = (__ldg(drop_mask + row * (d >> 5) + (c >> 3)) >> (4 * (c & 7))) & 0xFu;
+      g.x = (b4 & 1u) ? g.x * scale : 0.f;
+      g.y = (b4 & 2u) ? g.y * scale : 0.f;
+      g.z = (b4 & 4u) ? g.z * scale : 0.f;
+      g.w = (b4 & 8u) ? g.w * scale : 0.f;
+    }
+    atomicAdd(dst + c, g);
+  }
 }
 
 // ============================================================================ cross entropy
@@ -1075,8 +1121,11 @@ extern "C" int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w,
                                 float alpha, int M, int d, const float* g_in, float* g_out, void* g_bf16,
                                 const float* ls, const float* raw, float* dls, float* dw, float* dtemp,
                                 const float* dq, const float* qw, const void* h, float* dqw, float* dqb,
-                                void* stream) {
+                                const unsigned* drop_mask, float drop_p, void* stream) {
   const int nv = norm_nv(d);
+  if (drop_mask != nullptr && !(drop_p >= 0.0f && drop_p < 1.0f))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", drop_p);
+  const float drop_scale = (float)(1.0 / (1.0 - (double)drop_p));
   if (nv == 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rownorm needs d in {128,256,512,1024,2048} (got %d)", d);
   if (dy == nullptr && dq == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "rownorm_bwd needs dy or dq");
   if (dq && (qw == nullptr)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "q_head mode needs qw");
@@ -1096,7 +1145,8 @@ extern "C" int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w,
     constexpr int N = decltype(nv_tag)::value;
     const int cap2 = rgpt_num_sms(dev) * (N <= 4 ? 2 : 1);
     launch_pdl(rownorm_bwd_kernel<N, decltype(qm_tag)::value, decltype(dw_tag)::value, decltype(dls_tag)::value>, dim3(grid < cap2 ? grid : cap2), dim3(block), smem, s, 1, x, dy, w, temp, kind, eps, alpha, M, d, g_in, g_out, gb, ls,
-                                                        raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb);
+                                                        raw, dls, dw, dtemp, dq, qw, hb, dqw, dqb,
+                                                        reinterpret_cast<const uint32_t*>(drop_mask), drop_scale);
   };
   auto with_flags = [&](auto nv_tag) {
     using T_ = std::true_type;
@@ -1198,23 +1248,40 @@ extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* 
   return rgpt_check_launch("qkv_prep_bwd_kernel");
 }
 
+// Dropout arguments of the embedding kernels: a mask (null = no dropout), p in [0, 1), rows of
+// d % 128 == 0 columns, and (forward only) the device seed.
+static int check_drop(const void* mask, bool need_seed, const void* seed, float p, int d) {
+  if (mask == nullptr) return 0;
+  if (!(p >= 0.0f && p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", p);
+  if (d % 128 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout needs d %% 128 == 0 (got %d)", d);
+  if (need_seed && seed == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout needs a device seed");
+  return 0;
+}
+
 extern "C" int rgpt_embedding_fwd(const long long* ids, const float* emb, float* x, int M, int d, int V,
-                                  void* stream) {
+                                  unsigned* drop_mask, const unsigned long long* drop_seed, unsigned drop_site,
+                                  float drop_p, void* stream) {
   if (d % 4 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "embedding dim must be a multiple of 4");
+  if (int st = check_drop(drop_mask, true, drop_seed, drop_p, d)) return st;
   const int block = 256, rows_per = block / 32;
   int* err = nullptr;
   cudaGetSymbolAddress(reinterpret_cast<void**>(&err), g_rgpt_device_error);
+  const uint32_t thresh = (uint32_t)lrintf(drop_p * 65536.0f);
+  const float scale = (float)(1.0 / (1.0 - (double)drop_p));
   launch_pdl(embedding_fwd_kernel, dim3((M + rows_per - 1) / rows_per), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
-      ids, emb, x, M, d, V, err);
+      ids, emb, x, M, d, V, err, reinterpret_cast<uint32_t*>(drop_mask), drop_seed, (uint32_t)drop_site, thresh,
+      scale);
   return rgpt_check_launch("embedding_fwd_kernel");
 }
 
 extern "C" int rgpt_embedding_bwd(const long long* ids, const float* dx, float* demb, int M, int d, int V,
-                                  void* stream) {
+                                  const unsigned* drop_mask, float drop_p, void* stream) {
   if (d % 4 != 0) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "embedding dim must be a multiple of 4");
+  if (int st = check_drop(drop_mask, false, nullptr, drop_p, d)) return st;
   const int block = 256, rows_per = block / 32;
+  const float scale = (float)(1.0 / (1.0 - (double)drop_p));
   launch_pdl(embedding_bwd_kernel, dim3((M + rows_per - 1) / rows_per), dim3(block), 0, reinterpret_cast<cudaStream_t>(stream), 1, 
-      ids, dx, demb, M, d, V);
+      ids, dx, demb, M, d, V, reinterpret_cast<const uint32_t*>(drop_mask), scale);
   return rgpt_check_launch("embedding_bwd_kernel");
 }
 

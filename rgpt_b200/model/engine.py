@@ -26,7 +26,6 @@ gradient accumulation and shared (recurrent) layers need no extra adds.
 from __future__ import annotations
 
 import math
-import warnings
 
 from typing import Dict, List
 
@@ -116,6 +115,14 @@ class _Acts:
         self.losses = torch.zeros(4, device=dev, dtype=f32)
         self.scale_buf = torch.zeros(2, device=dev, dtype=f32)
         self.loss_rows = e(M, dt=f32)
+        # dropout keep bits, written by the forward and read by the backward (p > 0 only):
+        # embedding / residual branches [M, d/32], attention probabilities [B*H, ceil(T/32), T]
+        if eng.p_drop > 0:
+            i32 = torch.int32
+            self.drop_emb = e(M, d // 32, dt=i32)
+            self.drop_a = [e(M, d // 32, dt=i32) for _ in range(napp)]
+            self.drop_f = [e(M, d // 32, dt=i32) for _ in range(napp)]
+            self.drop_att = [e(B * H, (T + 31) // 32, T, dt=i32) for _ in range(napp)]
 
 
 class Engine:
@@ -142,10 +149,19 @@ class Engine:
         self.device = model.lm_head.weight.device
         if self.device.type != "cuda":
             raise RuntimeError("the native engine runs on CUDA devices only (no CPU path)")
+        self.p_drop = float(c.get("dropout", 0.0) or 0.0)
+        if not 0.0 <= self.p_drop < 1.0:
+            raise ValueError(f"dropout must be in [0, 1), got {self.p_drop}")
+        if self.p_drop > 0 and self.d % 128 != 0:
+            raise ValueError("native dropout needs d_model % 128 == 0")
+        # Philox key of the dropout masks: drawn from torch's default generator (so torch.manual_seed
+        # makes runs repeatable), kept on the device and advanced by one before every dropout forward,
+        # inside a captured step too.
+        self.drop_seed = torch.randint(0, 2 ** 62, (1,), dtype=torch.int64).to(self.device)
+        self._drop_active = False
         self._build_param_views()
         self._acts = {}
         self._spec_cache = {}
-        self._warned_dropout = False
 
     # ------------------------------------------------------------------ parameters
     def _build_param_views(self):
@@ -304,9 +320,6 @@ class Engine:
 
         Returns the _Acts holding logits / losses. grad_scale multiplies the stored dlogits."""
         m = self.model
-        if m.training and self.cfg.get("dropout", 0.0) > 0 and not self._warned_dropout:
-            warnings.warn("rgpt_b200: dropout is not implemented in the native kernels; running with p=0")
-            self._warned_dropout = True
         self.sync_shadows()
         B, T = input_ids.shape
         A = self.acts(B, T)
@@ -320,7 +333,11 @@ class Engine:
             lab = labels.reshape(-1)
             lab = (lab if lab.dtype == torch.int64 else lab.long()).contiguous()
         self._labels = lab
-        nv.embedding_fwd(self._ids, m.embs.weight, A.x[0])
+        # nn.Dropout is active in training mode (model/gpt.py:96, transformer_block.py:45,52, attention.py:57)
+        self._drop_active = m.training and self.p_drop > 0
+        if self._drop_active:
+            self.drop_seed.add_(1)
+        nv.embedding_fwd(self._ids, m.embs.weight, A.x[0], drop=self._drop(A, "emb"))
         halting = self.halting and lab is not None
         self._halting_active = halting
         app = 0
@@ -348,6 +365,22 @@ class Engine:
             torch.sum(A.losses[1:4], dim=0, keepdim=True, out=A.losses[0:1])
         return A
 
+    # dropout sites: the embedding, and per layer application app: 4*app + 0 (attention branch),
+    # + 1 (FFN branch), + 2 (attention probabilities)
+    EMB_DROP_SITE = 0xFFFFFF
+
+    def _drop(self, A, kind, app=0):
+        """The Drop spec of one site, or None when dropout is off for this pass."""
+        if not self._drop_active:
+            return None
+        if kind == "emb":
+            return nv.Drop(A.drop_emb, self.drop_seed, self.EMB_DROP_SITE, self.p_drop)
+        if kind == "attn_out":
+            return nv.Drop(A.drop_a[app], self.drop_seed, 4 * app, self.p_drop)
+        if kind == "ff_out":
+            return nv.Drop(A.drop_f[app], self.drop_seed, 4 * app + 1, self.p_drop)
+        return nv.Drop(A.drop_att[app], self.drop_seed, 4 * app + 2, self.p_drop)
+
     def _layer_fwd(self, blk, W, A, app):
         d, H, B, T, M = self.d, self.H, A.B, A.T, A.M
         at = blk.attn
@@ -363,15 +396,17 @@ class Engine:
             nv.gemm(A.qn[app].view(M * H, 64), W["wg"], A.gate[app].view(M * H, 64),
                     epi=nv.EPI_BIAS_SIGMOID_BF16, colscale=at.gate_proj.bias)
         nv.attn_fwd(A.qk[app], A.qkv[app], A.gate[app], A.o[app], A.og[app] if self.g1 else None, A.lse[app],
-                    B, T, H)
+                    B, T, H, drop=self._drop(A, "attn_p", app))
         nv.gemm(A.og[app], W["wo"], A.h[app], epi=nv.EPI_RESID_F32, c=x,
-                colscale=blk.attn_layer_scale if self.ls else None, out2=A.a_raw[app])
+                colscale=blk.attn_layer_scale if self.ls else None, out2=A.a_raw[app],
+                drop=self._drop(A, "attn_out", app))
         kind, eps, alpha, w, temp = self._resid_norm(blk, "ff_norm")
         nv.rownorm_fwd(A.h[app], A.hn2[app], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0,
                        alpha=alpha)
         nv.gemm(A.hn2[app], W["w1"], A.pre[app], epi=nv.EPI_ACT_FWD, act=self.act, out2=A.post[app])
         nv.gemm(A.post[app], W["w2"], A.x[app + 1], epi=nv.EPI_RESID_F32, c=A.h[app],
-                colscale=blk.ff_layer_scale if self.ls else None, out2=A.f_raw[app])
+                colscale=blk.ff_layer_scale if self.ls else None, out2=A.f_raw[app],
+                drop=self._drop(A, "ff_out", app))
 
     # ------------------------------------------------------------------ backward
     @torch.no_grad()
@@ -406,7 +441,8 @@ class Engine:
                        ls=last_blk.ff_layer_scale if (self.ls and need_gb_now) else None,
                        raw=A.f_raw[napp - 1] if need_gb_now else None,
                        dls=G[self._pname(last_blk, "ff_layer_scale")] if (self.ls and need_gb_now) else None,
-                       dw=G[lnf_w] if lnf_w else None, dtemp=G[lnf_t] if lnf_t else None)
+                       dw=G[lnf_w] if lnf_w else None, dtemp=G[lnf_t] if lnf_t else None,
+                       drop=self._drop(A, "ff_out", napp - 1) if need_gb_now else None)
         if halting:
             if alpha_dev is not None:
                 A.dq.mul_(alpha_dev)
@@ -422,7 +458,7 @@ class Engine:
                                raw=A.f_raw[app - 1], dls=G[self._pname(blk, "ff_layer_scale")] if self.ls else None,
                                dw=G[lnf_w] if lnf_w else None, dtemp=G[lnf_t] if lnf_t else None,
                                dq=A.dq[r], qw=m.q_head.weight, h=A.hq[r], dqw=G["q_head.weight"],
-                               dqb=G["q_head.bias"])
+                               dqb=G["q_head.bias"], drop=self._drop(A, "ff_out", app - 1))
             for li in reversed(range(self.L)):
                 app -= 1
                 first = app == 0
@@ -438,7 +474,7 @@ class Engine:
                 if cut:
                     A.g.zero_()
                     A.gb.zero_()
-        nv.embedding_bwd(self._ids, A.g, G["embs.weight"])
+        nv.embedding_bwd(self._ids, A.g, G["embs.weight"], drop=self._drop(A, "emb"))
         if sync is not None:
             if "pre" in self.grad_buckets:
                 sync.ready(self.grad_arena, *self.grad_buckets["pre"])
@@ -463,14 +499,16 @@ class Engine:
                        alpha=alpha, g_in=A.g, g_bf16=A.gb, ls=blk.attn_layer_scale if self.ls else None,
                        raw=A.a_raw[app], dls=G[pre + "attn_layer_scale"] if self.ls else None,
                        dw=G[pre + "ff_norm.weight"] if kind == nv.NORM_RMS_AFFINE else None,
-                       dtemp=G[pre + "ff_norm.temp"] if kind == nv.NORM_L2_TEMP else None)
+                       dtemp=G[pre + "ff_norm.temp"] if kind == nv.NORM_L2_TEMP else None,
+                       drop=self._drop(A, "attn_out", app))
         # ---------------- attention
         at = blk.attn
         nv.gemm(A.gb, W["wo"].t(), A.dog)
         nv.gemm(A.gb.t(), A.og[app].t(), G[pre + "attn.out_proj.weight"], epi=nv.EPI_ACCUM_F32, splitk=0)
         nv.attn_bwd_prep(A.dog, A.o[app], A.gate[app], A.do, A.dgp if self.g1 else None, A.D, B, T, H,
                          dq_zero=A.dqa)
-        nv.attn_bwd(A.qk[app], A.qkv[app], A.do, A.lse[app], A.D, A.dqa, A.dka, A.dqkv[:, 2 * d:], B, T, H)
+        nv.attn_bwd(A.qk[app], A.qkv[app], A.do, A.lse[app], A.D, A.dqa, A.dka, A.dqkv[:, 2 * d:], B, T, H,
+                    drop=self._drop(A, "attn_p", app))
         qs = self._qk_spec(at)
         qn = pre + "attn.qk_norm."
         dqn_gate = None
@@ -498,4 +536,5 @@ class Engine:
                        raw=None if first else A.f_raw[app - 1],
                        dls=G[self._pname(prev_blk, "ff_layer_scale")] if (self.ls and prev_blk is not None) else None,
                        dw=G[pre + "attn_norm.weight"] if kind == nv.NORM_RMS_AFFINE else None,
-                       dtemp=G[pre + "attn_norm.temp"] if kind == nv.NORM_L2_TEMP else None)
+                       dtemp=G[pre + "attn_norm.temp"] if kind == nv.NORM_L2_TEMP else None,
+                       drop=None if first else self._drop(A, "ff_out", app - 1))

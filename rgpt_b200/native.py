@@ -30,6 +30,30 @@ def act_id(name: str) -> int:
         raise ValueError(f"unknown activation {name!r}") from e
 
 
+class Drop:
+    """Dropout of one site: keep bits are drawn from Philox4x32-10 under the device seed (int64 [1])
+    and the site number, and stored in `mask` (int32 words) for the backward; p is the drop rate."""
+
+    __slots__ = ("mask", "seed", "site", "p")
+
+    def __init__(self, mask: torch.Tensor, seed: torch.Tensor | None, site: int, p: float):
+        if mask.dtype != torch.int32 or not mask.is_contiguous():
+            raise ValueError("dropout masks are contiguous int32 words")
+        if seed is not None and (seed.dtype != torch.int64 or seed.numel() != 1):
+            raise ValueError("dropout seed is a device int64 [1]")
+        if not 0.0 <= p < 1.0:
+            raise ValueError(f"dropout p must be in [0, 1), got {p}")
+        self.mask, self.seed, self.site, self.p = mask, seed, int(site), float(p)
+
+
+def _drop_args(drop: "Drop | None", seed_needed: bool = True):
+    if drop is None:
+        return None, None, 0, 0.0
+    if seed_needed and drop.seed is None:
+        raise ValueError("this dropout call draws new bits and needs the seed")
+    return ptr(drop.mask), ptr(drop.seed) if drop.seed is not None else None, drop.site & 0xFFFFFFFF, drop.p
+
+
 def _operand(t: torch.Tensor):
     """(mn_major, ld, bstride) for a logical [.., rows, K] bf16 operand view."""
     if t.dtype != torch.bfloat16:
@@ -60,7 +84,7 @@ gemm_events: list | None = None
 def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_STORE_BF16,
          act: int = 0, alpha: float = 1.0, beta: float = 0.0, out2: torch.Tensor | None = None,
          c: torch.Tensor | None = None, colscale: torch.Tensor | None = None, splitk: int = 1,
-         alpha_dev: torch.Tensor | None = None) -> torch.Tensor:
+         alpha_dev: torch.Tensor | None = None, drop: Drop | None = None) -> torch.Tensor:
     """out = epilogue(A @ B^T) for logical A [(b,) M, K] and B [(b,) N, K] (bf16).
 
     Either operand may be K-major (unit stride on K) or MN-major (unit stride
@@ -86,11 +110,20 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-    _lib.call("rgpt_gemm_bf16",
-              ptr(A), a_mn, lda, abs_, ptr(B), b_mn, ldb, bbs,
-              M, N, K, batch, epi, act, float(alpha), float(beta),
-              d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
-              ptr(colscale), splitk, ptr(alpha_dev), _lib.stream_ptr(out.device))
+    if drop is None:
+        _lib.call("rgpt_gemm_bf16",
+                  ptr(A), a_mn, lda, abs_, ptr(B), b_mn, ldb, bbs,
+                  M, N, K, batch, epi, act, float(alpha), float(beta),
+                  d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
+                  ptr(colscale), splitk, ptr(alpha_dev), _lib.stream_ptr(out.device))
+    else:
+        dm, ds, dsite, dp = _drop_args(drop)
+        _lib.call("rgpt_gemm_bf16_dropout",
+                  ptr(A), a_mn, lda, abs_, ptr(B), b_mn, ldb, bbs,
+                  M, N, K, batch, epi, act, float(alpha), float(beta),
+                  d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
+                  ptr(colscale), splitk, ptr(alpha_dev), dm, drop.mask.shape[-1], ds, dsite, dp,
+                  _lib.stream_ptr(out.device))
     if ev is not None:
         e1.record()
         ev.append((e0, e1, 2.0 * M * N * K * batch))
@@ -106,7 +139,7 @@ def _check(t, dtype, name):
 
 
 def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: torch.Tensor,
-             og: torch.Tensor | None, lse: torch.Tensor, B: int, T: int, H: int) -> None:
+             og: torch.Tensor | None, lse: torch.Tensor, B: int, T: int, H: int, drop: Drop | None = None) -> None:
     """Causal attention over token-major q/k (qk [B*T, 2d]) and v (qkv[:, 2d:3d]).
 
     Writes o [B*T, d] (bf16), og = o * gate (if gate given) and lse [B, H, T] (fp32)."""
@@ -117,8 +150,10 @@ def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: 
         raise ValueError("attention shapes do not match [B*T, 2d] / [B*T, 3d] / [B*T, d]")
     if lse.dtype != torch.float32 or lse.numel() != B * H * T:
         raise ValueError("lse must be fp32 [B, H, T]")
+    if drop is not None and drop.mask.numel() < B * H * ((T + 31) // 32) * T:
+        raise ValueError("attention dropout mask must hold [B*H, ceil(T/32), T] words")
     _lib.call("rgpt_attn_fwd", ptr(qk), ptr(qkv), ptr(gate), ptr(o), ptr(og), ptr(lse), B, T, H, d,
-              _lib.stream_ptr(o.device))
+              *_drop_args(drop), _lib.stream_ptr(o.device))
 
 
 def attn_bwd_prep(dog: torch.Tensor, o: torch.Tensor, gate: torch.Tensor | None, do: torch.Tensor,
@@ -135,13 +170,19 @@ def attn_bwd_prep(dog: torch.Tensor, o: torch.Tensor, gate: torch.Tensor | None,
 
 
 def attn_bwd(qk: torch.Tensor, qkv: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, D: torch.Tensor,
-             dq: torch.Tensor, dk: torch.Tensor, dv: torch.Tensor, B: int, T: int, H: int) -> None:
-    """dq (fp32, accumulated: caller zeroes), dk (fp32) and dv (bf16, may be a strided column view)."""
+             dq: torch.Tensor, dk: torch.Tensor, dv: torch.Tensor, B: int, T: int, H: int,
+             drop: Drop | None = None) -> None:
+    """dq (fp32, accumulated: caller zeroes), dk (fp32) and dv (bf16, may be a strided column view).
+
+    drop: the forward's attention dropout (its mask is read back; no new bits are drawn)."""
     d = H * 64
     if dq.dtype != torch.float32 or dk.dtype != torch.float32 or dv.dtype != torch.bfloat16:
         raise TypeError("dq/dk must be fp32 and dv bf16")
+    if drop is not None and drop.mask.numel() < B * H * ((T + 31) // 32) * T:
+        raise ValueError("attention dropout mask must hold [B*H, ceil(T/32), T] words")
+    dm, _, _, dp = _drop_args(drop, seed_needed=False)
     _lib.call("rgpt_attn_bwd", ptr(qk), ptr(qkv), ptr(do), ptr(lse), ptr(D), ptr(dq), ptr(dk), dk.stride(0),
-              ptr(dv), dv.stride(0), B, T, H, d, _lib.stream_ptr(do.device))
+              ptr(dv), dv.stride(0), B, T, H, d, dm, dp, _lib.stream_ptr(do.device))
 
 
 # ----------------------------------------------------------------------------- norms
@@ -164,11 +205,15 @@ def rownorm_bwd(x: torch.Tensor, dy: torch.Tensor | None, kind: int, eps: float,
                 ls: torch.Tensor | None = None, raw: torch.Tensor | None = None, dls: torch.Tensor | None = None,
                 dw: torch.Tensor | None = None, dtemp: torch.Tensor | None = None,
                 dq: torch.Tensor | None = None, qw: torch.Tensor | None = None, h: torch.Tensor | None = None,
-                dqw: torch.Tensor | None = None, dqb: torch.Tensor | None = None) -> None:
+                dqw: torch.Tensor | None = None, dqb: torch.Tensor | None = None, drop: Drop | None = None) -> None:
+    """drop: the dropout of the branch whose gradient g_bf16 is (its mask, read back; no new bits)."""
     M, d = x.shape
+    if drop is not None and drop.mask.numel() < M * (d // 32):
+        raise ValueError("branch dropout mask must hold [M, d/32] words")
+    dm, _, _, dp = _drop_args(drop, seed_needed=False)
     _lib.call("rgpt_rownorm_bwd", ptr(x), ptr(dy), ptr(w), float(temp), kind, float(eps), float(alpha), M, d,
               ptr(g_in), ptr(g_out), ptr(g_bf16), ptr(ls), ptr(raw), ptr(dls), ptr(dw), ptr(dtemp),
-              ptr(dq), ptr(qw), ptr(h), ptr(dqw), ptr(dqb), _lib.stream_ptr(x.device))
+              ptr(dq), ptr(qw), ptr(h), ptr(dqw), ptr(dqb), dm, dp, _lib.stream_ptr(x.device))
 
 
 # ----------------------------------------------------------------------------- QKV prep
@@ -186,16 +231,21 @@ def qkv_prep_bwd(qkv, dq, dk, dqn_gate, dgp, dqkv, inv_freq, qk_kind, eps, alpha
 
 
 # ----------------------------------------------------------------------------- embedding / loss
-def embedding_fwd(ids: torch.Tensor, emb: torch.Tensor, x: torch.Tensor) -> None:
+def embedding_fwd(ids: torch.Tensor, emb: torch.Tensor, x: torch.Tensor, drop: Drop | None = None) -> None:
     M = ids.numel()
     V, d = emb.shape
-    _lib.call("rgpt_embedding_fwd", ptr(ids), ptr(emb), ptr(x), M, d, V, _lib.stream_ptr(x.device))
+    if drop is not None and drop.mask.numel() < M * (d // 32):
+        raise ValueError("embedding dropout mask must hold [M, d/32] words")
+    _lib.call("rgpt_embedding_fwd", ptr(ids), ptr(emb), ptr(x), M, d, V, *_drop_args(drop), _lib.stream_ptr(x.device))
 
 
-def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, demb: torch.Tensor) -> None:
+def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, demb: torch.Tensor, drop: Drop | None = None) -> None:
     M = ids.numel()
     V, d = demb.shape
-    _lib.call("rgpt_embedding_bwd", ptr(ids), ptr(dx), ptr(demb), M, d, V, _lib.stream_ptr(dx.device))
+    if drop is not None and drop.mask.numel() < M * (d // 32):
+        raise ValueError("embedding dropout mask must hold [M, d/32] words")
+    dm, _, _, dp = _drop_args(drop, seed_needed=False)
+    _lib.call("rgpt_embedding_bwd", ptr(ids), ptr(dx), ptr(demb), M, d, V, dm, dp, _lib.stream_ptr(dx.device))
 
 
 def cross_entropy(logits: torch.Tensor, labels: torch.Tensor, *, ignore_index: int = -100, grad_scale: float = 1.0,

@@ -145,3 +145,27 @@ def test_training_loss_curve_matches_reference(tag, accum):
     # q_head starts at zero, so it is judged by absolute difference as well.
     for k, v in final.items():
         assert rel(v, t["final"][k]) < 1e-2 or (v - t["final"][k]).abs().max().item() < 5e-4, k
+
+
+def test_oracle_philox_matches_published_known_answers():
+    """The oracle's Philox4x32-10 (dropout masks) against the known-answer vectors published with
+    Random123 (Salmon et al., SC 2011): counter/key all zeros, all ones, and the digits of pi."""
+    kat = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+           ((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2, (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+           ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+            (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in kat:
+        got = tuple(int(w) for w in O.philox4x32_10(*ctr, *key))
+        assert got == want, (ctr, key, [hex(g) for g in got])
+
+
+def test_oracle_dropout_masks_rate_and_independence():
+    """keep rate ~ 1 - p; different sites, seeds and heads give different masks."""
+    m = O.resid_drop_mask(2024, 5, 256, 512, 0.1)
+    assert abs(m.float().mean().item() - 0.9) < 0.005
+    assert not torch.equal(m, O.resid_drop_mask(2024, 6, 256, 512, 0.1))
+    assert not torch.equal(m, O.resid_drop_mask(2025, 5, 256, 512, 0.1))
+    a = O.attn_drop_mask(1, 2, 1, 2, 128, 0.3)
+    assert abs(a.float().mean().item() - 0.7) < 0.01
+    assert not torch.equal(a[0, 0], a[0, 1])
+    assert O.resid_drop_mask(9, 1, 8, 64, 0.0).all()
