@@ -43,7 +43,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-COMMON = dict(detach_recur=False, max_seq_len=1024, dropout=0.0, norm_type="rmsnorm", norm_eps=1e-5,
+# dropout 0.1: the value of every model config of the reference (conf/model/*.yaml)
+COMMON = dict(detach_recur=False, max_seq_len=1024, dropout=0.1, norm_type="rmsnorm", norm_eps=1e-5,
               qk_normtype="f_rmsnorm", activation_type="squared_relu", g1_gate=True, pad_token_id=-100,
               tie_word_embeddings=False, vocab_size=50304)
 WORKLOADS = {
@@ -303,7 +304,8 @@ def _cpu_train_steps(cfg, T, n_steps, threads):
     for micro in batches:
         t0 = time.perf_counter()
         ids, labels = micro[0]
-        out = O.gpt_forward(params, ids[:, :-1], cfg, labels=labels[:, 1:].contiguous(), training=True)
+        out = O.gpt_forward(params, ids[:, :-1], cfg, labels=labels[:, 1:].contiguous(), training=True,
+                            drop_seed="torch")
         loss, _ = O.compute_loss(out, labels[:, 1:])
         grads = dict(zip(params, torch.autograd.grad(loss, list(params.values()), allow_unused=True)))
         opt.step({k: v for k, v in grads.items() if v is not None})
@@ -318,7 +320,8 @@ def cpu_baseline(cfg, T, budget_s=30.0):
     times = _cpu_train_steps(cfg, T, n, threads)
     per_step = statistics.median(times)
     return {"value": round(T / per_step, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} oracle training steps (forward, CE, backward, Muon+AdamW) on 1 sequence x {T} tokens, "
+            "sample": f"{n} oracle training steps (forward, CE, backward, Muon+AdamW, dropout "
+                      f"{cfg['dropout']} from torch's generator) on 1 sequence x {T} tokens, "
                       f"fp32 CPU, median step {per_step:.2f} s"}
 
 
@@ -326,7 +329,9 @@ def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    cfg, T = wl["cfg"], wl["T"]
+    cfg, T = dict(wl["cfg"]), wl["T"]
+    if args.dropout is not None:
+        cfg["dropout"] = args.dropout
     threads = os.cpu_count() or 1
     _cpu_train_steps(cfg, T, max(1, min(args.warmup, 2)), threads)
     times = _cpu_train_steps(cfg, T, args.steps, threads)
@@ -338,7 +343,8 @@ def run_reference(args, wl):
         "ms_per_step": round(ms, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic: uniform random token ids, random-init weights (seeded)",
         "config": {"workload": args.workload, "model": cfg["name"], "seq_len": T, "micro_batch": 1,
-                   "parallelism": "cpu", "note": "one 1024-token sequence per step (bounded CPU sample)"},
+                   "parallelism": "cpu", "dropout": cfg["dropout"],
+                   "note": "one 1024-token sequence per step (bounded CPU sample)"},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} oracle training steps on 1 x {T} tokens (fp32, all host threads)"},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -270,7 +270,10 @@ def attention_forward(x, params, prefix, cfg, drop=None):
     q, k = rope_apply(q, k, cos, sin)
     keep = None
     if drop is not None:
-        keep = attn_drop_mask(drop["seed"], drop["site"] + 2, B, H, T, drop["p"])
+        if drop["seed"] == "torch":  # torch's own generator, as the reference draws it (timing only)
+            keep = torch.rand(B, H, T, T) >= drop["p"]
+        else:
+            keep = attn_drop_mask(drop["seed"], drop["site"] + 2, B, H, T, drop["p"])
     o = causal_attention(q, k, v, 1.0 / math.sqrt(Dh), keep, drop["p"] if drop else 0.0)
     if gate is not None:
         o = o * gate
@@ -282,6 +285,8 @@ def _dropped(y, drop, site):
     """nn.Dropout with the native kernels' mask of `site` over the rows of y [B, T, d]."""
     if drop is None:
         return y
+    if drop["seed"] == "torch":  # torch's own dropout, as the reference runs it (timing only)
+        return F.dropout(y, drop["p"], training=True)
     B, T, d = y.shape
     keep = resid_drop_mask(drop["seed"], site, B * T, d, drop["p"]).view(B, T, d)
     return y * keep.to(y.dtype) * (1.0 / (1.0 - drop["p"]))
@@ -312,6 +317,8 @@ def gpt_forward(params, input_ids, cfg, labels=None, training=True, drop_seed=No
     Dropout is off unless drop_seed is given (with training and cfg["dropout"] > 0): then the
     embedding output uses site EMB_DROP_SITE and layer application `app` (recurrence i, layer li,
     app = i * n_layers + li) sites 4 * app + {0, 1, 2}, the masks of the native kernels.
+    drop_seed="torch" draws the masks from torch's generator instead, as the reference does; only
+    the timed CPU baseline uses it (its masks cannot be compared with anything).
     Returns (final_logits, accum_halt_loss, all_step_q, target_q_continues)."""
     d = cfg["d_model"]
     nt, eps = cfg["norm_type"], cfg["norm_eps"]
