@@ -157,7 +157,11 @@ class Engine:
         # Philox key of the dropout masks: drawn from torch's default generator (so torch.manual_seed
         # makes runs repeatable), kept on the device and advanced by one before every dropout forward,
         # inside a captured step too.
-        self.drop_seed = torch.randint(0, 2 ** 62, (1,), dtype=torch.int64).to(self.device)
+        seed = int(torch.randint(0, 2 ** 62, (1,), dtype=torch.int64))
+        if torch.distributed.is_available() and torch.distributed.is_initialized():
+            # data-parallel ranks seeded alike still draw independent masks
+            seed ^= (torch.distributed.get_rank() * 0x9E3779B97F4A7C15) & (2 ** 62 - 1)
+        self.drop_seed = torch.tensor([seed], dtype=torch.int64).to(self.device)
         self._drop_active = False
         self._build_param_views()
         self._acts = {}
