@@ -14,7 +14,20 @@ sizes (16 x 1024 tokens, d_model 512, 8 heads, FFN 2048, vocabulary 50304):
   7. lm_head forward GEMM  logits = h Wlm^T  (4096 x 50304, K = 512; CTA pairs, bf16 store)
   8. G1 gate GEMM          gate = sigmoid(q_n Wg^T + bg)  (131072 x 64, K = 64; bias+sigmoid epilogue)
 Device memory stays under 2 GB, so a multi-pass profiler capture saves and restores little.
+
+    python -m rgpt_b200.prof bw
+
+runs instead the bandwidth-bound kernels and the optimizer of the same step, once each:
+  rownorm forward / backward (16384 x 512), QKV prep forward / backward (QK-norm + RoPE + gate
+  input), attention backward prep, embedding forward / backward, cross entropy over all 16384 rows,
+  then one Muon + AdamW step over the gpt-small parameter shapes (AdamW over 51.5 M parameters;
+  Muon: momentum/transposition, the batched Newton-Schulz GEMMs of the [512, 512] x 32 and
+  [512, 2048] x 16 classes, apply), one fp32 Newton-Schulz iteration of one [512, 2048] matrix,
+  and the dropout-0.1 variants of the attention forward and the residual GEMM. Device memory stays
+  under 3 GB.
 """
+import sys
+
 import torch
 
 from rgpt_b200 import native as nv
@@ -69,5 +82,94 @@ def main() -> None:
     print("rgpt_b200.prof: ok")
 
 
+def bandwidth_and_optimizer() -> None:
+    from rgpt_b200.optimizer import Muon, newton_schulz_batched_f32, _NSWorkspaceF32
+
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(1)
+    def rb(*shape):
+        return torch.randn(*shape, device=dev, generator=g).bfloat16()
+    def rf(*shape):
+        return torch.randn(*shape, device=dev, generator=g)
+
+    B, T, H, d, V = 16, 1024, 8, 512, 50304
+    M = B * T
+    # rownorm forward (RMSNorm, (1 + w)) and backward with the residual-gradient add and dw
+    x, w = rf(M, d), rf(d) * 0.1
+    y = torch.empty(M, d, device=dev, dtype=torch.bfloat16)
+    nv.rownorm_fwd(x, y, nv.NORM_RMS_AFFINE, 1e-5, w=w)
+    dy, gi = rf(M, d), rf(M, d)
+    go = torch.empty(M, d, device=dev); gb = torch.empty(M, d, device=dev, dtype=torch.bfloat16)
+    dw = torch.zeros(d, device=dev)
+    nv.rownorm_bwd(x, dy, nv.NORM_RMS_AFFINE, 1e-5, go, w=w, g_in=gi, g_bf16=gb, dw=dw)
+    # QKV prep (f_rmsnorm QK norm, RoPE, normalised q for the G1 gate) forward and backward
+    qkv = rb(M, 3 * d)
+    qk = torch.empty(M, 2 * d, device=dev, dtype=torch.bfloat16); qn = torch.empty(M, d, device=dev,
+                                                                                     dtype=torch.bfloat16)
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device=dev, dtype=torch.float32) / 64))
+    nv.qkv_prep_fwd(qkv, qk, qn, inv_freq, nv.NORM_RMS, nv.FLT_EPS, 0.5, M, T, H)
+    dq, dk, dqn, dgp = rf(M, d), rf(M, d), rf(M, d), rb(M, d)
+    dqkv = torch.empty(M, 3 * d, device=dev, dtype=torch.bfloat16); dbg = torch.zeros(64, device=dev)
+    nv.qkv_prep_bwd(qkv, dq, dk, dqn, dgp, dqkv, inv_freq, nv.NORM_RMS, nv.FLT_EPS, 0.5, M, T, H, dbg=dbg)
+    # attention backward prep (gate product, D = rowsum(do * o), dq zeroing)
+    dog, o = rb(M, d), rb(M, d)
+    gate = torch.sigmoid(rf(M, d)).bfloat16()
+    do, dgate = torch.empty_like(o), torch.empty_like(o)
+    D = torch.empty(B, H, T, device=dev)
+    nv.attn_bwd_prep(dog, o, gate, do, dgate, D, B, T, H, dq_zero=dq)
+    del qkv, qk, qn, dqkv, dk, dqn, dgp, dog, do, dgate
+    # embedding forward / backward
+    ids = torch.randint(0, V, (M,), device=dev, generator=g)
+    emb = rf(V, d) * 0.02
+    xe = torch.empty(M, d, device=dev)
+    nv.embedding_fwd(ids, emb, xe)
+    demb = torch.zeros(V, d, device=dev)
+    nv.embedding_bwd(ids, dy, demb)
+    del emb, demb, xe
+    # cross entropy over the whole step's logits, gradient in place
+    logits = rb(M, V)
+    labels = torch.randint(0, V, (M,), device=dev, generator=g)
+    rows = torch.empty(M, device=dev); sb = torch.empty(4, device=dev); lo = torch.empty(1, device=dev)
+    nv.cross_entropy(logits, labels, loss_rows=rows, scale_buf=sb, loss_out=lo, write_grad=True)
+    del logits
+    torch.cuda.synchronize(); torch.cuda.empty_cache()
+    # one optimizer step over the gpt-small parameter shapes (the Trainer's groups)
+    L = 8
+    mats = [torch.nn.Parameter(rf(*s) * 0.02) for _ in range(L)
+            for s in [(d, d)] * 4 + [(4 * d, d), (d, 4 * d), (64, 64)]]
+    big = [torch.nn.Parameter(rf(V, d) * 0.02), torch.nn.Parameter(rf(V, d) * 0.02)]  # embs, lm_head
+    vecs = [torch.nn.Parameter(torch.zeros(d, device=dev)) for _ in range(2 * L + 1)] + \
+           [torch.nn.Parameter(torch.zeros(64, device=dev)) for _ in range(L)]
+    for p_ in mats + big + vecs:
+        p_.grad = torch.randn(p_.shape, device=dev, generator=g) * 1e-3
+    opt = Muon([{"params": mats, "use_muon": True}, {"params": big[1:], "use_muon": False, "weight_decay": 0.1},
+                {"params": big[:1] + vecs, "use_muon": False, "weight_decay": 0.0}],
+               lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
+    opt.step()
+    torch.cuda.synchronize()
+    del opt, mats, big, vecs; torch.cuda.empty_cache()
+    # one fp32 Newton-Schulz iteration of one [512, 2048] matrix (hi/lo split, POLY_F32)
+    ws = _NSWorkspaceF32(1, d, 4 * d, dev)
+    ws.X.copy_(rf(1, d, 4 * d) * (1.0 / 1024))
+    newton_schulz_batched_f32(ws, 1)
+    # dropout 0.1: attention forward and the residual GEMM with the branch mask
+    qk2, qkv2 = rb(M, 2 * d), rb(M, 3 * d)
+    o2, og2 = torch.empty(M, d, device=dev, dtype=torch.bfloat16), torch.empty(M, d, device=dev,
+                                                                                  dtype=torch.bfloat16)
+    lse = torch.empty(B, H, T, device=dev)
+    seed = torch.tensor([12345], dtype=torch.int64, device=dev)
+    amask = torch.empty(B * H, T // 32, T, device=dev, dtype=torch.int32)
+    nv.attn_fwd(qk2, qkv2, gate, o2, og2, lse, B, T, H, drop=nv.Drop(amask, seed, 2, 0.1))
+    wo = rb(d, d)
+    hout = torch.empty(M, d, device=dev)
+    rmask = torch.empty(M, d // 32, device=dev, dtype=torch.int32)
+    nv.gemm(og2, wo, hout, epi=nv.EPI_RESID_F32, c=x, drop=nv.Drop(rmask, seed, 0, 0.1))
+    torch.cuda.synchronize()
+    print("rgpt_b200.prof bw: ok")
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "bw":
+        bandwidth_and_optimizer()
+    else:
+        main()
