@@ -188,6 +188,12 @@ class Muon(torch.optim.Optimizer):
         super().__init__(params, defaults)
         self._cache: Dict[Any, Any] = {}
         self._hp_dev: Optional[torch.Tensor] = None
+        # Independent update jobs (each Newton-Schulz shape class, each AdamW group) run on their own
+        # CUDA streams, forked from and joined back into the caller's stream (inside a captured step
+        # too), so the HBM-bound AdamW overlaps the small Newton-Schulz GEMMs and the shape classes
+        # overlap each other's tails. Set to False to issue everything on the caller's stream.
+        self.concurrent = True
+        self._streams: List[torch.cuda.Stream] = []
 
     # ------------------------------------------------------------------ device scalars
     def use_device_hparams(self) -> None:
@@ -273,16 +279,46 @@ class Muon(torch.optim.Optimizer):
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        jobs = []
         for gi, group in enumerate(self.param_groups):
+            ps = [p for p in group["params"] if p.grad is not None]
             if group.get("use_muon", False):
-                self._muon_group(gi, group, [p for p in group["params"] if p.grad is not None])
+                jobs += self._muon_jobs(gi, group, ps)
             else:
-                self._adamw_group(gi, group, [p for p in group["params"] if p.grad is not None])
+                jobs += self._adamw_jobs(gi, group, ps)
+        self._run_jobs(jobs)
         return loss
 
-    def _muon_group(self, gi, group, params, owned=None):
-        if not params:
+    def _run_jobs(self, jobs) -> None:
+        """Run the launch-only closures: the first on the current stream, the others each on a
+        side stream that waits for the current stream first and is waited for at the end."""
+        if len(jobs) <= 1 or not self.concurrent:
+            for job in jobs:
+                job()
             return
+        main = torch.cuda.current_stream()
+        while len(self._streams) < len(jobs) - 1:
+            self._streams.append(torch.cuda.Stream(device=main.device))
+        side = self._streams[:len(jobs) - 1]
+        for st in side:
+            st.wait_stream(main)
+        for job, st in zip(jobs[1:], side):
+            with torch.cuda.stream(st):
+                job()
+        jobs[0]()
+        for st in side:
+            main.wait_stream(st)
+
+    def _muon_group(self, gi, group, params):
+        """Plan and run one Muon group on the current stream."""
+        for job in self._muon_jobs(gi, group, params):
+            job()
+
+    def _muon_jobs(self, gi, group, params):
+        """Per Newton-Schulz shape class, a closure that launches its kernels. State, descriptor
+        tables and workspaces are created here, on the caller's stream."""
+        if not params:
+            return []
         lr = float(group["lr"])
         wd = float(group["weight_decay"])
         muon_lr = lr * float(group["muon_lr_multiplier"])
@@ -300,6 +336,7 @@ class Muon(torch.optim.Optimizer):
             R, C = p.shape[0], p.numel() // p.shape[0]
             xr, xc = (C, R) if R > C else (R, C)
             classes.setdefault((xr, xc), {}).setdefault((R, C), []).append(p)
+        jobs = []
         for (xr, xc), subs in classes.items():
             ordered = [(rc, ps) for rc, ps in sorted(subs.items())]
             all_ps = [p for _, ps in ordered for p in ps]
@@ -315,18 +352,30 @@ class Muon(torch.optim.Optimizer):
                 ent = (tables, _NSWorkspace(len(all_ps), xr, xc, dev))
                 self._cache[key] = ent
             tables, ws = ent
-            ws.sumsq.zero_()
-            for R, C, off, n, table in tables:
-                nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n],
-                             hp=self._hp(gi))
-            nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
-            out = newton_schulz_batched(ws, steps, coeffs)
-            for R, C, off, n, table in tables:
-                nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C), hp=self._hp(gi))
+
+            def run(tables=tables, ws=ws):
+                ws.sumsq.zero_()
+                for R, C, off, n, table in tables:
+                    nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n],
+                                 hp=self._hp(gi))
+                nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
+                out = newton_schulz_batched(ws, steps, coeffs)
+                for R, C, off, n, table in tables:
+                    nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C),
+                                  hp=self._hp(gi))
+            jobs.append(run)
+        return jobs
 
     def _adamw_group(self, gi, group, params):
+        """Plan and run one AdamW group on the current stream."""
+        for job in self._adamw_jobs(gi, group, params):
+            job()
+
+    def _adamw_jobs(self, gi, group, params):
+        """A closure launching the group's multi-tensor AdamW kernel (the step counter and the
+        optimizer state are advanced / created here, on the caller's stream)."""
         if not params:
-            return
+            return []
         lr = float(group["lr"])
         wd = float(group["weight_decay"])
         beta1, beta2 = group["adam_betas"]
@@ -359,7 +408,8 @@ class Muon(torch.optim.Optimizer):
                    torch.tensor(cs, dtype=torch.int64).to(dev))
             self._cache[key] = ent
         table, ct, cs = ent
-        nv.adamw(table, ct, cs, _ADAM_CHUNK, lr, wd, float(beta1), float(beta2), eps, step_i, hp=self._hp(gi))
+        return [lambda: nv.adamw(table, ct, cs, _ADAM_CHUNK, lr, wd, float(beta1), float(beta2), eps, step_i,
+                                 hp=self._hp(gi))]
 
 
 class DistMuon(Muon):
