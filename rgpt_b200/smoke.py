@@ -1,5 +1,8 @@
 """One tiny native training step on cuda:0 checked against the CPU oracle.
 
+The step is an rGPT one (recurrence, halting loss, layer scale) with dropout 0.1, the reference
+configs' rate; the oracle regenerates the kernels' dropout masks from the same seed.
+
 The oracle is imported here only as the checker (this module backs
 __graft_entry__.smoke()); the step itself runs the native kernels."""
 import torch
@@ -12,7 +15,7 @@ def run_smoke() -> None:
     from .optimizer import Muon, trainer_param_groups
 
     cfg = dict(name="rgpt", n_layers=1, n_recur=2, detach_recur=False, cal_halt_loss=True, n_heads=2, d_model=128,
-               vocab_size=384, max_seq_len=128, dropout=0.0, norm_type="rmsnorm", norm_eps=1e-5,
+               vocab_size=384, max_seq_len=128, dropout=0.1, norm_type="rmsnorm", norm_eps=1e-5,
                qk_normtype="f_rmsnorm", activation_type="squared_relu", g1_gate=True, use_layer_scale=True,
                pad_token_id=-100, tie_word_embeddings=False)
     dev = torch.device("cuda", 0)
@@ -23,6 +26,7 @@ def run_smoke() -> None:
     model = model.to(dev).train()
     opt = Muon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
     total, tok, q = model.forward_loss(ids[:, :-1].to(dev), ids[:, 1:].contiguous().to(dev))
+    drop_seed = int(model.engine().drop_seed.item())  # the Philox key of this forward's masks
     total.backward()
     g_ours = model.lm_head.weight.grad.detach().cpu().clone()
     opt.step()
@@ -30,7 +34,8 @@ def run_smoke() -> None:
 
     params = {k: v.clone().requires_grad_(True) for k, v in state.items()
               if v.is_floating_point() and not k.endswith((".eps", "inv_freq"))}
-    out = O.gpt_forward(params, ids[:, :-1], cfg, labels=ids[:, 1:].contiguous(), training=True)
+    out = O.gpt_forward(params, ids[:, :-1], cfg, labels=ids[:, 1:].contiguous(), training=True,
+                        drop_seed=drop_seed)
     ref_loss, _ = O.compute_loss(out, ids[:, 1:])
     ref_loss.backward()
     lrel = abs(total.item() - ref_loss.item()) / abs(ref_loss.item())
