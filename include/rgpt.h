@@ -68,18 +68,21 @@ int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bst
                    const void* C, long long ldc, long long c_bstride,
                    const float* colscale, int splitk, const float* alpha_dev, void* stream);
 /* RGPT_DROPOUT. rgpt_gemm_bf16 with the residual-branch dropout of model/transformer_block.py:45,52 fused
- * into the RESID_F32 epilogue (batch 1 only): the branch output alpha*acc*colscale becomes
- * alpha*acc*keep/(1-drop_p) (D2 stores that dropped branch output), keep drawn for (row, column) from
- * Philox4x32-10 block (column/8, row, drop_site, 0) under key (*drop_seed low, high 32 bits), element
- * column%8 = 16-bit half (column%2) of word (column%8)/2, kept iff >= round(drop_p*65536); the bits go to
- * drop_mask[row*drop_ldm + column/32]. */
+ * into the RESID_F32 epilogue (batch 1 only): the branch output alpha*acc becomes alpha*acc*keep/(1-drop_p)
+ * (D2 stores that dropped branch output), keep = bit column%32 of drop_mask[row*drop_ldm + column/32]. */
 int rgpt_gemm_bf16_dropout(const void* A, int a_mn_major, long long lda, long long a_bstride,
                            const void* B, int b_mn_major, long long ldb, long long b_bstride,
                            int M, int N, int K, int batch, int epi, int act, float alpha, float beta,
                            void* D, long long ldd, long long d_bstride, void* D2, long long ldd2, long long d2_bstride,
                            const void* C, long long ldc, long long c_bstride, const float* colscale, int splitk,
-                           const float* alpha_dev, void* drop_mask, long long drop_ldm, const void* drop_seed,
-                           unsigned drop_site, float drop_p, void* stream);
+                           const float* alpha_dev, const void* drop_mask, long long drop_ldm, float drop_p,
+                           void* stream);
+/* Row-layout keep bits [M, N] for the residual-branch dropout: bit column%32 of mask[row*ldm + column/32]
+ * from Philox4x32-10 block (column/8, row, drop_site, 0) under key (*drop_seed low, high 32 bits), element
+ * column%8 = 16-bit half (column%2) of word (column%8)/2, kept iff >= round(drop_p*65536). No counterpart
+ * in the reference (nn.Dropout draws its mask internally). */
+int rgpt_drop_mask(unsigned* mask, long long ldm, const unsigned long long* drop_seed, unsigned drop_site,
+                   float drop_p, int M, int N, void* stream);
 
 
 /* ------------------------------------------------------------------ attention
@@ -88,14 +91,19 @@ int rgpt_gemm_bf16_dropout(const void* A, int a_mn_major, long long lda, long lo
  *   gate/o/og/dout/dgate_pre [B*T, d] bf16, lse/Dvec [B, H, T] fp32.
  * Replaces F.scaled_dot_product_attention(is_causal=True, dropout_p) and the G1 gate multiply,
  * model/attention.py:56-61 (forward) and their autograd backward.
- * Dropout (drop_mask != null and drop_p > 0): the forward draws the keep bit of (query q, key k) of head
- * bh = b*H + h from Philox4x32-10 block (k/8, q, drop_site, bh) under key (*drop_seed low, high 32 bits)
- * -- 16-bit uniform (k%8 picks word (k%8)/2, half k%2) >= round(p*65536) -- scales the kept
- * probabilities by 1/(1-p) and stores the bits in drop_mask [B*H][ceil(T/32)][T] (word = 32 queries of
- * one key); the backward reads them back. See RGPT_DROPOUT below for the other sites. */
+ * Dropout (drop_mask != null and drop_p > 0): the keep bit of (query q, key k) of head bh = b*H + h is
+ * bit q%32 of drop_mask[(bh*ceil(T/32) + q/32)*T + k], filled by rgpt_attn_drop_mask from Philox4x32-10
+ * block (k/8, q, drop_site, bh) under key (*drop_seed low, high 32 bits) -- 16-bit uniform (k%8 picks
+ * word (k%8)/2, half k%2) >= round(p*65536). The forward scales the kept probabilities by 1/(1-p) (the
+ * softmax normaliser keeps all of them); the backward applies the same bits. See RGPT_DROPOUT below for
+ * the other sites. */
 int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse,
-                  int B, int T, int H, int d, unsigned* drop_mask, const unsigned long long* drop_seed,
-                  unsigned drop_site, float drop_p, void* stream);
+                  int B, int T, int H, int d, const unsigned* drop_mask, float drop_p, void* stream);
+/* Keep bits of the attention-probability dropout for rgpt_attn_fwd / rgpt_attn_bwd, drawn for every causal
+ * (query, key) pair into drop_mask [B*H][ceil(T/32)][T] (see above); no counterpart in the reference, whose
+ * SDPA draws them internally. */
+int rgpt_attn_drop_mask(unsigned* drop_mask, const unsigned long long* drop_seed, unsigned drop_site, float drop_p,
+                        int B, int T, int H, void* stream);
 /* dout = dog*gate; dgate_pre = dog*o*gate*(1-gate); Dvec = rowsum(dout*o). gate may be null (ungated).
  * dq_zero (optional, [B*T, d] fp32, 16-byte aligned) is zeroed: the dq accumulator of rgpt_attn_bwd. */
 int rgpt_attn_bwd_prep(const void* dog, const void* o, const void* gate, void* dout, void* dgate_pre,

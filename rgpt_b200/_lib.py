@@ -41,9 +41,11 @@ _SIGNATURES: dict[str, list] = {
         _c_vp, _c_int, _c_ll, _c_ll, _c_vp, _c_int, _c_ll, _c_ll, _c_int, _c_int, _c_int, _c_int,
         _c_int, _c_int, _c_float, _c_float, _c_vp, _c_ll, _c_ll, _c_vp, _c_ll, _c_ll, _c_vp, _c_ll, _c_ll,
         _c_vp, _c_int, _c_vp,  # colscale, splitk, alpha_dev
-        _c_vp, _c_ll, _c_vp, ctypes.c_uint, _c_float,  # drop_mask, drop_ldm, drop_seed, drop_site, drop_p
+        _c_vp, _c_ll, _c_float,  # drop_mask, drop_ldm, drop_p
         _c_vp,
     ],
+    "rgpt_drop_mask": [_c_vp, _c_ll, _c_vp, ctypes.c_uint, _c_float, _c_int, _c_int, _c_vp],
+    "rgpt_attn_drop_mask": [_c_vp, _c_vp, ctypes.c_uint, _c_float, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_rownorm_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
                          _c_vp, _c_vp, _c_vp, _c_vp],
     "rgpt_rownorm_bwd": [_c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,
@@ -71,7 +73,7 @@ _SIGNATURES: dict[str, list] = {
     "rgpt_muon_apply": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_float, _c_float,
                         _c_float, _c_vp, _c_vp],
     "rgpt_attn_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int,
-                      _c_vp, _c_vp, ctypes.c_uint, _c_float, _c_vp],
+                      _c_vp, _c_float, _c_vp],
     "rgpt_attn_bwd_prep": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_attn_bwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_ll, _c_vp, _c_ll,
                       _c_int, _c_int, _c_int, _c_int, _c_vp, _c_float, _c_vp],

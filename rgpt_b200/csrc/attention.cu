@@ -160,11 +160,9 @@ struct AttnFwdParams {
   const __nv_bfloat16* gate;  // [B*T, d] or null
   float* lse;        // [B, H, T] natural-log LSE of the scaled scores
   // dropout of the attention probabilities (SDPA dropout_p, model/attention.py:57), DROP kernels only:
-  // keep bit of (query q, key k) of head bh from Philox block (k / 8, q, site, bh), written to
-  // drop_mask[(bh * ceil(T/32) + q / 32) * T + k] bit q % 32 (one word per key and 32 queries)
-  uint32_t* drop_mask;
-  const unsigned long long* drop_seed;
-  uint32_t drop_site, drop_thresh;
+  // the keep bit of (query q, key k) of head bh is bit q % 32 of drop_mask[(bh * ceil(T/32) + q / 32) * T
+  // + k], filled beforehand by attn_drop_mask_kernel (one word per key and 32 queries)
+  const uint32_t* drop_mask;
   float drop_scale;
 };
 
@@ -344,12 +342,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    uint32_t rk0 = 0, rk1 = 0;
-    if constexpr (DROP) {
-      const unsigned long long sd = *p.drop_seed;
-      rk0 = (uint32_t)sd;
-      rk1 = (uint32_t)(sd >> 32);
-    }
+    const int drop_qb = (q0 >> 5) + quarter;  // this warp's 32-query block of the dropout mask
 
     auto wait_all = [&](uint64_t* bar, uint32_t ph) -> bool {
       int v = 1;
@@ -359,6 +352,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 
     for (int j = 0; j < nkv; ++j) {
       const int sb = j & 1;
+      uint32_t mw[2] = {0u, 0u};  // dropout words of keys j*64 + c*32 + lane over this warp's queries
+      if constexpr (DROP) {
+        const int nqb = (p.T + 31) >> 5;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int key = j * FWD_KT + c * 32 + lane;
+          if (key < p.T && drop_qb < nqb) mw[c] = __ldg(p.drop_mask + ((long long)bh * nqb + drop_qb) * p.T + key);
+        }
+      }
       if (!wait_all(&s_full[sb], (j >> 1) & 1)) {
         ok = false;
         break;
@@ -439,17 +441,12 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
           sum_b = fadd2(sum_b, make_float2(pv[t + 2], pv[t + 3]));
         }
         if constexpr (DROP) {
-          // the row sum keeps every probability; P V sees only the kept ones (1/(1-p) is applied to O)
-          const int key0 = kbase + c * 32;
-          const uint32_t keep = keep32((uint32_t)key0, (uint32_t)qrow, p.drop_site, (uint32_t)bh, rk0, rk1,
-                                       p.drop_thresh);
+          // the row sum keeps every probability; P V sees only the kept ones (1/(1-p) is applied to O).
+          // The loaded words hold one key's bits over the warp's 32 queries; transposed, lane t holds
+          // its own query's bits over the chunk's 32 keys.
+          const uint32_t keep = warp_transpose_bits(mw[c], lane);
 #pragma unroll
           for (int t = 0; t < 32; ++t) pv[t] = ((keep >> t) & 1u) ? pv[t] : 0.f;
-          // lane t gets key key0 + t's bits over this warp's 32 queries: one coalesced 128-byte store
-          const uint32_t kw = warp_transpose_bits(keep, lane);
-          const int qb = (q0 >> 5) + quarter;
-          if (key0 + lane < p.T && qb * 32 < p.T)
-            p.drop_mask[((long long)bh * ((p.T + 31) >> 5) + qb) * p.T + key0 + lane] = kw;
         }
 #pragma unroll
         for (int t = 0; t < 4; ++t) st_sw128_chunk(pbuf, r, c * 4 + t, pv + 8 * t);
@@ -516,6 +513,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
+  }
+}
+
+// ============================================================================ dropout mask
+// Keep bits of the attention probabilities for every causal (query, key) pair: the bit of (q, k) of head
+// bh comes from Philox4x32-10 block (k / 8, q, site, bh) under key (seed low, high 32 bits) -- the 16-bit
+// uniform (k % 8) -> word (k % 8) / 2, half k % 2 -- kept iff >= thresh. A warp draws 32 keys for its 32
+// queries (one row of bits per lane), transposes them and stores one coalesced word per key:
+// mask[(bh * ceil(T/32) + q / 32) * T + k] bit q % 32. Block = one (bh, 32-query block), its 4 warps
+// stride over the key chunks that any of the block's queries can see.
+__global__ void __launch_bounds__(128) attn_drop_mask_kernel(uint32_t* __restrict__ mask,
+                                                             const unsigned long long* __restrict__ seed,
+                                                             uint32_t site, uint32_t thresh, int BH, int T) {
+  griddep_wait();
+  griddep_launch();
+  const int nqb = (T + 31) >> 5;
+  const int bh = blockIdx.x / nqb, qb = blockIdx.x % nqb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned long long sd = *seed;
+  const uint32_t k0 = (uint32_t)sd, k1 = (uint32_t)(sd >> 32);
+  const int q = qb * 32 + lane;
+  uint32_t* row = mask + ((long long)bh * nqb + qb) * T;
+  for (int c = warp; c <= qb; c += 4) {  // keys [32c, 32c + 32) reach the block's last query
+    const uint32_t keep = keep32((uint32_t)(c * 32), (uint32_t)q, site, (uint32_t)bh, k0, k1, thresh);
+    const uint32_t kw = warp_transpose_bits(keep, lane);
+    if (c * 32 + lane < T) row[c * 32 + lane] = kw;
   }
 }
 
@@ -1003,8 +1026,7 @@ static int check_attn_args(int B, int T, int H, int d) {
 }
 
 extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, void* o, void* og, float* lse, int B,
-                             int T, int H, int d, unsigned* drop_mask, const unsigned long long* drop_seed,
-                             unsigned drop_site, float drop_p, void* stream) {
+                             int T, int H, int d, const unsigned* drop_mask, float drop_p, void* stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
@@ -1038,12 +1060,8 @@ extern "C" int rgpt_attn_fwd(const void* qk, const void* qkv, const void* gate, 
   p.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
   p.lse = lse;
   const bool drop = drop_mask != nullptr && drop_p > 0.0f;
-  if (drop && (!(drop_p < 1.0f) || drop_seed == nullptr))
-    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout needs p in [0, 1) and a device seed");
-  p.drop_mask = drop ? reinterpret_cast<uint32_t*>(drop_mask) : nullptr;
-  p.drop_seed = drop_seed;
-  p.drop_site = drop_site;
-  p.drop_thresh = drop ? (uint32_t)lrintf(drop_p * 65536.0f) : 0u;
+  if (drop && !(drop_p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout needs p in [0, 1)");
+  p.drop_mask = drop ? reinterpret_cast<const uint32_t*>(drop_mask) : nullptr;
   p.drop_scale = drop ? (float)(1.0 / (1.0 - (double)drop_p)) : 1.0f;
   static bool attr[2][64] = {{false}};
   if (!attr[drop][dev]) {
@@ -1135,4 +1153,17 @@ extern "C" int rgpt_attn_bwd(const void* qk, const void* qkv, const void* dout, 
     launch_pdl(attn_bwd_kernel<false>, dim3(grid), dim3(ATT_BWD_THREADS), BWD_SMEM, st_, 1, tq, tk, tv, tdo, tdq,
                tdk, tdv, p);
   return rgpt_check_launch("attn_bwd_kernel");
+}
+
+extern "C" int rgpt_attn_drop_mask(unsigned* mask, const unsigned long long* seed, unsigned site, float p, int B,
+                                   int T, int H, void* stream) {
+  if (mask == nullptr || seed == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout mask and seed needed");
+  if (!(p >= 0.0f && p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", p);
+  if (B < 1 || T < 1 || H < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout mask: empty shape");
+  const long long blocks = (long long)B * H * ((T + 31) / 32);
+  if (blocks > 0x7fffffffLL) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "attention dropout mask too large");
+  // 4-warp blocks: small enough to run beside the resident CTAs of the kernels they overlap
+  launch_pdl(attn_drop_mask_kernel, dim3((unsigned)blocks), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream), 1,
+             reinterpret_cast<uint32_t*>(mask), seed, (uint32_t)site, (uint32_t)lrintf(p * 65536.0f), B * H, T);
+  return rgpt_check_launch("attn_drop_mask_kernel");
 }

@@ -55,12 +55,10 @@ struct EpiParams {
   const float* alpha_dev;  // optional device scalar multiplying alpha (loss-gradient scale)
   int has_d2;
   // RESID_F32 only: dropout of the branch output (nn.Dropout, model/transformer_block.py:45,52).
-  // Null mask = no dropout; else keep bits are drawn per (row, column) from Philox and written to
-  // drop_mask[row * drop_ldm + column / 32] for the backward.
-  uint32_t* drop_mask;
+  // Null mask = no dropout; else the keep bit of (row, column) is bit column % 32 of
+  // drop_mask[row * drop_ldm + column / 32] (filled beforehand by rgpt_drop_mask).
+  const uint32_t* drop_mask;
   long long drop_ldm;
-  const unsigned long long* drop_seed;
-  uint32_t drop_site, drop_thresh;
   float drop_scale;
 };
 
@@ -378,12 +376,7 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
     const bool dual = (EPI == RGPT_EPI_ACT_FWD) || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
     const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
     const bool scaled = alpha != 1.0f;
-    uint32_t drop_k0 = 0, drop_k1 = 0;
-    if (EPI == RGPT_EPI_RESID_F32 && ep.drop_mask != nullptr) {
-      const unsigned long long sd = *ep.drop_seed;
-      drop_k0 = (uint32_t)sd;
-      drop_k1 = (uint32_t)(sd >> 32);
-    }
+
     int acc = 0;
     uint32_t acc_phase = 0;
     // Epilogue input C (bf16 for ACT_BWD / POLY, fp32 for RESID): each thread reads its own output
@@ -546,11 +539,9 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
           if constexpr (resid) {
             if (ep.drop_mask != nullptr) {  // dropout of the branch output (warp-uniform branch)
               const int row = row0 + lane;
-              const uint32_t keep = keep32((uint32_t)gn0, (uint32_t)row, ep.drop_site, 0u, drop_k0, drop_k1,
-                                           ep.drop_thresh);
+              const uint32_t keep = row < sh.M ? __ldg(ep.drop_mask + (long long)row * ep.drop_ldm + (gn0 >> 5)) : 0u;
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = ((keep >> j) & 1u) ? v[j] * ep.drop_scale : 0.f;
-              if (row < sh.M) ep.drop_mask[(long long)row * ep.drop_ldm + (gn0 >> 5)] = keep;
             }
             if (ep.has_d2) stage_f32x32(s1, lane, v);  // raw (dropped) branch output
             const float* cs = reinterpret_cast<const float*>(cc);
@@ -775,10 +766,8 @@ static int dispatch_gemm(int BN, bool pair, int a_mn, int b_mn, int epi, const C
 using namespace rgpt;
 
 struct DropArgs {
-  void* mask;
+  const void* mask;
   long long ldm;
-  const void* seed;
-  unsigned site;
   float p;
 };
 
@@ -914,21 +903,16 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   ep.has_d2 = has_d2 ? 1 : 0;
   ep.drop_mask = nullptr;
   ep.drop_ldm = 0;
-  ep.drop_seed = nullptr;
-  ep.drop_site = ep.drop_thresh = 0;
   ep.drop_scale = 1.0f;
   if (drop != nullptr && drop->p > 0.0f) {
     if (epi != RGPT_EPI_RESID_F32)
       return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout is only fused into the RESID_F32 epilogue");
     if (!(drop->p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", drop->p);
     if (batch != 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout GEMMs are not batched");
-    if (drop->mask == nullptr || drop->seed == nullptr || drop->ldm < (N + 31) / 32)
-      return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout needs a mask of >= %d words per row and a seed", (N + 31) / 32);
-    ep.drop_mask = reinterpret_cast<uint32_t*>(drop->mask);
+    if (drop->mask == nullptr || drop->ldm < (N + 31) / 32)
+      return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout needs a mask of >= %d words per row", (N + 31) / 32);
+    ep.drop_mask = reinterpret_cast<const uint32_t*>(drop->mask);
     ep.drop_ldm = drop->ldm;
-    ep.drop_seed = reinterpret_cast<const unsigned long long*>(drop->seed);
-    ep.drop_site = drop->site;
-    ep.drop_thresh = (uint32_t)lrintf(drop->p * 65536.0f);
     ep.drop_scale = (float)(1.0 / (1.0 - (double)drop->p));
   }
 
@@ -952,10 +936,9 @@ extern "C" int rgpt_gemm_bf16_dropout(const void* A, int a_mn_major, long long l
                                       int K, int batch, int epi, int act, float alpha, float beta, void* D,
                                       long long ldd, long long d_bstride, void* D2, long long ldd2,
                                       long long d2_bstride, const void* C, long long ldc, long long c_bstride,
-                                      const float* colscale, int splitk, const float* alpha_dev, void* drop_mask,
-                                      long long drop_ldm, const void* drop_seed, unsigned drop_site, float drop_p,
-                                      void* stream) {
-  const DropArgs d = {drop_mask, drop_ldm, drop_seed, drop_site, drop_p};
+                                      const float* colscale, int splitk, const float* alpha_dev,
+                                      const void* drop_mask, long long drop_ldm, float drop_p, void* stream) {
+  const DropArgs d = {drop_mask, drop_ldm, drop_p};
   return gemm_entry(A, a_mn_major, lda, a_bstride, B, b_mn_major, ldb, b_bstride, M, N, K, batch, epi, act, alpha,
                     beta, D, ldd, d_bstride, D2, ldd2, d2_bstride, C, ldc, c_bstride, colscale, splitk, alpha_dev,
                     &d, stream);

@@ -1250,6 +1250,21 @@ extern "C" int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* 
 
 // Dropout arguments of the embedding kernels: a mask (null = no dropout), p in [0, 1), rows of
 // d % 128 == 0 columns, and (forward only) the device seed.
+// Row-layout dropout keep bits [M, N] (residual branches, model/transformer_block.py:45,52): the bit of
+// (row, column) comes from Philox4x32-10 block (column / 8, row, site, 0) under key (seed low, high 32
+// bits), the 16-bit uniform (column % 8) -> word (column % 8) / 2, half column % 2, kept iff >= thresh;
+// one thread per 32-column word: mask[row * ldm + column / 32] bit column % 32.
+__global__ void drop_mask_rows_kernel(uint32_t* __restrict__ mask, long long ldm, const unsigned long long* seed,
+                                      uint32_t site, uint32_t thresh, int M, int words) {
+  griddep_wait();
+  griddep_launch();
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)M * words) return;
+  const int row = (int)(i / words), w = (int)(i - (long long)row * words);
+  const unsigned long long sd = *seed;
+  mask[row * ldm + w] = keep32((uint32_t)(w * 32), (uint32_t)row, site, 0u, (uint32_t)sd, (uint32_t)(sd >> 32), thresh);
+}
+
 static int check_drop(const void* mask, bool need_seed, const void* seed, float p, int d) {
   if (mask == nullptr) return 0;
   if (!(p >= 0.0f && p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", p);
@@ -1364,4 +1379,17 @@ extern "C" int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int
     return st;
   launch_pdl(ce_finalize_kernel, dim3(1), dim3(1024), 0, s, 1, loss_rows, M, scale_buf + 1, loss_out);
   return rgpt_check_launch("cross_entropy_noalloc");
+}
+
+extern "C" int rgpt_drop_mask(unsigned* mask, long long ldm, const unsigned long long* seed, unsigned site, float p,
+                              int M, int N, void* stream) {
+  if (mask == nullptr || seed == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout mask and seed needed");
+  if (!(p >= 0.0f && p < 1.0f)) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout p must be in [0, 1), got %g", p);
+  const int words = (N + 31) / 32;
+  if (M < 1 || N < 1 || ldm < words) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout mask: bad shape");
+  const long long n = (long long)M * words;
+  launch_pdl(drop_mask_rows_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+             reinterpret_cast<cudaStream_t>(stream), 1, reinterpret_cast<uint32_t*>(mask), ldm, seed, (uint32_t)site,
+             (uint32_t)lrintf(p * 65536.0f), M, words);
+  return rgpt_check_launch("drop_mask_rows_kernel");
 }

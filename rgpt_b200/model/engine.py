@@ -163,6 +163,8 @@ class Engine:
             seed ^= (torch.distributed.get_rank() * 0x9E3779B97F4A7C15) & (2 ** 62 - 1)
         self.drop_seed = torch.tensor([seed], dtype=torch.int64).to(self.device)
         self._drop_active = False
+        self._rng_stream = None
+        self._mask_events = []
         self._build_param_views()
         self._acts = {}
         self._spec_cache = {}
@@ -341,6 +343,7 @@ class Engine:
         self._drop_active = m.training and self.p_drop > 0
         if self._drop_active:
             self.drop_seed.add_(1)
+            self._draw_masks(A)
         nv.embedding_fwd(self._ids, m.embs.weight, A.x[0], drop=self._drop(A, "emb"))
         halting = self.halting and lab is not None
         self._halting_active = halting
@@ -385,6 +388,25 @@ class Engine:
             return nv.Drop(A.drop_f[app], self.drop_seed, 4 * app + 1, self.p_drop)
         return nv.Drop(A.drop_att[app], self.drop_seed, 4 * app + 2, self.p_drop)
 
+    def _draw_masks(self, A):
+        """Draw every layer application's dropout masks (attention probabilities and both residual
+        branches) on a side stream that forks here, after the seed increment; each layer's attention
+        waits for its own masks (events), so the Philox work overlaps the layers before it and the
+        QKV projection and preparation of its own layer."""
+        main = torch.cuda.current_stream()
+        if self._rng_stream is None:
+            self._rng_stream = torch.cuda.Stream(device=self.device)
+        st = self._rng_stream
+        st.wait_stream(main)
+        if len(self._mask_events) < self.n_apps:
+            self._mask_events = [torch.cuda.Event() for _ in range(self.n_apps)]
+        with torch.cuda.stream(st):
+            for app in range(self.n_apps):
+                nv.attn_drop_mask(self._drop(A, "attn_p", app), A.B, A.T, self.H)
+                nv.drop_mask_rows(self._drop(A, "attn_out", app), A.M, self.d)
+                nv.drop_mask_rows(self._drop(A, "ff_out", app), A.M, self.d)
+                self._mask_events[app].record(st)
+
     def _layer_fwd(self, blk, W, A, app):
         d, H, B, T, M = self.d, self.H, A.B, A.T, A.M
         at = blk.attn
@@ -399,6 +421,8 @@ class Engine:
             # G1 gate = sigmoid(q_n Wg^T + bg), one [M*H, 64] x [64, 64] GEMM with a bias+sigmoid epilogue
             nv.gemm(A.qn[app].view(M * H, 64), W["wg"], A.gate[app].view(M * H, 64),
                     epi=nv.EPI_BIAS_SIGMOID_BF16, colscale=at.gate_proj.bias)
+        if self._drop_active:
+            torch.cuda.current_stream().wait_event(self._mask_events[app])
         nv.attn_fwd(A.qk[app], A.qkv[app], A.gate[app], A.o[app], A.og[app] if self.g1 else None, A.lse[app],
                     B, T, H, drop=self._drop(A, "attn_p", app))
         nv.gemm(A.og[app], W["wo"], A.h[app], epi=nv.EPI_RESID_F32, c=x,

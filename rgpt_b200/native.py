@@ -54,6 +54,22 @@ def _drop_args(drop: "Drop | None", seed_needed: bool = True):
     return ptr(drop.mask), ptr(drop.seed) if drop.seed is not None else None, drop.site & 0xFFFFFFFF, drop.p
 
 
+def drop_mask_rows(drop: Drop, M: int, N: int) -> None:
+    """Fill drop.mask [M, ceil(N/32)] with the residual-branch keep bits of (seed, site)."""
+    if drop.mask.dim() != 2 or drop.mask.shape[0] < M:
+        raise ValueError("row dropout mask must be [M, ceil(N/32)] words")
+    dm, ds, dsite, dp = _drop_args(drop)
+    _lib.call("rgpt_drop_mask", dm, drop.mask.stride(0), ds, dsite, dp, M, N, _lib.stream_ptr(drop.mask.device))
+
+
+def attn_drop_mask(drop: Drop, B: int, T: int, H: int) -> None:
+    """Fill drop.mask [B*H, ceil(T/32), T] with the attention-probability keep bits of (seed, site)."""
+    if drop.mask.numel() < B * H * ((T + 31) // 32) * T:
+        raise ValueError("attention dropout mask must hold [B*H, ceil(T/32), T] words")
+    dm, ds, dsite, dp = _drop_args(drop)
+    _lib.call("rgpt_attn_drop_mask", dm, ds, dsite, dp, B, T, H, _lib.stream_ptr(drop.mask.device))
+
+
 def _operand(t: torch.Tensor):
     """(mn_major, ld, bstride) for a logical [.., rows, K] bf16 operand view."""
     if t.dtype != torch.bfloat16:
@@ -87,6 +103,8 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
          alpha_dev: torch.Tensor | None = None, drop: Drop | None = None) -> torch.Tensor:
     """out = epilogue(A @ B^T) for logical A [(b,) M, K] and B [(b,) N, K] (bf16).
 
+    drop (RESID_F32 only): branch dropout whose mask drop_mask_rows filled.
+
     Either operand may be K-major (unit stride on K) or MN-major (unit stride
     on M/N), e.g. ``gemm(dy.t(), x.t(), dw, epi=EPI_ACCUM_F32)`` computes
     dW += dy^T x without materialising a transpose.
@@ -117,12 +135,12 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
                   d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
                   ptr(colscale), splitk, ptr(alpha_dev), _lib.stream_ptr(out.device))
     else:
-        dm, ds, dsite, dp = _drop_args(drop)
+        dm, _, _, dp = _drop_args(drop, seed_needed=False)
         _lib.call("rgpt_gemm_bf16_dropout",
                   ptr(A), a_mn, lda, abs_, ptr(B), b_mn, ldb, bbs,
                   M, N, K, batch, epi, act, float(alpha), float(beta),
                   d, ldd, dbs, d2, ldd2, d2bs, cp, ldc, cbs,
-                  ptr(colscale), splitk, ptr(alpha_dev), dm, drop.mask.shape[-1], ds, dsite, dp,
+                  ptr(colscale), splitk, ptr(alpha_dev), dm, drop.mask.shape[-1], dp,
                   _lib.stream_ptr(out.device))
     if ev is not None:
         e1.record()
@@ -142,7 +160,8 @@ def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: 
              og: torch.Tensor | None, lse: torch.Tensor, B: int, T: int, H: int, drop: Drop | None = None) -> None:
     """Causal attention over token-major q/k (qk [B*T, 2d]) and v (qkv[:, 2d:3d]).
 
-    Writes o [B*T, d] (bf16), og = o * gate (if gate given) and lse [B, H, T] (fp32)."""
+    Writes o [B*T, d] (bf16), og = o * gate (if gate given) and lse [B, H, T] (fp32).
+    drop: attention-probability dropout; its mask must have been filled by attn_drop_mask."""
     d = H * 64
     for t, n in ((qk, "qk"), (qkv, "qkv"), (o, "o")):
         _check(t, torch.bfloat16, n)
@@ -152,8 +171,9 @@ def attn_fwd(qk: torch.Tensor, qkv: torch.Tensor, gate: torch.Tensor | None, o: 
         raise ValueError("lse must be fp32 [B, H, T]")
     if drop is not None and drop.mask.numel() < B * H * ((T + 31) // 32) * T:
         raise ValueError("attention dropout mask must hold [B*H, ceil(T/32), T] words")
+    dm, _, _, dp = _drop_args(drop, seed_needed=False)
     _lib.call("rgpt_attn_fwd", ptr(qk), ptr(qkv), ptr(gate), ptr(o), ptr(og), ptr(lse), B, T, H, d,
-              *_drop_args(drop), _lib.stream_ptr(o.device))
+              dm, dp, _lib.stream_ptr(o.device))
 
 
 def attn_bwd_prep(dog: torch.Tensor, o: torch.Tensor, gate: torch.Tensor | None, do: torch.Tensor,

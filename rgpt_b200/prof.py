@@ -159,11 +159,15 @@ def bandwidth_and_optimizer() -> None:
     lse = torch.empty(B, H, T, device=dev)
     seed = torch.tensor([12345], dtype=torch.int64, device=dev)
     amask = torch.empty(B * H, T // 32, T, device=dev, dtype=torch.int32)
-    nv.attn_fwd(qk2, qkv2, gate, o2, og2, lse, B, T, H, drop=nv.Drop(amask, seed, 2, 0.1))
+    adrop = nv.Drop(amask, seed, 2, 0.1)
+    nv.attn_drop_mask(adrop, B, T, H)
+    nv.attn_fwd(qk2, qkv2, gate, o2, og2, lse, B, T, H, drop=adrop)
     wo = rb(d, d)
     hout = torch.empty(M, d, device=dev)
     rmask = torch.empty(M, d // 32, device=dev, dtype=torch.int32)
-    nv.gemm(og2, wo, hout, epi=nv.EPI_RESID_F32, c=x, drop=nv.Drop(rmask, seed, 0, 0.1))
+    rdrop = nv.Drop(rmask, seed, 0, 0.1)
+    nv.drop_mask_rows(rdrop, M, d)
+    nv.gemm(og2, wo, hout, epi=nv.EPI_RESID_F32, c=x, drop=rdrop)
     torch.cuda.synchronize()
     print("rgpt_b200.prof bw: ok")
 

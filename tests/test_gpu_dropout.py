@@ -3,7 +3,8 @@ SDPA dropout_p at model/attention.py:57) against the oracle.
 
 torch's own dropout stream cannot be reproduced outside torch, so the native kernels draw their keep
 bits from Philox4x32-10 with a documented counter layout, and the oracle (pinned to the published
-Philox known-answer vectors) regenerates the same masks. Checks:
+Philox known-answer vectors) regenerates the same masks. The mask kernels (rgpt_drop_mask, rgpt_attn_drop_mask) draw the bits; the GEMM epilogue and the
+attention kernels read them. Checks:
   * every stored mask bit equals the oracle's bit (bit-exact), and the keep rate is ~1 - p;
   * outputs and gradients equal the fp32 reference computed with that mask, at the tolerances of
     the dropout-free tests (1e-2 forward, 2e-2 attention gradients, 5e-2 model gradients);
@@ -48,8 +49,9 @@ def test_resid_gemm_dropout_bits_and_values(cuda, M, N, K, p):
     raw = torch.empty(M, N, device=cuda)
     mask = torch.full((M, N // 32), -1, device=cuda, dtype=torch.int32)
     seed = 0x1234_5678_9ABC_DEF0 + M
-    nv.gemm(A, W, out, epi=nv.EPI_RESID_F32, c=C, colscale=ls, out2=raw,
-            drop=nv.Drop(mask, seed_tensor(cuda, seed), 7, p))
+    drop = nv.Drop(mask, seed_tensor(cuda, seed), 7, p)
+    nv.drop_mask_rows(drop, M, N)
+    nv.gemm(A, W, out, epi=nv.EPI_RESID_F32, c=C, colscale=ls, out2=raw, drop=drop)
     torch.cuda.synchronize()
     keep = O.resid_drop_mask(seed, 7, M, N, p)
     assert torch.equal(unpack(mask), keep)
@@ -80,6 +82,7 @@ def test_attention_dropout_fwd_bwd(cuda, B, T, H, p):
     mask = torch.zeros(B * H, QB, T, device=cuda, dtype=torch.int32)
     seed, site = 987654321 + T, 4 * 3 + 2
     drop = nv.Drop(mask, seed_tensor(cuda, seed), site, p)
+    nv.attn_drop_mask(drop, B, T, H)
     nv.attn_fwd(qk, qkv, gate, o, og, lse, B, T, H, drop=drop)
     torch.cuda.synchronize()
     keep = O.attn_drop_mask(seed, site, B, H, T, p)                     # [B, H, Tq, Tk]
