@@ -162,7 +162,7 @@ def run_ours(args, wl):
     inv_accum = 1.0 / accum
 
     graphed = None
-    if world == 1 and not args.eager:
+    if not args.eager:
         # the whole step as one CUDA graph; 2 eager warm-up steps build the optimizer state first
         from rgpt_b200.graph import GraphedTrainStep
 
@@ -280,6 +280,9 @@ def run_ours(args, wl):
         res["cpu_baseline"] = cpu_baseline(cfg, T, budget_s=args.cpu_budget)
     if dist is not None:
         dist.barrier(device_ids=[local])
+        if graphed is not None:
+            graphed.release()  # a graph holding NCCL collectives must go before its process group
+            torch.cuda.synchronize()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res), flush=True)

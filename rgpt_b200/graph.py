@@ -17,13 +17,24 @@ What a graph fixes at capture, and how this class keeps each step correct:
 The first `warmup` calls run eagerly. They are real training steps, and they create the
 optimizer state and descriptor tables, whose synchronous allocation and upload cannot be
 captured. The next call captures the step and replays it; every later call replays.
+
+Data-parallel steps (DistMuon under an initialised NCCL process group) are captured the same way:
+the gradient-bucket all-reduces issued during the backward, the waits for them and the all-gather
+of the sharded Newton-Schulz results become nodes of the graph. Every rank makes the same calls, so
+every rank captures (and later replays) the same collectives in the same order. The first eager
+step installs DistMuon's bucket hooks, so the captured step is the steady-state one.
 """
 from __future__ import annotations
 
 import torch
-import torch.distributed as dist
 
 from . import _lib
+
+
+def _data_parallel() -> bool:
+    import torch.distributed as dist
+
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
 
 
 class GraphedTrainStep:
@@ -32,8 +43,6 @@ class GraphedTrainStep:
     ids[..., :-1], labels ids[..., 1:]). Returns the last micro-batch's total loss."""
 
     def __init__(self, model, optimizer, micro_batch: int, seq_len: int, accum: int = 1, warmup: int = 2):
-        if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
-            raise NotImplementedError("GraphedTrainStep captures single-GPU steps; data-parallel steps run eagerly")
         dev = next(model.parameters()).device
         if dev.type != "cuda":
             raise RuntimeError("GraphedTrainStep needs a CUDA model (there is no CPU path)")
@@ -68,7 +77,12 @@ class GraphedTrainStep:
         if self.graph is None:
             g = torch.cuda.CUDAGraph()
             n0 = _lib.launch_count
-            with torch.cuda.graph(g):
+            # every collective of the eager steps has completed before the capture starts; with a
+            # process group, other threads' CUDA calls (the NCCL watchdog's event queries) must not
+            # invalidate this thread's capture
+            torch.cuda.synchronize()
+            mode = "thread_local" if _data_parallel() else "global"
+            with torch.cuda.graph(g, capture_error_mode=mode):
                 self._loss = self._body()
             self.launches = _lib.launch_count - n0
             _lib.launch_count = n0
@@ -86,6 +100,7 @@ class GraphedTrainStep:
         return self._body()
 
     def release(self) -> None:
-        """Drop the captured graph (and its memory pool); the next call captures again."""
+        """Drop the captured graph (and its memory pool); the next call captures again. A graph that
+        holds collectives must be released before the process group is destroyed."""
         self.graph = None
         self._loss = None

@@ -171,3 +171,82 @@ def test_distmuon_overlapped_bucket_sync_matches_step_time_allreduce():
         assert hooked, rank
         assert err < 1e-5, (rank, err)
         assert same == 0.0, (rank, same)
+
+
+def _graph_worker(rank: int, world: int, port: int, q) -> None:
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    graphed = None
+    try:
+        from rgpt_b200.graph import GraphedTrainStep
+        from rgpt_b200.model import GPT
+        from rgpt_b200.optimizer import DistMuon, trainer_param_groups
+
+        cfg = dict(name="gpt", n_layers=2, n_recur=1, detach_recur=False, cal_halt_loss=False, n_heads=2,
+                   d_model=128, vocab_size=384, max_seq_len=256, dropout=0.1, norm_type="rmsnorm", norm_eps=1e-5,
+                   qk_normtype="f_rmsnorm", activation_type="squared_relu", g1_gate=True, use_layer_scale=True,
+                   pad_token_id=-100, tie_word_embeddings=False)
+        g = torch.Generator().manual_seed(20 + rank)
+        batches = [torch.randint(0, 384, (1, 2, 129), generator=g).to(dev) for _ in range(5)]
+
+        def build():
+            torch.manual_seed(0)
+            model = GPT(**cfg).to(dev).train()
+            model.engine()  # the dropout seed is drawn here, at the same generator state for both copies
+            return model, DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
+
+        model_g, opt_g = build()
+        graphed = GraphedTrainStep(model_g, opt_g, 2, 128, 1, warmup=2)
+        for b in batches:  # 2 eager steps, the capture + replay, then 2 replays
+            graphed(b)
+        model_e, opt_e = build()
+        opt_e.use_device_hparams()
+        for b in batches:  # the same steps issued eagerly (same device-scalar path as the graph)
+            opt_e.stage_device_hparams()
+            opt_e.zero_grad(set_to_none=True)
+            total, _, _ = model_e.forward_loss(b[0, :, :-1], b[0, :, 1:])
+            total.backward()
+            opt_e.step()
+        torch.cuda.synchronize()
+        diff = max(((pg - pe).norm() / pe.norm().clamp_min(1e-30)).item()
+                   for pg, pe in zip(model_g.parameters(), model_e.parameters()))
+        ref = [p.detach().clone() for p in model_g.parameters()]
+        for t in ref:
+            dist.broadcast(t, 0)
+        same = max((p - r).abs().max().item() for p, r in zip(model_g.parameters(), ref))
+        q.put((rank, diff, same))
+    finally:
+        if graphed is not None:
+            graphed.release()
+            torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_graphed_data_parallel_step_matches_eager():
+    # Five data-parallel training steps with dropout 0.1, the last three replayed from one captured
+    # CUDA graph that holds the gradient-bucket all-reduces and the Newton-Schulz all-gather, end on
+    # the same parameters as five eager steps (1e-5 relative: fp32 atomics vary in order), and every
+    # rank holds identical parameters.
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_graph_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, diff, same in res:
+        assert diff < 1e-5, (rank, diff)
+        assert same == 0.0, (rank, same)
