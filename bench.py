@@ -10,16 +10,17 @@ on the native sm_100a kernels. The default workload is the gpt-small training
 step (d_model 512, 8 heads, 8 layers, squared-ReLU FFN, RMSNorm pre-norm,
 f_rmsnorm QK norm, RoPE, G1 gate, vocab 50304, seq 1024, micro-batch 16,
 Muon for 2-D weights + AdamW) on synthetic uniform token ids with
-random-init weights. Multi-GPU runs (torchrun) are weak-scaling data parallel:
-16 sequences per GPU, gradients averaged over NCCL by DistMuon. On one GPU the
-step is replayed as one CUDA graph (rgpt_b200.graph.GraphedTrainStep; --eager
-issues every kernel from Python instead); multi-GPU steps run eagerly.
+random-init weights, dropout 0.1 (the reference's model configs). Multi-GPU runs
+(torchrun) are weak-scaling data parallel: 16 sequences per GPU, gradients
+averaged over NCCL by DistMuon. The step is replayed as one CUDA graph on one
+GPU and on every rank of a multi-GPU run (rgpt_b200.graph.GraphedTrainStep; the
+graph holds the collectives); --eager issues every kernel from Python instead.
 
 Printed (rank 0, one JSON line): value = whole-job tokens/s with inputs resident
 in HBM; e2e = tokens/s through the public API with the token ids copied from
 pinned host memory and the loss read back every step; roofline = achieved
-TF/s of the tcgen05 GEMM kernel (all its launches in the timed steps, CUDA
-events) vs the measured bf16 peak; cpu_baseline = the CPU oracle (a restatement
+TF/s of the tcgen05 GEMM kernel (every launch of K eager steps issued on one
+stream, CUDA events around each) vs the measured bf16 peak; cpu_baseline = the CPU oracle (a restatement
 of the reference's PyTorch step) timed on this host's cores on a bounded sample.
 
 --impl reference times that CPU implementation of the same workload on all host
@@ -230,13 +231,18 @@ def run_ours(args, wl):
     barrier()
     ms_e2e = max_over_ranks(e0.elapsed_time(e1) / args.steps)
 
-    # ---- GEMM kernel roofline: CUDA events around every tcgen05 GEMM launch of K timed steps
+    # ---- GEMM kernel roofline: CUDA events around every tcgen05 GEMM launch of K steps, issued launch by
+    # launch so each GEMM gets its own events, and on one stream (no side-stream mask or optimizer work
+    # running beside a GEMM and stretching its measured duration); the timed steps above keep the overlap
+    eng = model.engine()
+    eng.overlap_masks, opt.concurrent = False, False
     nv.gemm_events = []
     barrier()
     for i in range(args.steps):
-        step_eager(dev_batches[i % n_batches])  # launch by launch, so each GEMM gets its own events
+        step_eager(dev_batches[i % n_batches])
     barrier()
     ev, nv.gemm_events = nv.gemm_events, None
+    eng.overlap_masks, opt.concurrent = True, True
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in ev)
     gemm_flops = sum(f for _, _, f in ev)
     from rgpt_b200.peaks import load_peaks
@@ -266,6 +272,7 @@ def run_ours(args, wl):
         "model_tflops": round(fpt * value / world / 1e12, 1),
         "loss_last_step": round(loss_val, 4),
         "roofline": {"kernel": "gemm_bf16_tc_kernel (all launches)", "bound": "tensor",
+                     "method": "CUDA events around each GEMM launch of eager steps issued on one stream",
                      "achieved": round(gemm_tfs, 1), "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
                      "frac": round(gemm_tfs / peaks["bf16_tflops_sustained"], 3),
                      "peak_source": peaks["source"] + " (sustained bf16: kernels timed inside a long step)",

@@ -165,6 +165,7 @@ class Engine:
         self._drop_active = False
         self._rng_stream = None
         self._mask_events = []
+        self.overlap_masks = True  # draw the dropout masks on a side stream (False: on the caller's)
         self._build_param_views()
         self._acts = {}
         self._spec_cache = {}
@@ -394,10 +395,13 @@ class Engine:
         waits for its own masks (events), so the Philox work overlaps the layers before it and the
         QKV projection and preparation of its own layer."""
         main = torch.cuda.current_stream()
-        if self._rng_stream is None:
-            self._rng_stream = torch.cuda.Stream(device=self.device)
-        st = self._rng_stream
-        st.wait_stream(main)
+        if self.overlap_masks:
+            if self._rng_stream is None:
+                self._rng_stream = torch.cuda.Stream(device=self.device)
+            st = self._rng_stream
+            st.wait_stream(main)
+        else:
+            st = main  # in stream order, e.g. to time the other kernels without overlap
         if len(self._mask_events) < self.n_apps:
             self._mask_events = [torch.cuda.Event() for _ in range(self.n_apps)]
         with torch.cuda.stream(st):
