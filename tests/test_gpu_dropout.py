@@ -151,7 +151,11 @@ BASE = dict(name="gpt", n_layers=2, n_recur=1, detach_recur=False, cal_halt_loss
 
 
 @pytest.mark.parametrize("cfg", [BASE, dict(BASE, name="rgpt", n_layers=1, n_recur=3, cal_halt_loss=True,
-                                            use_layer_scale=True, dropout=0.2)], ids=["gpt", "rgpt"])
+                                            use_layer_scale=True, dropout=0.2),
+                                 # conf/model/rgpt.yaml's combination: detached recurrences + halting
+                                 dict(BASE, name="rgpt", n_layers=2, n_recur=2, cal_halt_loss=True,
+                                      use_layer_scale=True, detach_recur=True)],
+                         ids=["gpt", "rgpt", "rgpt_detach"])
 def test_training_step_with_dropout_matches_oracle(cuda, cfg):
     """Loss and every gradient of a dropout training step vs the oracle using the same masks."""
     from rgpt_b200.model import GPT

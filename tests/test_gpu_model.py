@@ -34,6 +34,8 @@ CFGS = {
     "asym_hyperball_silu": dict(BASE, qk_normtype="asymmetric_hyperball", activation_type="silu"),
     "dual_elasticball_mish": dict(BASE, qk_normtype="dual_elasticball", activation_type="mish"),
     "no_qk": dict(BASE, qk_normtype="identity"),
+    "elasticball": dict(BASE, qk_normtype="elasticball", use_layer_scale=True),
+    "hyperball": dict(BASE, qk_normtype="hyperball", use_layer_scale=True),
 }
 
 
