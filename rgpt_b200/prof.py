@@ -25,6 +25,11 @@ runs instead the bandwidth-bound kernels and the optimizer of the same step, onc
   [512, 2048] x 16 classes, apply), one fp32 Newton-Schulz iteration of one [512, 2048] matrix,
   and the dropout-0.1 variants of the attention forward and the residual GEMM. Device memory stays
   under 3 GB.
+
+    python -m rgpt_b200.prof ffn
+
+times the fused linear+activation sweep (forward + backward, M in {8192 .. 65536}, four activations)
+with CUDA events and prints a table.
 """
 import sys
 
@@ -172,8 +177,71 @@ def bandwidth_and_optimizer() -> None:
     print("rgpt_b200.prof bw: ok")
 
 
+def ffn_sweep() -> None:
+    """The fused linear+activation sweep: X bf16 [M, 512] ~ N(0, 1), W1 [2048, 512] and W2 [2048, 512]
+    ~ N(0, 0.02), no bias, upstream grad ~ N(0, 1), M in {8192, 16384, 32768, 65536}, the four
+    activations (model/kernels.py:289-374). Forward = fc1 GEMM with the activation epilogue (pre and
+    post stored) + the W2 GEMM; backward = dW2, dpre (activation-gradient epilogue), dW1, dX. Each pass
+    is replayed 10 times from a CUDA graph and timed with CUDA events; prints microseconds and TF/s
+    over 12 M 512 2048 FLOP (fc1 + act alone: 6 M 512 2048)."""
+    dev = torch.device('cuda')
+    g = torch.Generator(device=dev).manual_seed(3)
+    K, N = 512, 2048
+    w1 = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()
+    w2 = (torch.randn(N, K, device=dev, generator=g) * 0.02).bfloat16()  # [N, Out], fc2.weight^T
+    print("act           M   fwd us   bwd us  total TF/s  (fc1+act fwd us, TF/s)")
+    for M in (8192, 16384, 32768, 65536):
+        x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        dy = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        pre = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        post, dpre = torch.empty_like(pre), torch.empty_like(pre)
+        out = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+        dw1, dw2 = torch.zeros(N, K, device=dev), torch.zeros(N, K, device=dev)
+        dx = torch.empty(M, K, device=dev)
+        for name in ("squared_relu", "gelu", "silu", "mish"):
+            act = nv.act_id(name)
+
+            def fc1():
+                nv.gemm(x, w1, pre, epi=nv.EPI_ACT_FWD, act=act, out2=post)
+
+            def fwd():
+                fc1()
+                nv.gemm(post, w2.t(), out)
+
+            def bwd():
+                nv.gemm(post.t(), dy.t(), dw2, epi=nv.EPI_ACCUM_F32, splitk=0)
+                nv.gemm(dy, w2, dpre, epi=nv.EPI_ACT_BWD, act=act, c=pre)
+                nv.gemm(dpre.t(), x.t(), dw1, epi=nv.EPI_ACCUM_F32, splitk=0)
+                nv.gemm(dpre, w1.t(), dx, epi=nv.EPI_STORE_F32)
+
+            def timed(fn, n=10):
+                fn()
+                torch.cuda.synchronize()
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr):
+                    for _ in range(n):
+                        fn()
+                gr.replay()
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gr.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                return e0.elapsed_time(e1) / n * 1e3
+
+            tf, tb, t1 = timed(fwd), timed(bwd), timed(fc1)
+            flops = 12.0 * M * K * N
+            print(f"{name:12s} {M:6d} {tf:8.1f} {tb:8.1f} {flops / ((tf + tb) * 1e-6) / 1e12:11.1f}"
+                  f"  ({t1:.1f}, {2.0 * M * K * N / (t1 * 1e-6) / 1e12:.1f})")
+        del x, dy, pre, post, dpre, out, dx
+        torch.cuda.empty_cache()
+
+
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "bw":
         bandwidth_and_optimizer()
+    elif len(sys.argv) > 1 and sys.argv[1] == "ffn":
+        ffn_sweep()
     else:
         main()

@@ -100,6 +100,27 @@ def test_gemm_act_fwd_bwd(cuda, act):
     assert rel_err(dpre, ref) < 2e-2
 
 
+@pytest.mark.parametrize("act", ["squared_relu", "gelu", "silu", "mish"])
+def test_gemm_act_epilogue_elementwise_wide_range(cuda, act):
+    # Every pre-activation value in [-30, 30] (an identity weight passes A through exactly), so the
+    # saturated ends and Mish's x > 20 branch are exercised: post = act(pre) and dpre = act'(pre) per
+    # element, against torch's fp32 evaluation, within the bf16 rounding of the stored outputs.
+    n = 128
+    vals = torch.linspace(-30.0, 30.0, n * n, device=cuda).view(n, n).bfloat16()
+    eye = torch.eye(n, device=cuda).bfloat16()
+    pre = torch.empty(n, n, device=cuda, dtype=torch.bfloat16)
+    post = torch.empty_like(pre)
+    nv.gemm(vals, eye, pre, epi=nv.EPI_ACT_FWD, act=nv.act_id(act), out2=post)
+    x = vals.float()
+    assert torch.equal(pre.float(), x)
+    ref = ref_act(act, x)
+    assert torch.allclose(post.float(), ref, rtol=1e-2, atol=1e-5), (post.float() - ref).abs().max()
+    dpre = torch.empty_like(pre)
+    nv.gemm(torch.ones(n, n, device=cuda).bfloat16(), eye, dpre, epi=nv.EPI_ACT_BWD, act=nv.act_id(act), c=pre)
+    gref = ref_act_grad(act, x)
+    assert torch.allclose(dpre.float(), gref, rtol=1e-2, atol=1e-5), (dpre.float() - gref).abs().max()
+
+
 def test_gemm_resid_colscale(cuda):
     M, N, K = 1024, 512, 512
     g = torch.Generator(device=cuda).manual_seed(4)
