@@ -51,7 +51,9 @@ enum RgptEpilogue {
                               D2 f32 (optional) = alpha*acc, the unscaled branch output */
   RGPT_EPI_POLY_BF16 = 6,  /* D bf16 = beta*C + alpha*acc, C bf16                   */
   RGPT_EPI_BIAS_SIGMOID_BF16 = 7, /* D bf16 = sigmoid(alpha*acc + colscale[n]) (G1 gate)  */
-  RGPT_EPI_POLY_F32 = 8    /* D f32  = beta*C + alpha*acc, C f32 (fp32 Newton-Schulz)  */
+  RGPT_EPI_POLY_F32 = 8,   /* D f32  = beta*C + alpha*acc, C f32 (fp32 Newton-Schulz)  */
+  RGPT_EPI_ARGMAX_BF16 = 9 /* no D: per row and column tile, the first maximum of bf16(alpha*acc) and its
+                              column (rgpt_gemm_argmax only)                          */
 };
 enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4 };
 
@@ -67,6 +69,13 @@ int rgpt_gemm_bf16(const void* A, int a_mn_major, long long lda, long long a_bst
                    void* D2, long long ldd2, long long d2_bstride,
                    const void* C, long long ldc, long long c_bstride,
                    const float* colscale, int splitk, const float* alpha_dev, void* stream);
+/* Row argmax of bf16(A @ B^T) without writing the product: the rGPT per-recurrence lm_head whose logits
+ * only feed argmax (model/gpt.py:112-120). A [M, K] and B [N, K] bf16, K-major. The GEMM epilogue keeps,
+ * per row and column tile, the first maximum of the bf16-rounded values (part_val / part_idx, [M, ld_part]
+ * with ld_part >= ceil(N/128)); a second kernel combines the tiles into argmax[M] (int32): the first
+ * index of the row maximum, as torch.argmax over the stored bf16 logits. */
+int rgpt_gemm_argmax(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K, float* part_val,
+                     int* part_idx, long long ld_part, int* argmax, void* stream);
 /* RGPT_DROPOUT. rgpt_gemm_bf16 with the residual-branch dropout of model/transformer_block.py:45,52 fused
  * into the RESID_F32 epilogue (batch 1 only): the branch output alpha*acc becomes alpha*acc*keep/(1-drop_p)
  * (D2 stores that dropped branch output), keep = bit column%32 of drop_mask[row*drop_ldm + column/32]. */

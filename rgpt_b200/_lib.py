@@ -44,6 +44,7 @@ _SIGNATURES: dict[str, list] = {
         _c_vp, _c_ll, _c_float,  # drop_mask, drop_ldm, drop_p
         _c_vp,
     ],
+    "rgpt_gemm_argmax": [_c_vp, _c_ll, _c_vp, _c_ll, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_ll, _c_vp, _c_vp],
     "rgpt_drop_mask": [_c_vp, _c_ll, _c_vp, ctypes.c_uint, _c_float, _c_int, _c_int, _c_vp],
     "rgpt_attn_drop_mask": [_c_vp, _c_vp, ctypes.c_uint, _c_float, _c_int, _c_int, _c_int, _c_vp],
     "rgpt_rownorm_fwd": [_c_vp, _c_vp, _c_vp, _c_vp, _c_float, _c_int, _c_float, _c_float, _c_int, _c_int,

@@ -29,6 +29,8 @@
 //   RESID_F32    x_out = x_in + acc * layer_scale    (model/transformer_block.py:43-57)
 //   POLY_BF16    beta*C + alpha*acc                  (optimizer.py:36-41, Newton-Schulz)
 //   POLY_F32     the same in fp32 (C and D fp32)     (fp32 Newton-Schulz on split bf16 operands)
+//   ARGMAX_BF16  per row and column tile: the first maximum of bf16(acc) and its column; no output
+//                matrix (the rGPT per-step lm_head argmax, model/gpt.py:119-120)
 //   BIAS_SIGMOID sigmoid(acc + bias)                 (model/attention.py:45-48, G1 gate)
 //   ACCUM_F32    grad += acc (bulk reduce-add, so split-K needs no separate reduction)
 #include <cudaTypedefs.h>
@@ -60,6 +62,10 @@ struct EpiParams {
   const uint32_t* drop_mask;
   long long drop_ldm;
   float drop_scale;
+  // ARGMAX_BF16 only: per (row, column tile) maximum and its column, [M, amax_ld]
+  float* amax_val;
+  int* amax_idx;
+  long long amax_ld;
 };
 
 constexpr int GEMM_BM = 128;
@@ -428,7 +434,36 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if constexpr (bf16_out) {
+      if constexpr (EPI == RGPT_EPI_ARGMAX_BF16) {
+        // this thread's row over the tile's columns, in increasing order: a strict > keeps the first
+        // maximum of the bf16-rounded values (the order a row argmax over stored bf16 logits sees)
+        float best = -INFINITY;
+        int besti = 0x7fffffff;
+#pragma unroll 1
+        for (int c0 = cbeg; c0 < cend; c0 += 64) {
+          uint32_t rr[2][32];
+          tmem_ld32(t_row + c0, rr[0]);
+          tmem_ld32(t_row + c0 + 32, rr[1]);
+          tmem_wait_ld();
+          const int gn0 = nt * BN + c0;
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = gn0 + hf * 32 + j;
+              const float v = bf16_round(__uint_as_float(rr[hf][j]) * alpha);
+              if (col < sh.N && v > best) {
+                best = v;
+                besti = col;
+              }
+            }
+        }
+        const int row = row0 + lane;
+        if (row < sh.M) {
+          ep.amax_val[(long long)row * ep.amax_ld + nt] = best;
+          ep.amax_idx[(long long)row * ep.amax_ld + nt] = besti;
+        }
+      } else if constexpr (bf16_out) {
         auto chunk_bf16 = [&](int c0, const uint4 (&cc)[8]) {
           const int gn0 = nt * BN + c0;
           const bool live = rows_live && gn0 < sh.N;  // warp-uniform
@@ -733,6 +768,7 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
     RGPT_GEMM_EPI_CASE(RGPT_EPI_RESID_F32)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_BF16)
     RGPT_GEMM_EPI_CASE(RGPT_EPI_POLY_F32)
+    RGPT_GEMM_EPI_CASE(RGPT_EPI_ARGMAX_BF16)
     default: return launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_BIAS_SIGMOID_BF16, PAIR>(ta, tb, td, td2, sh, ep, s, dev);
   }
 #undef RGPT_GEMM_EPI_CASE
@@ -765,10 +801,47 @@ static int dispatch_gemm(int BN, bool pair, int a_mn, int b_mn, int epi, const C
 
 using namespace rgpt;
 
+// Row argmax from the ARGMAX_BF16 GEMM's per-tile results: one warp per row, the largest value and,
+// among equal values, the smallest column (so the first maximum of the row, as torch.argmax).
+__global__ void argmax_reduce_kernel(const float* __restrict__ val, const int* __restrict__ idx, long long ld,
+                                     int n_tiles, int M, int* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int t = lane; t < n_tiles; t += 32) {
+    const float v = val[(long long)row * ld + t];
+    const int i = idx[(long long)row * ld + t];
+    if (v > best || (v == best && i < besti)) {
+      best = v;
+      besti = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ov > best || (ov == best && oi < besti)) {
+      best = ov;
+      besti = oi;
+    }
+  }
+  if (lane == 0) out[row] = besti;
+}
+
 struct DropArgs {
   const void* mask;
   long long ldm;
   float p;
+};
+
+struct AmaxArgs {  // ARGMAX_BF16 partial results, [M, ld] each; n_tiles is set to the column tiles used
+  float* val;
+  int* idx;
+  long long ld;
+  int n_tiles;
 };
 
 static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_bstride, const void* B,
@@ -776,7 +849,7 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
                       int act, float alpha, float beta, void* D, long long ldd, long long d_bstride, void* D2,
                       long long ldd2, long long d2_bstride, const void* C, long long ldc, long long c_bstride,
                       const float* colscale, int splitk, const float* alpha_dev, const DropArgs* drop,
-                      void* stream) {
+                      void* stream, AmaxArgs* amax = nullptr) {
   int dev = 0;
   cudaGetDevice(&dev);
   int st = rgpt_check_device(dev);
@@ -785,13 +858,17 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   if (batch < 1) batch = 1;
   if (M < 1 || N < 1 || K < 1)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm needs M, N, K >= 1 (got M=%d N=%d K=%d)", M, N, K);
-  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_POLY_F32)
+  if (epi < RGPT_EPI_STORE_BF16 || epi > RGPT_EPI_ARGMAX_BF16 || (epi == RGPT_EPI_ARGMAX_BF16 && amax == nullptr))
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "unknown epilogue %d", epi);
-  if (D == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm output pointer is null");
+  const bool amx = epi == RGPT_EPI_ARGMAX_BF16;  // no output matrix: per-tile row maxima instead
+  if (amx && (batch != 1 || amax->val == nullptr || amax->idx == nullptr || amax->ld < (N + 127) / 128))
+    return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "argmax GEMM needs batch 1 and [M, >= %d] partial buffers",
+                          (N + 127) / 128);
+  if (D == nullptr && !amx) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "gemm output pointer is null");
   const bool out_f32 = (epi == RGPT_EPI_STORE_F32 || epi == RGPT_EPI_ACCUM_F32 || epi == RGPT_EPI_RESID_F32 ||
                         epi == RGPT_EPI_POLY_F32);
   const int vec = out_f32 ? 4 : 8;
-  if (ldd % vec != 0 || (reinterpret_cast<uintptr_t>(D) & 15) != 0)
+  if (!amx && (ldd % vec != 0 || (reinterpret_cast<uintptr_t>(D) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "output leading dim / pointer not 16-byte aligned");
   if (epi == RGPT_EPI_ACT_FWD && (D2 == nullptr || ldd2 % 8 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "ACT_FWD needs an aligned second output");
@@ -825,7 +902,7 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   // Short-K GEMMs with few tiles stay on single-CTA tiles, whose shorter signalling chain
   // finishes each tile sooner.
   const long long pair_tiles = (long long)batch * ((M + 255) / 256) * ((N + 255) / 256);
-  const bool plain_store = epi == RGPT_EPI_STORE_BF16 || epi == RGPT_EPI_STORE_F32;
+  const bool plain_store = epi == RGPT_EPI_STORE_BF16 || epi == RGPT_EPI_STORE_F32 || amx;
   const bool pair = BN == 256 && M > GEMM_BM &&
                     ((pair_tiles >= nsm / 2 && (sh.num_kb >= 16 || (plain_store && pair_tiles >= 8LL * nsm))) ||
                      (epi == RGPT_EPI_ACCUM_F32 && sh.num_kb >= 32));
@@ -873,7 +950,10 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   // Output maps: one 32-row x 128-byte box per epilogue warp and chunk.
   const int ob = out_f32 ? 4 : 2;
   const uint32_t obox = out_f32 ? 32 : 64;
-  if ((st = make_tmap_3d(&td, D, ob, N, M, batch, ldd, d_bstride, obox, 32))) return st;
+  if (amx)
+    td = ta;  // never used by the argmax epilogue (only its descriptor is prefetched)
+  else if ((st = make_tmap_3d(&td, D, ob, N, M, batch, ldd, d_bstride, obox, 32)))
+    return st;
   const bool has_d2 = (epi == RGPT_EPI_ACT_FWD) || (epi == RGPT_EPI_RESID_F32 && D2 != nullptr);
   if (has_d2) {
     if ((st = make_tmap_3d(&td2, D2, ob, N, M, batch, ldd2, d2_bstride, obox, 32))) return st;
@@ -904,6 +984,10 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   ep.drop_mask = nullptr;
   ep.drop_ldm = 0;
   ep.drop_scale = 1.0f;
+  if (amx) amax->n_tiles = sh.n_tiles;
+  ep.amax_val = amx ? amax->val : nullptr;
+  ep.amax_idx = amx ? amax->idx : nullptr;
+  ep.amax_ld = amx ? amax->ld : 0;
   if (drop != nullptr && drop->p > 0.0f) {
     if (epi != RGPT_EPI_RESID_F32)
       return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "dropout is only fused into the RESID_F32 epilogue");
@@ -942,4 +1026,17 @@ extern "C" int rgpt_gemm_bf16_dropout(const void* A, int a_mn_major, long long l
   return gemm_entry(A, a_mn_major, lda, a_bstride, B, b_mn_major, ldb, b_bstride, M, N, K, batch, epi, act, alpha,
                     beta, D, ldd, d_bstride, D2, ldd2, d2_bstride, C, ldc, c_bstride, colscale, splitk, alpha_dev,
                     &d, stream);
+}
+
+extern "C" int rgpt_gemm_argmax(const void* A, long long lda, const void* B, long long ldb, int M, int N, int K,
+                                float* part_val, int* part_idx, long long ld_part, int* argmax, void* stream) {
+  if (argmax == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "argmax output pointer is null");
+  AmaxArgs a = {part_val, part_idx, ld_part, 0};
+  int st = gemm_entry(A, 0, lda, 0, B, 0, ldb, 0, M, N, K, 1, RGPT_EPI_ARGMAX_BF16, 0, 1.0f, 0.0f, nullptr, 0, 0,
+                      nullptr, 0, 0, nullptr, 0, 0, nullptr, 1, nullptr, nullptr, stream, &a);
+  if (st) return st;
+  // a.n_tiles: the column tiles of the width the GEMM chose (128 or 256), each written for every row
+  launch_pdl(argmax_reduce_kernel, dim3((unsigned)((M + 7) / 8)), dim3(256), 0, reinterpret_cast<cudaStream_t>(stream), 1,
+             (const float*)part_val, (const int*)part_idx, ld_part, a.n_tiles, M, argmax);
+  return rgpt_check_launch("argmax_reduce_kernel");
 }

@@ -99,6 +99,9 @@ class _Acts:
             self.q = e(R, M, 2, dt=f32)
             self.dq = e(R, M, 2, dt=f32)
             self.argmax = e(R, M, dt=torch.int32)
+            # per-column-tile partial maxima of the per-recurrence lm_head (its logits are never stored)
+            self.amax_val = e(M, (V + 127) // 128, dt=f32)
+            self.amax_idx = e(M, (V + 127) // 128, dt=torch.int32)
         # backward scratch
         self.g = e(M, d, dt=f32)
         self.gb = e(M, d)
@@ -357,9 +360,9 @@ class Engine:
                 kind, eps, alpha, w, temp = self._resid_norm(m, "ln_f")
                 nv.rownorm_fwd(A.x[app], A.hq[r], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0,
                                alpha=alpha, qw=m.q_head.weight, qb=m.q_head.bias, qout=A.q[r])
-                # per-step logits feed only the no-grad argmax (their CE is discarded, model/gpt.py:113-117)
-                nv.gemm(A.hq[r], self.lm_w, A.logits)
-                nv.cross_entropy(A.logits, lab, ignore_index=self.ignore_index, argmax=A.argmax[r])
+                # per-step logits feed only the no-grad argmax (their CE is discarded, model/gpt.py:113-117):
+                # the lm_head GEMM reduces each row to its argmax in the epilogue instead of storing them
+                nv.gemm_argmax(A.hq[r], self.lm_w, A.amax_val, A.amax_idx, A.argmax[r])
         kind, eps, alpha, w, temp = self._resid_norm(m, "ln_f")
         nv.rownorm_fwd(A.x[app], A.hf, kind, eps, w=w, temp=float(temp) if temp is not None else 1.0, alpha=alpha)
         nv.gemm(A.hf, self.lm_w, A.logits)

@@ -19,6 +19,7 @@ EPI_RESID_F32 = 5
 EPI_POLY_BF16 = 6
 EPI_BIAS_SIGMOID_BF16 = 7
 EPI_POLY_F32 = 8
+EPI_ARGMAX_BF16 = 9
 
 ACTIVATIONS = {"none": 0, "identity": 0, "squared_relu": 1, "gelu": 2, "silu": 3, "mish": 4}
 
@@ -52,6 +53,26 @@ def _drop_args(drop: "Drop | None", seed_needed: bool = True):
     if seed_needed and drop.seed is None:
         raise ValueError("this dropout call draws new bits and needs the seed")
     return ptr(drop.mask), ptr(drop.seed) if drop.seed is not None else None, drop.site & 0xFFFFFFFF, drop.p
+
+
+def gemm_argmax(A: torch.Tensor, B: torch.Tensor, part_val: torch.Tensor, part_idx: torch.Tensor,
+                argmax: torch.Tensor) -> None:
+    """argmax[m] = first index of the maximum of bf16(A @ B^T)[m, :] without writing the product.
+
+    A [M, K], B [N, K] bf16 with unit stride on K; part_val (fp32) / part_idx (int32) [M, >= ceil(N/128)]
+    hold the per-column-tile partial results; argmax int32 [M]."""
+    M, K = A.shape
+    N = B.shape[0]
+    for t, n in ((A, "A"), (B, "B")):
+        if t.dtype != torch.bfloat16 or t.stride(-1) != 1 or t.dim() != 2:
+            raise ValueError(f"gemm_argmax: {n} must be 2-D bf16 with unit stride on K")
+    if part_val.dtype != torch.float32 or part_idx.dtype != torch.int32 or argmax.dtype != torch.int32:
+        raise TypeError("gemm_argmax: partial values fp32, partial indices and argmax int32")
+    ld = part_val.stride(0)
+    if part_idx.stride(0) != ld or part_val.shape[0] < M or part_val.shape[1] < (N + 127) // 128:
+        raise ValueError("gemm_argmax: partial buffers must be [M, >= ceil(N/128)] with equal row strides")
+    _lib.call("rgpt_gemm_argmax", ptr(A), A.stride(0), ptr(B), B.stride(0), M, N, K, ptr(part_val), ptr(part_idx),
+              ld, ptr(argmax), _lib.stream_ptr(A.device))
 
 
 def drop_mask_rows(drop: Drop, M: int, N: int) -> None:

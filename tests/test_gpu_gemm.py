@@ -258,3 +258,27 @@ def test_gemm_c_epilogues_ragged_edges(cuda, M, N, K):
     out = torch.full((M, ldb), 7.0, device=cuda, dtype=torch.bfloat16)[:, :N]
     nv.gemm(a, w, out, epi=nv.EPI_POLY_BF16, alpha=0.5, beta=-1.5, c=c)
     assert rel_err(out, 0.5 * ref - 1.5 * c.float()) < 1e-2
+
+
+@pytest.mark.parametrize("M,N", [(4096, 50304), (333, 1000), (300, 200)])
+def test_gemm_argmax_equals_stored_logits_argmax(cuda, M, N):
+    # The argmax epilogue (no logits stored) against the stored bf16 logits of the same GEMM, reduced
+    # by the cross-entropy kernel's argmax: identical indices (first maximum on ties), including rows
+    # with planted exact ties.
+    g = torch.Generator(device=cuda).manual_seed(M + N)
+    a = torch.randn(M, 512, device=cuda, generator=g).bfloat16()
+    b = (torch.randn(N, 512, device=cuda, generator=g) * 0.05).bfloat16()
+    b[N // 2] = b[N // 3]  # two equal columns: the first one must win where they are the maximum
+    a[0] = b[N // 3]       # row 0 peaks at those two columns
+    logits = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    nv.gemm(a, b, logits)
+    ref = torch.empty(M, device=cuda, dtype=torch.int32)
+    nv.cross_entropy(logits, torch.zeros(M, device=cuda, dtype=torch.long), argmax=ref)
+    pv = torch.empty(M, (N + 127) // 128, device=cuda)
+    pi = torch.empty(M, (N + 127) // 128, device=cuda, dtype=torch.int32)
+    out = torch.empty(M, device=cuda, dtype=torch.int32)
+    nv.gemm_argmax(a, b, pv, pi, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    assert torch.equal(out.long(), logits.float().argmax(dim=1).int().long())
+    assert out[0].item() == N // 3
