@@ -181,10 +181,15 @@ class Muon(torch.optim.Optimizer):
     def __init__(self, params: List[Dict[str, Any]], lr: float = 3e-4, weight_decay: float = 0.01,
                  momentum: float = 0.95, nesterov: bool = True, adam_betas: Tuple[float, float] = (0.9, 0.95),
                  adam_eps: float = 1e-8, muon_lr_multiplier: float = 100.0, ns_steps: int = 5,
-                 ns_coeffs: Tuple[float, float, float] = NS_COEFFS):
+                 ns_coeffs: Tuple[float, float, float] = NS_COEFFS, ns_precision: str = "bf16"):
+        """ns_precision: "bf16" iterates Newton-Schulz in bf16 as the reference does (optimizer.py:20-44);
+        "fp32" iterates it at fp32 accuracy (hi/lo bf16 operands, fp32 accumulation) from the same bf16
+        input, the update still rounded to bf16 as the reference rounds it (optimizer.py:68)."""
+        if ns_precision not in ("bf16", "fp32"):
+            raise ValueError(f"ns_precision must be 'bf16' or 'fp32', got {ns_precision!r}")
         defaults = dict(lr=lr, weight_decay=weight_decay, momentum=momentum, nesterov=nesterov,
                         adam_betas=adam_betas, adam_eps=adam_eps, muon_lr_multiplier=muon_lr_multiplier,
-                        ns_steps=ns_steps, ns_coeffs=tuple(ns_coeffs))
+                        ns_steps=ns_steps, ns_coeffs=tuple(ns_coeffs), ns_precision=ns_precision)
         super().__init__(params, defaults)
         self._cache: Dict[Any, Any] = {}
         self._hp_dev: Optional[torch.Tensor] = None
@@ -326,6 +331,7 @@ class Muon(torch.optim.Optimizer):
         nesterov = bool(group["nesterov"])
         steps = int(group.get("ns_steps", 5))
         coeffs = tuple(group.get("ns_coeffs", NS_COEFFS))
+        fp32 = group.get("ns_precision", "bf16") == "fp32"
         # batch by the shape Newton-Schulz sees (rows <= cols after transposing), so e.g. fc1 [4d, d]
         # and fc2 [d, 4d] share one stack; prep/apply run per original shape on slices of it
         classes: Dict[Tuple[int, int], Dict[Tuple[int, int], List[torch.Tensor]]] = {}
@@ -341,7 +347,7 @@ class Muon(torch.optim.Optimizer):
             ordered = [(rc, ps) for rc, ps in sorted(subs.items())]
             all_ps = [p for _, ps in ordered for p in ps]
             rows_all = _muon_rows(all_ps, [p.grad for p in all_ps], [self.state[p]["momentum_buffer"] for p in all_ps])
-            key = ("muon", gi, xr, xc, tuple(r[0] for r in rows_all), tuple(r[1] for r in rows_all))
+            key = ("muon", gi, xr, xc, fp32, tuple(r[0] for r in rows_all), tuple(r[1] for r in rows_all))
             ent = self._cache.get(key)
             if ent is None:
                 dev = all_ps[0].device
@@ -349,17 +355,27 @@ class Muon(torch.optim.Optimizer):
                 for (R, C), ps in ordered:
                     tables.append((R, C, off, len(ps), _table(rows_all[off:off + len(ps)], dev)))
                     off += len(ps)
-                ent = (tables, _NSWorkspace(len(all_ps), xr, xc, dev))
+                ent = (tables, _NSWorkspace(len(all_ps), xr, xc, dev),
+                       _NSWorkspaceF32(len(all_ps), xr, xc, dev) if fp32 else None)
                 self._cache[key] = ent
-            tables, ws = ent
+            tables, ws, ws32 = ent
 
-            def run(tables=tables, ws=ws):
+            def run(tables=tables, ws=ws, ws32=ws32):
                 ws.sumsq.zero_()
                 for R, C, off, n, table in tables:
                     nv.muon_prep(table, n, R, C, ws.X[off:off + n], beta, nesterov, ws.sumsq[off:off + n],
                                  hp=self._hp(gi))
-                nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
-                out = newton_schulz_batched(ws, steps, coeffs)
+                if ws32 is None:
+                    nv.ns_scale(ws.X, ws.xr, _pad8(ws.xc), ws.n, ws.sumsq)
+                    out = newton_schulz_batched(ws, steps, coeffs)
+                else:
+                    # the bf16 Nesterov stack, normalised into fp32, iterated at fp32 accuracy, and the
+                    # result written back as bf16 (one hi block) for the apply kernel
+                    r_, c_ = ws.xr, ws.xc  # this class's shape (the loop variables move on before jobs run)
+                    nv.ns_split(ws.X[:, :r_, :c_], sumsq=ws.sumsq, xout=ws32.X[:, :r_, :c_])
+                    res = newton_schulz_batched_f32(ws32, steps, coeffs)
+                    nv.ns_split(res[:, :r_, :c_], dst=ws.X[:, :r_, :c_], nblk=1, blk_off=0, lo_mask=0)
+                    out = ws.X
                 for R, C, off, n, table in tables:
                     nv.muon_apply(table, n, R, C, out[off:off + n], lr, wd, muon_lr, _muon_scale(R, C),
                                   hp=self._hp(gi))
@@ -451,8 +467,8 @@ class DistMuon(Muon):
         if world <= 1:
             return super().step(closure)
         self._average_grads()
-        if not self.shard_ns:
-            return super().step(closure)
+        if not self.shard_ns or any(g.get("ns_precision", "bf16") == "fp32" for g in self.param_groups):
+            return super().step(closure)  # the fp32 iteration runs replicated on every rank
         loss = None
         if closure is not None:
             with torch.enable_grad():

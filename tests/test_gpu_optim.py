@@ -221,3 +221,36 @@ def test_ns_split_hi_lo_blocks_and_transposed_source(cuda):
     assert ((recon - X[:, :45, :70].double()).abs() <= X[:, :45, :70].double().abs() * 2.0 ** -17).all()
     assert (X[:, 45:, :] == 7.0).all() and (X[:, :, 70:] == 7.0).all()      # padding untouched
     assert (W[:, 45:, :] == 9.0).all() and (W[:, :45, 70:72] == 9.0).all()
+
+
+def test_muon_fp32_newton_schulz_option(cuda):
+    """Muon(ns_precision="fp32"): one step's weight change equals the reference update with the fp32
+    Newton-Schulz restatement (update rounded to bf16 as optimizer.py:68 rounds it), within 5e-3
+    relative (a few update elements may land on the other side of a bf16 rounding boundary), and it is
+    closer to that than the default bf16 iteration is (measured on a B200: 3.5e-4 to 5.4e-4 against
+    1.1e-2 to 1.4e-2 for the bf16 mode). Momentum 0 makes the Newton-Schulz input exactly
+    bf16(G) on both sides: the iteration amplifies last-bit input differences (slope 3.44 per step
+    near zero), which would otherwise blur what is compared."""
+    g = torch.Generator().manual_seed(21)
+    shapes = [(512, 512), (2048, 512), (512, 2048), (64, 64)]
+    W0 = [torch.randn(*s, generator=g) * 0.02 for s in shapes]
+    G = [torch.randn(*s, generator=g) * 1e-2 for s in shapes]
+    lr, wd, mult = 0.02, 0.1, 1.0
+    deltas = {}
+    for prec in ("fp32", "bf16"):
+        ps = [torch.nn.Parameter(w.clone().to(cuda)) for w in W0]
+        for p, gr in zip(ps, G):
+            p.grad = gr.to(cuda)
+        opt = Muon([{"params": ps, "use_muon": True}], lr=lr, weight_decay=wd, muon_lr_multiplier=mult,
+                   momentum=0.0, ns_precision=prec)
+        opt.step()
+        torch.cuda.synchronize()
+        deltas[prec] = [p.detach().cpu() - w * (1 - lr * wd) for p, w in zip(ps, W0)]
+    for i, (w, gr) in enumerate(zip(W0, G)):
+        m = torch.zeros(*gr.shape, dtype=torch.bfloat16)
+        upd = O.muon_update(gr, m, 0.0, 5, True, O.muon_scale(*gr.shape), ns_dtype=torch.float32)
+        ref = -lr * mult * upd.float()
+        e32, e16 = rel(deltas["fp32"][i], ref), rel(deltas["bf16"][i], ref)
+        print(f"{shapes[i]}: fp32 mode {e32:.2e}, bf16 mode {e16:.2e}")
+        assert e32 < 5e-3, (shapes[i], e32, e16)
+        assert e32 < e16, (shapes[i], e32, e16)
