@@ -36,6 +36,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -87,7 +88,7 @@ class ClockSampler:
 
     def __init__(self):
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        self.path = os.path.join(tempfile.gettempdir(), f"rgpt_clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
