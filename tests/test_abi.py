@@ -47,3 +47,19 @@ def test_version_and_error_buffer_without_gpu():
     assert lib.rgpt_version() >= 100
     buf = ctypes.create_string_buffer(64)
     assert lib.rgpt_last_error(buf, 64) == 0
+
+
+def test_binding_argument_counts_match_the_header():
+    """Each ctypes binding passes exactly as many arguments as the header declares (a missing or extra
+    argument would shift every later one)."""
+    from rgpt_b200 import _lib
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = dict(re.findall(r"\bint\s+(rgpt_\w+)\s*\(([^)]*)\)\s*;", text))
+    mismatched = []
+    for name, params in decls.items():
+        params = params.strip()
+        n = 0 if params in ("", "void") else len(params.split(","))
+        if len(_lib._SIGNATURES[name]) != n:
+            mismatched.append((name, n, len(_lib._SIGNATURES[name])))
+    assert not mismatched, mismatched
