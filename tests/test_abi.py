@@ -63,3 +63,29 @@ def test_binding_argument_counts_match_the_header():
         if len(_lib._SIGNATURES[name]) != n:
             mismatched.append((name, n, len(_lib._SIGNATURES[name])))
     assert not mismatched, mismatched
+
+
+def test_binding_argument_types_match_the_header():
+    """Each ctypes argument type is the one the header's parameter needs (a float bound as an int, or a
+    64-bit size bound as 32 bits, would be read wrongly by the library)."""
+    import ctypes
+
+    from rgpt_b200 import _lib
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    decls = dict(re.findall(r"\bint\s+(rgpt_\w+)\s*\(([^)]*)\)\s*;", text))
+    scalar = {"int": ctypes.c_int, "float": ctypes.c_float, "long long": ctypes.c_longlong,
+              "unsigned": ctypes.c_uint, "size_t": ctypes.c_ulonglong}
+
+    def ctype_of(param):
+        if "*" in param:
+            return ctypes.c_char_p if re.match(r"\s*(const\s+)?char\s*\*", param) else ctypes.c_void_p
+        words = [w for w in param.split()[:-1] if w != "const"]  # the type, without the name
+        return scalar[" ".join(words)]
+
+    bad = []
+    for name, params in decls.items():
+        ps = [] if params.strip() in ("", "void") else params.split(",")
+        want = [ctype_of(p) for p in ps]
+        if want != list(_lib._SIGNATURES[name]):
+            bad.append(name)
+    assert not bad, bad
