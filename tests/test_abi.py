@@ -74,7 +74,7 @@ def test_binding_argument_types_match_the_header():
     text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
     decls = dict(re.findall(r"\bint\s+(rgpt_\w+)\s*\(([^)]*)\)\s*;", text))
     scalar = {"int": ctypes.c_int, "float": ctypes.c_float, "long long": ctypes.c_longlong,
-              "unsigned": ctypes.c_uint, "size_t": ctypes.c_ulonglong}
+              "unsigned": ctypes.c_uint, "size_t": ctypes.c_ulonglong, "unsigned long long": ctypes.c_ulonglong}
 
     def ctype_of(param):
         if "*" in param:
