@@ -169,3 +169,19 @@ def test_oracle_dropout_masks_rate_and_independence():
     assert abs(a.float().mean().item() - 0.7) < 0.01
     assert not torch.equal(a[0, 0], a[0, 1])
     assert O.resid_drop_mask(9, 1, 8, 64, 0.0).all()
+
+
+def test_engine_and_oracle_number_dropout_sites_alike():
+    """The engine draws the embedding mask at EMB_DROP_SITE and layer application app's masks at
+    4*app + {0: attention branch, 1: FFN branch, 2: attention probabilities}; the oracle must regenerate
+    the same sites (gpt_forward's drop_seed path) or a dropout step would be compared against other bits."""
+    import inspect
+
+    from rgpt_b200.model.engine import Engine
+    assert Engine.EMB_DROP_SITE == O.EMB_DROP_SITE
+    src = inspect.getsource(Engine._drop)
+    for frag in ("4 * app,", "4 * app + 1,", "4 * app + 2,"):
+        assert frag in src, frag
+    osrc = inspect.getsource(O.gpt_forward) + inspect.getsource(O.block_forward) + inspect.getsource(O.attention_forward)
+    for frag in ('"site": 4 * (i * cfg["n_layers"] + li)', 'drop["site"] + 1', 'drop["site"] + 2'):
+        assert frag in osrc, frag
