@@ -25,64 +25,12 @@
 #include <cuda_fp16.h>
 
 #include "common.cuh"
+#include "norm.cuh"
 #include "rgpt.h"
 
 #include <type_traits>
 
 namespace rgpt {
-
-struct NS2 {
-  float s, ds;
-};
-
-__device__ __forceinline__ NS2 norm_scale(int kind, float S, int d, float eps, float alpha) {
-  NS2 r;
-  switch (kind) {
-    case RGPT_NORM_RMS_AFFINE:
-    case RGPT_NORM_RMS: {
-      const float v = S / d + eps;
-      r.s = rsqrtf(v);
-      r.ds = -0.5f * r.s / v / d;
-      break;
-    }
-    case RGPT_NORM_L2_TEMP:
-    case RGPT_NORM_L2: {
-      const float n = sqrtf(S);
-      r.s = 1.0f / (n + eps);
-      r.ds = n > 0.f ? -r.s * r.s / (2.0f * n) : 0.f;
-      break;
-    }
-    case RGPT_NORM_ELASTIC: {
-      const float Sc = fmaxf(S, eps);
-      const float hs = sqrtf((float)d) * rsqrtf(Sc);
-      const float dh = (S >= eps) ? -hs / (2.0f * Sc) : 0.f;
-      if (hs < 1.0f) {
-        r.s = hs;
-        r.ds = dh;
-      } else {
-        r.s = powf(hs, alpha);
-        r.ds = alpha * powf(hs, alpha - 1.0f) * dh;
-      }
-      break;
-    }
-    case RGPT_NORM_ELASTICBALL: {
-      const float v = S + eps;
-      r.s = powf((float)d / v, 0.5f * alpha);
-      r.ds = -0.5f * alpha * r.s / v;
-      break;
-    }
-    case RGPT_NORM_HYPERBALL: {
-      const float v = 1.0f + S / d;
-      r.s = rsqrtf(v);
-      r.ds = -0.5f * r.s / v / d;
-      break;
-    }
-    default:
-      r.s = 1.f;
-      r.ds = 0.f;
-  }
-  return r;
-}
 
 // ============================================================================ residual norm
 // One warp per row; each lane owns NV float4 (d = 128 * NV).
@@ -118,7 +66,8 @@ __global__ void rownorm_fwd_kernel(const float* __restrict__ x, __nv_bfloat16* _
       float4 ww = reinterpret_cast<const float4*>(w)[lane + 32 * i];
       a = make_float4(1.f + ww.x, 1.f + ww.y, 1.f + ww.z, 1.f + ww.w);
     } else if (kind == RGPT_NORM_L2_TEMP) {
-      a = make_float4(temp, temp, temp, temp);
+      const float t = w ? w[0] : temp;  // the learned temperature, read on the device when given
+      a = make_float4(t, t, t, t);
     }
     float4 o = make_float4(v[i].x * ns.s * a.x, v[i].y * ns.s * a.y, v[i].z * ns.s * a.z, v[i].w * ns.s * a.w);
     yr[lane + 32 * i] = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
@@ -186,7 +135,10 @@ __global__ void __launch_bounds__(256, NV <= 4 ? 2 : 1) rownorm_bwd_kernel(const
       float4 ww = reinterpret_cast<const float4*>(w)[lane + 32 * i];
       return make_float4(1.f + ww.x, 1.f + ww.y, 1.f + ww.z, 1.f + ww.w);
     }
-    if (kind == RGPT_NORM_L2_TEMP) return make_float4(temp, temp, temp, temp);
+    if (kind == RGPT_NORM_L2_TEMP) {
+      const float t = w ? w[0] : temp;
+      return make_float4(t, t, t, t);
+    }
     return make_float4(1.f, 1.f, 1.f, 1.f);
   };
 
@@ -375,7 +327,12 @@ __device__ __forceinline__ float4 qk_affine4(const QkNormArgs& a, bool is_q, int
     const float4 w = *reinterpret_cast<const float4*>((is_q ? a.wq : a.wk) + i0);
     return make_float4((1.0f + w.x) * post, (1.0f + w.y) * post, (1.0f + w.z) * post, (1.0f + w.w) * post);
   }
-  const float t = (a.kind == RGPT_NORM_L2_TEMP ? (is_q ? a.tq : a.tk) : 1.0f) * post;
+  float t = 1.0f;
+  if (a.kind == RGPT_NORM_L2_TEMP) {
+    const float* tp = is_q ? a.wq : a.wk;  // learned temperature on the device, else the by-value one
+    t = tp ? *tp : (is_q ? a.tq : a.tk);
+  }
+  t *= post;
   return make_float4(t, t, t, t);
 }
 

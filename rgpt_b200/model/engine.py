@@ -57,11 +57,44 @@ def norm_spec(kind_name: str, module, eps: float, is_qk: bool = False):
     kind = NORM_KINDS[kind_name]
     if kind == nv.NORM_RMS:
         return kind, nv.FLT_EPS, 0.5, None, None
-    w = getattr(module, "weight", None) if kind == nv.NORM_RMS_AFFINE else None
     temp = getattr(module, "temp", None) if kind == nv.NORM_L2_TEMP else None
+    # RMSNorm's weight, or L2Norm's learned temperature: the kernels read either from the device, so a
+    # captured step sees the optimizer's latest value and nothing waits for a host copy
+    w = getattr(module, "weight", None) if kind == nv.NORM_RMS_AFFINE else temp
     e = float(getattr(module, "eps", eps)) if module is not None and not torch.is_tensor(
         getattr(module, "eps", None)) else float(eps)
     return kind, e, 0.5, w, temp
+
+
+def qk_norm_spec(attn, qk: str, norm_eps: float) -> dict:
+    """Arguments of the QKV-prep kernels for an Attention module's QK norm (QKNorm, model/norm.py:182-204):
+    kind, eps, alpha, wq/wk (RMSNorm weights, or L2Norm temperatures read on the device), tq/tk (unused
+    by-value temperatures) and the constant post-scales sq/sk (asymmetric hyperball)."""
+    if qk in ("none", "identity", None) or attn.qk_norm is None:
+        return dict(kind=nv.NORM_IDENTITY, eps=0.0, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0)
+    qn = attn.qk_norm
+    if qk == "f_rmsnorm":
+        return dict(kind=nv.NORM_RMS, eps=nv.FLT_EPS, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0)
+    if qk == "dual_elasticball":
+        nm = qn.norm_module
+        return dict(kind=nv.NORM_ELASTICBALL, eps=nm.q_norm.eps, alpha=nm.q_norm.alpha, wq=None, wk=None,
+                    tq=1.0, tk=1.0, sq=1.0, sk=1.0)
+    if qk == "asymmetric_hyperball":
+        nm = qn.norm_module
+        return dict(kind=nv.NORM_HYPERBALL, eps=0.0, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0,
+                    sq=float(nm.scale_q), sk=float(nm.scale_k))
+    kind, e, alpha, _, _ = norm_spec(qk, qn.q_norm_fn, norm_eps)
+    spec = dict(kind=kind, eps=e, alpha=alpha, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0)
+    if kind == nv.NORM_ELASTIC or kind == nv.NORM_ELASTICBALL:
+        spec["eps"] = float(qn.q_norm_fn.eps)
+        spec["alpha"] = float(qn.q_norm_fn.alpha)
+    if kind == nv.NORM_RMS_AFFINE:
+        spec["eps"] = float(qn.q_norm_fn.eps)
+        spec["wq"], spec["wk"] = qn.q_norm_fn.weight, qn.k_norm_fn.weight
+    if kind == nv.NORM_L2_TEMP:
+        spec["eps"] = float(qn.q_norm_fn.eps)
+        spec["wq"], spec["wk"] = qn.q_norm_fn.temp, qn.k_norm_fn.temp  # read on the device
+    return spec
 
 
 class _Acts:
@@ -178,7 +211,10 @@ class Engine:
         m = self.model
         dev = self.device
         named = list(m.named_parameters())
-        total = sum(p.numel() for _, p in named)
+        # every gradient starts on a 16-byte boundary (the GEMM epilogues' TMA and vector stores need
+        # it), so 1-element parameters such as L2Norm's temperature are padded to 4 floats
+        slot = lambda n: (n + 3) // 4 * 4  # noqa: E731
+        total = sum(slot(p.numel()) for _, p in named)
         self.grad_arena = torch.zeros(total, device=dev, dtype=torch.float32)
         off = 0
         self.grads = {}
@@ -196,8 +232,8 @@ class Engine:
             sp = spans.setdefault(key, [off, off])
             if sp[1] != off:
                 raise RuntimeError(f"gradient bucket {key} is not contiguous in the arena")
-            sp[1] = off + p.numel()
-            off += p.numel()
+            sp[1] = off + slot(p.numel())
+            off += slot(p.numel())
         self.grad_buckets = spans
         # bf16 shadows: fused QKV per layer, out, fc1, fc2, lm_head
         d = self.d
@@ -267,39 +303,11 @@ class Engine:
         spec = self._spec_cache.get(("qk", id(attn)))
         if spec is None:
             spec = self._qk_spec_uncached(attn)
-            if spec["kind"] != nv.NORM_L2_TEMP:  # learned temps change every step: not cached
-                self._spec_cache[("qk", id(attn))] = spec
+            self._spec_cache[("qk", id(attn))] = spec
         return spec
 
     def _qk_spec_uncached(self, attn):
-        qk = self.cfg.get("qk_normtype", "f_rmsnorm")
-        if qk in ("none", "identity", None) or attn.qk_norm is None:
-            return dict(kind=nv.NORM_IDENTITY, eps=0.0, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0)
-        qn = attn.qk_norm
-        eps = self.cfg["norm_eps"]
-        if qk == "f_rmsnorm":
-            return dict(kind=nv.NORM_RMS, eps=nv.FLT_EPS, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0,
-                        sk=1.0)
-        if qk == "dual_elasticball":
-            nm = qn.norm_module
-            return dict(kind=nv.NORM_ELASTICBALL, eps=nm.q_norm.eps, alpha=nm.q_norm.alpha, wq=None, wk=None,
-                        tq=1.0, tk=1.0, sq=1.0, sk=1.0)
-        if qk == "asymmetric_hyperball":
-            nm = qn.norm_module
-            return dict(kind=nv.NORM_HYPERBALL, eps=0.0, alpha=0.5, wq=None, wk=None, tq=1.0, tk=1.0,
-                        sq=float(nm.scale_q), sk=float(nm.scale_k))
-        kind, e, alpha, _, _ = norm_spec(qk, qn.q_norm_fn, eps)
-        spec = dict(kind=kind, eps=e, alpha=alpha, wq=None, wk=None, tq=1.0, tk=1.0, sq=1.0, sk=1.0)
-        if kind == nv.NORM_ELASTIC or kind == nv.NORM_ELASTICBALL:
-            spec["eps"] = float(qn.q_norm_fn.eps)
-            spec["alpha"] = float(qn.q_norm_fn.alpha)
-        if kind == nv.NORM_RMS_AFFINE:
-            spec["eps"] = float(qn.q_norm_fn.eps)
-            spec["wq"], spec["wk"] = qn.q_norm_fn.weight, qn.k_norm_fn.weight
-        if kind == nv.NORM_L2_TEMP:
-            spec["eps"] = float(qn.q_norm_fn.eps)
-            spec["tq"], spec["tk"] = float(qn.q_norm_fn.temp), float(qn.k_norm_fn.temp)
-        return spec
+        return qk_norm_spec(attn, self.cfg.get("qk_normtype", "f_rmsnorm"), self.cfg["norm_eps"])
 
     def _resid_norm(self, blk_or_model, which):
         """(kind, eps, alpha, w, temp) for the residual-stream norm `which` of a block / the model."""
@@ -307,8 +315,7 @@ class Engine:
         spec = self._spec_cache.get(key)
         if spec is None:
             spec = self._resid_norm_uncached(blk_or_model, which)
-            if spec[0] != nv.NORM_L2_TEMP:
-                self._spec_cache[key] = spec
+            self._spec_cache[key] = spec
         return spec
 
     def _resid_norm_uncached(self, blk_or_model, which):
@@ -358,13 +365,13 @@ class Engine:
                 app += 1
             if halting:
                 kind, eps, alpha, w, temp = self._resid_norm(m, "ln_f")
-                nv.rownorm_fwd(A.x[app], A.hq[r], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0,
+                nv.rownorm_fwd(A.x[app], A.hq[r], kind, eps, w=w, temp=1.0,
                                alpha=alpha, qw=m.q_head.weight, qb=m.q_head.bias, qout=A.q[r])
                 # per-step logits feed only the no-grad argmax (their CE is discarded, model/gpt.py:113-117):
                 # the lm_head GEMM reduces each row to its argmax in the epilogue instead of storing them
                 nv.gemm_argmax(A.hq[r], self.lm_w, A.amax_val, A.amax_idx, A.argmax[r])
         kind, eps, alpha, w, temp = self._resid_norm(m, "ln_f")
-        nv.rownorm_fwd(A.x[app], A.hf, kind, eps, w=w, temp=float(temp) if temp is not None else 1.0, alpha=alpha)
+        nv.rownorm_fwd(A.x[app], A.hf, kind, eps, w=w, temp=1.0, alpha=alpha)
         nv.gemm(A.hf, self.lm_w, A.logits)
         if want_loss:
             A.losses.zero_()
@@ -419,7 +426,7 @@ class Engine:
         at = blk.attn
         x = A.x[app]
         kind, eps, alpha, w, temp = self._resid_norm(blk, "attn_norm")
-        nv.rownorm_fwd(x, A.hn[app], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0, alpha=alpha)
+        nv.rownorm_fwd(x, A.hn[app], kind, eps, w=w, temp=1.0, alpha=alpha)
         nv.gemm(A.hn[app], W["wqkv"], A.qkv[app])
         qs = self._qk_spec(at)
         nv.qkv_prep_fwd(A.qkv[app], A.qk[app], A.qn[app], self.inv_freq, qs["kind"], qs["eps"], qs["alpha"],
@@ -436,7 +443,7 @@ class Engine:
                 colscale=blk.attn_layer_scale if self.ls else None, out2=A.a_raw[app],
                 drop=self._drop(A, "attn_out", app))
         kind, eps, alpha, w, temp = self._resid_norm(blk, "ff_norm")
-        nv.rownorm_fwd(A.h[app], A.hn2[app], kind, eps, w=w, temp=float(temp) if temp is not None else 1.0,
+        nv.rownorm_fwd(A.h[app], A.hn2[app], kind, eps, w=w, temp=1.0,
                        alpha=alpha)
         nv.gemm(A.hn2[app], W["w1"], A.pre[app], epi=nv.EPI_ACT_FWD, act=self.act, out2=A.post[app])
         nv.gemm(A.post[app], W["w2"], A.x[app + 1], epi=nv.EPI_RESID_F32, c=A.h[app],
@@ -460,7 +467,7 @@ class Engine:
         kind, eps, alpha, w, temp = self._resid_norm(m, "ln_f")
         lnf_w = "ln_f.weight" if kind == nv.NORM_RMS_AFFINE else None
         lnf_t = "ln_f.temp" if kind == nv.NORM_L2_TEMP else None
-        tval = float(temp) if temp is not None else 1.0
+        tval = 1.0
         halting = self._halting_active
         need_gb_now = not halting
         # A data-parallel optimizer may hook the arena to reduce each gradient bucket as soon as the
@@ -530,7 +537,7 @@ class Engine:
         nv.gemm(A.dpre, W["w1"].t(), A.dy32, epi=nv.EPI_STORE_F32)
         nv.gemm(A.dpre.t(), A.hn2[app].t(), G[pre + "ff.fc1.weight"], epi=nv.EPI_ACCUM_F32, splitk=0)
         kind, eps, alpha, w, temp = self._resid_norm(blk, "ff_norm")
-        nv.rownorm_bwd(A.h[app], A.dy32, kind, eps, A.g, w=w, temp=float(temp) if temp is not None else 1.0,
+        nv.rownorm_bwd(A.h[app], A.dy32, kind, eps, A.g, w=w, temp=1.0,
                        alpha=alpha, g_in=A.g, g_bf16=A.gb, ls=blk.attn_layer_scale if self.ls else None,
                        raw=A.a_raw[app], dls=G[pre + "attn_layer_scale"] if self.ls else None,
                        dw=G[pre + "ff_norm.weight"] if kind == nv.NORM_RMS_AFFINE else None,
@@ -564,7 +571,7 @@ class Engine:
         nv.gemm(A.dqkv, W["wqkv"].t(), A.dy32, epi=nv.EPI_STORE_F32)
         kind, eps, alpha, w, temp = self._resid_norm(blk, "attn_norm")
         prev_blk = None if first else self.model.layers[(app - 1) % self.L]
-        nv.rownorm_bwd(A.x[app], A.dy32, kind, eps, A.g, w=w, temp=float(temp) if temp is not None else 1.0,
+        nv.rownorm_bwd(A.x[app], A.dy32, kind, eps, A.g, w=w, temp=1.0,
                        alpha=alpha, g_in=A.g,
                        g_bf16=None if first else A.gb,
                        ls=prev_blk.ff_layer_scale if (self.ls and prev_blk is not None) else None,

@@ -36,6 +36,13 @@ CFGS = {
     "no_qk": dict(BASE, qk_normtype="identity"),
     "elasticball": dict(BASE, qk_normtype="elasticball", use_layer_scale=True),
     "hyperball": dict(BASE, qk_normtype="hyperball", use_layer_scale=True),
+    # residual-stream norm kinds other than rmsnorm (model/norm.py:37-95): L2Norm with its learned
+    # temperature (and gradient), the functional L2 and RMS norms, the hybrid elastic norm
+    "resid_l2norm": dict(BASE, norm_type="l2norm", use_layer_scale=True),
+    "resid_f_l2norm": dict(BASE, norm_type="f_l2norm"),
+    "resid_f_rmsnorm": dict(BASE, norm_type="f_rmsnorm", qk_normtype="l2norm"),
+    "resid_elastic_rgpt": dict(BASE, name="rgpt", n_layers=1, n_recur=2, cal_halt_loss=True, use_layer_scale=True,
+                               norm_type="elastic"),
 }
 
 
