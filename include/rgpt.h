@@ -136,7 +136,9 @@ enum RgptNormKind {
 };
 /* Residual-stream norm: x fp32 [M, d] -> y bf16 [M, d]; stat[M] = s (optional).
  * With qout != null also computes the 2-way q_head, qout[M,2] = y @ qw^T + qb (model/gpt.py:107-109).
- * d in {128, 256, 512, 1024, 2048}. Replaces RMSNorm.forward & co (model/norm.py). */
+ * d in {128, 256, 512, 1024, 2048}. Replaces RMSNorm.forward & co (model/norm.py).
+ * w: RMS_AFFINE's weight [d]; for L2_TEMP, when w is not null, the learned temperature is read from w[0]
+ * on the device (L2Norm.temp, model/norm.py:48) and the by-value temp is ignored. */
 int rgpt_rownorm_fwd(const float* x, void* y, float* stat, const float* w, float temp, int kind, float eps,
                      float alpha, int M, int d, const float* qw, const float* qb, float* qout, void* stream);
 /* Norm backward fused with the residual-gradient add (model/transformer_block.py:43-57):
@@ -156,13 +158,32 @@ int rgpt_rownorm_bwd(const float* x, const float* dy, const float* w, float temp
 int rgpt_qkv_prep_fwd(const void* qkv, void* qk, void* qn, const float* inv_freq, int qk_kind, float eps,
                       float alpha, const float* wq, const float* wk, float tq, float tk, float sq, float sk,
                       int M, int T, int H, void* stream);
-/* Backward: dq, dk fp32 [M, d] (grads of the roped q, k) and dqn_gate fp32 [M, d] (= dgp Wg from the
+/* wq/wk: RMS_AFFINE's q/k weights [64]; for L2_TEMP, when not null, the learned q/k temperatures are read
+ * from wq[0]/wk[0] on the device and tq/tk are ignored.
+ * Backward: dq, dk fp32 [M, d] (grads of the roped q, k) and dqn_gate fp32 [M, d] (= dgp Wg from the
  * gate GEMM, may be null) -> the q/k column blocks of dqkv (bf16). dbg += column sums of dgp (bf16
  * [M, d]); dwq/dwk (RMS_AFFINE QK norms) and dtq/dtk (L2_TEMP) are ACCUMULATED. */
 int rgpt_qkv_prep_bwd(const void* qkv, const float* dq, const float* dk, const float* dqn_gate, const void* dgp,
                       void* dqkv, float* dbg, float* dwq, float* dwk, float* dtq, float* dtk, const float* inv_freq,
                       int qk_kind, float eps, float alpha, const float* wq, const float* wk, float tq, float tk,
                       float sq, float sk, int M, int T, int H, void* stream);
+
+/* ------------------------------------------------------------------ standalone modules
+ * The reference's submodules called on their own, outside GPT's engine (which fuses them into its
+ * kernels). Row norm of any kind over rows of ANY length d (1..16384; the QK norms' d_head = 64 too),
+ * x fp32 [M, d] -> y fp32 [M, d]; w as rgpt_rownorm_fwd (RMS_AFFINE weight, or the L2_TEMP temperature
+ * read from w[0]). Replaces RMSNorm / L2Norm / HybridElasticNorm / ElasticBallNorm / HyperballNorm and
+ * the functional norms, model/norm.py:8-162, as QKNorm.forward (:200-204) calls them. */
+int rgpt_rownorm_any_fwd(const float* x, float* y, const float* w, int kind, float eps, float alpha, long long M, int d,
+                         void* stream);
+/* dx fp32 [M, d] (written); dw [d] (RMS_AFFINE) and dtemp [1] (L2_TEMP) ACCUMULATED, each optional. */
+int rgpt_rownorm_any_bwd(const float* x, const float* dy, const float* w, int kind, float eps, float alpha,
+                         long long M, int d, float* dx, float* dw, float* dtemp, void* stream);
+/* RotaryEmbedding.forward (model/rope.py:38-57) on one [B, H, T, D] fp32 tensor: in at element strides
+ * (sb, sh, st, 1), out contiguous [B, H, T, D]; angle t * inv_freq[j] (inv_freq [D/2], model/rope.py:11),
+ * y = x cos + rotate_half(x) sin. backward != 0 applies the transposed rotation (the gradient). */
+int rgpt_rope(const float* in, long long sb, long long sh, long long st, float* out, const float* inv_freq, int B,
+              int H, int T, int D, int backward, void* stream);
 
 /* ------------------------------------------------------------------ embedding / loss
  * nn.Embedding forward (model/gpt.py:95) and its backward (dx rows ACCUMULATED into demb), with the

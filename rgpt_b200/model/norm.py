@@ -1,9 +1,9 @@
 """Norm modules with the reference's names, parameters and buffers (model/norm.py).
 
-Inside GPT the native engine fuses these into its kernels (rownorm_fwd/bwd for
-the residual stream, qkv_prep for QK norms). Called on their own, the residual
-norms run the native row-norm kernels through _RowNormFunction (CUDA tensors,
-last dim in {128, 256, 512, 1024, 2048}); other shapes raise.
+Inside GPT the native engine fuses these into its kernels (rownorm_fwd/bwd for the residual stream,
+qkv_prep for the QK norms). Called on their own, every norm runs the native row-norm kernels through
+_RowNormFunction: CUDA tensors, any last dimension (the QK norms' d_head = 64 included), fp32 math,
+with the gradients of the input and of the learned weight (RMSNorm) or temperature (L2Norm).
 """
 import torch
 import torch.nn as nn
@@ -12,32 +12,39 @@ from .. import native as nv
 
 
 class _RowNormFunction(torch.autograd.Function):
+    """y = norm(x) over the last dim. `param` is RMSNorm's weight [d], L2Norm's temperature [1] or None;
+    the kernels read it on the device."""
+
     @staticmethod
-    def forward(ctx, x, weight, kind, eps, alpha, temp):
+    def forward(ctx, x, param, kind, eps, alpha):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).float().contiguous()
-        y = torch.empty(x2.shape, device=x.device, dtype=torch.bfloat16)
-        nv.rownorm_fwd(x2, y, kind, eps, w=weight, alpha=alpha, temp=float(temp) if temp is not None else 1.0)
-        ctx.save_for_backward(x2, weight if weight is not None else torch.empty(0, device=x.device))
-        ctx.meta = (kind, eps, alpha, temp, shape, x.dtype, weight is not None)
-        return y.view(shape).to(x.dtype)
+        p = param.detach().float().contiguous() if param is not None else None
+        y = torch.empty_like(x2)
+        nv.rownorm_any_fwd(x2, y, kind, eps, w=p, alpha=alpha)
+        ctx.save_for_backward(x2, p)
+        ctx.meta = (kind, eps, alpha, shape, x.dtype, param.dtype if param is not None else None)
+        # the reference's output dtype: x's, promoted with the parameter's (model/norm.py:27-34, :50-51)
+        out_dt = torch.promote_types(x.dtype, param.dtype) if param is not None else x.dtype
+        return y.view(shape).to(out_dt)
 
     @staticmethod
     def backward(ctx, gy):
-        x2, weight = ctx.saved_tensors
-        kind, eps, alpha, temp, shape, dtype, has_w = ctx.meta
+        x2, p = ctx.saved_tensors
+        kind, eps, alpha, shape, xdt, pdt = ctx.meta
         dy = gy.reshape(-1, shape[-1]).float().contiguous()
         dx = torch.empty_like(x2)
-        dw = torch.zeros(shape[-1], device=x2.device, dtype=torch.float32) if has_w else None
-        nv.rownorm_bwd(x2, dy, kind, eps, dx, w=weight if has_w else None, alpha=alpha,
-                       temp=float(temp) if temp is not None else 1.0, dw=dw)
-        return dx.view(shape).to(dtype), (dw if has_w else None), None, None, None, None
+        dp = torch.zeros_like(p) if p is not None else None
+        nv.rownorm_any_bwd(x2, dy, kind, eps, dx, w=p, alpha=alpha,
+                           dw=dp if kind == nv.NORM_RMS_AFFINE else None,
+                           dtemp=dp if kind == nv.NORM_L2_TEMP else None)
+        return dx.view(shape).to(xdt), (dp.to(pdt) if dp is not None else None), None, None, None
 
 
-def _native_norm(x, kind, eps, weight=None, alpha=0.5, temp=None):
+def _native_norm(x, kind, eps, param=None, alpha=0.5):
     if not x.is_cuda:
         raise RuntimeError("rgpt_b200 norms run on CUDA tensors only (no CPU path)")
-    return _RowNormFunction.apply(x, weight, kind, eps, alpha, temp)
+    return _RowNormFunction.apply(x, param, kind, float(eps), float(alpha))
 
 
 class RMSNorm(nn.Module):
@@ -56,8 +63,8 @@ class RMSNorm(nn.Module):
 
 
 def functional_rms_norm(x, eps=1e-5):
-    """F.rms_norm with its default eps (finfo(dtype).eps); `eps` is ignored (model/norm.py:37-38)."""
-    return _native_norm(x, nv.NORM_RMS, nv.FLT_EPS)
+    """F.rms_norm with its default eps, finfo(x.dtype).eps; `eps` is ignored (model/norm.py:37-38)."""
+    return _native_norm(x, nv.NORM_RMS, torch.finfo(x.dtype).eps)
 
 
 def functional_hyperball_norm(x):
@@ -73,7 +80,7 @@ class L2Norm(nn.Module):
         self.temp = nn.Parameter(torch.ones(1))
 
     def forward(self, x):
-        return _native_norm(x, nv.NORM_L2_TEMP, self.eps, temp=self.temp.item())
+        return _native_norm(x, nv.NORM_L2_TEMP, self.eps, self.temp)
 
 
 def functional_l2_norm(x, eps=1e-5):
@@ -171,4 +178,8 @@ class QKNorm(nn.Module):
             self.k_norm_fn = get_norm_fn(norm_type, d_head, norm_eps)
 
     def forward(self, q, k):
-        raise RuntimeError("QKNorm runs fused inside the attention QKV-prep kernel; call Attention or GPT")
+        """Normalise q and k over d_head (model/norm.py:200-204) with the native row-norm kernels. Inside
+        Attention and GPT the same norm runs fused in the QKV-prep kernel instead."""
+        if hasattr(self, "norm_module"):
+            return self.norm_module(q, k)
+        return self.q_norm_fn(q), self.k_norm_fn(k)

@@ -1,5 +1,10 @@
-"""TransformerBlock (model/transformer_block.py:10-57): pre-norm attention + FFN
-residuals with optional layer scale. Executed by GPT's native engine."""
+"""TransformerBlock (model/transformer_block.py:10-57): pre-norm attention + FFN residuals with
+optional layer scale and branch dropout.
+
+Inside GPT the engine runs the block as fused kernels (the residual add, layer scale and branch dropout
+live in the epilogue of each branch's output GEMM). Called on its own, forward(x) composes the native
+submodules: the norm kernels, Attention's native forward and the fused linear+activation FFN; the
+branch dropout is this module's nn.Dropout, as in the reference."""
 import torch
 import torch.nn as nn
 
@@ -35,4 +40,12 @@ class TransformerBlock(nn.Module):
             self.ff.out_proj.RESIDUAL_SCALE_FLAG = True
 
     def forward(self, x):
-        raise RuntimeError("TransformerBlock runs inside GPT's native engine (rgpt_b200.model.GPT)")
+        """x [B, T, d] (CUDA) -> h + drop(ff(ff_norm(h))) * ls_ff, h = x + drop(attn(attn_norm(x))) * ls_attn."""
+        h = self._residual_branch(x, self.attn_norm, self.attn, "attn_layer_scale")
+        return self._residual_branch(h, self.ff_norm, self.ff, "ff_layer_scale")
+
+    def _residual_branch(self, x, norm, sublayer, scale_name):
+        branch = self.dropout(sublayer(norm(x)))
+        if self.use_layer_scale:
+            branch = branch * getattr(self, scale_name)
+        return x + branch

@@ -257,6 +257,49 @@ def rownorm_bwd(x: torch.Tensor, dy: torch.Tensor | None, kind: int, eps: float,
               ptr(dq), ptr(qw), ptr(h), ptr(dqw), ptr(dqb), dm, dp, _lib.stream_ptr(x.device))
 
 
+# ----------------------------------------------------------------------------- standalone modules
+def _rows_f32(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.float32 or t.dim() != 2 or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous fp32 [M, d] tensor")
+
+
+def rownorm_any_fwd(x: torch.Tensor, y: torch.Tensor, kind: int, eps: float, *, w: torch.Tensor | None = None,
+                    alpha: float = 0.5) -> None:
+    """y = norm(x) over rows of any length (fp32 [M, d] both); w: RMSNorm weight [d] or L2Norm temp [1]."""
+    _rows_f32(x, "x")
+    _rows_f32(y, "y")
+    if y.shape != x.shape:
+        raise ValueError("rownorm_any_fwd: y must have x's shape")
+    M, d = x.shape
+    _lib.call("rgpt_rownorm_any_fwd", ptr(x), ptr(y), ptr(w), kind, float(eps), float(alpha), M, d,
+              _lib.stream_ptr(x.device))
+
+
+def rownorm_any_bwd(x: torch.Tensor, dy: torch.Tensor, kind: int, eps: float, dx: torch.Tensor, *,
+                    w: torch.Tensor | None = None, alpha: float = 0.5, dw: torch.Tensor | None = None,
+                    dtemp: torch.Tensor | None = None) -> None:
+    """dx = norm'(x)^T dy (written); dw (RMSNorm weight) and dtemp (L2Norm temp) are accumulated."""
+    for t, n in ((x, "x"), (dy, "dy"), (dx, "dx")):
+        _rows_f32(t, n)
+    M, d = x.shape
+    _lib.call("rgpt_rownorm_any_bwd", ptr(x), ptr(dy), ptr(w), kind, float(eps), float(alpha), M, d, ptr(dx),
+              ptr(dw), ptr(dtemp), _lib.stream_ptr(x.device))
+
+
+def rope(inp: torch.Tensor, out: torch.Tensor, inv_freq: torch.Tensor, backward: bool = False) -> None:
+    """out (contiguous fp32 [B, H, T, D]) = RoPE(inp) for fp32 inp [B, H, T, D] with unit stride on D."""
+    if inp.dtype != torch.float32 or inp.dim() != 4 or inp.stride(-1) != 1:
+        raise ValueError("rope input must be a 4-D fp32 [B, H, T, D] tensor with unit stride on D")
+    if out.dtype != torch.float32 or out.shape != inp.shape or not out.is_contiguous():
+        raise ValueError("rope output must be a contiguous fp32 tensor of the input's shape")
+    B, H, T, D = inp.shape
+    if inv_freq.dtype != torch.float32 or inv_freq.numel() != D // 2 or not inv_freq.is_contiguous():
+        raise ValueError("inv_freq must be a contiguous fp32 [D/2] tensor")
+    sb, sh, st, _ = inp.stride()
+    _lib.call("rgpt_rope", ptr(inp), sb, sh, st, ptr(out), ptr(inv_freq), B, H, T, D, int(backward),
+              _lib.stream_ptr(inp.device))
+
+
 # ----------------------------------------------------------------------------- QKV prep
 def qkv_prep_fwd(qkv, qk, qn, inv_freq, qk_kind, eps, alpha, M, T, H, *, wq=None, wk=None,
                  tq=1.0, tk=1.0, sq=1.0, sk=1.0) -> None:
