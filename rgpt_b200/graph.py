@@ -70,6 +70,9 @@ class GraphedTrainStep:
             raise ValueError(f"ids must have shape {tuple(self.ids.shape)}, got {tuple(ids.shape)}")
         if ids.data_ptr() != self.ids.data_ptr():
             self.ids.copy_(ids, non_blocking=True)
+        # parameters changed outside the optimizer kernels (a checkpoint load, a manual edit) refresh
+        # their bf16 GEMM copies here: a replay does not run the engine's Python
+        self.model.engine().sync_shadows()
         self.opt.stage_device_hparams()
         self.calls += 1
         if self.calls <= self.warmup:

@@ -19,10 +19,9 @@ class Config(dict):
 
 
 def as_config(obj):
-    if isinstance(obj, Config):
-        return obj
+    """Config view of a mapping (nested mappings too, so cfg.training.optimizer.lr works on plain dicts)."""
     if _DictConfig is not None and isinstance(obj, _DictConfig):
         from omegaconf import OmegaConf  # type: ignore
 
-        return Config(OmegaConf.to_container(obj, resolve=True))
-    return Config(dict(obj))
+        obj = OmegaConf.to_container(obj, resolve=True)
+    return Config({k: as_config(v) if isinstance(v, dict) else v for k, v in dict(obj).items()})

@@ -167,6 +167,14 @@ class GPT(nn.Module):
         logits = A.logits.view(B, T, -1).clone()
         return logits, torch.zeros((), device=logits.device), [], []
 
+    @torch.no_grad()
+    def token_losses(self, input_ids, labels):
+        """Per-token cross entropy [B, T] (fp32; 0 where labels == pad_token_id) of an eval-mode forward,
+        e.g. to score the endings of a multiple-choice item."""
+        eng = self.engine()
+        A = eng.forward(input_ids, labels, training=False, want_loss=True)
+        return A.loss_rows.view(input_ids.shape).clone()
+
     def forward_loss(self, input_ids, labels):
         """Fused forward + loss; returns (total, token, q) 0-d tensors, total differentiable."""
         eng = self.engine()

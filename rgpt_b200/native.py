@@ -114,7 +114,7 @@ def _out(t: torch.Tensor | None):
 
 
 # Optional GEMM timing hook: when set to a list, every gemm() call appends
-# (start_event, end_event, flops) recorded on the launching stream.
+# (start_event, end_event, flops, (epi, M, N, K, batch)) recorded on the launching stream.
 gemm_events: list | None = None
 
 
@@ -165,7 +165,7 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor, *, epi: int = EPI_
                   _lib.stream_ptr(out.device))
     if ev is not None:
         e1.record()
-        ev.append((e0, e1, 2.0 * M * N * K * batch))
+        ev.append((e0, e1, 2.0 * M * N * K * batch, (epi, M, N, K, batch)))
     return out
 
 

@@ -258,6 +258,27 @@ class Muon(torch.optim.Optimizer):
             return None
         return self._hp_dev.data_ptr() + gi * nv.HP_FLOATS * 4
 
+    # ------------------------------------------------------------------ state
+    def load_state_dict(self, state_dict):
+        """torch's loader casts every state tensor to its parameter's dtype, which would turn the bf16
+        momentum buffers into fp32. Restore the kernels' dtypes (momentum_buffer bf16, AdamW moments
+        fp32), and copy into the state tensors that already exist: their addresses are baked into the
+        update kernels' descriptor tables and into captured CUDA graphs of the step."""
+        before = {p: dict(st) for p, st in self.state.items()}
+        super().load_state_dict(state_dict)
+        with torch.no_grad():
+            for p, st in self.state.items():
+                for k, v in list(st.items()):
+                    if not torch.is_tensor(v) or not v.is_floating_point():
+                        continue
+                    want = torch.bfloat16 if k == "momentum_buffer" else torch.float32
+                    old = before.get(p, {}).get(k)
+                    if old is not None and old.shape == v.shape and old.dtype == want:
+                        old.copy_(v)
+                        st[k] = old
+                    else:
+                        st[k] = v.to(want).contiguous()
+
     # ------------------------------------------------------------------ grads
     @torch.no_grad()
     def zero_grad(self, set_to_none: bool = True):

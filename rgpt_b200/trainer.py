@@ -15,7 +15,14 @@ Differences, all on purpose:
   * The per-parameter gradient-norm print (one host sync per parameter) is
     opt-in (training.log_grad_norm) and done as one reduction.
   * load_checkpoint() resumes from save_checkpoint()'s dictionary (the
-    reference saves but never loads).
+    reference saves but never loads); the dictionary gains the scheduler's
+    state under an extra key so a resumed run continues the same schedule.
+  * Validation and test batches may use either collate schema: {"src", "tgt"}
+    (dataset.py:45-51) or the multiple-choice {"input_ids", "labels", ...}
+    (dataset.py:144-149), which the reference's _validate_loss cannot read
+    (it looks up batch["src"], trainer.py:278). Multiple-choice batches are
+    also scored: accuracy of the ending with the lowest summed loss (acc) and
+    with the lowest mean loss per token (acc_norm).
 """
 from __future__ import annotations
 
@@ -203,32 +210,82 @@ class Trainer:
         if self.is_main_process:
             print(f"Training complete. Best Loss: {self.best_metric:.4f}")
 
+    def _inputs_labels(self, batch):
+        """(inputs, next-token labels) on the device from a batch of either collate schema."""
+        if "src" in batch:
+            src, tgt = batch["src"], batch["tgt"]
+        elif "input_ids" in batch:
+            src, tgt = batch["input_ids"], batch["labels"]
+        else:
+            raise KeyError("a batch needs 'src'/'tgt' (token stream) or 'input_ids'/'labels' (multiple choice)")
+        src = src.to(self.device, non_blocking=True)
+        tgt = tgt.to(self.device, non_blocking=True)
+        return src[:, :-1], tgt[:, 1:].contiguous()
+
     @torch.no_grad()
-    def _validate_loss(self, dataloader):
+    def _evaluate(self, dataloader):
+        """Mean token loss over the loader's batches (trainer.py:272-292) and, for multiple-choice batches,
+        (correct by summed loss, correct by mean loss, items). Data-parallel ranks are averaged / summed."""
         self.model.eval()
         total = torch.zeros((), device=self.device)
+        mc = torch.zeros(3, device=self.device, dtype=torch.float64)
         count = 0
         for batch in dataloader:
-            src = batch["src"].to(self.device)
-            tgt = batch["tgt"].to(self.device)
-            tot, tok, _ = self.model.forward_loss(src[:, :-1], tgt[:, 1:].contiguous())
+            inp, lab = self._inputs_labels(batch)
+            _, tok, _ = self.model.forward_loss(inp, lab)
             total += tok
             count += 1
+            if "example_indices" in batch:
+                mc += self._score_choices(inp, lab, batch["example_indices"], batch["correct_labels"])
         avg = total / count if count > 0 else total
         if self.is_ddp:
             import torch.distributed as dist
 
             dist.all_reduce(avg, op=dist.ReduceOp.AVG)
+            dist.all_reduce(mc, op=dist.ReduceOp.SUM)
         self.model.train()
-        return avg.item()
+        return avg.item(), mc.tolist()
+
+    def _score_choices(self, inp, lab, owner, correct):
+        """Per item, the ending with the lowest summed / mean loss over its scored tokens."""
+        losses = self.model.token_losses(inp, lab)
+        scored = (lab != self.pad_id).float()
+        tot = losses.sum(dim=1)
+        mean = tot / scored.sum(dim=1).clamp_min(1.0)
+        owner = owner.to(self.device)
+        n_items = int(correct.numel())
+        correct = correct.to(self.device)
+        res = torch.zeros(3, device=self.device, dtype=torch.float64)
+        for i in range(n_items):
+            rows = (owner == i).nonzero().flatten()
+            if rows.numel() == 0:
+                continue
+            res[0] += float(torch.argmin(tot[rows]) == correct[i])
+            res[1] += float(torch.argmin(mean[rows]) == correct[i])
+            res[2] += 1
+        return res
+
+    def _validate_loss(self, dataloader):
+        loss, _ = self._evaluate(dataloader)
+        return loss
 
     def test(self):
+        """Test loss (trainer.py:294-305); multiple-choice loaders also report accuracy."""
         if self.is_main_process:
             print("Testing the model...")
-        loss = self._validate_loss(self.test_loader)
+        loss, (acc, acc_norm, n) = self._evaluate(self.test_loader)
+        metrics = {"Loss/test": loss}
+        if n > 0:
+            metrics.update({"Acc/test": acc / n, "Acc/test_norm": acc_norm / n})
+        self.test_metrics = metrics
         if self.is_main_process:
-            self.logger.log({"Loss/test": loss}, self.global_step)
-            print(f"Test Loss: {loss:.4f}")
+            self.logger.log(metrics, self.global_step)
+            print(f"Test Loss: {loss:.4f}" + (f"  accuracy {acc / n:.4f} (length-normalised {acc_norm / n:.4f})"
+                                              if n > 0 else ""))
+        if self.is_ddp:
+            import torch.distributed as dist
+
+            dist.barrier()
         return loss
 
     # ------------------------------------------------------------------ checkpoints
@@ -241,9 +298,12 @@ class Trainer:
         if not self.is_main_process:
             return
         Path(path).parent.mkdir(parents=True, exist_ok=True)
-        torch.save({"model_state_dict": self._get_model_for_saving().state_dict(),
-                    "optimizer_state_dict": self.optimizer.state_dict(),
-                    "best_metric": self.best_metric, "global_step": self.global_step}, path)
+        ck = {"model_state_dict": self._get_model_for_saving().state_dict(),
+              "optimizer_state_dict": self.optimizer.state_dict(),
+              "best_metric": self.best_metric, "global_step": self.global_step}
+        if self.scheduler is not None:
+            ck["scheduler_state_dict"] = self.scheduler.state_dict()
+        torch.save(ck, path)
 
     def load_checkpoint(self, path):
         """Resume from a save_checkpoint() file (model, optimizer state, counters)."""
@@ -252,4 +312,10 @@ class Trainer:
         self.optimizer.load_state_dict(ck["optimizer_state_dict"])
         self.best_metric = ck.get("best_metric", float("inf"))
         self.global_step = ck.get("global_step", 0)
+        if self.scheduler is not None:
+            if "scheduler_state_dict" in ck:
+                self.scheduler.load_state_dict(ck["scheduler_state_dict"])
+            else:  # a checkpoint of the reference's format: replay the schedule up to the saved step
+                for _ in range(self.global_step):
+                    self.scheduler.step()
         return ck

@@ -11,7 +11,10 @@ the interpreter cannot call libdevice.
 Outputs tests/golden/*.pt (small, CPU fp32). tests/test_oracle_golden.py checks
 the oracle against them; GPU parity tests use them as fixed inputs/outputs.
 
-    python tests/golden/gen_golden.py
+    RGPT_REFERENCE=<reference checkout> python tests/golden/gen_golden.py [fixture ...]
+
+The reference checkout defaults to /root/reference; with no fixture names every
+fixture is regenerated.
 """
 import os
 import sys
@@ -20,7 +23,7 @@ import types
 os.environ["TORCHDYNAMO_DISABLE"] = "1"
 os.environ["TRITON_INTERPRET"] = "1"
 
-REF = "/root/reference"
+REF = os.environ.get("RGPT_REFERENCE", "/root/reference")
 OUT = os.path.dirname(os.path.abspath(__file__))
 
 
@@ -49,6 +52,13 @@ def install_shims():
     hy.core = types.SimpleNamespace(hydra_config=types.SimpleNamespace(HydraConfig=None))
     hy.main = lambda **kw: (lambda f: f)
     sys.modules["hydra"] = hy
+    ds = types.ModuleType("datasets")  # dataset.py imports it at module level; nothing here downloads
+
+    def _no_download(*a, **k):
+        raise RuntimeError("no dataset downloads in the golden generator")
+
+    ds.load_dataset = _no_download
+    sys.modules.setdefault("datasets", ds)
     sys.path.insert(0, REF)
 
 
@@ -267,13 +277,41 @@ def gen_train(tag, cfg, seed, n_steps, accum):
                              "final": {k: v.detach().clone() for k, v in model.state_dict().items()}})
 
 
+class ToyTokenizer:
+    """A deterministic stand-in for a GPT-2 tokenizer: one id per character. No pad token, so the
+    collate falls back to EOS for padding, as it does with GPT-2."""
+
+    pad_token_id = None
+    eos_token_id = 1
+    bos_token_id = 2
+
+    def encode(self, text, add_special_tokens=True):
+        return [3 + (ord(c) % 97) for c in text]
+
+
+# synthetic multiple-choice items (invented strings, not HellaSwag's)
+MC_ITEMS = [
+    {"context": "the cat sat on", "endings": ["the mat", "a hat", "the moon and stars", "x"], "label": 0},
+    {"context": "numbers go up by one: 1 2 3", "endings": [" 4", " 9", " 4 5 6 7 8 9 10", ""], "label": 0},
+    {"context": "a long context " * 3, "endings": ["ends here", "or there", "maybe", "never"], "label": 3},
+]
+
+
+def gen_hellaswag_collate():
+    from dataset import hellaswag_collate_fn  # the reference's collate (dataset.py:71-153)
+
+    out = hellaswag_collate_fn(MC_ITEMS, ToyTokenizer(), max_seq_len=24)
+    save("hellaswag_collate.pt", {"items": MC_ITEMS, "max_seq_len": 24, "out": out})
+
+
+GENERATORS = {
+    "ffn": gen_ffn, "norms": gen_norms, "rope_attention": gen_rope_attention,
+    "model_gpt": lambda: gen_model("gpt", TINY, 11), "model_rgpt": lambda: gen_model("rgpt", TINY_RGPT, 12),
+    "model_elastic": lambda: gen_model("elastic", TINY_ELASTIC, 13), "optim": gen_optim,
+    "train_gpt": lambda: gen_train("gpt", TINY, 21, 6, 1), "train_rgpt": lambda: gen_train("rgpt", TINY_RGPT, 22, 4, 2),
+    "hellaswag_collate": gen_hellaswag_collate,
+}
+
 if __name__ == "__main__":
-    gen_ffn()
-    gen_norms()
-    gen_rope_attention()
-    gen_model("gpt", TINY, 11)
-    gen_model("rgpt", TINY_RGPT, 12)
-    gen_model("elastic", TINY_ELASTIC, 13)
-    gen_optim()
-    gen_train("gpt", TINY, 21, 6, 1)
-    gen_train("rgpt", TINY_RGPT, 22, 4, 2)
+    for name in sys.argv[1:] or list(GENERATORS):
+        GENERATORS[name]()
