@@ -55,10 +55,10 @@ from rgpt_b200.workloads import FFN_SWEEP, MUON_SINGLE, OPT, WORKLOADS  # noqa: 
 TRAIN_WORKLOADS = list(WORKLOADS)
 ALL_WORKLOADS = TRAIN_WORKLOADS + ["muon-step", "ffn-sweep", "kernels"]
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of the weight-gradient GEMM launches of one
-# gpt-small step, per launch, from one ncu capture of `bench.py --workload gpt-small --eager`; None until
-# measured for a workload.
-WGRAD_TRAFFIC_PER_LAUNCH = {}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per weight-gradient GEMM launch, averaged
+# over one gpt-small step's 33 launches (8 each of the fc1, fc2, out_proj and QKV shapes, 1 lm_head), from
+# one ncu capture of each shape (bench.py --workload kernels --only wgrad_*); absent for other workloads.
+WGRAD_TRAFFIC_PER_LAUNCH = {"gpt-small": 145.2e6}
 
 
 def log(*a):
@@ -329,6 +329,18 @@ def run_train(args, wl):
     for i in range(args.warmup):
         step(dev_batches[i % n_batches])
     barrier()
+    if args.profile_region:
+        # K eager steps inside cudaProfilerStart/Stop, for a profiler run with --profile-from-start off
+        torch.cuda.cudart().cudaProfilerStart()
+        for i in range(args.steps):
+            step_eager(dev_batches[i % n_batches])
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        if dist is not None:
+            if graphed is not None:
+                graphed.release()
+            dist.destroy_process_group()
+        return
 
     # ---- device-resident timing: exactly K steps between barriers, clocks sampled meanwhile
     sampler = ClockSampler(local) if rank == 0 else None
@@ -679,6 +691,21 @@ def kernel_cases(dev):
         dpre, hn2, dw = rb(M, F), rb(M, d), torch.zeros(F, d, device=dev)
         return lambda: nv.gemm(dpre.t(), hn2.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
 
+    @add("wgrad_fc2", "tensor", 2.0 * d * F * M)
+    def _():
+        dy, post, dw = rb(M, d), rb(M, F), torch.zeros(d, F, device=dev)
+        return lambda: nv.gemm(dy.t(), post.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
+
+    @add("wgrad_out", "tensor", 2.0 * d * d * M)
+    def _():
+        da, og, dw = rb(M, d), rb(M, d), torch.zeros(d, d, device=dev)
+        return lambda: nv.gemm(da.t(), og.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
+
+    @add("wgrad_qkv", "tensor", 2.0 * 3 * d * d * M)
+    def _():
+        dqkv, hn, dw = rb(M, 3 * d), rb(M, d), torch.zeros(3 * d, d, device=dev)
+        return lambda: nv.gemm(dqkv.t(), hn.t(), dw, epi=nv.EPI_ACCUM_F32, splitk=0)
+
     @add("wgrad_lm_head", "tensor", 2.0 * V * d * M)
     def _():
         dl, hf, dw = rb(M, V), rb(M, d), torch.zeros(V, d, device=dev)
@@ -1008,6 +1035,9 @@ def main():
     ap.add_argument("--dropout", type=float, default=None,
                     help="dropout rate of the embedding, attention probabilities and residual branches "
                          "(default: the workload's)")
+    ap.add_argument("--profile-region", action="store_true",
+                    help="training workloads: after the warm-up, run K eager steps between cudaProfilerStart and "
+                         "cudaProfilerStop and exit (for a profiler capture of exactly those steps)")
     ap.add_argument("--only", default=None, help="kernels workload: comma-separated case names")
     ap.add_argument("--launches", type=int, default=5, help="kernels workload: timed launches per case")
     args = ap.parse_args()
