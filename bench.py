@@ -289,7 +289,8 @@ def run_train(args, wl):
         cfg["dropout"] = args.dropout
     torch.manual_seed(1234)
     model = GPT(**cfg).to(dev).train()
-    opt = (DistMuon if world > 1 else Muon)(trainer_param_groups(model), **OPT)
+    opt = (DistMuon(trainer_param_groups(model), sharded_state=args.dp == "sharded", **OPT) if world > 1
+           else Muon(trainer_param_groups(model), **OPT))
     g = torch.Generator().manual_seed(1000 + rank)
     n_batches = 4
     host = [torch.randint(0, cfg["vocab_size"], (accum, B, T + 1), generator=g).pin_memory() for _ in range(n_batches)]
@@ -427,6 +428,7 @@ def run_train(args, wl):
                    "n_layers": cfg["n_layers"], "n_recur": cfg.get("n_recur", 1), "n_heads": cfg["n_heads"],
                    "vocab": cfg["vocab_size"], "seq_len": T, "micro_batch": B, "grad_accum": accum,
                    "global_batch": B * accum * world, "parallelism": f"dp{world}",
+                   "dp_step": (args.dp if world > 1 else None),
                    "optimizer": "Muon (5 NS steps) + AdamW", "dropout": cfg["dropout"],
                    "launch": "one CUDA graph replay per step" if graphed is not None else "eager",
                    "l2": "no flush: each step's working set (activations + weights) is several GB, far above "
@@ -535,13 +537,14 @@ def run_muon_step(args):
     e1.record()
     torch.cuda.synchronize()
     ms_e2e = e0.elapsed_time(e1) / args.steps
-    # Newton-Schulz GEMMs: CUDA events around each of the 15 GEMMs of one eager step
-    nv.gemm_events = []
-    one()
-    torch.cuda.synchronize()
-    ev, nv.gemm_events = nv.gemm_events, None
-    ns_ms = sum(a.elapsed_time(b) for a, b, _, _ in ev)
+    # the Newton-Schulz iteration alone (one persistent chain kernel, or the batched GEMMs), on a
+    # workspace of this matrix's shape holding a normalised input
+    from rgpt_b200.optimizer import NS_IMPL, _NSWorkspace, newton_schulz_batched
+
     R, C = c["shape"]
+    ws = _NSWorkspace(1, min(R, C), max(R, C), dev)
+    ws.X[0, :min(R, C), :max(R, C)].copy_((G0 if R <= C else G0.t()).to(dev) / G0.norm())
+    ns_ms = time_launches(lambda: newton_schulz_batched(ws, c["ns_steps"]), 20)
     r, cc = min(R, C), max(R, C)
     ns_flops = c["ns_steps"] * (2 * r * r * cc + 2 * r ** 3 + 2 * r * r * cc)
     peaks = load_peaks()
@@ -557,8 +560,10 @@ def run_muon_step(args):
                    "l2": "no flush: the working set (a few MB) stays in L2, as it does inside a training step"},
         "e2e": {"value": round(ms_e2e, 4), "unit": "ms", "h2d_bytes_per_step": G0.numel() * 4,
                 "d2h_bytes_per_step": W0.numel() * 4},
-        "gpu_launches": len(ev) + 4,
-        "roofline": {"kernel": "gemm_bf16_tc_kernel: the 15 Newton-Schulz GEMMs (A = X X^T; b A + c A^2; a X + B X)",
+        "gpu_launches": 5 if NS_IMPL == "chain" else 19,
+        "roofline": {"kernel": ("ns_chain_kernel: the whole Newton-Schulz iteration (A = X X^T; b A + c A^2; a X + B X, "
+                                "5 steps) in one persistent launch") if NS_IMPL == "chain" else
+                               "gemm_bf16_tc_kernel: the 15 Newton-Schulz GEMMs (A = X X^T; b A + c A^2; a X + B X)",
                      "bound": "tensor", "achieved": round(ns_tfs, 1), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(ns_tfs / peaks["bf16_tflops"], 3),
                      "peak_source": peaks["source"] + " (burst bf16: the GEMMs are timed alone)",
@@ -833,6 +838,18 @@ def kernel_cases(dev):
         opt.concurrent = False
         return opt.step
 
+    def ns_case(n, xr, xc):
+        from rgpt_b200.optimizer import _NSWorkspace, newton_schulz_batched
+
+        ws = _NSWorkspace(n, xr, xc, dev)
+        x = rf(n, xr, xc)
+        ws.X[:, :xr, :xc].copy_((x / x.flatten(1).norm(dim=1)[:, None, None]).bfloat16())
+        return lambda: newton_schulz_batched(ws, 5)
+
+    for n_, xr_, xc_ in ((32, d, d), (16, d, 4 * d), (8, 64, 64), (1, d, 4 * d)):
+        add(f"ns_{n_}x{xr_}x{xc_}", "tensor", n_ * 5 * (2.0 * xr_ * xr_ * xc_ * 2 + 2.0 * xr_ ** 3))(
+            lambda n_=n_, xr_=xr_, xc_=xc_: ns_case(n_, xr_, xc_))
+
     @add("attn_drop_mask", "alu", B * H * T * T / 2)
     def _():
         seed = torch.tensor([12345], dtype=torch.int64, device=dev)
@@ -1038,6 +1055,10 @@ def main():
     ap.add_argument("--profile-region", action="store_true",
                     help="training workloads: after the warm-up, run K eager steps between cudaProfilerStart and "
                          "cudaProfilerStop and exit (for a profiler capture of exactly those steps)")
+    ap.add_argument("--dp", choices=["sharded", "allreduce"], default="allreduce",
+                    help="data-parallel step: sharded (bf16 gradient reduce-scatter, each rank updates what it owns, "
+                         "all-gather of the updated weights) or allreduce (fp32 gradient all-reduce overlapped with "
+                         "the backward, Newton-Schulz sharded by owner)")
     ap.add_argument("--only", default=None, help="kernels workload: comma-separated case names")
     ap.add_argument("--launches", type=int, default=5, help="kernels workload: timed launches per case")
     args = ap.parse_args()

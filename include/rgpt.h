@@ -223,6 +223,35 @@ typedef struct RgptAdamwTensor {
 typedef struct RgptMuonTensor {
   float* param; const float* grad; unsigned short* mom; unsigned short* shadow;
 } RgptMuonTensor;
+/* One segment of the data-parallel staging copies (rgpt_segment_copy): tensor t (and t2, a bf16 copy written on
+ * unpack, or 0), its element count n and its element offset in the packed buffer. */
+typedef struct RgptSegment {
+  void* t;
+  void* t2;
+  long long buf_off;
+  long long n;
+} RgptSegment;
+/* The whole quintic Newton-Schulz iteration (zeropower_via_newtonschulz5, optimizer.py:18-45) of n same-shape
+ * matrices in ONE persistent, cooperative launch: `steps` x {A = X X^T; B = b A + c A A; X' = a X + B X}, bf16
+ * operands and results, fp32 accumulation, the polynomial combines fused into the GEMM epilogues (the same
+ * roundings as the batched GEMM path). X, X2: [n][rows >= xr][x_ld] bf16 (batch stride x_bstride), X holding the
+ * normalised input (rows <= cols: 1 <= xr <= xc); the result lands in X2 for odd `steps`, else in X. A, B:
+ * [n][>= xr][a_ld] bf16 scratch. counters: n * 3 * steps unsigned ints, zeroed by this call (a memset on the
+ * stream): each work unit waits (bounded, 1 s) only for the previous phase of its own matrix. Row strides are
+ * multiples of 8 elements, base pointers 16-byte aligned. */
+int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr, int xc, long long x_ld, long long x_bstride,
+                  long long a_ld, long long a_bstride, int steps, float a, float b, float c, unsigned* counters,
+                  void* stream);
+
+/* Staging copies of the sharded data-parallel optimizer step (no kernel in the reference, whose DDP
+ * all-reduces every gradient and whose DistMuon repeats the whole update on every rank, trainer.py:47-53,
+ * optimizer.py:317-415): pack (unpack == 0) buf[off + i] = scale * t[i] for every segment, or unpack
+ * t[i] = scale * buf[off + i] (and t2[i] = bf16 of it when t2 != 0). buf_bf16 / tensor_bf16 select bf16
+ * instead of fp32 storage. Work items: n_chunks (segment index, start element) pairs of up to chunk_elems
+ * elements each. */
+int rgpt_segment_copy(const RgptSegment* table, const int* chunk_seg, const long long* chunk_start, int n_chunks,
+                      int chunk_elems, void* buf, int buf_bf16, int tensor_bf16, float scale, int unpack,
+                      void* stream);
 /* Per-step scalars read from DEVICE memory instead of the by-value arguments when the `hp` pointer
  * of an optimizer entry point is non-null (so that a captured CUDA graph of the step sees each
  * step's learning rate and bias corrections). Layout, 8 floats per parameter group:

@@ -73,6 +73,9 @@ _SIGNATURES: dict[str, list] = {
                       _c_vp, _c_ll, _c_ll, _c_int, _c_ll, ctypes.c_uint, _c_vp],
     "rgpt_muon_apply": [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_ll, _c_int, _c_float, _c_float, _c_float,
                         _c_float, _c_vp, _c_vp],
+    "rgpt_ns_chain": [_c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int, _c_ll, _c_ll, _c_ll, _c_ll, _c_int, _c_float,
+                      _c_float, _c_float, _c_vp, _c_vp],
+    "rgpt_segment_copy": [_c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_vp, _c_int, _c_int, _c_float, _c_int, _c_vp],
     "rgpt_rownorm_any_fwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_ll, _c_int, _c_vp],
     "rgpt_rownorm_any_bwd": [_c_vp, _c_vp, _c_vp, _c_int, _c_float, _c_float, _c_ll, _c_int, _c_vp, _c_vp, _c_vp,
                              _c_vp],

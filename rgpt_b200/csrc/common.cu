@@ -1,5 +1,6 @@
 // Host-side error plumbing, device checks and small utility entry points.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -48,6 +49,14 @@ int rgpt_check_device(int device) {
 int rgpt_num_sms(int device) {
   if (device < 0 || device >= kMaxDevices || g_sm_count[device] == 0) rgpt_check_device(device);
   return g_sm_count[device] > 0 ? g_sm_count[device] : 148;
+}
+
+int rgpt_pdl_enabled() {
+  static const int enabled = [] {
+    const char* v = getenv("RGPT_PDL");
+    return (v != nullptr && v[0] == '0') ? 0 : 1;
+  }();
+  return enabled;
 }
 
 extern "C" int rgpt_last_error(char* buf, unsigned long long buflen) {

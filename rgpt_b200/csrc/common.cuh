@@ -483,6 +483,9 @@ int rgpt_check_launch(const char* what);
 // earlier work in the stream writes or reads. While the stream is being captured into a CUDA graph
 // the launch is an ordinary one (griddep_wait() then returns at once): a replayed graph already
 // starts each kernel node right behind the previous one, and programmatic edges measured slower.
+// RGPT_PDL=0 in the environment turns programmatic launches off for the process (every launch ordinary).
+int rgpt_pdl_enabled();
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
                               int cluster_x, Args... args) {
@@ -498,7 +501,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     (void)cudaGetLastError();  // an unanswerable query leaves no error behind for the launch check
     cap = cudaStreamCaptureStatusActive;  // and takes the ordinary launch
   }
-  if (cap == cudaStreamCaptureStatusNone) {
+  if (cap == cudaStreamCaptureStatusNone && rgpt_pdl_enabled()) {
     at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;

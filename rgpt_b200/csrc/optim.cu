@@ -402,6 +402,44 @@ __global__ void __launch_bounds__(256) ns_split_kernel(const void* __restrict__ 
   }
 }
 
+// ============================================================================ data-parallel staging
+// Copies between per-segment tensors and one packed buffer: the staging of the sharded data-parallel
+// optimizer step (gradients packed owner-major for a reduce-scatter, averaged gradients unpacked into
+// the owner's gradient slots, updated parameters packed for an all-gather and unpacked everywhere).
+// One block per chunk of `chunk_elems` elements of one segment; the cast and the scale are the only
+// arithmetic. Pack: buf[off + i] = cast(scale * t[i]). Unpack: t[i] = cast(scale * buf[off + i]) and,
+// when the segment has one, t2[i] = bf16(t[i]) (the parameter's bf16 GEMM copy).
+__device__ __forceinline__ float seg_load(const void* p, long long i, int bf) {
+  return bf ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]) : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void seg_store(void* p, long long i, int bf, float v) {
+  if (bf)
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else
+    reinterpret_cast<float*>(p)[i] = v;
+}
+
+__global__ void segment_copy_kernel(const RgptSegment* __restrict__ tab, const int* __restrict__ chunk_seg,
+                                    const long long* __restrict__ chunk_start, int n_chunks, int chunk_elems,
+                                    void* __restrict__ buf, int buf_bf16, int tensor_bf16, float scale, int unpack) {
+  griddep_wait();
+  griddep_launch();
+  for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+    const RgptSegment sg = tab[chunk_seg[c]];
+    const long long start = chunk_start[c];
+    const long long end = min(start + (long long)chunk_elems, sg.n);
+    for (long long i = start + threadIdx.x; i < end; i += blockDim.x) {
+      if (unpack) {
+        const float v = scale * seg_load(buf, sg.buf_off + i, buf_bf16);
+        seg_store(sg.t, i, tensor_bf16, v);
+        if (sg.t2) reinterpret_cast<__nv_bfloat16*>(sg.t2)[i] = __float2bfloat16_rn(v);
+      } else {
+        seg_store(buf, sg.buf_off + i, buf_bf16, scale * seg_load(sg.t, i, tensor_bf16));
+      }
+    }
+  }
+}
+
 }  // namespace rgpt
 
 using namespace rgpt;
@@ -482,4 +520,18 @@ extern "C" int rgpt_ns_split(const void* src, int src_bf16, long long s_b, long 
              s_b, s_i, s_j, rows, cols, sumsq, xout, o_bstride, ldo, reinterpret_cast<__nv_bfloat16*>(dst),
              d_bstride, ldd, dst != nullptr ? nblk : 0, blk_off, lo_mask);
   return rgpt_check_launch("ns_split_kernel");
+}
+
+extern "C" int rgpt_segment_copy(const RgptSegment* table, const int* chunk_seg, const long long* chunk_start,
+                                 int n_chunks, int chunk_elems, void* buf, int buf_bf16, int tensor_bf16, float scale,
+                                 int unpack, void* stream) {
+  if (n_chunks <= 0) return RGPT_OK;
+  if (chunk_elems < 1) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "segment_copy: chunk_elems must be >= 1");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int cap = 8 * rgpt_num_sms(dev);
+  launch_pdl(segment_copy_kernel, dim3(n_chunks < cap ? n_chunks : cap), dim3(256), 0,
+             reinterpret_cast<cudaStream_t>(stream), 1, table, chunk_seg, chunk_start, n_chunks, chunk_elems, buf,
+             buf_bf16 ? 1 : 0, tensor_bf16 ? 1 : 0, scale, unpack ? 1 : 0);
+  return rgpt_check_launch("segment_copy_kernel");
 }

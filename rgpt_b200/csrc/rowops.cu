@@ -28,6 +28,7 @@
 #include "norm.cuh"
 #include "rgpt.h"
 
+#include <atomic>
 #include <type_traits>
 
 namespace rgpt {
@@ -1292,14 +1293,18 @@ extern "C" int rgpt_halt_losses(const float* q, const int* argmax, const long lo
 static __device__ __align__(256) float g_ce_noalloc_scratch[RGPT_CE_NOALLOC_MAX_ROWS + 64];
 
 // Device address of the scratch array for `dev`, resolved once per device with that device
-// current. (In host code the array's name only stands in for the symbol.)
+// current. (In host code the array's name only stands in for the symbol.) The cache is atomic, so
+// threads making their first call on one device at the same time are safe (both store the same
+// address). It belongs to the device context that resolved it: after cudaDeviceReset the cached
+// address is stale, so a process that resets a device must not call this entry point on it again.
 static float* ce_noalloc_scratch(int dev, int* status) {
-  static float* addr[64] = {nullptr};
+  static std::atomic<float*> addr[64];
   if (dev < 0 || dev >= 64) {
     *status = rgpt_set_error(RGPT_ERR_INTERNAL, "device index %d out of range", dev);
     return nullptr;
   }
-  if (addr[dev] == nullptr) {
+  float* a = addr[dev].load(std::memory_order_acquire);
+  if (a == nullptr) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_ce_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr) {
@@ -1307,9 +1312,10 @@ static float* ce_noalloc_scratch(int dev, int* status) {
                                cudaGetErrorString(e));
       return nullptr;
     }
-    addr[dev] = reinterpret_cast<float*>(p);
+    a = reinterpret_cast<float*>(p);
+    addr[dev].store(a, std::memory_order_release);
   }
-  return addr[dev];
+  return a;
 }
 
 extern "C" int rgpt_cross_entropy_noalloc(void* logits, long long ld, int M, int V, const long long* labels,

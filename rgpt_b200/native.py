@@ -407,3 +407,52 @@ def ns_split(src: torch.Tensor, *, sumsq: torch.Tensor | None = None, xout: torc
 def muon_apply(table, n, R, C, X, lr, wd, muon_lr, scale, hp: int | None = None) -> None:
     _lib.call("rgpt_muon_apply", ptr(table), n, R, C, ptr(X), X.stride(0), X.stride(1), float(lr), float(wd),
               float(muon_lr), float(scale), hp, _lib.stream_ptr(X.device))
+
+
+# ----------------------------------------------------------------------------- data-parallel staging
+SEG_CHUNK = 16384
+
+
+def segment_table(segs, device):
+    """Device table and work list of rgpt_segment_copy for segments (tensor, bf16 copy or None, buffer
+    offset, element offset in the tensor, count): (table int64 [n, 4], chunk_seg int32, chunk_start int64)."""
+    rows, cs, cst = [], [], []
+    for i, (t, t2, off, lo, n) in enumerate(segs):
+        if not t.is_contiguous() or (t2 is not None and (not t2.is_contiguous() or t2.dtype != torch.bfloat16)):
+            raise ValueError("segment tensors must be contiguous (second tensors bf16)")
+        rows.append([t.data_ptr() + lo * t.element_size(), t2.data_ptr() + lo * 2 if t2 is not None else 0, off, n])
+        for st in range(0, n, SEG_CHUNK):
+            cs.append(i)
+            cst.append(st)
+    if not rows:
+        return None
+    return (torch.tensor(rows, dtype=torch.int64).to(device), torch.tensor(cs, dtype=torch.int32).to(device),
+            torch.tensor(cst, dtype=torch.int64).to(device))
+
+
+def segment_copy(plan, buf: torch.Tensor, tensor_bf16: bool, scale: float = 1.0, unpack: bool = False) -> None:
+    """Pack the plan's segments into buf (unpack=False) or write buf back into them (unpack=True)."""
+    if plan is None:
+        return
+    table, cs, cst = plan
+    if buf.dtype not in (torch.float32, torch.bfloat16) or not buf.is_contiguous():
+        raise ValueError("staging buffers are contiguous fp32 or bf16")
+    _lib.call("rgpt_segment_copy", ptr(table), ptr(cs), ptr(cst), cs.numel(), SEG_CHUNK, ptr(buf),
+              int(buf.dtype == torch.bfloat16), int(tensor_bf16), float(scale), int(unpack), _lib.stream_ptr(buf.device))
+
+
+def ns_chain(X: torch.Tensor, X2: torch.Tensor, A: torch.Tensor, B: torch.Tensor, xr: int, xc: int, steps: int,
+             a: float, b: float, c: float, counters: torch.Tensor) -> None:
+    """The whole quintic Newton-Schulz iteration of the n matrices X[:, :xr, :xc] (normalised, bf16) in one
+    persistent launch; the result lands in X2 for odd `steps`, else in X. A, B [n, >=xr, >=xr] scratch,
+    counters int32 [>= n * 3 * steps] (zeroed by the call)."""
+    for t, nme in ((X, "X"), (X2, "X2"), (A, "A"), (B, "B")):
+        if t.dtype != torch.bfloat16 or t.dim() != 3 or t.stride(2) != 1:
+            raise ValueError(f"ns_chain: {nme} must be a 3-D bf16 tensor with unit column stride")
+    if X2.stride() != X.stride() or B.stride() != A.stride():
+        raise ValueError("ns_chain: X/X2 and A/B must share strides")
+    n = X.shape[0]
+    if counters.dtype != torch.int32 or counters.numel() < n * 3 * steps:
+        raise ValueError("ns_chain: counters must be int32 with >= n * 3 * steps entries")
+    _lib.call("rgpt_ns_chain", ptr(X), ptr(X2), ptr(A), ptr(B), n, xr, xc, X.stride(1), X.stride(0), A.stride(1),
+              A.stride(0), int(steps), float(a), float(b), float(c), ptr(counters), _lib.stream_ptr(X.device))

@@ -19,6 +19,7 @@ exported with the code's semantics; the NS coefficients are a parameter.
 from __future__ import annotations
 
 import math
+import os
 from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
@@ -69,6 +70,11 @@ def _table(rows: List[List[int]], device) -> torch.Tensor:
     return torch.tensor(rows, dtype=torch.int64).to(device, non_blocking=False)
 
 
+# How the bf16 Newton-Schulz iteration runs: "chain" = the whole iteration of a shape class in one persistent
+# kernel (rgpt_ns_chain), "batched" = 3 batched GEMM launches per step. RGPT_NS_IMPL overrides the default.
+NS_IMPL = os.environ.get("RGPT_NS_IMPL", "chain")
+
+
 class _NSWorkspace:
     """bf16 Newton-Schulz buffers for n matrices of one shape class (rows <= cols after transpose)."""
 
@@ -80,11 +86,17 @@ class _NSWorkspace:
         self.A = torch.zeros(n, rp, rp, device=device, dtype=torch.bfloat16)
         self.B = torch.zeros_like(self.A)
         self.sumsq = torch.zeros(n, device=device, dtype=torch.float32)
+        self.ctr = torch.zeros(n * 3 * 8, device=device, dtype=torch.int32)  # the chain kernel's counters
 
 
-def newton_schulz_batched(ws: _NSWorkspace, steps: int, coeffs=NS_COEFFS) -> torch.Tensor:
+def newton_schulz_batched(ws: _NSWorkspace, steps: int, coeffs=NS_COEFFS, impl: Optional[str] = None) -> torch.Tensor:
     """Run the quintic NS iteration in place on ws.X (already normalised); returns the result buffer."""
     a, b, c = coeffs
+    if (impl or NS_IMPL) == "chain":
+        if ws.ctr.numel() < ws.n * 3 * steps:
+            ws.ctr = torch.zeros(ws.n * 3 * steps, device=ws.X.device, dtype=torch.int32)
+        nv.ns_chain(ws.X, ws.X2, ws.A, ws.B, ws.xr, ws.xc, steps, a, b, c, ws.ctr)
+        return ws.X2 if steps % 2 else ws.X
     X, X2 = ws.X, ws.X2
     for _ in range(steps):
         nv.gemm(X, X, ws.A)                                                     # A = X X^T
@@ -148,6 +160,7 @@ class _NSView:
         self.n, self.xr, self.xc = e - s, ws.xr, ws.xc
         self.X, self.X2, self.A, self.B = ws.X[s:e], ws.X2[s:e], ws.A[s:e], ws.B[s:e]
         self.sumsq = ws.sumsq[s:e]
+        self.ctr = ws.ctr
 
 
 def assign_ns_owners(shapes: List[Tuple[int, int]], world: int) -> List[int]:
@@ -165,6 +178,73 @@ def assign_ns_owners(shapes: List[Tuple[int, int]], world: int) -> List[int]:
         owner[i] = r
         load[r] += cost[i]
     return owner
+
+
+def _slot(n: int, a: int = 8) -> int:
+    return (n + a - 1) // a * a
+
+
+class ShardLayout:
+    """Which rank updates what in the sharded data-parallel step, and where it sits in a packed buffer.
+
+    Rank r owns elements [r*S, (r+1)*S) of the flat AdamW space (every AdamW tensor of every group, in
+    group order, each starting on an 8-element boundary) and the Muon matrices that assign_ns_owners
+    gives it (whole matrices: Newton-Schulz needs all of one). A packed buffer is `world` chunks of C
+    elements; rank r's chunk holds its AdamW slice at [0, S) and its Muon matrices from S on. Gradients
+    travel in this layout through one reduce-scatter (rank r receives chunk r, summed over ranks) and
+    updated parameters through one all-gather (every rank receives every chunk)."""
+
+    def __init__(self, muon: List[torch.Tensor], adam: List[Tuple[int, torch.Tensor]], world: int):
+        self.world = world
+        self.adam = []  # (group index, param, flat start)
+        off = 0
+        for gi, p in adam:
+            self.adam.append((gi, p, off))
+            off += _slot(p.numel())
+        self.adam_total = off
+        self.S = _slot(-(-off // world)) if off else 0
+        shapes = []
+        for p in muon:
+            R, C = p.shape[0], p.numel() // p.shape[0]
+            shapes.append((C, R) if R > C else (R, C))
+        owners = assign_ns_owners(shapes, world) if muon else []
+        used = [self.S] * world
+        self.muon = []  # (param, owner, offset in the owner's chunk)
+        for p, o in zip(muon, owners):
+            self.muon.append((p, o, used[o]))
+            used[o] += _slot(p.numel())
+        self.C = _slot(max(used)) if used else 0
+
+    def owned_muon(self, r: int) -> List[torch.Tensor]:
+        return [p for p, o, _ in self.muon if o == r]
+
+    def adam_slices(self, r: int):
+        """(group, param, lo, hi, flat start) of every AdamW element range rank r owns."""
+        a, b = r * self.S, (r + 1) * self.S
+        out = []
+        for gi, p, f0 in self.adam:
+            lo, hi = max(a, f0), min(b, f0 + p.numel())
+            if lo < hi:
+                out.append((gi, p, lo - f0, hi - f0, f0))
+        return out
+
+    def segments(self, ranks, tensor_of, second_of=None, base_of=None):
+        """(tensor, bf16 copy or None, buffer offset, element offset, count) of the chunks of `ranks`;
+        tensor_of(param) gives the tensor a segment reads or writes (None: skipped); base_of(rank) the
+        buffer offset of the rank's chunk (default rank * C)."""
+        segs = []
+        for r in ranks:
+            base = r * self.C if base_of is None else base_of(r)
+            for gi, p, lo, hi, f0 in self.adam_slices(r):
+                t = tensor_of(p)
+                if t is not None:
+                    segs.append((t, second_of(p) if second_of else None, base + f0 + lo - r * self.S, lo, hi - lo))
+            for p, o, off in self.muon:
+                if o == r:
+                    t = tensor_of(p)
+                    if t is not None:
+                        segs.append((t, second_of(p) if second_of else None, base + off, 0, p.numel()))
+        return segs
 
 
 def _muon_rows(params, grads, moms) -> List[List[int]]:
@@ -408,10 +488,14 @@ class Muon(torch.optim.Optimizer):
         for job in self._adamw_jobs(gi, group, params):
             job()
 
-    def _adamw_jobs(self, gi, group, params):
+    def _adamw_jobs(self, gi, group, params, slices=None):
         """A closure launching the group's multi-tensor AdamW kernel (the step counter and the
-        optimizer state are advanced / created here, on the caller's stream)."""
-        if not params:
+        optimizer state are advanced / created here, on the caller's stream). slices: optional
+        (param, lo, hi) element ranges to update instead of whole parameters (the sharded step); the
+        counter advances even when the list is empty, so every rank keeps the same step."""
+        if slices is not None:
+            params = list(dict.fromkeys(p for p, _, _ in slices))
+        elif not params:
             return []
         lr = float(group["lr"])
         wd = float(group["weight_decay"])
@@ -421,23 +505,27 @@ class Muon(torch.optim.Optimizer):
         if self._hp_dev is None:  # else stage_device_hparams() advanced it
             step_i += 1
             group["_adam_step"] = step_i
+        if not params:
+            return []
         for p in params:
             st = self.state[p]
             if len(st) == 0:
                 st["exp_avg"] = torch.zeros_like(p)
                 st["exp_avg_sq"] = torch.zeros_like(p)
+        ranges = slices if slices is not None else [(p, 0, p.numel()) for p in params]
         rows = []
-        for p in params:
+        for p, lo, hi in ranges:
             st = self.state[p]
             sh = getattr(p, "_rgpt_shadow", None)
-            rows.append([p.data_ptr(), p.grad.data_ptr(), st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(),
-                         sh.data_ptr() if sh is not None else 0, p.numel()])
+            rows.append([p.data_ptr() + 4 * lo, p.grad.data_ptr() + 4 * lo, st["exp_avg"].data_ptr() + 4 * lo,
+                         st["exp_avg_sq"].data_ptr() + 4 * lo, sh.data_ptr() + 2 * lo if sh is not None else 0,
+                         hi - lo])
         key = ("adamw", gi, tuple(tuple(r) for r in rows))
         ent = self._cache.get(key)
         if ent is None:
             ct, cs = [], []
-            for ti, p in enumerate(params):
-                for s in range(0, p.numel(), _ADAM_CHUNK):
+            for ti, (_, lo, hi) in enumerate(ranges):
+                for s in range(0, hi - lo, _ADAM_CHUNK):
                     ct.append(ti)
                     cs.append(s)
             dev = params[0].device
@@ -452,22 +540,36 @@ class Muon(torch.optim.Optimizer):
 class DistMuon(Muon):
     """Data-parallel Muon (optimizer.py:278-415).
 
-    The reference relies on DDP to all-reduce gradients and then repeats the whole update on
-    every rank. Here gradients are averaged across ranks by this optimizer (the model is not
-    wrapped in DDP): one fp32 all-reduce of the flat gradient arena per step. The momentum and
-    AdamW updates then run on every rank as in the reference, but each Muon matrix's
-    Newton-Schulz iteration runs on one owner rank only (balanced by NS FLOPs) and the bf16
-    results are all-gathered, so every rank applies identical updates while doing 1/N of the
-    NS work. `shard_ns=False` repeats the full NS on every rank instead."""
+    The reference wraps the model in DDP (an fp32 all-reduce of every gradient) and repeats the whole
+    update on every rank. Here the model is not wrapped; this optimizer moves the data itself, in one of
+    two ways:
+
+    sharded_state=True: each rank owns part of the update (ShardLayout): whole Muon matrices,
+      balanced by Newton-Schulz FLOPs, and an equal slice of every AdamW element. Per step:
+        1. the gradients, packed owner-major in `reduce_dtype` (bf16 by default), go through ONE
+           reduce-scatter (average over ranks): each rank receives the averaged gradients of what it owns;
+        2. each rank runs momentum + Newton-Schulz + apply on its own matrices and AdamW on its own slices,
+           and keeps optimizer state current only there (momentum buffers exist only for its matrices);
+        3. the updated fp32 parameters go through ONE all-gather, and every rank rewrites its parameters
+           and their bf16 GEMM copies from it.
+      consolidate_state_dict() (a collective) gathers the full state, e.g. before a checkpoint.
+    sharded_state=False (default): an fp32 all-reduce (average) of the gradient arena, bucket by bucket as the
+      native backward finishes each layer, then momentum and AdamW on every rank with each Newton-Schulz
+      run by one owner rank and its bf16 result all-gathered (shard_ns=False: repeated on every rank)."""
 
     def __init__(self, params, *args, process_group=None, shard_ns: bool = True, overlap_grad_sync: bool = True,
-                 **kwargs):
+                 sharded_state: bool = False, reduce_dtype: torch.dtype = torch.bfloat16, **kwargs):
         super().__init__(params, *args, **kwargs)
         self.process_group = process_group
         self.shard_ns = shard_ns
         self.overlap_grad_sync = overlap_grad_sync
+        self.sharded_state = sharded_state
+        if reduce_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError("reduce_dtype must be torch.bfloat16 or torch.float32")
+        self.reduce_dtype = reduce_dtype
         self._pending: List[Any] = []    # async all-reduces launched during the backward
         self._synced: Dict[int, bool] = {}  # arena id -> every bucket reduced in the latest backward
+        self._layout_cache: Dict[Any, Any] = {}
 
     # -- gradient-bucket hooks called by the native backward (see Engine.backward) --
     def begin(self, arena):
@@ -482,13 +584,24 @@ class DistMuon(Muon):
     def end(self, arena):
         self._synced[id(arena)] = True
 
+    def _world(self) -> int:
+        return dist.get_world_size(self.process_group) if dist.is_available() and dist.is_initialized() else 1
+
     @torch.no_grad()
     def step(self, closure: Optional[Any] = None):
-        world = dist.get_world_size(self.process_group) if dist.is_available() and dist.is_initialized() else 1
+        world = self._world()
         if world <= 1:
             return super().step(closure)
+        fp32_ns = any(g.get("ns_precision", "bf16") == "fp32" for g in self.param_groups)
+        if self.sharded_state and not fp32_ns:
+            loss = None
+            if closure is not None:
+                with torch.enable_grad():
+                    loss = closure()
+            self._sharded_step(dist.get_rank(self.process_group), world)
+            return loss
         self._average_grads()
-        if not self.shard_ns or any(g.get("ns_precision", "bf16") == "fp32" for g in self.param_groups):
+        if not self.shard_ns or fp32_ns:
             return super().step(closure)  # the fp32 iteration runs replicated on every rank
         loss = None
         if closure is not None:
@@ -501,6 +614,117 @@ class DistMuon(Muon):
             else:
                 self._adamw_group(gi, group, [p for p in group["params"] if p.grad is not None])
         return loss
+
+    # ------------------------------------------------------------------ sharded-state step
+    def layout(self, world: int) -> "ShardLayout":
+        """The ShardLayout of this optimizer's parameters that have gradients (identical on every rank)."""
+        muon, adam = [], []
+        for gi, group in enumerate(self.param_groups):
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                if group.get("use_muon", False):
+                    muon.append(p)
+                else:
+                    adam.append((gi, p))
+        key = ("layout", world, tuple(id(p) for p in muon), tuple(id(p) for _, p in adam))
+        lay = self._layout_cache.get(key)
+        if lay is None:
+            lay = ShardLayout(muon, adam, world)
+            self._layout_cache[key] = lay
+        return lay
+
+    def _staging(self, lay: ShardLayout, rank: int, world: int):
+        """Packed buffers and segment tables of the sharded step (built once per parameter/gradient set)."""
+        params = [p for p, _, _ in lay.muon] + [p for _, p, _ in lay.adam]
+        key = ("staging", id(lay), rank, tuple(p.data_ptr() for p in params), tuple(p.grad.data_ptr() for p in params))
+        st = self._layout_cache.get(key)
+        if st is not None:
+            return st
+        for p in params:
+            if p.dtype != torch.float32 or p.grad.dtype != torch.float32 or not p.grad.is_contiguous():
+                raise ValueError("the sharded step needs fp32 parameters with contiguous fp32 gradients")
+        dev = params[0].device
+        C = lay.C
+        shadow = lambda p: getattr(p, "_rgpt_shadow", None)  # noqa: E731
+        st = dict(
+            send=torch.zeros(world * C, device=dev, dtype=self.reduce_dtype),
+            recv=torch.zeros(C, device=dev, dtype=self.reduce_dtype),
+            send32=torch.zeros(C, device=dev, dtype=torch.float32),
+            recv32=torch.zeros(world * C, device=dev, dtype=torch.float32),
+            # every rank's chunk of the gradients, in the owner-major layout
+            pack_grads=nv.segment_table(lay.segments(range(world), lambda p: p.grad), dev),
+            # the averaged gradients of what this rank owns, back into their fp32 gradient slots
+            unpack_grads=nv.segment_table(lay.segments([rank], lambda p: p.grad, base_of=lambda r: 0), dev),
+            # this rank's updated parameters
+            pack_params=nv.segment_table(lay.segments([rank], lambda p: p, base_of=lambda r: 0), dev),
+            # every rank's updated parameters, into the fp32 parameters and their bf16 GEMM copies
+            unpack_params=nv.segment_table(lay.segments(range(world), lambda p: p, second_of=shadow), dev),
+        )
+        self._layout_cache[key] = st
+        return st
+
+    def _sharded_step(self, rank: int, world: int) -> None:
+        for w in self._pending:  # hooks of an earlier all-reduce step
+            w.wait()
+        self._pending = []
+        lay = self.layout(world)
+        st = self._staging(lay, rank, world)
+        pg = self.process_group
+        # 1. averaged gradients of what this rank owns: pack, reduce-scatter, unpack
+        nv.segment_copy(st["pack_grads"], st["send"], tensor_bf16=False)
+        dist.reduce_scatter_tensor(st["recv"], st["send"], op=dist.ReduceOp.AVG, group=pg)
+        nv.segment_copy(st["unpack_grads"], st["recv"], tensor_bf16=False, unpack=True)
+        # 2. the update of the owned matrices and AdamW slices
+        jobs = []
+        owned = set(lay.owned_muon(rank))
+        slices = {}
+        for gi, p, lo, hi, _ in lay.adam_slices(rank):
+            slices.setdefault(gi, []).append((p, lo, hi))
+        for gi, group in enumerate(self.param_groups):
+            if group.get("use_muon", False):
+                jobs += self._muon_jobs(gi, group, [p for p in group["params"] if p in owned])
+            else:
+                jobs += self._adamw_jobs(gi, group, None, slices=slices.get(gi, []))
+        self._run_jobs(jobs)
+        # 3. every rank's updated parameters to every rank (fp32, so replicas stay identical)
+        nv.segment_copy(st["pack_params"], st["send32"], tensor_bf16=False)
+        dist.all_gather_into_tensor(st["recv32"], st["send32"], group=pg)
+        nv.segment_copy(st["unpack_params"], st["recv32"], tensor_bf16=False, unpack=True)
+
+    @torch.no_grad()
+    def consolidate_state_dict(self) -> Dict[str, Any]:
+        """Collective: give every rank the full optimizer state (each Muon matrix's momentum from its owner,
+        each AdamW moment slice from its owner), then return state_dict(). Call it on every rank, e.g.
+        before rank 0 writes a checkpoint."""
+        world = self._world()
+        if world <= 1 or not self.sharded_state:
+            return self.state_dict()
+        rank = dist.get_rank(self.process_group)
+        lay = self.layout(world)
+        dev = lay.muon[0][0].device if lay.muon else lay.adam[0][1].device
+        for p, _, _ in lay.muon:
+            st = self.state[p]
+            if "momentum_buffer" not in st:
+                st["momentum_buffer"] = torch.zeros_like(p, dtype=torch.bfloat16)
+        for _, p, _ in lay.adam:
+            st = self.state[p]
+            if "exp_avg" not in st:
+                st["exp_avg"] = torch.zeros_like(p)
+                st["exp_avg_sq"] = torch.zeros_like(p)
+        send = torch.zeros(lay.C, device=dev, dtype=torch.float32)
+        recv = torch.zeros(world * lay.C, device=dev, dtype=torch.float32)
+        keys = (("momentum_buffer", True), ("exp_avg", False), ("exp_avg_sq", False))
+        for k, is_bf in keys:
+            def of(p, k=k):
+                return self.state[p].get(k)
+            mine = nv.segment_table(lay.segments([rank], of, base_of=lambda r: 0), dev)
+            allr = nv.segment_table(lay.segments(range(world), of), dev)
+            # segments of one key are all bf16 (momentum) or all fp32 (moments)
+            nv.segment_copy(mine, send, tensor_bf16=is_bf)
+            dist.all_gather_into_tensor(recv, send, group=self.process_group)
+            nv.segment_copy(allr, recv, tensor_bf16=is_bf, unpack=True)
+        return self.state_dict()
 
     def _muon_group_sharded(self, gi, group, params, rank: int, world: int):
         if not params:

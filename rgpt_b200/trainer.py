@@ -192,15 +192,14 @@ class Trainer:
                                 self.global_step)
             final = self.global_step == self.total_steps
             if (self.global_step > 0 and self.global_step % val_every == 0) or final:
-                val = self._validate_loss(self.val_loader)
-                if self.is_main_process:
-                    self.logger.log({"Loss/val_fineweb": val}, self.global_step)
-                    if val < self.best_metric:
-                        self.best_metric, self.best_epoch = val, self.global_step
-                        self.save_checkpoint(self.best_model_path, self.global_step)
-                        self.epochs_no_improve = 0
-                    else:
-                        self.epochs_no_improve += 1
+                val = self._validate_loss(self.val_loader)  # averaged over ranks: every rank decides alike
+                self.logger.log({"Loss/val_fineweb": val}, self.global_step)
+                if val < self.best_metric:
+                    self.best_metric, self.best_epoch = val, self.global_step
+                    self.save_checkpoint(self.best_model_path, self.global_step)  # every rank: may gather
+                    self.epochs_no_improve = 0
+                else:
+                    self.epochs_no_improve += 1
                 if self.is_ddp:
                     import torch.distributed as dist
 
@@ -294,12 +293,15 @@ class Trainer:
         return m._orig_mod if hasattr(m, "_orig_mod") else m
 
     def save_checkpoint(self, path, epoch):
-        """Same dictionary as the reference (trainer.py:311-322), written by rank 0."""
+        """Same dictionary as the reference (trainer.py:311-322), written by rank 0. Call it on every rank:
+        a sharded data-parallel optimizer first gathers its state (a collective)."""
+        consolidate = getattr(self.optimizer, "consolidate_state_dict", None)
+        opt_state = consolidate() if (self.is_ddp and consolidate is not None) else None
         if not self.is_main_process:
             return
         Path(path).parent.mkdir(parents=True, exist_ok=True)
         ck = {"model_state_dict": self._get_model_for_saving().state_dict(),
-              "optimizer_state_dict": self.optimizer.state_dict(),
+              "optimizer_state_dict": opt_state if opt_state is not None else self.optimizer.state_dict(),
               "best_metric": self.best_metric, "global_step": self.global_step}
         if self.scheduler is not None:
             ck["scheduler_state_dict"] = self.scheduler.state_dict()

@@ -46,7 +46,7 @@ def _worker(rank: int, world: int, port: int, q) -> None:
                 p.grad = g.clone().to(dev)
             groups = [dict(params=ps[:-1], use_muon=True, lr=0.02, weight_decay=0.01),
                       dict(params=ps[-1:], use_muon=False, lr=0.001, weight_decay=0.0)]
-            return ps, DistMuon(groups, shard_ns=shard, muon_lr_multiplier=1.0)
+            return ps, DistMuon(groups, shard_ns=shard, sharded_state=False, muon_lr_multiplier=1.0)
 
         pa, oa = make(True)
         pb, ob = make(False)
@@ -112,7 +112,8 @@ def _train_worker(rank: int, world: int, port: int, q) -> None:
         batches = [torch.randint(0, 384, (2, 129), generator=g).to(dev) for _ in range(3)]
         torch.manual_seed(0)
         model = GPT(**cfg).to(dev)
-        opt = DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
+        opt = DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3,
+                       sharded_state=False)
 
         def backward(ids):
             total, _, _ = model.forward_loss(ids[:, :-1], ids[:, 1:].contiguous())
@@ -173,7 +174,7 @@ def test_distmuon_overlapped_bucket_sync_matches_step_time_allreduce():
         assert same == 0.0, (rank, same)
 
 
-def _graph_worker(rank: int, world: int, port: int, q) -> None:
+def _graph_worker(rank: int, world: int, port: int, q, sharded: bool = True) -> None:
     import torch.distributed as dist
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -198,7 +199,8 @@ def _graph_worker(rank: int, world: int, port: int, q) -> None:
             torch.manual_seed(0)
             model = GPT(**cfg).to(dev).train()
             model.engine()  # the dropout seed is drawn here, at the same generator state for both copies
-            return model, DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3)
+            return model, DistMuon(trainer_param_groups(model), lr=6e-4, weight_decay=0.1, muon_lr_multiplier=33.3,
+                                   sharded_state=sharded)
 
         model_g, opt_g = build()
         graphed = GraphedTrainStep(model_g, opt_g, 2, 128, 1, warmup=2)
@@ -240,7 +242,8 @@ def _graph_worker(rank: int, world: int, port: int, q) -> None:
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs two GPUs")
-def test_graphed_data_parallel_step_matches_eager():
+@pytest.mark.parametrize("sharded", [True, False], ids=["sharded_state", "all_reduce"])
+def test_graphed_data_parallel_step_matches_eager(sharded):
     # Five data-parallel training steps with dropout 0.1, the last three replayed from one captured
     # CUDA graph that holds the gradient-bucket all-reduces and the Newton-Schulz all-gather, against
     # five eager steps: every rank holds identical parameters, the per-step losses agree to 1e-3 and
@@ -254,7 +257,7 @@ def test_graphed_data_parallel_step_matches_eager():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_graph_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_graph_worker, args=(r, world, port, q, sharded)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
@@ -266,3 +269,97 @@ def test_graphed_data_parallel_step_matches_eager():
         assert same == 0.0, (rank, same)
         assert ldiff < 1e-3, (rank, ldiff)
         assert diff < 1e-2, (rank, diff, diff_ee)
+
+
+def _sharded_worker(rank: int, world: int, port: int, q) -> None:
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from rgpt_b200.optimizer import DistMuon
+
+        shapes = [(512, 512)] * 4 + [(2048, 512), (512, 2048), (64, 64)]
+        g0 = torch.Generator().manual_seed(0)
+        init = [torch.randn(*s, generator=g0) * 0.02 for s in shapes] + [torch.ones(512), torch.randn(1000, 64) * 0.02]
+        grads = [[torch.randn(t.shape, generator=torch.Generator().manual_seed(100 * step + 10 * rank + i)) * 1e-2
+                  for i, t in enumerate(init)] for step in range(3)]
+
+        def make(**kw):
+            ps = [torch.nn.Parameter(t.clone().to(dev)) for t in init]
+            for p in ps:
+                p.grad = torch.zeros_like(p)
+            groups = [dict(params=ps[:7], use_muon=True, lr=0.02, weight_decay=0.01),
+                      dict(params=ps[7:8], use_muon=False, lr=0.001, weight_decay=0.0),
+                      dict(params=ps[8:], use_muon=False, lr=0.001, weight_decay=0.1)]
+            return ps, DistMuon(groups, muon_lr_multiplier=1.0, **kw)
+
+        runs = {"ar": make(sharded_state=False, shard_ns=False),
+                "rs32": make(sharded_state=True, reduce_dtype=torch.float32),
+                "rs16": make(sharded_state=True, reduce_dtype=torch.bfloat16)}
+        for step in range(3):
+            for ps, opt in runs.values():
+                for p, g in zip(ps, grads[step]):
+                    p.grad.copy_(g.to(dev))
+                opt.step()
+        torch.cuda.synchronize()
+        ref = runs["ar"][0]
+
+        def upd_err(ps):
+            return max(((a - i.to(dev)) - (b - i.to(dev))).norm().item() / (b - i.to(dev)).norm().item()
+                       for a, b, i in zip(ps, ref, init))
+        err32, err16 = upd_err(runs["rs32"][0]), upd_err(runs["rs16"][0])
+        # every rank holds the same parameters
+        same = 0.0
+        for ps, _ in runs.values():
+            for p in ps:
+                t = p.detach().clone()
+                dist.broadcast(t, 0)
+                same = max(same, (p - t).abs().max().item())
+        # the gathered state equals the replicated optimizer's
+        sd_ar = runs["ar"][1].state_dict()["state"]
+        sd_rs = runs["rs32"][1].consolidate_state_dict()["state"]
+        st_err = 0.0
+        for k, st in sd_ar.items():
+            for name, v in st.items():
+                if torch.is_tensor(v) and v.is_floating_point():
+                    w = sd_rs[k][name]
+                    assert w.dtype == v.dtype and w.shape == v.shape, (k, name)
+                    st_err = max(st_err, ((w.float() - v.float()).norm() / v.float().norm().clamp_min(1e-30)).item())
+        q.put((rank, err32, err16, same, st_err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs two GPUs")
+def test_sharded_state_step_matches_replicated_on_two_gpus():
+    # The sharded data-parallel step (owner-major reduce-scatter of the gradients, each rank updating its
+    # own Muon matrices and AdamW slices, all-gather of the updated parameters) against the all-reduce
+    # step that repeats the whole update on every rank, over 3 steps with different gradients per rank.
+    # With an fp32 reduce-scatter the updates agree to 1e-5 relative (only the order of the cross-rank sums
+    # differs); with the bf16 reduce-scatter to 2e-2 (bf16 rounding of the averaged gradient, amplified by
+    # Newton-Schulz); every rank ends with identical parameters; consolidate_state_dict() gathers momentum
+    # and AdamW moments equal (1e-5) to the replicated optimizer's.
+    import torch.multiprocessing as mp
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err32, err16, same, st_err in res:
+        print(f"rank {rank}: fp32 RS {err32:.2e}, bf16 RS {err16:.2e}, state {st_err:.2e}")
+        assert same == 0.0, (rank, same)
+        assert err32 < 1e-5, (rank, err32)
+        assert err16 < 2e-2, (rank, err16)
+        assert st_err < 1e-5, (rank, st_err)

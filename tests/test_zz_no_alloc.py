@@ -45,14 +45,18 @@ def _call_noalloc(logits, labels, grad_scale, write_grad):
 def test_noalloc_cross_entropy_matches_allocating_entry_point():
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    M, V = 4096, 50304
-    for call, scale in enumerate((1.0, 0.25)):  # two calls in a row: the shared scratch must not leak
-        logits = (torch.randn(M, V, device=dev, generator=g) * (2.0 + call)).to(torch.bfloat16)
+    # calls in a row: a smaller M after a larger one (stale per-row losses of the first call must not
+    # reach the second's mean), and a vocabulary that is not a multiple of 8 (the streaming kernel
+    # instead of the row-in-shared-memory one; the rows keep a 16-byte-aligned stride)
+    cases = [(4096, 50304, 50304, 1.0), (1000, 50304, 50304, 0.25), (3000, 50257, 50264, 0.5)]
+    for call, (M, V, ld, scale) in enumerate(cases):
+        buf = (torch.randn(M, ld, device=dev, generator=g) * (2.0 + call)).to(torch.bfloat16)
+        logits = buf[:, :V]
         labels = torch.randint(0, V, (M,), device=dev, generator=g)
         labels[:: 7 + call] = -100  # ignored positions change the valid count between calls
-        a, b = logits.clone(), logits.clone()
-        loss_a, amax_a = _call_alloc(a, labels, scale, True)
-        loss_b, amax_b = _call_noalloc(b, labels, scale, True)
+        a, b = buf.clone(), buf.clone()
+        loss_a, amax_a = _call_alloc(a[:, :V], labels, scale, True)
+        loss_b, amax_b = _call_noalloc(b[:, :V], labels, scale, True)
         torch.cuda.synchronize()
         assert torch.equal(loss_a, loss_b), (call, loss_a.item(), loss_b.item())
         assert torch.equal(amax_a, amax_b)
