@@ -46,6 +46,7 @@ struct GemmShape {
   int M, N, K, batch;
   int m_tiles, n_tiles, splitk, kb_per_split, num_kb;
   int num_units;
+  int group_m;  // row tiles per visiting group (see decode_unit)
 };
 
 struct EpiParams {
@@ -117,9 +118,9 @@ __device__ __forceinline__ void decode_unit(int u, const GemmShape& sh, int& b, 
   const int per_batch = sh.m_tiles * sh.n_tiles;
   b = t / per_batch;
   t %= per_batch;
-  const int group_span = GROUP_M * sh.n_tiles;
-  const int first_m = (t / group_span) * GROUP_M;
-  const int gsize = min(sh.m_tiles - first_m, GROUP_M);
+  const int group_span = sh.group_m * sh.n_tiles;
+  const int first_m = (t / group_span) * sh.group_m;
+  const int gsize = min(sh.m_tiles - first_m, sh.group_m);
   const int r = t % group_span;
   mt = first_m + r % gsize;
   nt = r / gsize;
@@ -934,6 +935,12 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   sh.kb_per_split = (sh.num_kb + splitk - 1) / splitk;
   sh.splitk = (sh.num_kb + sh.kb_per_split - 1) / sh.kb_per_split;  // no empty splits
   sh.num_units = tiles * sh.splitk;
+  // Visiting order: groups of GROUP_M row tiles, each swept across all column tiles. A very wide
+  // output (the vocabulary-sized lm_head logits, N / BN >= 64) with a small A (<= 32 MB) is swept
+  // column by column over ALL row tiles instead: A stays in L2 and B streams through once, where
+  // groups of 8 row tiles would read the 51 MB lm_head weight once per group (m_tiles / 8 times).
+  sh.group_m = GROUP_M;
+  if (sh.n_tiles >= 64 && (long long)M * K * 2 <= (32LL << 20)) sh.group_m = sh.m_tiles;
 
   // Operand maps. K-major: (inner=K, outer=rows); MN-major: (inner=rows, outer=K).
   CUtensorMap ta, tb, td, td2;
