@@ -17,9 +17,11 @@
 // k-blocks of A and B into a 5-stage ring), warp 1 TMEM allocation + tcgen05.mma issue (one elected
 // thread), warps 2-9 epilogue, two per TMEM lane quadrant, each taking one 64-column half of the tile
 // (TMEM -> registers, + beta * C for B and X', bf16 -> swizzled smem -> TMA bulk store; then the
-// completion counter). A warp publishes a tile once its store has landed, but only when it is about
-// to wait anyway or once the next tile's store is issued, so stores stay in flight under the math. Operands and outputs are bf16, accumulation fp32:
-// the same roundings as the batched path (one per GEMM, the polynomial combine fused).
+// completion counter). A warp publishes its part of a tile as soon as the store has landed: the phase
+// chain is latency-bound, so a deferred publish (to keep the store in flight under the next tile's
+// math) measured slower. A diagonal tile of A = X X^T or of A A reads the same panel as both MMA
+// operands, so it is loaded once. Operands and outputs are bf16, accumulation fp32: the same
+// roundings as the batched path (one per GEMM, the polynomial combine fused).
 //
 // Memory ordering between units of different CTAs: a tile's TMA stores complete (bulk wait_group 0),
 // a proxy fence orders them before the generic-proxy release increment of the counter; the consumer
@@ -126,7 +128,6 @@ __device__ __forceinline__ void ns_tma_store_3d(const CUtensorMap* map, const vo
 }
 __device__ __forceinline__ void ns_bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void ns_bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-__device__ __forceinline__ void ns_bulk_wait_1() { asm volatile("cp.async.bulk.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void ns_bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ uint8_t* ns_stage_ptr(uint8_t* buf, int lane, int j) {
   return buf + lane * 128 + ((j ^ (lane & 7)) << 4);
@@ -226,9 +227,11 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         const int N = U.kind == 2 ? P.xc : P.xr;
         const int num_kb = (K + NS_BK - 1) / NS_BK;
         const int a_row = U.mt * NS_BM, b_row = U.nt * NS_BN;
-        // the MN-major B arrives as 64-column sub-boxes; those wholly past N are not loaded
-        const int b_sub = U.kind == 2 ? max(0, min(2, (N - b_row + 63) / 64)) : 1;
-        const uint32_t expect = NS_A_BYTES + (U.kind == 2 ? b_sub * (64 * NS_BK * 2) : NS_B_BYTES);
+        // the MN-major B arrives as 64-column sub-boxes; those wholly past N are not loaded; a diagonal
+        // tile of A or B loads its one panel (the MMA reads it as both operands)
+        const bool diag = U.kind != 2 && U.mt == U.nt;
+        const int b_sub = U.kind == 2 ? max(0, min(2, (N - b_row + 63) / 64)) : (diag ? 0 : 1);
+        const uint32_t expect = NS_A_BYTES + (U.kind == 2 ? b_sub * (64 * NS_BK * 2) : (diag ? 0u : NS_B_BYTES));
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
           if (U.kind == 2) {
             for (int i = 0; i < b_sub; ++i)
               tma_load_3d(b_dst + i * (64 * NS_BK * 2), mB, &full_bar[stage], b_row + i * 64, k0, U.m);
-          } else {
+          } else if (!diag) {
             tma_load_3d(b_dst, mB, &full_bar[stage], k0, b_row, U.m);
           }
           if (++stage == NS_STAGES) {
@@ -270,6 +273,7 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         const int K = U.kind == 0 ? P.xc : P.xr;
         const int num_kb = (K + NS_BK - 1) / NS_BK;
         const bool bmn = U.kind == 2;
+        const bool diag = !bmn && U.mt == U.nt;  // B operand = the A stage
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * NS_BN;
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * NS_A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * NS_B_BYTES);
+          const uint32_t b_addr = diag ? a_addr : smem_u32(sB + stage * NS_B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < NS_BK / 16; ++kk) {
             const uint64_t adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
@@ -310,16 +314,14 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
     uint8_t* sbuf = sEpi + (warp - 2) * NS_EPI_STAGE;
     int acc = 0;
     uint32_t acc_phase = 0;
-    unsigned* pending = nullptr;  // counter of this warp's last stored tile, not yet published
-    auto publish = [&](bool wait_all) {
+    // this warp's part of a tile is complete: its store has landed (and is ordered before the release)
+    auto publish = [&](unsigned* ctr) {
       if (lane == 0) {
-        if (wait_all) ns_bulk_wait_all();
-        else ns_bulk_wait_1();  // every store group but the newest has landed
+        ns_bulk_wait_all();
         fence_proxy_async_global();
-        red_release_add(pending, 1u);
+        red_release_add(ctr, 1u);
       }
       __syncwarp();
-      pending = nullptr;
     };
     for (long long u = blockIdx.x; u < P.num_units; u += gridDim.x) {
       const NsUnit U = ns_decode(u, P);
@@ -337,11 +339,6 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         const int prev_kind = (U.kind + 2) % 3;
         const unsigned* dctr = P.ctr + (long long)U.m * P3 + U.phase - 1;
         const unsigned target = (unsigned)((prev_kind == 2 ? P.t2 : P.t01) * NS_EW);
-        // never block while holding a publication: the previous phase may be waiting for exactly it
-        // (the decision is lane 0's, so the whole warp takes the same path)
-        int must = 0;
-        if (lane == 0) must = (pending != nullptr && ld_acquire_u32(dctr) < target) ? 1 : 0;
-        if (__shfl_sync(0xffffffffu, must, 0)) publish(true);
         ok = dep_wait(dctr, target, abort_flag);
       }
       uint4 cc[8];
@@ -365,13 +362,6 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
             cc[j] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-      }
-      // about to block on the accumulator: first publish the previous tile, whose store may be what
-      // another unit (perhaps this CTA's own producer) is waiting for
-      {
-        int must = 0;
-        if (lane == 0) must = (pending != nullptr && !mbar_try_wait(&tfull_bar[acc], acc_phase)) ? 1 : 0;
-        if (__shfl_sync(0xffffffffu, must, 0)) publish(true);
       }
       int okw = ok ? 1 : 0;
       if (lane == 0 && okw) okw = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
@@ -426,16 +416,13 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
           ns_tma_store_3d(dmap, sbuf, gn0, row0, U.m);
           ns_bulk_commit();
         }
-        if (pending != nullptr) publish(false);  // the store before this one has landed
-        pending = my_ctr;
+        publish(my_ctr);
       } else {
         // nothing to store: this warp's share of the tile is complete at once
-        if (pending != nullptr) publish(true);
         if (lane == 0) red_release_add(my_ctr, 1u);
         __syncwarp();
       }
     }
-    if (pending != nullptr) publish(true);
     if (lane == 0) ns_bulk_wait_all();
     __syncwarp();
   }

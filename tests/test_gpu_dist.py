@@ -283,8 +283,9 @@ def _sharded_worker(rank: int, world: int, port: int, q) -> None:
         from rgpt_b200.optimizer import DistMuon
 
         shapes = [(512, 512)] * 4 + [(2048, 512), (512, 2048), (64, 64)]
-        g0 = torch.Generator().manual_seed(0)
-        init = [torch.randn(*s, generator=g0) * 0.02 for s in shapes] + [torch.ones(512), torch.randn(1000, 64) * 0.02]
+        g0 = torch.Generator().manual_seed(0)  # every parameter from this generator: the same on every rank
+        init = ([torch.randn(*s, generator=g0) * 0.02 for s in shapes]
+                + [torch.ones(512), torch.randn(1000, 64, generator=g0) * 0.02])
         grads = [[torch.randn(t.shape, generator=torch.Generator().manual_seed(100 * step + 10 * rank + i)) * 1e-2
                   for i, t in enumerate(init)] for step in range(3)]
 
