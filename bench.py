@@ -781,7 +781,8 @@ def kernel_cases(dev):
 
     inv_freq = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device=dev, dtype=torch.float32) / 64))
 
-    @add("qkv_prep_fwd", "hbm", M * d * (3 * 2 + 2 * 2 + 2))
+    # reads the q and k blocks of qkv (v is never touched), writes roped q | k and the normed q
+    @add("qkv_prep_fwd", "hbm", M * d * (2 * 2 + 2 * 2 + 2))
     def _():
         qkv = rb(M, 3 * d)
         qk, qn = torch.empty(M, 2 * d, device=dev, dtype=torch.bfloat16), torch.empty(M, d, device=dev,

@@ -578,8 +578,8 @@ class DistMuon(Muon):
     def ready(self, arena, start: int, end: int):
         # the collective waits for the kernels already queued on the current stream, then runs
         # alongside the rest of the backward; AVG averages over the ranks like the reference's DDP
-        self._pending.append(dist.all_reduce(arena[start:end], op=dist.ReduceOp.AVG, group=self.process_group,
-                                             async_op=True))
+        self._pending.append((dist.all_reduce(arena[start:end], op=dist.ReduceOp.AVG, group=self.process_group,
+                                              async_op=True), arena, start, end))
 
     def end(self, arena):
         self._synced[id(arena)] = True
@@ -600,9 +600,13 @@ class DistMuon(Muon):
                     loss = closure()
             self._sharded_step(dist.get_rank(self.process_group), world)
             return loss
-        self._average_grads()
         if not self.shard_ns or fp32_ns:
+            self._average_grads()
             return super().step(closure)  # the fp32 iteration runs replicated on every rank
+        # The last gradient bucket (the embedding's, finished by the last kernel of the backward) holds no
+        # Muon matrix, so its all-reduce keeps running under the Newton-Schulz work and is only waited for
+        # before AdamW.
+        deferred = self._average_grads(defer_last=True)
         loss = None
         if closure is not None:
             with torch.enable_grad():
@@ -611,7 +615,10 @@ class DistMuon(Muon):
         for gi, group in enumerate(self.param_groups):
             if group.get("use_muon", False):
                 self._muon_group_sharded(gi, group, [p for p in group["params"] if p.grad is not None], rank, world)
-            else:
+        if deferred is not None:
+            deferred.wait()
+        for gi, group in enumerate(self.param_groups):
+            if not group.get("use_muon", False):
                 self._adamw_group(gi, group, [p for p in group["params"] if p.grad is not None])
         return loss
 
@@ -665,7 +672,7 @@ class DistMuon(Muon):
         return st
 
     def _sharded_step(self, rank: int, world: int) -> None:
-        for w in self._pending:  # hooks of an earlier all-reduce step
+        for w, *_ in self._pending:  # hooks of an earlier all-reduce step
             w.wait()
         self._pending = []
         lay = self.layout(world)
@@ -805,11 +812,23 @@ class DistMuon(Muon):
                                   gathered=torch.zeros(world * maxc, rp, cp, device=dev, dtype=torch.bfloat16))
         return plan
 
-    def _average_grads(self):
+    def _average_grads(self, defer_last: bool = False):
+        """Finish the averaging of every gradient (waits for the bucket all-reduces issued during the
+        backward, all-reduces what was not hooked). defer_last: leave the last bucket's all-reduce
+        running and return its work handle, if no Muon gradient lies in that bucket."""
         ws = dist.get_world_size(self.process_group)
-        for w in self._pending:
+        pending, self._pending = self._pending, []
+        deferred = None
+        if defer_last and pending:
+            w, arena, start, end = pending[-1]
+            base = arena.data_ptr()
+            muon_in = any(p.grad is not None and start <= (p.grad.data_ptr() - base) // 4 < end
+                          for g in self.param_groups if g.get("use_muon", False) for p in g["params"])
+            if not muon_in:
+                deferred = w
+                pending = pending[:-1]
+        for w, *_ in pending:
             w.wait()
-        self._pending = []
         nccl = dist.get_backend(self.process_group) == "nccl"
         arenas, loose = {}, []
         for group in self.param_groups:
@@ -831,6 +850,7 @@ class DistMuon(Muon):
         for g in loose:
             dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.process_group)
             g.mul_(1.0 / ws)
+        return deferred
 
 
 # Names used by the reference's README.
