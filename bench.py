@@ -742,6 +742,13 @@ def kernel_cases(dev):
         pre, post = (torch.empty(M, F, device=dev, dtype=torch.bfloat16) for _ in range(2))
         return lambda: nv.gemm(x, w, pre, epi=nv.EPI_ACT_FWD, act=1, out2=post)
 
+    # the training step's fc1: squared ReLU with the post-activation as its only output
+    @add("fc1_sqrelu_post", "tensor", 2.0 * M * F * d)
+    def _():
+        x, w = rb(M, d), rb(F, d)
+        post = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+        return lambda: nv.gemm(x, w, post, epi=nv.EPI_ACT_FWD, act=nv.ACT_SQRELU_POST)
+
     @add("fc2_resid", "tensor", 2.0 * M * d * F)
     def _():
         post, w, h, x = rb(M, F), rb(d, F), rf(M, d), torch.empty(M, d, device=dev)

@@ -55,7 +55,10 @@ enum RgptEpilogue {
   RGPT_EPI_ARGMAX_BF16 = 9 /* no D: per row and column tile, the first maximum of bf16(alpha*acc) and its
                               column (rgpt_gemm_argmax only)                          */
 };
-enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4 };
+enum RgptActivation { RGPT_ACT_NONE = 0, RGPT_ACT_SQUARED_RELU = 1, RGPT_ACT_GELU = 2, RGPT_ACT_SILU = 3, RGPT_ACT_MISH = 4,
+                      /* squared ReLU, post-activation only: ACT_FWD writes D = relu(acc)^2 and no D2 (pass
+                         D2 = NULL); ACT_BWD takes C = that post-activation and forms act' = 2 sqrt(C) */
+                      RGPT_ACT_SQUARED_RELU_POST = 5 };
 
 /* Requirements: M, N, K >= 1 (tiles past the edges are zero-filled / masked); 16-byte aligned base pointers;
  * leading dimensions and batch strides multiples of 8 elements (16 bytes).

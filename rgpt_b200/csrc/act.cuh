@@ -25,7 +25,10 @@
 
 namespace rgpt {
 
-enum ActKind : int { ACT_NONE = 0, ACT_SQRELU = 1, ACT_GELU = 2, ACT_SILU = 3, ACT_MISH = 4 };
+enum ActKind : int { ACT_NONE = 0, ACT_SQRELU = 1, ACT_GELU = 2, ACT_SILU = 3, ACT_MISH = 4, ACT_SQRELU_POST = 5 };
+// ACT_SQRELU_POST: squared ReLU whose forward stores only post = relu(x)^2 and whose backward takes its
+// derivative from post: relu(x) = sqrt(post), so act'(x) = 2 sqrt(post). The pre-activation is never
+// written, halving the forward GEMM's output bytes.
 
 constexpr float ACT_LOG2E = 1.4426950408889634f;
 constexpr float GELU_K = 0.7978845608028654f;  // sqrt(2 / pi)
@@ -37,7 +40,7 @@ __device__ __forceinline__ float sigmoid_fast(float x) { return rcp_approx(1.0f 
 // Compile-time activation (one instantiation per kind keeps unrolled epilogues small).
 template <int ACT>
 __device__ __forceinline__ float act_fwd_t(float x) {
-  if constexpr (ACT == ACT_SQRELU) {
+  if constexpr (ACT == ACT_SQRELU || ACT == ACT_SQRELU_POST) {
     const float r = fmaxf(x, 0.0f);
     return r * r;
   } else if constexpr (ACT == ACT_GELU) {
@@ -59,6 +62,10 @@ template <int ACT>
 __device__ __forceinline__ float act_grad_t(float x) {
   if constexpr (ACT == ACT_SQRELU) {
     return 2.0f * fmaxf(x, 0.0f);
+  } else if constexpr (ACT == ACT_SQRELU_POST) {
+    // x = post = relu(pre)^2 >= 0; one MUFU operation (an IEEE sqrtf here slowed the epilogue-bound
+    // backward GEMM more than dropping the pre-activation saved in the forward)
+    return 2.0f * sqrt_approx(fmaxf(x, 0.0f));
   } else if constexpr (ACT == ACT_GELU) {
     const float x2 = x * x;
     const float u = GELU_K * fmaf(GELU_C * x, x2, x);

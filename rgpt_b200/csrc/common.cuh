@@ -341,6 +341,13 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// sqrt(x) with the hardware approximation (PTX sqrt.approx.ftz.f32: one MUFU operation; sqrt(0) = 0).
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // 1/x with the hardware approximation (PTX rcp.approx.ftz.f32; 1/inf = 0).
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;

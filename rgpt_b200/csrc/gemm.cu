@@ -24,7 +24,7 @@
 // GROUP_M row tiles so that consecutive CTAs share A and B panels in L2.
 //
 // Epilogues fuse what the reference runs as separate torch ops:
-//   ACT_FWD      pre = acc, post = act(acc)          (model/kernels.py:127-200)
+//   ACT_FWD      pre = acc, post = act(acc)          (model/kernels.py:127-200); post only for ACT_SQRELU_POST
 //   ACT_BWD      dpre = acc * act'(pre)              (model/kernels.py:207-281)
 //   RESID_F32    x_out = x_in + acc * layer_scale    (model/transformer_block.py:43-57)
 //   POLY_BF16    beta*C + alpha*acc                  (optimizer.py:36-41, Newton-Schulz)
@@ -380,7 +380,8 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
     int which = 0;
     constexpr bool bf16_out = (EPI == RGPT_EPI_STORE_BF16 || EPI == RGPT_EPI_ACT_FWD || EPI == RGPT_EPI_ACT_BWD ||
                                EPI == RGPT_EPI_POLY_BF16 || EPI == RGPT_EPI_BIAS_SIGMOID_BF16);
-    const bool dual = (EPI == RGPT_EPI_ACT_FWD) || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
+    constexpr bool act_two_out = EPI == RGPT_EPI_ACT_FWD && ACT != ACT_SQRELU_POST;  // pre and post
+    const bool dual = act_two_out || (EPI == RGPT_EPI_RESID_F32 && ep.has_d2);
     const float alpha = ep.alpha_dev ? ep.alpha * __ldg(ep.alpha_dev) : ep.alpha;
     const bool scaled = alpha != 1.0f;
 
@@ -513,13 +514,15 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
                 const float bias = (col < sh.N) ? __ldg(ep.colscale + col) : 0.f;
                 v[j] = rcp_approx(1.0f + ex2_approx(-(v[j] + bias) * 1.4426950408889634f));
               }
+            } else if constexpr (EPI == RGPT_EPI_ACT_FWD && !act_two_out) {
+              act_fwd32<ACT>(v);  // the post-activation is the only output
             }
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               *reinterpret_cast<uint4*>(stage_ptr(s0, lane, hf * 4 + j)) =
                   make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
                              pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
-            if constexpr (EPI == RGPT_EPI_ACT_FWD) {
+            if constexpr (act_two_out) {
               act_fwd32<ACT>(v);
 #pragma unroll
               for (int j = 0; j < 4; ++j)
@@ -533,7 +536,7 @@ __global__ void __launch_bounds__(gemm_threads(gemm_epi_warps(EPI)), 1)
           __syncwarp();
           if (lane == 0) {
             tma_store_3d(&tmD, s0, gn0, row0, b);
-            if constexpr (EPI == RGPT_EPI_ACT_FWD) tma_store_3d(&tmD2, s1, gn0, row0, b);
+            if constexpr (act_two_out) tma_store_3d(&tmD2, s1, gn0, row0, b);
             bulk_commit_g();
           }
           if (!dual) which ^= 1;
@@ -758,6 +761,7 @@ static int dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, c
         RGPT_GEMM_ACT_CASE(ACT_GELU)
         RGPT_GEMM_ACT_CASE(ACT_SILU)
         RGPT_GEMM_ACT_CASE(ACT_MISH)
+        RGPT_GEMM_ACT_CASE(ACT_SQRELU_POST)
         default:
           return fwd ? launch_gemm<BN, STAGES, A_MN, B_MN, RGPT_EPI_ACT_FWD, PAIR, ACT_NONE>(ta, tb, td, td2, sh,
                                                                                           ep, s, dev)
@@ -871,7 +875,8 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
   const int vec = out_f32 ? 4 : 8;
   if (!amx && (ldd % vec != 0 || (reinterpret_cast<uintptr_t>(D) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "output leading dim / pointer not 16-byte aligned");
-  if (epi == RGPT_EPI_ACT_FWD && (D2 == nullptr || ldd2 % 8 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
+  if (epi == RGPT_EPI_ACT_FWD && act != ACT_SQRELU_POST &&
+      (D2 == nullptr || ldd2 % 8 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "ACT_FWD needs an aligned second output");
   if (epi == RGPT_EPI_RESID_F32 && D2 != nullptr && (ldd2 % 4 != 0 || (reinterpret_cast<uintptr_t>(D2) & 15) != 0))
     return rgpt_set_error(RGPT_ERR_MISALIGNED, "RESID_F32 raw output must be 16-byte aligned");
@@ -961,7 +966,7 @@ static int gemm_entry(const void* A, int a_mn_major, long long lda, long long a_
     td = ta;  // never used by the argmax epilogue (only its descriptor is prefetched)
   else if ((st = make_tmap_3d(&td, D, ob, N, M, batch, ldd, d_bstride, obox, 32)))
     return st;
-  const bool has_d2 = (epi == RGPT_EPI_ACT_FWD) || (epi == RGPT_EPI_RESID_F32 && D2 != nullptr);
+  const bool has_d2 = (epi == RGPT_EPI_ACT_FWD && act != ACT_SQRELU_POST) || (epi == RGPT_EPI_RESID_F32 && D2 != nullptr);
   if (has_d2) {
     if ((st = make_tmap_3d(&td2, D2, ob, N, M, batch, ldd2, d2_bstride, obox, 32))) return st;
   } else {

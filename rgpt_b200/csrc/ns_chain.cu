@@ -40,17 +40,15 @@ int make_tmap_bf16_3d(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_
 
 namespace {
 
-constexpr int NS_BM = 128;   // output tile rows (= MMA M)
-constexpr int NS_BN = 128;   // output tile columns (= MMA N)
-constexpr int NS_BK = 64;    // k-block
+constexpr int NS_BK = 64;       // k-block
+constexpr int NS_PANEL = 128;   // rows of each operand panel one CTA stages per k-block (= the MMA M per CTA)
 constexpr int NS_STAGES = 5;
-constexpr int NS_EW = 8;     // epilogue warps: two per TMEM lane quadrant, one 64-column half of the tile each
+constexpr int NS_EW = 8;        // epilogue warps: two per TMEM lane quadrant, each taking half of the tile's columns
 constexpr int NS_THREADS = 64 + 32 * NS_EW;
-constexpr int NS_ACC = 4;    // TMEM accumulators of 128 columns
-constexpr uint32_t NS_A_BYTES = NS_BM * NS_BK * 2;
-constexpr uint32_t NS_B_BYTES = NS_BN * NS_BK * 2;
-constexpr uint32_t NS_EPI_STAGE = 4096;  // one warp's 32 rows x 128 bytes
-constexpr uint32_t NS_SMEM = NS_STAGES * (NS_A_BYTES + NS_B_BYTES) + NS_EW * NS_EPI_STAGE + 512 + 1024;
+constexpr uint32_t NS_PANEL_BYTES = NS_PANEL * NS_BK * 2;  // 16 KB
+constexpr uint32_t NS_EPI_STAGE = 4096;                     // one warp's 32 rows x 128 bytes
+// two staging buffers per epilogue warp (a warp stores two 64-column chunks of a 256-wide pair tile)
+constexpr uint32_t NS_SMEM = NS_STAGES * 2 * NS_PANEL_BYTES + NS_EW * 2 * NS_EPI_STAGE + 512 + 1024;
 
 struct NsMaps {
   CUtensorMap xk[2];   // X buffers as K-major operands: (inner xc, outer xr, batch), box (64, 128)
@@ -63,7 +61,7 @@ struct NsMaps {
 
 struct NsParams {
   int n, xr, xc, steps;
-  int mt, nt_r, nt_c;   // 128-row tiles of xr; 128-column tiles of xr and of xc
+  int mt, nt_r, nt_c;   // tile rows of xr; tile columns of xr and of xc (tiles of 128, or 256 for CTA pairs)
   int t01, t2;          // tiles of phases A/B and of X'
   long long units_per_step, num_units;
   float a, b, c;
@@ -127,7 +125,6 @@ __device__ __forceinline__ void ns_tma_store_3d(const CUtensorMap* map, const vo
                : "memory");
 }
 __device__ __forceinline__ void ns_bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void ns_bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void ns_bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ uint8_t* ns_stage_ptr(uint8_t* buf, int lane, int j) {
   return buf + lane * 128 + ((j ^ (lane & 7)) << 4);
@@ -151,33 +148,46 @@ __device__ __forceinline__ bool dep_wait(const unsigned* ctr, unsigned target, v
 
 }  // namespace
 
+// PAIR = false: one CTA per 128 x 128 tile. PAIR = true: a cluster of two CTAs per 256 x 256 tile
+// (tcgen05.mma.cta_group::2 issued by the even CTA): each CTA stages 128 rows of A and 128 rows (columns
+// of the output) of B per k-block, so each SM moves 32 KB of operands per 256 x 256 x 64 step instead of
+// per 128 x 128 x 64 step, and each CTA holds 128 rows x 256 columns of the accumulator in its TMEM.
+template <bool PAIR>
 __global__ void __launch_bounds__(NS_THREADS, 1)
     ns_chain_kernel(const __grid_constant__ NsMaps maps, const NsParams P) {
-  constexpr uint32_t IDESC_KK = make_idesc_bf16(NS_BM, NS_BN, 0, 0);
-  constexpr uint32_t IDESC_KM = make_idesc_bf16(NS_BM, NS_BN, 0, 1);
+  constexpr int TILE = PAIR ? 2 * NS_PANEL : NS_PANEL;  // output tile edge
+  constexpr int NUM_ACC = 512 / TILE;                   // TMEM accumulators of TILE columns
+  constexpr int COLS = TILE / 2;                        // columns of a tile one epilogue warp writes
+  constexpr uint32_t IDESC_KK = make_idesc_bf16(TILE, TILE, 0, 0);
+  constexpr uint32_t IDESC_KM = make_idesc_bf16(TILE, TILE, 0, 1);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + NS_STAGES * NS_A_BYTES;
-  uint8_t* sEpi = sB + NS_STAGES * NS_B_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + NS_EW * NS_EPI_STAGE);
+  uint8_t* sB = smem + NS_STAGES * NS_PANEL_BYTES;
+  uint8_t* sEpi = sB + NS_STAGES * NS_PANEL_BYTES;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sEpi + NS_EW * 2 * NS_EPI_STAGE);
   uint64_t* empty_bar = full_bar + NS_STAGES;
   uint64_t* tfull_bar = empty_bar + NS_STAGES;
-  uint64_t* tempty_bar = tfull_bar + NS_ACC;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + NS_ACC);
+  uint64_t* tempty_bar = tfull_bar + NUM_ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + NUM_ACC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int P3 = 3 * P.steps;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;  // 0 = the CTA that issues the pair's MMAs
+  const long long first_unit = PAIR ? (long long)cluster_id_x() : (long long)blockIdx.x;
+  const long long unit_step = PAIR ? (long long)cluster_count_x() : (long long)gridDim.x;
+  // every epilogue warp of every CTA working on a tile raises the tile's phase counter once
+  constexpr unsigned PUBS = PAIR ? 2 * NS_EW : NS_EW;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS_STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < NS_ACC; ++a) {
+    for (int a = 0; a < NUM_ACC; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], NS_EW);
+      mbar_init(&tempty_bar[a], PUBS);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -194,26 +204,35 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
     tma_prefetch_desc(&maps.db);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, NS_ACC * NS_BN);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, NUM_ACC * TILE);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, NUM_ACC * TILE);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   griddep_wait();  // the normalised X comes from the previous kernel; the counters were zeroed before
+  // the pair's shared barriers live in the even CTA (shared::cluster addresses)
+  const uint32_t full_bar0 = PAIR ? mapa_shared(smem_u32(full_bar), 0) : smem_u32(full_bar);
+  const uint32_t tempty_bar0 = PAIR ? mapa_shared(smem_u32(tempty_bar), 0) : smem_u32(tempty_bar);
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (both CTAs of a pair)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < P.num_units && ok; u += gridDim.x) {
+      for (long long u = first_unit; u < P.num_units && ok; u += unit_step) {
         const NsUnit U = ns_decode(u, P);
         if (U.phase > 0) {
           const int prev_kind = (U.kind + 2) % 3;
-          const unsigned target = (unsigned)((prev_kind == 2 ? P.t2 : P.t01) * NS_EW);
+          const unsigned target = (unsigned)((prev_kind == 2 ? P.t2 : P.t01) * PUBS);
           if (!dep_wait(P.ctr + (long long)U.m * P3 + U.phase - 1, target, abort_flag)) {
             ok = false;
             break;
@@ -226,27 +245,36 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         const int K = U.kind == 0 ? P.xc : P.xr;
         const int N = U.kind == 2 ? P.xc : P.xr;
         const int num_kb = (K + NS_BK - 1) / NS_BK;
-        const int a_row = U.mt * NS_BM, b_row = U.nt * NS_BN;
-        // the MN-major B arrives as 64-column sub-boxes; those wholly past N are not loaded; a diagonal
-        // tile of A or B loads its one panel (the MMA reads it as both operands)
+        const int a_row = U.mt * TILE + rank * NS_PANEL, b_row = U.nt * TILE + rank * NS_PANEL;
+        // A diagonal tile of A or B has the same rows as both operands: its one panel is loaded once and
+        // the MMA reads it as both. The MN-major B of X' arrives as 64-column sub-boxes; those wholly
+        // past N are not loaded.
         const bool diag = U.kind != 2 && U.mt == U.nt;
-        const int b_sub = U.kind == 2 ? max(0, min(2, (N - b_row + 63) / 64)) : (diag ? 0 : 1);
-        const uint32_t expect = NS_A_BYTES + (U.kind == 2 ? b_sub * (64 * NS_BK * 2) : (diag ? 0u : NS_B_BYTES));
+        auto b_subs = [&](int rk) {
+          return U.kind == 2 ? max(0, min(2, (N - (U.nt * TILE + rk * NS_PANEL) + 63) / 64)) : (diag ? 0 : 2);
+        };
+        const int b_sub = b_subs(rank);
+        const uint32_t expect = PAIR ? 2 * NS_PANEL_BYTES + (uint32_t)(b_subs(0) + b_subs(1)) * (64 * NS_BK * 2)
+                                     : NS_PANEL_BYTES + (uint32_t)b_sub * (64 * NS_BK * 2);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], expect);
+          // the pair's barrier lives in the even CTA, which posts the byte count of both CTAs' loads
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], expect);
           const int k0 = kb * NS_BK;
-          uint8_t* a_dst = sA + stage * NS_A_BYTES;
-          uint8_t* b_dst = sB + stage * NS_B_BYTES;
-          tma_load_3d(a_dst, mA, &full_bar[stage], k0, a_row, U.m);
+          uint8_t* a_dst = sA + stage * NS_PANEL_BYTES;
+          uint8_t* b_dst = sB + stage * NS_PANEL_BYTES;
+          auto load = [&](uint8_t* dst, const CUtensorMap* map, int c0, int c1) {
+            if constexpr (PAIR) tma_load_3d_pair(dst, map, full_bar0 + stage * 8, c0, c1, U.m);
+            else tma_load_3d(dst, map, &full_bar[stage], c0, c1, U.m);
+          };
+          load(a_dst, mA, k0, a_row);
           if (U.kind == 2) {
-            for (int i = 0; i < b_sub; ++i)
-              tma_load_3d(b_dst + i * (64 * NS_BK * 2), mB, &full_bar[stage], b_row + i * 64, k0, U.m);
+            for (int i = 0; i < b_sub; ++i) load(b_dst + i * (64 * NS_BK * 2), mB, b_row + i * 64, k0);
           } else if (!diag) {
-            tma_load_3d(b_dst, mB, &full_bar[stage], k0, b_row, U.m);
+            load(b_dst, mB, k0, b_row);
           }
           if (++stage == NS_STAGES) {
             stage = 0;
@@ -255,20 +283,30 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         }
       }
       griddep_launch();
-      if (!ok) {
-        for (int s = 0; s < NS_STAGES; ++s) mbar_wait(&full_bar[s], phase, nullptr);  // bounded drain
+      if (!ok && rank == 0) {
+        // bounded drain of the loads already issued (a pair's loads all complete on the even CTA's
+        // barriers; the final cluster barrier keeps the odd CTA alive meanwhile)
+        for (int s = 0; s < NS_STAGES; ++s) mbar_wait(&full_bar[s], phase, nullptr);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (long long u = blockIdx.x; u < P.num_units && ok; u += gridDim.x) {
+      auto commit = [&](uint64_t* bar) {  // completion signals go to both CTAs of a pair (same offsets)
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(bar), 0));
+          umma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (long long u = first_unit; u < P.num_units && ok; u += unit_step) {
         const NsUnit U = ns_decode(u, P);
         const int K = U.kind == 0 ? P.xc : P.xr;
         const int num_kb = (K + NS_BK - 1) / NS_BK;
@@ -276,31 +314,34 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
         const bool diag = !bmn && U.mt == U.nt;  // B operand = the A stage
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * NS_BN;
+        const uint32_t d_tmem = tmem_base + acc * TILE;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * NS_A_BYTES);
-          const uint32_t b_addr = diag ? a_addr : smem_u32(sB + stage * NS_B_BYTES);
+          const uint32_t a_addr = smem_u32(sA + stage * NS_PANEL_BYTES);
+          const uint32_t b_addr = diag ? a_addr : smem_u32(sB + stage * NS_PANEL_BYTES);
 #pragma unroll
           for (int kk = 0; kk < NS_BK / 16; ++kk) {
             const uint64_t adesc = make_sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bdesc = bmn ? make_sw128_desc(b_addr + kk * 2048, 64 * NS_BK * 2, 1024)
                                        : make_sw128_desc(b_addr + kk * 32, 16, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, bmn ? IDESC_KM : IDESC_KK, (kb > 0 || kk > 0) ? 1u : 0u);
+            const uint32_t idesc = bmn ? IDESC_KM : IDESC_KK;
+            const uint32_t accum = (kb > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (PAIR) umma_bf16_pair(d_tmem, adesc, bdesc, idesc, accum);
+            else umma_bf16(d_tmem, adesc, bdesc, idesc, accum);
           }
-          umma_commit(&empty_bar[stage]);
+          commit(&empty_bar[stage]);
           if (++stage == NS_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull_bar[acc]);
-        if (++acc == NS_ACC) {
+        commit(&tfull_bar[acc]);
+        if (++acc == NUM_ACC) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -309,27 +350,17 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps
-    const int quarter = warp & 3;          // TMEM lane quadrant: rows quarter*32 .. +31 of the tile
-    const int c0 = ((warp - 2) >> 2) * 64;  // this warp's 64 columns of the tile
-    uint8_t* sbuf = sEpi + (warp - 2) * NS_EPI_STAGE;
+    const int quarter = warp & 3;                // TMEM lane quadrant: rows quarter*32 .. +31 of this CTA's half
+    const int c0 = ((warp - 2) >> 2) * COLS;     // this warp's columns of the tile
+    uint8_t* sbuf = sEpi + (warp - 2) * 2 * NS_EPI_STAGE;
     int acc = 0;
     uint32_t acc_phase = 0;
-    // this warp's part of a tile is complete: its store has landed (and is ordered before the release)
-    auto publish = [&](unsigned* ctr) {
-      if (lane == 0) {
-        ns_bulk_wait_all();
-        fence_proxy_async_global();
-        red_release_add(ctr, 1u);
-      }
-      __syncwarp();
-    };
-    for (long long u = blockIdx.x; u < P.num_units; u += gridDim.x) {
+    for (long long u = first_unit; u < P.num_units; u += unit_step) {
       const NsUnit U = ns_decode(u, P);
       const int M = P.xr, N = U.kind == 2 ? P.xc : P.xr;
-      const int row0 = U.mt * NS_BM + quarter * 32;
+      const int row0 = U.mt * TILE + rank * NS_PANEL + quarter * 32;
       const int row = row0 + lane;
-      const int gn0 = U.nt * NS_BN + c0;
-      const bool live = row0 < M && gn0 < N;  // warp-uniform: this warp stores something
+      const int gn0 = U.nt * TILE + c0;
       // C of the polynomial: A (for B = b A + c A A) or the current X (for X' = a X + B X)
       const bool reads_c = U.kind != 0;
       const float alpha = U.kind == 1 ? P.c : 1.0f;
@@ -338,59 +369,65 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
       if (reads_c && U.phase > 0) {
         const int prev_kind = (U.kind + 2) % 3;
         const unsigned* dctr = P.ctr + (long long)U.m * P3 + U.phase - 1;
-        const unsigned target = (unsigned)((prev_kind == 2 ? P.t2 : P.t01) * NS_EW);
-        ok = dep_wait(dctr, target, abort_flag);
+        ok = dep_wait(dctr, (unsigned)((prev_kind == 2 ? P.t2 : P.t01) * PUBS), abort_flag);
       }
-      uint4 cc[8];
-      if (reads_c && live && ok) {
-        const __nv_bfloat16* cbase = U.kind == 1 ? P.abuf : P.x[U.step & 1];
-        const long long c_ld = U.kind == 1 ? P.a_ld : P.x_ld;
-        const long long c_bs = U.kind == 1 ? P.a_bs : P.x_bs;
-        const uint8_t* base = reinterpret_cast<const uint8_t*>(cbase) + ((long long)U.m * c_bs + (long long)row * c_ld) * 2;
+      const __nv_bfloat16* cbase = U.kind == 1 ? P.abuf : P.x[U.step & 1];
+      const long long c_ld = U.kind == 1 ? P.a_ld : P.x_ld;
+      const long long c_bs = U.kind == 1 ? P.a_bs : P.x_bs;
+      const uint8_t* crow = reinterpret_cast<const uint8_t*>(cbase) + ((long long)U.m * c_bs + (long long)row * c_ld) * 2;
+      // this row's C for a 64-column chunk: L1-bypassing 16-byte loads (bounds-checked at the edges)
+      auto c_load = [&](int gc, uint4 (&cc)[8]) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const int c = gn0 + 8 * j;
+          const int c = gc + 8 * j;
           if (row < M && c + 8 <= N) {
-            cc[j] = ld_cg_v4(base + (long long)c * 2);
+            cc[j] = ld_cg_v4(crow + (long long)c * 2);
           } else {
             uint32_t w[4] = {0u, 0u, 0u, 0u};
             if (row < M)
               for (int i = 0; i < 8; ++i)
                 if (c + i < N)
-                  w[i >> 1] |= (uint32_t)(*reinterpret_cast<const volatile unsigned short*>(base + (long long)(c + i) * 2))
+                  w[i >> 1] |= (uint32_t)(*reinterpret_cast<const volatile unsigned short*>(crow + (long long)(c + i) * 2))
                                << (16 * (i & 1));
             cc[j] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-      }
+      };
+      uint4 cc[8];
+      if (reads_c && ok && row0 < M && gn0 < N) c_load(gn0, cc);  // the first chunk's C, ahead of the accumulator
       int okw = ok ? 1 : 0;
       if (lane == 0 && okw) okw = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag) ? 1 : 0;
       okw = __shfl_sync(0xffffffffu, okw, 0) & (ok ? 1 : 0);
       if (!__all_sync(0xffffffffu, okw)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * NS_BN + c0;
-      uint32_t rr[2][32];
-      tmem_ld32(t_row, rr[0]);
-      tmem_ld32(t_row + 32, rr[1]);
-      tmem_wait_ld();
-      // the accumulator is free for the next tile's MMAs
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (++acc == NS_ACC) {
-        acc = 0;
-        acc_phase ^= 1u;
-      }
-      unsigned* my_ctr = P.ctr + (long long)U.m * P3 + U.phase;
-      if (live) {
-        const CUtensorMap* dmap = U.kind == 0 ? &maps.da : (U.kind == 1 ? &maps.db : &maps.dx[(U.step + 1) & 1]);
-        if (lane == 0) ns_bulk_wait_read0();  // the previous tile's store has read the staging buffer
-        __syncwarp();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TILE + c0;
+      const CUtensorMap* dmap = U.kind == 0 ? &maps.da : (U.kind == 1 ? &maps.db : &maps.dx[(U.step + 1) & 1]);
+      bool stored = false;
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
+      for (int ch = 0; ch < COLS / 64; ++ch) {
+        const int gc = gn0 + ch * 64;
+        const bool live = row0 < M && gc < N;  // warp-uniform: this warp stores something of this chunk
+        uint4 cn[8];
+        if (reads_c && live && ch + 1 < COLS / 64 && gc + 64 < N) c_load(gc + 64, cn);  // the next chunk's C
+        uint8_t* buf = sbuf + ch * NS_EPI_STAGE;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {  // two 32-column halves of the 64-column chunk
+          uint32_t r[32];
+          tmem_ld32(t_row + ch * 64 + hf * 32, r);
+          tmem_wait_ld();
+          if (ch == COLS / 64 - 1 && hf == 1) {
+            // every TMEM read of this warp is done: the accumulator is free for the next tile's MMAs
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (PAIR) mbar_arrive_cluster(tempty_bar0 + acc * 8);
+              else mbar_arrive(&tempty_bar[acc]);
+            }
+          }
+          if (!live) continue;
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rr[hf][j]) * alpha;
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
           if (reads_c) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
@@ -406,37 +443,112 @@ __global__ void __launch_bounds__(NS_THREADS, 1)
           }
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint4*>(ns_stage_ptr(sbuf, lane, hf * 4 + j)) =
+            *reinterpret_cast<uint4*>(ns_stage_ptr(buf, lane, hf * 4 + j)) =
                 make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          ns_tma_store_3d(dmap, sbuf, gn0, row0, U.m);
-          ns_bulk_commit();
+        if (live) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            ns_tma_store_3d(dmap, buf, gc, row0, U.m);
+            ns_bulk_commit();
+          }
+          stored = true;
         }
-        publish(my_ctr);
-      } else {
-        // nothing to store: this warp's share of the tile is complete at once
-        if (lane == 0) red_release_add(my_ctr, 1u);
-        __syncwarp();
+        if (ch + 1 < COLS / 64) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cc[j] = cn[j];
+        }
       }
+      if (++acc == NUM_ACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+      // this warp's part of the tile is complete once its stores have landed (ordered before the release)
+      unsigned* my_ctr = P.ctr + (long long)U.m * P3 + U.phase;
+      if (lane == 0) {
+        if (stored) {
+          ns_bulk_wait_all();
+          fence_proxy_async_global();
+        }
+        red_release_add(my_ctr, 1u);
+      }
+      __syncwarp();
     }
     if (lane == 0) ns_bulk_wait_all();
     __syncwarp();
   }
 
   __syncthreads();
+  if constexpr (PAIR) cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still works
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, NS_ACC * NS_BN);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, NUM_ACC * TILE);
+    else tmem_dealloc(tmem_base, NUM_ACC * TILE);
   }
 }
 
 }  // namespace rgpt
 
 using namespace rgpt;
+
+// One persistent launch of ns_chain_kernel<PAIR>. Its CTAs wait on one another, so the launch is
+// cooperative: all of them are resident at once (one CTA per SM at this shared-memory size), whatever
+// else runs on the GPU. Grid: one CTA (or CTA pair) per SM (pair of SMs), at most one per unit.
+template <bool PAIR>
+static int launch_ns_chain(const NsMaps& maps, const NsParams& P, cudaStream_t s, int dev) {
+  auto kern = ns_chain_kernel<PAIR>;
+  static bool attr_set[64] = {false};
+  static int max_groups[64] = {0};  // co-resident CTAs (CTA pairs)
+  const int d = dev < 64 ? dev : 63;
+  if (!attr_set[d]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)NS_SMEM) != cudaSuccess)
+      return rgpt_check_launch("ns_chain smem attribute");
+    if constexpr (PAIR) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = dim3(2 * rgpt_num_sms(dev), 1, 1);
+      q.blockDim = dim3(NS_THREADS, 1, 1);
+      q.dynamicSmemBytes = NS_SMEM;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n < 1)
+        return rgpt_set_error(RGPT_ERR_INTERNAL, "no ns_chain CTA pair fits on this GPU (%s)",
+                              cudaGetErrorString(cudaGetLastError()));
+      max_groups[d] = n;
+    } else {
+      int per_sm = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NS_THREADS, NS_SMEM) != cudaSuccess ||
+          per_sm < 1)
+        return rgpt_set_error(RGPT_ERR_INTERNAL, "ns_chain_kernel does not fit on an SM");
+      max_groups[d] = per_sm * rgpt_num_sms(dev);
+    }
+    attr_set[d] = true;
+  }
+  const int groups = P.num_units < max_groups[d] ? (int)P.num_units : max_groups[d];
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(PAIR ? 2 * groups : groups);
+  cfg.blockDim = dim3(NS_THREADS);
+  cfg.dynamicSmemBytes = NS_SMEM;
+  cfg.stream = s;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  at[1].id = cudaLaunchAttributeClusterDimension;
+  at[1].val.clusterDim.x = 2;
+  at[1].val.clusterDim.y = 1;
+  at[1].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = PAIR ? 2 : 1;
+  cudaLaunchKernelEx(&cfg, kern, maps, P);
+  return rgpt_check_launch(PAIR ? "ns_chain_kernel (CTA pairs)" : "ns_chain_kernel");
+}
 
 extern "C" int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr, int xc, long long x_ld,
                              long long x_bstride, long long a_ld, long long a_bstride, int steps, float a, float b,
@@ -451,15 +563,24 @@ extern "C" int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr,
   if (counters == nullptr) return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_chain needs its counters buffer");
   if (x_ld < xc || a_ld < xr || x_bstride < x_ld * xr || a_bstride < a_ld * xr)
     return rgpt_set_error(RGPT_ERR_BAD_SHAPE, "ns_chain: strides too small");
+  // Batches of matrices taller than one 128-row panel run on CTA pairs (256 x 256 tiles: half the operand
+  // bytes per SM and MMA); a few matrices (fewer than 32 pair tiles in the A = X X^T phase, e.g. the
+  // single-matrix step) keep single-CTA 128 x 128 tiles, whose 4x more units per phase spread each
+  // phase over more SMs (measured: 16 x [512, 2048] 303 -> 281 us and 32 x [512, 512] 209 -> 199 us on
+  // pairs, but 1 x [512, 2048] 154 -> 197 us).
+  const long long pair_tiles = (long long)n * ((xr + 2 * NS_PANEL - 1) / (2 * NS_PANEL)) *
+                               ((xr + 2 * NS_PANEL - 1) / (2 * NS_PANEL));
+  const bool pair = xr > NS_PANEL && pair_tiles >= 32;
+  const int tile = pair ? 2 * NS_PANEL : NS_PANEL;
   NsMaps maps;
   const void* xs[2] = {X, X2};
   for (int i = 0; i < 2; ++i) {
-    if ((st = make_tmap_bf16_3d(&maps.xk[i], xs[i], xc, xr, n, x_ld, x_bstride, NS_BK, NS_BM))) return st;
+    if ((st = make_tmap_bf16_3d(&maps.xk[i], xs[i], xc, xr, n, x_ld, x_bstride, NS_BK, NS_PANEL))) return st;
     if ((st = make_tmap_bf16_3d(&maps.xmn[i], xs[i], xc, xr, n, x_ld, x_bstride, 64, NS_BK))) return st;
     if ((st = make_tmap_bf16_3d(&maps.dx[i], xs[i], xc, xr, n, x_ld, x_bstride, 64, 32))) return st;
   }
-  if ((st = make_tmap_bf16_3d(&maps.ak, A, xr, xr, n, a_ld, a_bstride, NS_BK, NS_BM))) return st;
-  if ((st = make_tmap_bf16_3d(&maps.bk, B, xr, xr, n, a_ld, a_bstride, NS_BK, NS_BM))) return st;
+  if ((st = make_tmap_bf16_3d(&maps.ak, A, xr, xr, n, a_ld, a_bstride, NS_BK, NS_PANEL))) return st;
+  if ((st = make_tmap_bf16_3d(&maps.bk, B, xr, xr, n, a_ld, a_bstride, NS_BK, NS_PANEL))) return st;
   if ((st = make_tmap_bf16_3d(&maps.da, A, xr, xr, n, a_ld, a_bstride, 64, 32))) return st;
   if ((st = make_tmap_bf16_3d(&maps.db, B, xr, xr, n, a_ld, a_bstride, 64, 32))) return st;
   NsParams P;
@@ -467,9 +588,9 @@ extern "C" int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr,
   P.xr = xr;
   P.xc = xc;
   P.steps = steps;
-  P.mt = (xr + NS_BM - 1) / NS_BM;
-  P.nt_r = (xr + NS_BN - 1) / NS_BN;
-  P.nt_c = (xc + NS_BN - 1) / NS_BN;
+  P.mt = (xr + tile - 1) / tile;
+  P.nt_r = P.mt;
+  P.nt_c = (xc + tile - 1) / tile;
   P.t01 = P.mt * P.nt_r;
   P.t2 = P.mt * P.nt_c;
   P.units_per_step = (long long)n * (2LL * P.t01 + P.t2);
@@ -489,34 +610,5 @@ extern "C" int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr,
   // counters start at zero (a memset node when captured)
   if (cudaMemsetAsync(counters, 0, sizeof(unsigned) * (size_t)n * 3 * steps, s) != cudaSuccess)
     return rgpt_check_launch("ns_chain counter reset");
-  static bool attr_set[64] = {false};
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(ns_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)NS_SMEM) != cudaSuccess)
-      return rgpt_check_launch("ns_chain smem attribute");
-    attr_set[dev] = true;
-  }
-  // The CTAs wait on one another, so the launch is cooperative: all of them are resident at once (one
-  // per SM at this shared-memory size), whatever else runs on the GPU.
-  static int max_blocks[64] = {0};
-  if (dev < 64 && max_blocks[dev] == 0) {
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ns_chain_kernel, NS_THREADS, NS_SMEM) != cudaSuccess ||
-        per_sm < 1)
-      return rgpt_set_error(RGPT_ERR_INTERNAL, "ns_chain_kernel does not fit on an SM");
-    max_blocks[dev] = per_sm * rgpt_num_sms(dev);
-  }
-  const int cap = dev < 64 ? max_blocks[dev] : rgpt_num_sms(dev);
-  const int grid = P.num_units < cap ? (int)P.num_units : cap;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(NS_THREADS);
-  cfg.dynamicSmemBytes = NS_SMEM;
-  cfg.stream = s;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeCooperative;
-  at[0].val.cooperative = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, ns_chain_kernel, maps, P);
-  return rgpt_check_launch("ns_chain_kernel");
+  return pair ? launch_ns_chain<true>(maps, P, s, dev) : launch_ns_chain<false>(maps, P, s, dev);
 }

@@ -120,7 +120,8 @@ class _Acts:
         self.lse = [e(B, H, T, dt=f32) for _ in range(napp)]
         self.h = [e(M, d, dt=f32) for _ in range(napp)]
         self.hn2 = [e(M, d) for _ in range(napp)]
-        self.pre = [e(M, F) for _ in range(napp)]
+        # squared ReLU keeps only the post-activation (its derivative is 2 sqrt(post)); the others the pre too
+        self.pre = [e(M, F) for _ in range(napp)] if eng.act != nv.ACT_SQRELU else [None] * napp
         self.post = [e(M, F) for _ in range(napp)]
         self.a_raw = [e(M, d, dt=f32) for _ in range(napp)] if eng.ls else [None] * napp
         self.f_raw = [e(M, d, dt=f32) for _ in range(napp)] if eng.ls else [None] * napp
@@ -445,7 +446,10 @@ class Engine:
         kind, eps, alpha, w, temp = self._resid_norm(blk, "ff_norm")
         nv.rownorm_fwd(A.h[app], A.hn2[app], kind, eps, w=w, temp=1.0,
                        alpha=alpha)
-        nv.gemm(A.hn2[app], W["w1"], A.pre[app], epi=nv.EPI_ACT_FWD, act=self.act, out2=A.post[app])
+        if self.act == nv.ACT_SQRELU:  # post = relu(h W1^T)^2 only (no pre-activation written)
+            nv.gemm(A.hn2[app], W["w1"], A.post[app], epi=nv.EPI_ACT_FWD, act=nv.ACT_SQRELU_POST)
+        else:
+            nv.gemm(A.hn2[app], W["w1"], A.pre[app], epi=nv.EPI_ACT_FWD, act=self.act, out2=A.post[app])
         nv.gemm(A.post[app], W["w2"], A.x[app + 1], epi=nv.EPI_RESID_F32, c=A.h[app],
                 colscale=blk.ff_layer_scale if self.ls else None, out2=A.f_raw[app],
                 drop=self._drop(A, "ff_out", app))
@@ -532,7 +536,10 @@ class Engine:
         d, H, B, T, M = self.d, self.H, A.B, A.T, A.M
         pre = f"layers.{li}."
         # ---------------- FFN
-        nv.gemm(A.gb, W["w2"].t(), A.dpre, epi=nv.EPI_ACT_BWD, act=self.act, c=A.pre[app])
+        if self.act == nv.ACT_SQRELU:  # act'(pre) = 2 sqrt(post)
+            nv.gemm(A.gb, W["w2"].t(), A.dpre, epi=nv.EPI_ACT_BWD, act=nv.ACT_SQRELU_POST, c=A.post[app])
+        else:
+            nv.gemm(A.gb, W["w2"].t(), A.dpre, epi=nv.EPI_ACT_BWD, act=self.act, c=A.pre[app])
         nv.gemm(A.gb.t(), A.post[app].t(), G[pre + "ff.fc2.weight"], epi=nv.EPI_ACCUM_F32, splitk=0)
         nv.gemm(A.dpre, W["w1"].t(), A.dy32, epi=nv.EPI_STORE_F32)
         nv.gemm(A.dpre.t(), A.hn2[app].t(), G[pre + "ff.fc1.weight"], epi=nv.EPI_ACCUM_F32, splitk=0)

@@ -22,6 +22,8 @@ EPI_POLY_F32 = 8
 EPI_ARGMAX_BF16 = 9
 
 ACTIVATIONS = {"none": 0, "identity": 0, "squared_relu": 1, "gelu": 2, "silu": 3, "mish": 4}
+ACT_SQRELU = 1
+ACT_SQRELU_POST = 5  # squared ReLU with the post-activation as the only forward output and the backward's C
 
 
 def act_id(name: str) -> int:

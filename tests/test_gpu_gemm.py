@@ -100,6 +100,32 @@ def test_gemm_act_fwd_bwd(cuda, act):
     assert rel_err(dpre, ref) < 2e-2
 
 
+@pytest.mark.parametrize("shape", [(512, 1024, 256), (16384, 2048, 512), (16384, 2048, 1024)],
+                         ids=["tile128", "fc1_tile256", "cta_pair"])
+def test_gemm_squared_relu_post_only(cuda, shape):
+    # ACT_SQRELU_POST: the forward writes only post = relu(acc)^2 (equal, bit for bit, to the two-output
+    # epilogue's post), and the backward forms act'(pre) = 2 sqrt(post) from it, within bf16 rounding of
+    # 2 relu(pre). Shapes: 128-wide tiles, the model's fc1 (128 x 256 tiles) and a long-K GEMM on CTA pairs.
+    M, N, K = shape
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(M, K, device=cuda, generator=g).bfloat16()
+    w = (torch.randn(N, K, device=cuda, generator=g) * 0.05).bfloat16()
+    pre = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    post = torch.empty_like(pre)
+    nv.gemm(x, w, pre, epi=nv.EPI_ACT_FWD, act=nv.ACT_SQRELU, out2=post)
+    post_only = torch.full_like(pre, 7.0)
+    nv.gemm(x, w, post_only, epi=nv.EPI_ACT_FWD, act=nv.ACT_SQRELU_POST)
+    assert torch.equal(post_only, post)
+    dy = torch.randn(M, 128, device=cuda, generator=g).bfloat16()
+    w2 = (torch.randn(N, 128, device=cuda, generator=g) * 0.05).bfloat16()
+    d_pre, d_post = torch.empty_like(pre), torch.empty_like(pre)
+    nv.gemm(dy, w2, d_pre, epi=nv.EPI_ACT_BWD, act=nv.ACT_SQRELU, c=pre)
+    nv.gemm(dy, w2, d_post, epi=nv.EPI_ACT_BWD, act=nv.ACT_SQRELU_POST, c=post_only)
+    ref = (dy.float() @ w2.float().t()) * 2.0 * (x.float() @ w.float().t()).clamp_min(0)
+    assert rel_err(d_post, ref) < 1e-2
+    assert rel_err(d_post, d_pre.float()) < 1e-2
+
+
 @pytest.mark.parametrize("act", ["squared_relu", "gelu", "silu", "mish"])
 def test_gemm_act_epilogue_elementwise_wide_range(cuda, act):
     # Every pre-activation value in [-30, 30] (an identity weight passes A through exactly), so the

@@ -6,7 +6,8 @@ fused polynomial epilogues, so their results agree to within bf16 rounding of th
 Against the oracle's bf16 restatement of optimizer.py:18-45 (which rounds after every op) the bound is
 the 5e-2 of the other Newton-Schulz tests. Shapes cover every shape class of the training step and the
 single-matrix Muon step, including a matrix narrower than one 128-wide tile and a batch whose unit
-count is far below the SM count.
+count is far below the SM count, on both tile schemes (single-CTA 128 x 128 tiles and CTA-pair 256 x 256
+tiles, the latter also with padded rows and columns).
 """
 import pytest
 import torch
@@ -34,7 +35,9 @@ def _ws(G, dev):
     return ws, xr, xc
 
 
-@pytest.mark.parametrize("shape", [(32, 512, 512), (16, 512, 2048), (8, 64, 64), (1, 2048, 512), (3, 200, 328)])
+# CTA-pair tiles: (32, 512, 512), (16, 512, 2048) and the padded (32, 200, 328); single-CTA tiles: the rest
+@pytest.mark.parametrize("shape", [(32, 512, 512), (16, 512, 2048), (8, 64, 64), (1, 2048, 512), (3, 200, 328),
+                                   (32, 200, 328)])
 def test_chain_matches_batched_and_oracle(cuda, shape):
     g = torch.Generator().manual_seed(sum(shape))
     G = torch.randn(*shape, generator=g) * 1e-2
@@ -51,10 +54,11 @@ def test_chain_matches_batched_and_oracle(cuda, shape):
     assert rel(out_c, ref.float()) < 5e-2, rel(out_c, ref.float())
 
 
-def test_chain_twice_in_a_row_and_padding_untouched(cuda):
+@pytest.mark.parametrize("n", [4, 32], ids=["single_cta_tiles", "cta_pair_tiles"])
+def test_chain_twice_in_a_row_and_padding_untouched(cuda, n):
     """Two calls on the same workspace (the counters are re-zeroed each call); the padded rows/columns
     of the buffers stay zero."""
-    G = torch.randn(4, 196, 324, generator=torch.Generator().manual_seed(3)) * 1e-2
+    G = torch.randn(n, 196, 324, generator=torch.Generator().manual_seed(3)) * 1e-2
     ws, xr, xc = _ws(G, cuda)
     first = newton_schulz_batched(ws, 5, impl="chain").clone()
     ws2, _, _ = _ws(G, cuda)
