@@ -3,8 +3,9 @@
 //
 // The batched-GEMM path launches the 3 * steps GEMMs one after another; each is one or two waves of
 // small tiles with its own pipeline fill and drain, and the chain is a string of dependent launches.
-// Here the 3 * steps GEMMs are phases of one kernel. Every (phase, matrix, 128 x 128 output tile) is a
-// work unit; units are dealt round-robin to persistent CTAs (at most one per SM, all resident) in
+// Here the 3 * steps GEMMs are phases of one kernel. Every (phase, matrix, output tile) is a work unit
+// (128 x 128 tiles on single CTAs, or 256 x 256 tiles on CTA pairs, see ns_chain_kernel); units are
+// dealt round-robin to persistent CTAs or CTA pairs (at most one CTA per SM, all resident) in
 // phase-major order, and a unit only waits for the previous phase of ITS OWN matrix: a per (matrix,
 // phase) counter that the epilogue warps raise once their part of a tile has landed in global memory.
 // So while some matrices are still in phase p, SMs already run phase p + 1 of others: no grid-wide
@@ -15,7 +16,7 @@
 //
 // CTA: 320 threads. Warp 0 TMA producer (waits for the unit's dependency, then streams 64-deep
 // k-blocks of A and B into a 5-stage ring), warp 1 TMEM allocation + tcgen05.mma issue (one elected
-// thread), warps 2-9 epilogue, two per TMEM lane quadrant, each taking one 64-column half of the tile
+// thread), warps 2-9 epilogue, two per TMEM lane quadrant, each taking one half of the tile's columns
 // (TMEM -> registers, + beta * C for B and X', bf16 -> swizzled smem -> TMA bulk store; then the
 // completion counter). A warp publishes its part of a tile as soon as the store has landed: the phase
 // chain is latency-bound, so a deferred publish (to keep the store in flight under the next tile's
