@@ -30,6 +30,7 @@
 // C (A or X) with L1-bypassing loads after its own acquire: a persistent CTA's L1 may hold lines of a
 // buffer that an earlier phase rewrote.
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "rgpt.h"
@@ -571,7 +572,13 @@ extern "C" int rgpt_ns_chain(void* X, void* X2, void* A, void* B, int n, int xr,
   // pairs, but 1 x [512, 2048] 154 -> 197 us).
   const long long pair_tiles = (long long)n * ((xr + 2 * NS_PANEL - 1) / (2 * NS_PANEL)) *
                                ((xr + 2 * NS_PANEL - 1) / (2 * NS_PANEL));
-  const bool pair = xr > NS_PANEL && pair_tiles >= 32;
+  // RGPT_NS_PAIRS=0 in the environment keeps every class on single-CTA tiles (ncu, for one, cannot replay
+  // the cooperative cluster launch of the pair kernel)
+  static const bool pairs_allowed = [] {
+    const char* v = getenv("RGPT_NS_PAIRS");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  const bool pair = pairs_allowed && xr > NS_PANEL && pair_tiles >= 32;
   const int tile = pair ? 2 * NS_PANEL : NS_PANEL;
   NsMaps maps;
   const void* xs[2] = {X, X2};
